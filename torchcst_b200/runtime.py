@@ -1,0 +1,188 @@
+"""Thin host wrappers over the C ABI: shapes, workspaces and stream plumbing.
+
+Tensors are allocated with torch (device memory and the current CUDA stream are
+torch's); every computation happens in the native sm_100a library. There is no
+CPU path: calling these with CPU tensors raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .spec import AxisDecl, KernelSpec, PolarRadius, RationalRadius, _f32
+
+
+def pad4(n: int) -> int:
+    return (int(n) + 3) & ~3
+
+
+def _vp(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device=None):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and (not t.is_cuda):
+            raise ValueError("the B200 backend requires CUDA tensors (it has no CPU fallback)")
+
+
+def native_axis(a: AxisDecl) -> N.Axis:
+    return N.Axis(a.site_count, a.base_tile_sites, a.merge_factor, a.modes, float(a.spacing),
+                  float(a.origin))
+
+
+def native_coordinates(kernel: KernelSpec) -> N.Coordinates:
+    c = kernel.coordinates
+    out = N.Coordinates()
+    if isinstance(c, RationalRadius):
+        out.kind = N.TCST_RATIONAL
+        out.amplitude_max = _f32(c.amplitude_max)
+        out.radius_min = _f32(c.radius_min)
+        out.radius_birth = _f32(c.radius_birth)
+        out.radius_max = _f32(c.radius_max)
+    elif isinstance(c, PolarRadius):
+        out.kind = N.TCST_POLAR
+        out.amplitude_max = _f32(c.amplitude_max)
+        out.w_c = _f32(c.w_c)
+        out.kappa = _f32(c.kappa)
+        out.lower_kappa = _f32(c.lower_kappa)
+        out.upper_decay_power = _f32(c.upper_decay_power)
+        ob, ib = c.output_bounds, c.input_bounds
+        for i, v in enumerate((ob.minimum, ob.birth, ob.maximum, ob.upper_floor)):
+            out.out_bounds[i] = _f32(v)
+        for i, v in enumerate((ib.minimum, ib.birth, ib.maximum, ib.upper_floor)):
+            out.in_bounds[i] = _f32(v)
+    else:
+        raise TypeError("unsupported coordinates")
+    return out
+
+
+@dataclass
+class Plan:
+    """Static native description of one layer."""
+
+    out_axis: N.Axis
+    in_axis: N.Axis
+    coords: N.Coordinates
+    n_out: int
+    n_in: int
+    kind: int
+
+    @classmethod
+    def make(cls, axes, kernel):
+        oa, ia = axes
+        return cls(native_axis(oa), native_axis(ia), native_coordinates(kernel), oa.site_count,
+                   ia.site_count, native_coordinates(kernel).kind)
+
+    def table_bytes(self, atoms: int) -> int:
+        return int(N.load().tcst_atom_table_bytes(atoms, ctypes.byref(self.out_axis),
+                                                   ctypes.byref(self.in_axis)))
+
+
+class Workspace:
+    """Persistent per-device scratch of one layer: the int64 weight accumulator
+    (kept all-zero between calls by the native finalize pass) and the status word."""
+
+    def __init__(self, plan: Plan, device):
+        self.device = torch.device(device)
+        self.acc = torch.zeros(plan.n_out * plan.n_in, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+
+def decode_route(plan: Plan, p, status, *, owner_keys=None, routing=None):
+    require_cuda(p)
+    atoms = p.shape[0]
+    table = torch.empty(max(plan.table_bytes(atoms) // 4, 1), dtype=torch.float32, device=p.device)
+    N.call("tcst_decode_route", _vp(p), atoms, ctypes.byref(plan.out_axis),
+           ctypes.byref(plan.in_axis), ctypes.byref(plan.coords), _vp(table), _vp(owner_keys),
+           _vp(routing), _vp(status), _stream(p.device))
+    return table
+
+
+def assemble_weight(plan: Plan, table, atoms, acc, *, dense=False, split=True):
+    dev = acc.device
+    ld = pad4(plan.n_in)
+    w = torch.empty(plan.n_out, plan.n_in, dtype=torch.float32, device=dev) if dense else None
+    hi = lo = None
+    if split:
+        hi = torch.empty(plan.n_out, ld, dtype=torch.float32, device=dev)
+        lo = torch.empty(plan.n_out, ld, dtype=torch.float32, device=dev)
+    N.call("tcst_assemble_weight", _vp(table), atoms, ctypes.byref(plan.out_axis),
+           ctypes.byref(plan.in_axis), _vp(acc), _vp(w), plan.n_in, _vp(hi), _vp(lo), ld,
+           _stream(dev))
+    return w, hi, lo, ld
+
+
+def split_tf32(x):
+    """Two-term TF32 split of a 2-D float32 CUDA tensor into padded planes."""
+    require_cuda(x)
+    rows, cols = x.shape
+    ld = pad4(cols)
+    hi = torch.empty(rows, ld, dtype=torch.float32, device=x.device)
+    lo = torch.empty(rows, ld, dtype=torch.float32, device=x.device)
+    if rows * cols == 0:
+        return hi, lo, ld
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    N.call("tcst_split_tf32", _vp(x), rows, cols, x.stride(0), _vp(hi), _vp(lo), ld,
+           _stream(x.device))
+    return hi, lo, ld
+
+
+def gemm(M, N_, K, a, lda, a_mn, b, ldb, b_mn, c, ldc, status, *, split_k=1, split_stride=0):
+    """C[s] = A B^T over a K slice s (three-product TF32 split on tcgen05)."""
+    N.call("tcst_gemm_tf32x3", M, N_, K, _vp(a[0]), _vp(a[1]), lda, int(a_mn), _vp(b[0]),
+           _vp(b[1]), ldb, int(b_mn), _vp(c), ldc, split_k, split_stride, _vp(status),
+           _stream(c.device))
+
+
+def pullback(plan: Plan, table, atoms, g, ldg, split, split_stride, device):
+    grad = torch.empty(atoms, 4, dtype=torch.float32, device=device)
+    N.call("tcst_pullback", _vp(table), atoms, ctypes.byref(plan.out_axis),
+           ctypes.byref(plan.in_axis), _vp(g), ldg, split, split_stride, _vp(grad),
+           _stream(device))
+    return grad
+
+
+def weight_split_k(plan: Plan, rows: int, sm_count: int = 148) -> int:
+    """Split-K factor of the dW = dY^T X GEMM: enough CTAs to cover the SMs."""
+    tiles = -(-plan.n_out // 128) * -(-plan.n_in // 256)
+    kblocks = max(1, -(-rows // 32))
+    return int(max(1, min(8, kblocks, sm_count // max(tiles, 1))))
+
+
+def atom_energies(plan: Plan, table, atoms, device):
+    e = torch.empty(atoms, dtype=torch.float64, device=device)
+    N.call("tcst_atom_energies", _vp(table), atoms, ctypes.byref(plan.out_axis),
+           ctypes.byref(plan.in_axis), _vp(e), _stream(device))
+    return e
+
+
+def status_error(code: int) -> str | None:
+    if code == 0:
+        return None
+    parts = []
+    if code & N.STATUS_NONFINITE:
+        parts.append("atom parameters must be finite")
+    if code & N.STATUS_BOUNDS:
+        parts.append("rational radius requires finite rows, q in [0,1] and bounded amplitude")
+    if code & N.STATUS_RADIUS:
+        parts.append("radius must lie in (0, chart period/2]")
+    if code & N.STATUS_TIMEOUT:
+        parts.append("a bounded device wait expired")
+    if code & N.STATUS_FOOTPRINT:
+        parts.append("footprint exceeds this build's limits")
+    return "; ".join(parts)
+
+
+def f32(x) -> float:
+    return float(np.float32(x))
