@@ -1,0 +1,375 @@
+"""Benchmark: CSTLinear training steps/s on B200 (config 2 of the reference north star).
+
+Workload (N=1): CSTLinear 1024 -> 1024, flat-torus grids, 65,536 atoms (64N),
+Chebyshev M=8 cell masses, rational radius (radius_max 512, q=0), He init
+(kaiming_normal_, relu, q=0, seed 0), X ~ N(0,1) [4096, 1024], target ~ N(0,1),
+MSE loss, CSTAdamW lr=1e-3 with field_lrs amplitude=2.4e-3, radius_fraction=9.6e-3.
+One step = forward, backward (dX and atom gradients) and one optimizer step.
+
+``value``: steps/s with inputs resident in HBM, timed with CUDA events over
+exactly --steps steps (inputs rotate through buffers larger than L2).
+``e2e``: the same steps through the drop-in API (layer(x), loss.backward(),
+opt.step()) with pinned host inputs copied in and the loss read back every step.
+Multi-GPU (torchrun): data parallel, each rank runs the full config-2 step on
+its own 4096 rows with replicated atoms and an NCCL all-reduce of the atom
+gradient; ``value`` is the aggregate (rows/s / 4096).
+``--impl reference``: the reference's factored CPU algorithm (the oracle port)
+on the host cores over a bounded row sample: row-independent phases plus the
+row-proportional phases scaled to 4096 rows.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "train steps/s (fwd+bwd+CSTAdamW) at N=1024, 64N atoms"
+CONFIG = {"workload": "config2: CSTLinear 1024->1024, 65536 atoms, rational radius "
+                      "radius_max=512 q=0 He init, M=8 cell masses, MSE, CSTAdamW field_lrs",
+          "global_batch": 4096, "n_in": 1024, "n_out": 1024, "atoms": 65536}
+ROWS, N_IO, ATOMS = 4096, 1024, 65536
+FIELD_LRS = {"amplitude": 2.4e-3, "radius_fraction": 9.6e-3}
+
+
+def dist_info():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9
+                          for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(sm)}
+
+
+def build_layer(device):
+    import torch
+    from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
+    from torchcst_b200.init import kaiming_normal_
+    torch.manual_seed(0)
+    grid = chart_presets.regular_grid(N_IO, geometry="flat_torus")
+    layer = CSTLinear(charts=(grid, grid), atoms=ATOMS, device=device, validate="off",
+                      kernel=kernels.product(kernels.cell_mass(ChebyshevSpec(modes=8)),
+                                             coordinates=kernels.rational_radius(
+                                                 radius_max=512.0, radius_fraction=0.0)))
+    report = kaiming_normal_(layer, nonlinearity="relu", q=0.0)
+    opt = CSTAdamW(layer.parameters(), model=layer, lr=1e-3, field_lrs=FIELD_LRS)
+    return layer, opt, report
+
+
+def cpu_reference(steps, warmup, sample_rows=512, log=None):
+    """Time the reference factored algorithm (oracle port) on the host cores.
+
+    Each step runs the whole algorithm on ``sample_rows`` of the 4096 rows and
+    times its phases; the config-2 step time is the row-independent part
+    (decode, factor build, factor chain, optimizer) plus the row-proportional
+    part (six GEMMs, loss) scaled to 4096 rows.
+    """
+    import numpy as np
+    from oracle import cst_oracle as O
+    rng = np.random.default_rng(0)
+    # He-initialized atoms of the same config (reference-generated fixture).
+    d = np.load(os.path.join(ROOT, "tests", "golden", "config2.npz"))
+    p = d["p0"].copy()
+    oa, ia, spec = O.Axis(N_IO), O.Axis(N_IO), O.Rational(radius_max=512.0)
+    state = O.AdamState(0, np.zeros_like(p), np.zeros_like(p))
+    x = rng.standard_normal((sample_rows, N_IO), dtype=np.float32)
+    t = rng.standard_normal((sample_rows, N_IO), dtype=np.float32)
+    ratios = O.field_ratios(spec, FIELD_LRS, 1e-3)
+    est = []
+    for i in range(warmup + steps):
+        c0 = time.perf_counter()
+        lay = O.decode(oa, ia, spec, p)
+        phi_in, phi_out = O.factors32(lay)
+        c1 = time.perf_counter()
+        atom_values = x @ phi_in
+        y = atom_values @ phi_out.T
+        dy = ((y - t) * np.float32(2.0 / (ROWS * N_IO))).astype(np.float32)
+        dx, d_phi_out, d_phi_in = O.factored_backward_gemms32(x, dy, (phi_in, phi_out,
+                                                                      atom_values))
+        c2 = time.perf_counter()
+        grad = O.factor_chain(lay, d_phi_out, d_phi_in)
+        p = O.optimizer_step(p, grad, state, spec, lr=1e-3, field_ratios=ratios)
+        c3 = time.perf_counter()
+        fixed = (c1 - c0) + (c3 - c2)
+        full = fixed + (c2 - c1) * (ROWS / sample_rows)
+        if i >= warmup:
+            est.append(full)
+        if log:
+            log(f"reference step {i}: sample {c3 - c0:.2f}s, config-2 estimate {full:.2f}s")
+    per_step = statistics.median(est)
+    return {"value": 1.0 / per_step, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{sample_rows} of {ROWS} rows, all {ATOMS} atoms per step; reference "
+                      f"factored algorithm (float64 factors, float32 numpy-BLAS GEMMs, float64 "
+                      f"factor chain, float32 AdamW); config-2 time = row-independent phases + "
+                      f"GEMM/loss phases x {ROWS // sample_rows}; median of {len(est)} steps",
+            "seconds_per_step": per_step}
+
+
+def run_reference_arm(args):
+    ws, rank, _ = dist_info()
+    if rank != 0:
+        return 0
+    import numpy as np  # noqa: F401
+    steps = args.steps
+    warmup = min(args.warmup, 1)
+    base = cpu_reference(steps, warmup, sample_rows=args.ref_rows)
+    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "steps/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
+            "ms_per_step": 1000.0 / base["value"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": CONFIG,
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": base["value"], "unit": "steps/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--ref-rows", type=int, default=512)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    from torchcst_b200 import _native
+    from torchcst_b200.train import MSETrainStep
+
+    world, rank, local = dist_info()
+    if args.warmup < 3:
+        raise SystemExit("at least 3 warm-up steps are required")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the backend has no CPU path)")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        pg = dist.group.WORLD
+    log = (lambda m: print(m, file=sys.stderr, flush=True)) if args.verbose else (lambda m: None)
+
+    layer, opt, report = build_layer(device)
+    log(f"init: {report}")
+    step = MSETrainStep(layer, opt, ROWS, need_dx=True, process_group=pg,
+                        world_rows=ROWS * world)
+    # Rotating inputs: > 2x L2 (126 MB) of X/target so no step starts with them cached.
+    nbuf = 10
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    xs = [torch.randn(ROWS, N_IO, device=device, generator=gen) for _ in range(nbuf)]
+    ts = [torch.randn(ROWS, N_IO, device=device, generator=gen) for _ in range(nbuf)]
+
+    # GEMM timing hooks: events around the three GEMM launches of every step.
+    lib = _native.load()
+    gemm_events = []
+    orig_gemm = lib.tcst_gemm_tf32x3
+
+    class Timed:
+        def __init__(self):
+            self.on = False
+
+        def __call__(self, *a):
+            if not self.on:
+                return orig_gemm(*a)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            rc = orig_gemm(*a)
+            e1.record()
+            M, N_, K = int(a[0]), int(a[1]), int(a[2])
+            gemm_events.append((e0, e1, 2.0 * M * N_ * K))
+            return rc
+
+    timed = Timed()
+    lib.tcst_gemm_tf32x3 = timed
+
+    for i in range(args.warmup):
+        step(xs[i % nbuf], ts[i % nbuf])
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    # Clock samples bracket the timed region: the sampler starts first and the GPU
+    # keeps running the same step until at least two samples landed on each side.
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_wait = time.perf_counter()
+    i_pre = 0
+    while len(sampler.rows) < 2 and time.perf_counter() - t_wait < 5.0:
+        step(xs[i_pre % nbuf], ts[i_pre % nbuf])
+        i_pre += 1
+        torch.cuda.synchronize()
+    timed.on = True
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    wall0 = time.perf_counter()
+    start.record()
+    loss = None
+    for i in range(args.steps):
+        loss = step(xs[i % nbuf], ts[i % nbuf])
+    end.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    timed.on = False
+    n_before = len(sampler.rows)
+    t_wait = time.perf_counter()
+    i_post = 0
+    while len(sampler.rows) < n_before + 2 and time.perf_counter() - t_wait < 5.0:
+        step(xs[i_post % nbuf], ts[i_post % nbuf])
+        i_post += 1
+        torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end)
+    ms_t = torch.tensor([ms], device=device)
+    if pg is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    ms_per_step = ms / args.steps
+    value = world * 1000.0 / ms_per_step
+    gemm_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in gemm_events)
+    gemm_flops = sum(f for _, _, f in gemm_events)
+    log(f"timed {args.steps} steps: {ms:.3f} ms device, {wall * 1e3:.3f} ms wall, "
+        f"loss {float(loss):.5f}, gemm {gemm_ms:.3f} ms")
+
+    # End-to-end through the drop-in API with pinned host inputs.
+    hx = [xs[i].cpu().pin_memory() for i in range(2)]
+    ht = [ts[i].cpu().pin_memory() for i in range(2)]
+    dx_buf = torch.empty(ROWS, N_IO, device=device)
+    dt_buf = torch.empty(ROWS, N_IO, device=device)
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        dx_buf.copy_(hx[i % 2], non_blocking=True)
+        dt_buf.copy_(ht[i % 2], non_blocking=True)
+        opt.zero_grad(set_to_none=True)
+        y = layer(dx_buf)
+        lo = (y - dt_buf).square().mean()
+        lo.backward()
+        if pg is not None:
+            dist.all_reduce(layer.atoms.p.grad, group=pg)
+            layer.atoms.p.grad.div_(world)
+        opt.step()
+        loss_host.copy_(lo.detach().reshape(1), non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps // 2)
+    e0.record()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=device)
+    if pg is not None:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * 1000.0 / float(e2e_ms.item())
+
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    peak_src = "measured" if "bf16_tflops" in peaks else "fallback"
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
+    roofline = {
+        "bound": "tensor", "kernel": "tcst gemm_tf32x3_kernel (Y, dX, dW launches)",
+        "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
+        "peak_source": f"bf16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
+        "traffic": None,
+        "note": "achieved = algorithmic fp32 GEMM flops 2*M*N*K per launch / CUDA-event time; "
+                "each flop costs 3 TF32 tensor products (hi*hi+hi*lo+lo*hi) and TF32 issues at "
+                "half the bf16 rate, so 3xTF32 caps frac at 1/6",
+        "frac_of_3xtf32_ceiling": achieved * 6.0 / bf16,
+        "gemm_share_of_step": gemm_ms / ms if ms > 0 else None,
+    }
+    line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}",
+                                                l2="rotating inputs, 10 x 32 MiB buffers > L2"),
+            "e2e": {"value": e2e_value, "unit": "steps/s",
+                    "h2d_bytes_per_step": 2 * ROWS * N_IO * 4, "d2h_bytes_per_step": 4,
+                    "api": "layer(x); loss.backward(); CSTAdamW.step()"},
+            "gpu_launches": MSETrainStep.LAUNCHES_PER_STEP * args.steps,
+            "roofline": roofline, "clocks": clocks,
+            "init": {"amplitude_scale": report.amplitude_scale,
+                     "relative_error": report.relative_error},
+            "wall_s_timed": wall}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = {k: v for k, v in cpu_reference(2, 1, args.ref_rows).items()
+                                if k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

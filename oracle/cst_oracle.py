@@ -371,11 +371,12 @@ class AxisProfiles:
 
     def dense(self, atoms, which=0):
         """Dense [N, A] float64 matrix of column ``which`` (0=m, 1=dmu, 2=dR)."""
-        out = np.zeros((self.axis.site_count, atoms), F64)
+        n = self.axis.site_count
+        out = np.zeros(n * atoms, F64)
         for idx, sites, *vals in self.groups:
-            cols = np.broadcast_to(idx[:, None], sites.shape)
-            np.add.at(out, (sites, cols), vals[which])
-        return out
+            flat = (sites * atoms + idx[:, None]).ravel()
+            out += np.bincount(flat, weights=vals[which].ravel(), minlength=n * atoms)
+        return out.reshape(n, atoms)
 
 
 def axis_profiles(axis: Axis, radius, centers):
@@ -557,9 +558,8 @@ def factored_forward32(lay: Layer, x):
     return atom_values @ phi_out.T, (phi_in, phi_out, atom_values)
 
 
-def factored_backward32(lay: Layer, x, dy, saved):
-    """Autograd backward of the factored path: four float32 GEMMs, then the
-    float64 factor chain (the ``.to(p.dtype)`` cast backward promotes to f64)."""
+def factored_backward_gemms32(x, dy, saved):
+    """The four float32 GEMMs of the factored path's autograd backward."""
     phi_in, phi_out, atom_values = saved
     x = np.asarray(x, F32)
     dy = np.asarray(dy, F32)
@@ -567,21 +567,28 @@ def factored_backward32(lay: Layer, x, dy, saved):
     d_phi_out = dy.T @ atom_values
     dx = d_atom_values @ phi_in.T
     d_phi_in = x.T @ d_atom_values
+    return dx, d_phi_out, d_phi_in
+
+
+def factor_chain(lay: Layer, d_phi_out, d_phi_in):
+    """float64 chain from d phi to d p (the ``.to(p.dtype)`` cast backward
+    promotes to float64): gather each atom's footprint entries and contract with
+    dm/d(amp, mu, R), then the rational or Polar coordinate chain."""
     A = lay.atoms
     amp = lay.dec["amplitude"]
     d_amp = np.zeros(A)
     d_mu_out = np.zeros(A)
     d_mu_in = np.zeros(A)
     d_R = np.zeros(A)
-    dpo = d_phi_out.astype(F64)
-    dpi = d_phi_in.astype(F64)
+    fo = np.ascontiguousarray(d_phi_out).ravel()
+    fi = np.ascontiguousarray(d_phi_in).ravel()
     for idx, sites, m, dmu, dR in lay.out_prof.groups:
-        g = dpo[sites, idx[:, None]]
+        g = fo[sites * A + idx[:, None]].astype(F64)
         d_amp[idx] += (g * m).sum(-1)
         d_mu_out[idx] += amp[idx] * (g * dmu).sum(-1)
         d_R[idx] += amp[idx] * (g * dR).sum(-1)
     for idx, sites, m, dmu, dR in lay.in_prof.groups:
-        g = dpi[sites, idx[:, None]]
+        g = fi[sites * A + idx[:, None]].astype(F64)
         d_mu_in[idx] += (g * dmu).sum(-1)
         d_R[idx] += (g * dR).sum(-1)
     grad = np.zeros((A, 4))
@@ -593,7 +600,14 @@ def factored_backward32(lay: Layer, x, dy, saved):
         grad[:, 1] = d_amp * lay.dec["damp_dt"]
     grad[:, 2] = d_mu_out
     grad[:, 3] = d_mu_in
-    return dx, grad.astype(F32)
+    return grad.astype(F32)
+
+
+def factored_backward32(lay: Layer, x, dy, saved):
+    """Autograd backward of the factored path: four float32 GEMMs, then the
+    float64 factor chain."""
+    dx, d_phi_out, d_phi_in = factored_backward_gemms32(x, dy, saved)
+    return dx, factor_chain(lay, d_phi_out, d_phi_in)
 
 
 # ---------------------------------------------------------------------------

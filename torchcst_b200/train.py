@@ -1,0 +1,107 @@
+"""Fused MSE training step of one B200 CSTLinear (forward, backward, CSTAdamW).
+
+Computes exactly what ``y = layer(x); ((y - t)**2).mean().backward();
+optimizer.step()`` computes, without autograd bookkeeping: the MSE upstream
+gradient is produced directly as TF32 split planes by the loss kernel, every
+buffer is allocated once, and the step is a fixed sequence of ten native
+launches on the current stream:
+
+    decode/route -> weight scatter -> weight finalize -> split X -> GEMM Y
+    -> MSE dY -> GEMM dX -> GEMM dW (split-K) -> pullback -> optimizer
+
+With ``process_group`` set (data parallel, rows sharded across ranks, atoms
+replicated), the atom gradient is all-reduced (sum) before the optimizer so
+every rank applies the identical update.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+from . import runtime as R
+from .linear import CSTLinear
+from .optim import CSTAdamW
+from .spec import PolarRadius
+
+
+class MSETrainStep:
+    LAUNCHES_PER_STEP = 10
+
+    def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
+                 process_group=None, world_rows=None):
+        self.layer, self.opt, self.rows = layer, optimizer, int(rows)
+        self.need_dx = need_dx
+        self.pg = process_group
+        p = layer.atoms.p
+        dev = p.device
+        plan = layer._plan
+        self.plan = plan
+        self.ws = layer._workspace(dev)
+        A = p.shape[0]
+        self.atoms = A
+        f32 = torch.float32
+        self.table = torch.empty(max(plan.table_bytes(A) // 4, 1), dtype=f32, device=dev)
+        self.ldw = R.pad4(plan.n_in)
+        self.w_hi = torch.empty(plan.n_out, self.ldw, dtype=f32, device=dev)
+        self.w_lo = torch.empty_like(self.w_hi)
+        self.ldx = R.pad4(plan.n_in)
+        self.x_hi = torch.empty(self.rows, self.ldx, dtype=f32, device=dev)
+        self.x_lo = torch.empty_like(self.x_hi)
+        self.y = torch.empty(self.rows, plan.n_out, dtype=f32, device=dev)
+        self.ldy = R.pad4(plan.n_out)
+        self.dy_hi = torch.empty(self.rows, self.ldy, dtype=f32, device=dev)
+        self.dy_lo = torch.empty_like(self.dy_hi)
+        self.dx = torch.empty(self.rows, plan.n_in, dtype=f32, device=dev) if need_dx else None
+        self.split = R.weight_split_k(plan, self.rows)
+        self.ldg = R.pad4(plan.n_in)
+        self.gstride = plan.n_out * self.ldg
+        self.g = torch.empty(self.split * self.gstride, dtype=f32, device=dev)
+        self.grad = torch.empty(A, 4, dtype=f32, device=dev)
+        self.partial = torch.empty(1024, dtype=torch.float64, device=dev)
+        total_rows = self.rows if world_rows is None else int(world_rows)
+        self.scale = float(torch.tensor(2.0 / (total_rows * plan.n_out), dtype=f32))
+        self.kind = N.TCST_POLAR if isinstance(layer.kernel.coordinates, PolarRadius) else N.TCST_RATIONAL
+        self.nblocks = ctypes.c_int32(0)
+        self._x = None
+
+    def __call__(self, x, target):
+        """Run one step on device tensors x [rows, in], target [rows, out]; returns the
+        loss as a 0-d float64 device tensor (no host synchronization)."""
+        plan, ws, vp = self.plan, self.ws, R._vp
+        p = self.layer.atoms.p
+        st = R._stream(p.device)
+        oa, ia = ctypes.byref(plan.out_axis), ctypes.byref(plan.in_axis)
+        lib = N.load()
+        A, rows = self.atoms, self.rows
+        N.check(lib.tcst_decode_route(vp(p), A, oa, ia, ctypes.byref(plan.coords), vp(self.table),
+                                      None, None, vp(ws.status), st), "decode")
+        N.check(lib.tcst_assemble_weight(vp(self.table), A, oa, ia, vp(ws.acc), None, plan.n_in,
+                                         vp(self.w_hi), vp(self.w_lo), self.ldw, st), "weight")
+        N.check(lib.tcst_split_tf32(vp(x), rows, plan.n_in, x.stride(0), vp(self.x_hi),
+                                    vp(self.x_lo), self.ldx, st), "split")
+        N.check(lib.tcst_gemm_tf32x3(rows, plan.n_out, plan.n_in, vp(self.x_hi), vp(self.x_lo),
+                                     self.ldx, 0, vp(self.w_hi), vp(self.w_lo), self.ldw, 0,
+                                     vp(self.y), plan.n_out, 1, 0, vp(ws.status), st), "gemm y")
+        N.check(lib.tcst_mse_grad(vp(self.y), vp(target), rows, plan.n_out, plan.n_out,
+                                  ctypes.c_float(self.scale), vp(self.dy_hi), vp(self.dy_lo),
+                                  self.ldy, vp(self.partial), ctypes.byref(self.nblocks), st),
+                "mse")
+        if self.need_dx:
+            N.check(lib.tcst_gemm_tf32x3(rows, plan.n_in, plan.n_out, vp(self.dy_hi),
+                                         vp(self.dy_lo), self.ldy, 0, vp(self.w_hi),
+                                         vp(self.w_lo), self.ldw, 1, vp(self.dx), plan.n_in, 1, 0,
+                                         vp(ws.status), st), "gemm dx")
+        N.check(lib.tcst_gemm_tf32x3(plan.n_out, plan.n_in, rows, vp(self.dy_hi), vp(self.dy_lo),
+                                     self.ldy, 1, vp(self.x_hi), vp(self.x_lo), self.ldx, 1,
+                                     vp(self.g), self.ldg, self.split, self.gstride,
+                                     vp(ws.status), st), "gemm dw")
+        N.check(lib.tcst_pullback(vp(self.table), A, oa, ia, vp(self.g), self.ldg, self.split,
+                                  self.gstride, vp(self.grad), st), "pullback")
+        if self.pg is not None:
+            torch.distributed.all_reduce(self.grad, group=self.pg)
+        p.grad = self.grad
+        self.opt.step()
+        return self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
