@@ -130,6 +130,23 @@ int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
                          float *weight_hi_dev, float *weight_lo_dev, int64_t ld_split,
                          void *stream);
 
+/* No counterpart in the reference. The same weight assembly as
+ * tcst_assemble_weight for callers that cannot allocate device memory (a plugin
+ * inside a host framework whose allocator owns the device, or a fixed-footprint
+ * deployment): the int64 accumulator is a fixed array built into this library,
+ * of tcst_static_weight_sites() = 1,048,576 sites (8 MiB), which every GPU that
+ * loads the library holds until exit. Larger N_out * N_in are rejected with
+ * TCST_ERR_UNSUPPORTED. The first call on a device looks up the array's device
+ * address and clears it on `stream`; make that first call before any stream
+ * capture. Every call shares the one array and leaves it all-zero; calls that
+ * overlap on the GPU (same device, different streams) race. Nothing is
+ * allocated. */
+int tcst_assemble_weight_static(const void *atom_table_dev, int64_t atoms,
+                                const tcst_axis *out_axis, const tcst_axis *in_axis,
+                                float *weight_dev, int64_t ld_weight, float *weight_hi_dev,
+                                float *weight_lo_dev, int64_t ld_split, void *stream);
+int64_t tcst_static_weight_sites(void);
+
 /* Two-term TF32 split: hi = rn_tf32(x), lo = rn_tf32(x - hi). */
 int tcst_split_tf32(const float *x_dev, int64_t rows, int64_t cols, int64_t ld_x,
                     float *hi_dev, float *lo_dev, int64_t ld_out, void *stream);

@@ -240,3 +240,98 @@ extern "C" int tcst_mse_grad(const float *y_dev, const float *target_dev, int64_
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Weight assembly without caller-provided scratch.
+//
+// Some callers cannot hand this library device memory for the accumulator:
+// a plugin running inside a host framework whose allocator owns every device
+// byte, or a fixed-footprint deployment that forbids allocation after start-up.
+// For them the accumulator lives in a fixed array compiled into this library.
+// Every GPU that loads the library holds the array until the process exits.
+// ---------------------------------------------------------------------------
+
+#include <mutex>
+
+namespace {
+
+constexpr long long STATIC_WEIGHT_SITES = 1LL << 20; // N_out * N_in limit (8 MiB of int64)
+constexpr int MAX_DEVICES = 64;
+
+static __device__ __align__(256) unsigned long long g_static_accumulator[STATIC_WEIGHT_SITES];
+
+std::mutex g_static_mutex;
+unsigned long long *g_static_ptr[MAX_DEVICES] = {};
+
+// Host code must not pass g_static_accumulator itself to a kernel: in host code
+// that name is only a stand-in. The device address comes from
+// cudaGetSymbolAddress, taken once per device with that device current; the
+// array is cleared once there, and every later call leaves it all-zero again.
+int static_accumulator(cudaStream_t stream, unsigned long long **out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return tcst_cuda_check(e, "cudaGetDevice");
+    if (dev < 0 || dev >= MAX_DEVICES) {
+        tcst_set_error("tcst_assemble_weight_static: device ordinal %d out of range", dev);
+        return TCST_ERR_UNSUPPORTED;
+    }
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (!g_static_ptr[dev]) {
+        void *ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_static_accumulator);
+        if (e != cudaSuccess) return tcst_cuda_check(e, "cudaGetSymbolAddress");
+        e = cudaMemsetAsync(ptr, 0, sizeof(g_static_accumulator), stream);
+        if (e != cudaSuccess) return tcst_cuda_check(e, "cudaMemsetAsync");
+        g_static_ptr[dev] = static_cast<unsigned long long *>(ptr);
+    }
+    *out = g_static_ptr[dev];
+    return TCST_OK;
+}
+
+} // namespace
+
+extern "C" int64_t tcst_static_weight_sites(void) { return STATIC_WEIGHT_SITES; }
+
+extern "C" int tcst_assemble_weight_static(const void *atom_table_dev, int64_t atoms,
+                                           const tcst_axis *out_axis, const tcst_axis *in_axis,
+                                           float *weight_dev, int64_t ld_weight,
+                                           float *weight_hi_dev, float *weight_lo_dev,
+                                           int64_t ld_split, void *stream) {
+    char err[256];
+    AxisCfg oa, ia;
+    int rc;
+    if ((rc = make_axis(out_axis, &oa, err, sizeof(err))) ||
+        (rc = make_axis(in_axis, &ia, err, sizeof(err)))) {
+        tcst_set_error("%s", err);
+        return rc;
+    }
+    if ((long long)oa.sites * ia.sites > STATIC_WEIGHT_SITES) {
+        tcst_set_error("tcst_assemble_weight_static: N_out * N_in = %lld exceeds the built-in "
+                       "accumulator of %lld sites; use tcst_assemble_weight with caller memory",
+                       (long long)oa.sites * ia.sites, STATIC_WEIGHT_SITES);
+        return TCST_ERR_UNSUPPORTED;
+    }
+    if (atoms < 0 || (atoms && !atom_table_dev) ||
+        ((weight_hi_dev == nullptr) != (weight_lo_dev == nullptr)) ||
+        (weight_dev && ld_weight < ia.sites) || (weight_hi_dev && ld_split < ia.sites)) {
+        tcst_set_error("tcst_assemble_weight_static: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    unsigned long long *acc = nullptr;
+    if ((rc = static_accumulator(st, &acc))) return rc;
+    int words = record_words(oa.modes, ia.modes);
+    if (atoms > 0) {
+        long long blocks = (atoms + 7) / 8;
+        long long cap = (long long)sm_count() * 16;
+        if (blocks > cap) blocks = cap;
+        weight_scatter_kernel<<<unsigned(blocks), 256, 0, st>>>(
+            (const float *)atom_table_dev, words, atoms, oa, ia, acc);
+        TCST_CUDA(cudaGetLastError());
+    }
+    long long total = (long long)oa.sites * ia.sites;
+    weight_finalize_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(
+        acc, oa.sites, ia.sites, weight_dev, ld_weight, weight_hi_dev, weight_lo_dev, ld_split);
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
