@@ -158,6 +158,41 @@ def cpu_reference(steps, warmup, sample_rows=512, log=None):
             "seconds_per_step": per_step}
 
 
+def breakdown(lib, step, x, t):
+    """Per-launch CUDA-event times of one step (diagnostic, stderr)."""
+    import torch
+    names = ["tcst_decode_route", "tcst_assemble_weight", "tcst_split_tf32", "tcst_gemm_tf32x3",
+             "tcst_mse_grad", "tcst_pullback", "tcst_optimizer_step"]
+    originals = {n: getattr(lib, n) for n in names}
+    records = []
+
+    def wrap(name, fn):
+        def call(*a):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            rc = fn(*a)
+            e1.record()
+            records.append((name, e0, e1))
+            return rc
+        return call
+
+    for n in names:
+        setattr(lib, n, wrap(n, originals[n]))
+    try:
+        step(x, t)
+        torch.cuda.synchronize()
+    finally:
+        for n in names:
+            setattr(lib, n, originals[n])
+    total = 0.0
+    for name, e0, e1 in records:
+        ms = e0.elapsed_time(e1)
+        total += ms
+        print(f"breakdown {name:24s} {ms * 1e3:9.1f} us", file=sys.stderr, flush=True)
+    print(f"breakdown total native        {total * 1e3:9.1f} us", file=sys.stderr, flush=True)
+
+
 def run_reference_arm(args):
     ws, rank, _ = dist_info()
     if rank != 0:
@@ -186,6 +221,8 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="print per-launch CUDA-event times of one step to stderr")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
@@ -250,6 +287,11 @@ def main():
         dist.barrier()
     # Clock samples bracket the timed region: the sampler starts first and the GPU
     # keeps running the same step until at least two samples landed on each side.
+    # Those extra steps train the model (atoms widen as q grows), so the atoms and
+    # the optimizer state are restored before the timed steps.
+    p = layer.atoms.p
+    saved_p = p.detach().clone()
+    saved_state = {k: (v.clone() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
     sampler = ClockSampler(local)
     sampler.start()
     t_wait = time.perf_counter()
@@ -257,6 +299,22 @@ def main():
     while len(sampler.rows) < 2 and time.perf_counter() - t_wait < 5.0:
         step(xs[i_pre % nbuf], ts[i_pre % nbuf])
         i_pre += 1
+        torch.cuda.synchronize()
+    with torch.no_grad():
+        p.copy_(saved_p)
+    for k, v in saved_state.items():
+        if torch.is_tensor(v):
+            opt.state[p][k].copy_(v)
+        else:
+            opt.state[p][k] = v
+    torch.cuda.synchronize()
+    if args.breakdown:
+        breakdown(lib, step, xs[0], ts[0])
+        with torch.no_grad():
+            p.copy_(saved_p)
+        for k, v in saved_state.items():
+            if torch.is_tensor(v):
+                opt.state[p][k].copy_(v)
         torch.cuda.synchronize()
     timed.on = True
     start = torch.cuda.Event(enable_timing=True)

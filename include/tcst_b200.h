@@ -100,7 +100,9 @@ typedef struct tcst_adamw {
 const char *tcst_version(void);
 const char *tcst_last_error(void);
 
-/* Bytes of the per-atom record table written by tcst_decode_route. */
+/* Bytes of the atom table written by tcst_decode_route: per-atom records,
+ * output footprint spans and the output-band bins used by the weight assembly
+ * and the pullback. */
 int64_t tcst_atom_table_bytes(int64_t atoms, const tcst_axis *out_axis,
                               const tcst_axis *in_axis);
 
@@ -120,32 +122,39 @@ int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_axis *out_ax
 
 /* Assemble the dense weight W = sum_a amp_a m_out,a (x) m_in,a (images folded
  * modulo N) from the atom table. Replaces the W side of factors/weight
- * (radius_cell_mass.py:225-263). Accumulation is 64-bit fixed point, so W is
- * bitwise independent of atom order. accumulator_dev is [N_out * N_in] int64,
- * all zero on entry and left all zero on return. Any of weight_dev / hi / lo may be
- * NULL; hi+lo is the two-term TF32 split consumed by tcst_gemm_tf32x3. */
+ * (radius_cell_mass.py:225-263). Uses the output-band bins that
+ * tcst_decode_route stored in the atom table; each band is accumulated in
+ * 64-bit fixed point and the overlapping band partials are merged, so W is
+ * bitwise independent of atom order. scratch_dev is 16-byte aligned and
+ * tcst_weight_scratch_bytes() long (3 x 8 x N_out x N_in bytes of band
+ * partials); its contents need no initialization. Any of
+ * weight_dev / hi / lo may be NULL; hi+lo is the two-term TF32 split consumed by
+ * tcst_gemm_tf32x3. */
+int64_t tcst_weight_scratch_bytes(int64_t atoms, const tcst_axis *out_axis,
+                                  const tcst_axis *in_axis);
 int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
                          const tcst_axis *out_axis, const tcst_axis *in_axis,
-                         int64_t *accumulator_dev, float *weight_dev, int64_t ld_weight,
-                         float *weight_hi_dev, float *weight_lo_dev, int64_t ld_split,
-                         void *stream);
+                         void *scratch_dev, int64_t scratch_bytes, float *weight_dev,
+                         int64_t ld_weight, float *weight_hi_dev, float *weight_lo_dev,
+                         int64_t ld_split, void *stream);
 
 /* No counterpart in the reference. The same weight assembly as
  * tcst_assemble_weight for callers that cannot allocate device memory (a plugin
  * inside a host framework whose allocator owns the device, or a fixed-footprint
- * deployment): the int64 accumulator is a fixed array built into this library,
- * of tcst_static_weight_sites() = 1,048,576 sites (8 MiB), which every GPU that
- * loads the library holds until exit. Larger N_out * N_in are rejected with
- * TCST_ERR_UNSUPPORTED. The first call on a device looks up the array's device
+ * deployment): the scratch is a fixed array built into this library,
+ * tcst_static_weight_scratch_bytes() = 32 MiB, which every GPU that loads the
+ * library holds until exit. That covers a 1024 x 1024 weight with up to a
+ * million atoms; a layer whose tcst_weight_scratch_bytes() exceeds it is
+ * rejected with TCST_ERR_UNSUPPORTED. The first call on a device looks up the array's device
  * address and clears it on `stream`; make that first call before any stream
- * capture. Every call shares the one array and leaves it all-zero; calls that
- * overlap on the GPU (same device, different streams) race. Nothing is
- * allocated. */
+ * capture. Every call shares the one array and leaves its counters at zero;
+ * calls that overlap on the GPU (same device, different streams) race. Nothing
+ * is allocated. */
 int tcst_assemble_weight_static(const void *atom_table_dev, int64_t atoms,
                                 const tcst_axis *out_axis, const tcst_axis *in_axis,
                                 float *weight_dev, int64_t ld_weight, float *weight_hi_dev,
                                 float *weight_lo_dev, int64_t ld_split, void *stream);
-int64_t tcst_static_weight_sites(void);
+int64_t tcst_static_weight_scratch_bytes(void);
 
 /* Two-term TF32 split: hi = rn_tf32(x), lo = rn_tf32(x - hi). */
 int tcst_split_tf32(const float *x_dev, int64_t rows, int64_t cols, int64_t ld_x,

@@ -109,7 +109,8 @@ def test_weight_matches_oracle(R, name):
     w = layer.weight().cpu().numpy()
     out_axis, in_axis, spec = CASES[name]
     lay = O.decode(out_axis, in_axis, spec, d["p0"])
-    assert rel(w, O.weight64(lay)) < 2e-6
+    # Profile coefficients are float32: W agrees with float64 to ~1e-6 of its scale.
+    assert rel(w, O.weight64(lay)) < 1e-5
 
 
 @pytest.mark.parametrize("name", ["config1", "hierarchy", "config4s", "config3", "config2",
@@ -140,9 +141,67 @@ def test_forward_backward_vs_oracle_and_golden(R, name):
         assert rel(grad[rows, c], d["grad"][:, c]) < TOL, c
 
 
-def test_bitwise_deterministic(R):
-    d = load("config2")
-    layer = make_layer("config2", d["p0"])
+def _align16(x):
+    return (x + 15) // 16 * 16
+
+
+def _table_sections(out_axis, in_axis, atoms):
+    """Byte offsets of the atom table sections, restating the device layout
+    (records, spans, site values, bin_of, offsets, ids)."""
+    aw = lambda m: 4 + 2 * (m + 1)
+    words = (4 + aw(out_axis.modes) + aw(in_axis.modes) + 3) // 4 * 4
+    rt, ct = -(-out_axis.site_count // 32), -(-in_axis.site_count // 32)
+    nbins = 3 * rt * ct + 1
+    if out_axis.modes != 8 or in_axis.modes != 8 or nbins > 49153:
+        rt = ct = 0
+        nbins = 1
+    spans = _align16(atoms * words * 4)
+    sites = _align16(spans + atoms * 16)
+    binof = _align16(sites + atoms * 96 * 4)
+    offsets = _align16(binof + atoms * 4)
+    ids = _align16(offsets + 4 * (nbins + 1))
+    return dict(spans=spans, binof=binof, offsets=offsets, ids=ids, rt=rt, ct=ct, nbins=nbins)
+
+
+@pytest.mark.parametrize("name", ["config1", "hierarchy", "config3", "config5s", "config2"])
+def test_bins_are_stable_and_complete(R, name):
+    d = load(name)
+    layer = make_layer(name, d["p0"])
+    out_axis, in_axis, _ = CASES[name]
+    ws = layer._workspace(layer.atoms.p.device)
+    table = R.decode_route(layer._plan, layer.atoms.p, ws.status)
+    raw = table.view(torch.int32).cpu().numpy()
+    A = d["p0"].shape[0]
+    sec = _table_sections(out_axis, in_axis, A)
+    spans = raw[sec["spans"] // 4: sec["spans"] // 4 + 4 * A].reshape(A, 4)
+    bin_of = raw[sec["binof"] // 4: sec["binof"] // 4 + A]
+    offsets = raw[sec["offsets"] // 4: sec["offsets"] // 4 + sec["nbins"] + 1]
+    ids = raw[sec["ids"] // 4: sec["ids"] // 4 + A]
+    # Spans: wrapped first sites and footprints of both axes, from the golden routing.
+    for side, (axis, col) in enumerate([(out_axis, 0), (in_axis, 2)]):
+        key = "out" if side == 0 else "in"
+        tile = axis.base_tile_sites * axis.merge_factor ** d[f"route_{key}_level"].astype(np.int64)
+        np.testing.assert_array_equal(spans[:, col], (d[f"route_{key}_first_tile"] * tile)
+                                      % axis.site_count)
+        np.testing.assert_array_equal(spans[:, col + 1], d[f"route_{key}_count"] * tile)
+    # Expected bin: footprint class x first-site tile, wide otherwise.
+    f = np.maximum(spans[:, 1], spans[:, 3])
+    cls = np.select([f <= 16, f <= 64, f <= 128], [0, 1, 2], 3)
+    rt, ct, nb = sec["rt"], sec["ct"], sec["nbins"]
+    if rt:
+        want = np.where(cls < 3, (cls * rt + spans[:, 0] // 32) * ct + spans[:, 2] // 32, nb - 1)
+    else:
+        want = np.full(A, nb - 1)
+    np.testing.assert_array_equal(bin_of, want)
+    np.testing.assert_array_equal(offsets, np.concatenate([[0], np.cumsum(np.bincount(want, minlength=nb))]))
+    # Stable: ids grouped by bin, increasing inside every bin.
+    np.testing.assert_array_equal(ids, np.argsort(want, kind="stable"))
+
+
+@pytest.mark.parametrize("name", ["config2", "config5s", "config3"])
+def test_bitwise_deterministic(R, name):
+    d = load(name)
+    layer = make_layer(name, d["p0"])
     x = torch.as_tensor(d["x"]).cuda().requires_grad_(True)
     dy = torch.as_tensor(d["dy"]).cuda()
     outs = []

@@ -2,7 +2,7 @@
 
 Callers that cannot hand the library device memory (for example a plugin whose
 host framework owns every device allocation) use tcst_assemble_weight_static,
-whose int64 accumulator is an array built into the library. This test calls it
+whose scratch is an array built into the library. This test calls it
 through the C ABI twice in a row and checks each result against
 tcst_assemble_weight run with caller-provided scratch. The fixed-point
 accumulation is exact, so the outputs must agree bit for bit (tighter than the
@@ -56,11 +56,12 @@ def test_static_weight_matches_caller_scratch(case, n_out, n_in, radius_max):
     stream = R._stream(p.device)
     oa, ia = ctypes.byref(plan.out_axis), ctypes.byref(plan.in_axis)
 
-    acc = torch.zeros(plan.n_out * plan.n_in, dtype=torch.int64, device="cuda")
+    need = lib.tcst_weight_scratch_bytes(p.shape[0], oa, ia)
+    scratch = torch.zeros((need + 3) // 4, dtype=torch.int32, device="cuda")
     w_ref, hi_ref, lo_ref, ld = _planes(plan, p.device)
-    N.check(lib.tcst_assemble_weight(R._vp(table), p.shape[0], oa, ia, R._vp(acc), R._vp(w_ref),
-                                     plan.n_in, R._vp(hi_ref), R._vp(lo_ref), ld, stream),
-            "tcst_assemble_weight")
+    N.check(lib.tcst_assemble_weight(R._vp(table), p.shape[0], oa, ia, R._vp(scratch), need,
+                                     R._vp(w_ref), plan.n_in, R._vp(hi_ref), R._vp(lo_ref), ld,
+                                     stream), "tcst_assemble_weight")
     for _ in range(2):
         w, hi, lo, ld = _planes(plan, p.device)
         N.check(lib.tcst_assemble_weight_static(R._vp(table), p.shape[0], oa, ia, R._vp(w),
@@ -79,11 +80,14 @@ def test_static_weight_rejects_oversized_layers():
         pytest.skip("needs a CUDA device")
     from torchcst_b200 import _native as N
     lib = N.load()
-    limit = lib.tcst_static_weight_sites()
-    assert limit == 1 << 20
-    big = N.Axis(2048, 1, 2, 8, 1.0, 0.0)
-    small = N.Axis(1024, 1, 2, 8, 1.0, 0.0)
-    rc = lib.tcst_assemble_weight_static(None, 0, ctypes.byref(big), ctypes.byref(small), None,
-                                         0, None, None, 0, None)
+    limit = lib.tcst_static_weight_scratch_bytes()
+    assert limit == 32 << 20
+    axis = N.Axis(1024, 1, 2, 8, 1.0, 0.0)
+    wide = N.Axis(8192, 1, 2, 8, 1.0, 0.0)
+    atoms = 65536
+    assert lib.tcst_weight_scratch_bytes(atoms, ctypes.byref(axis), ctypes.byref(axis)) <= limit
+    assert lib.tcst_weight_scratch_bytes(atoms, ctypes.byref(wide), ctypes.byref(axis)) > limit
+    rc = lib.tcst_assemble_weight_static(None, atoms, ctypes.byref(wide), ctypes.byref(axis),
+                                         None, 0, None, None, 0, None)
     assert rc == 3
-    assert b"exceeds the built-in accumulator" in lib.tcst_last_error()
+    assert b"more than the built-in" in lib.tcst_last_error()

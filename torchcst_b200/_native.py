@@ -87,11 +87,12 @@ SIGNATURES = {
     "tcst_atom_table_bytes": (I64, [I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis)]),
     "tcst_decode_route": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis),
                                          ctypes.POINTER(Coordinates), P, P, P, P, P]),
+    "tcst_weight_scratch_bytes": (I64, [I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis)]),
     "tcst_assemble_weight": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis),
-                                            P, P, I64, P, P, I64, P]),
+                                            P, I64, P, I64, P, P, I64, P]),
     "tcst_assemble_weight_static": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis),
                                                    ctypes.POINTER(Axis), P, I64, P, P, I64, P]),
-    "tcst_static_weight_sites": (I64, []),
+    "tcst_static_weight_scratch_bytes": (I64, []),
     "tcst_split_tf32": (ctypes.c_int, [P, I64, I64, I64, P, P, I64, P]),
     "tcst_gemm_tf32x3": (ctypes.c_int, [I64, I64, I64, P, P, I64, I32, P, P, I64, I32,
                                         P, I64, I32, I64, P, P]),

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 
 #include "common.cuh"
 
@@ -159,166 +160,317 @@ __device__ inline double polar_radius(double amp, double alpha, const double *b,
 }
 
 // Chebyshev-square density coefficients on local period P and their radius
-// derivative (_backends/torch/profiles/radius_fourier.py:14-58). The sample
-// scale and the 1/(2M+1) factor cancel in the c_0 = 1/P normalization, so the
-// unscaled squared recurrence is transformed directly.
-__device__ inline void profile_coefficients(double R, double P, int M, double *c, double *dc) {
-    int n = 2 * M + 1;
+// derivative (_backends/torch/profiles/radius_fourier.py:14-58). The reference
+// samples the scaled recurrence p_0 = 2, p_1 = u, p_n = u p_{n-1} - (z/4) p_{n-2}
+// (u = cos(theta/2), z = cos^2(pi R/P)) at 2M+1 angles, squares it and takes the
+// DFT. p_M^2 is an even polynomial of degree 2M in u, hence a trigonometric
+// polynomial of degree M in theta, so that DFT is exact and equals a polynomial
+// in y = -z/4:  C_k = sum_s W[k][s] y^s, with W built on the host from the
+// recurrence's integer coefficients and the binomial Fourier coefficients of
+// ((1 + cos theta)/2)^m. The sample scale and the 1/(2M+1) factor cancel in the
+// c_0 = 1/P normalization.
+struct ProfileTab {
+    int modes;
+    double w[(MAX_MODES + 1) * (MAX_MODES + 1)]; // w[k * (M + 1) + s]
+};
+
+__host__ inline void make_profile_tab(int M, ProfileTab *t) {
+    // p_n as coefficients of y^j u^(n-2j), y = -z/4.
+    double p[MAX_MODES + 1][MAX_MODES / 2 + 1] = {};
+    p[0][0] = 2.0;
+    if (M >= 1) p[1][0] = 1.0;
+    for (int n = 2; n <= M; ++n)
+        for (int j = 0; j <= n / 2; ++j)
+            p[n][j] = p[n - 1][j] + (j > 0 ? p[n - 2][j - 1] : 0.0);
+    double q[MAX_MODES + 1] = {}; // p_M^2 as coefficients of y^s u^(2M-2s)
+    for (int j = 0; j <= M / 2; ++j)
+        for (int l = 0; l <= M / 2; ++l)
+            if (j + l <= M) q[j + l] += p[M][j] * p[M][l];
+    t->modes = M;
+    for (int k = 0; k <= M; ++k)
+        for (int s = 0; s <= M; ++s) {
+            const int m = M - s;
+            double v = 0.0;
+            if (k <= m) {
+                double binom = 1.0; // C(2m, m + k)
+                for (int i = 1; i <= m - k; ++i) binom = binom * double(m + k + i) / double(i);
+                v = q[s] * binom * std::ldexp(1.0, -2 * m);
+            }
+            t->w[k * (M + 1) + s] = v;
+        }
+}
+
+template <int MT>
+__device__ inline void write_axis_block_t(float *blk, const Route &r, double R, const AxisCfg &ax,
+                                          const ProfileTab &tab, float *sites) {
+    constexpr int CAP = MT > 0 ? MT : MAX_MODES;
+    const int M = MT > 0 ? MT : ax.modes;
+    const double P = dmul(double(r.count * r.tile), ax.spacing);
     double sa, ca;
     sincospi(R / P, &sa, &ca);
-    double ibs = ca * ca;
-    double dibs = -2.0 * ca * sa * (PI / P);
-    double C[MAX_MODES + 1], dC[MAX_MODES + 1];
-    for (int k = 0; k <= M; ++k) C[k] = dC[k] = 0.0;
-    for (int j = 0; j < n; ++j) {
-        double cosine = cospi(double(j) / n);
-        double prev = 2.0, cur = cosine, dprev = 0.0, dcur = 0.0;
-        for (int i = 2; i <= M; ++i) {
-            double nxt = cosine * cur - ibs * prev * 0.25;
-            double dnxt = cosine * dcur - (dibs * prev + ibs * dprev) * 0.25;
-            prev = cur;
-            cur = nxt;
-            dprev = dcur;
-            dcur = dnxt;
+    const double y = -0.25 * ca * ca;
+    const double dy = 0.5 * ca * sa * (PI / P); // dy/dR
+    double C[CAP + 1], dC[CAP + 1];
+#pragma unroll
+    for (int k = 0; k <= CAP; ++k) {
+        if (k > M) break;
+        const double *w = tab.w + k * (M + 1);
+        double v = w[M], d = 0.0;
+        for (int s2 = M - 1; s2 >= 0; --s2) {
+            d = fma(d, y, v);
+            v = fma(v, y, w[s2]);
         }
-        double d = cur * cur, dd = 2.0 * cur * dcur;
-        // cos(2 pi j k / n) by the Chebyshev recurrence in k.
-        double w1 = cospi(2.0 * double(j) / n);
-        double wprev = 1.0, wcur = w1;
-        C[0] += d;
-        dC[0] += dd;
-        for (int k = 1; k <= M; ++k) {
-            C[k] += d * wcur;
-            dC[k] += dd * wcur;
-            double wn = 2.0 * w1 * wcur - wprev;
-            wprev = wcur;
-            wcur = wn;
-        }
+        C[k] = v;
+        dC[k] = d * dy;
     }
-    for (int k = 0; k <= M; ++k) {
-        c[k] = C[k] / (P * C[0]);
-        dc[k] = (dC[k] * C[0] - C[k] * dC[0]) / (P * C[0] * C[0]);
-    }
-}
-
-__device__ inline void write_axis_block(float *blk, const Route &r, double R, const AxisCfg &ax) {
-    int M = ax.modes;
-    double P = dmul(double(r.count * r.tile), ax.spacing);
-    double c[MAX_MODES + 1], dc[MAX_MODES + 1];
-    profile_coefficients(R, P, M, c, dc);
-    long long first = (long long)r.first_tile * r.tile;
+    const long long first = (long long)r.first_tile * r.tile;
+    const int F = r.count * r.tile;
     int *iblk = reinterpret_cast<int *>(blk);
     iblk[0] = int(first);
-    iblk[1] = r.count * r.tile;
+    iblk[1] = F;
     blk[2] = float(2.0 * (double(first) * ax.spacing - r.local) / P);
     blk[3] = float(2.0 * PI / P);
-    for (int k = 0; k <= M; ++k) {
-        double x = double(k) * ax.spacing / P;
-        double sinc = k == 0 ? 1.0 : sinpi(x) / (PI * x);
-        double w = (k == 0 ? 1.0 : 2.0) * ax.spacing * sinc;
-        blk[4 + k] = float(w * c[k]);
-        blk[5 + M + k] = float(w * dc[k]);
+    const double inv = 1.0 / (P * C[0]);
+#pragma unroll
+    for (int k = 0; k <= CAP; ++k) {
+        if (k > M) break;
+        const double x = double(k) * ax.spacing / P;
+        const double sinc = k == 0 ? 1.0 : sinpi(x) / (PI * x);
+        const double wk = (k == 0 ? 1.0 : 2.0) * ax.spacing * sinc;
+        blk[4 + k] = float(wk * C[k] * inv);
+        blk[5 + M + k] = float(wk * (dC[k] * C[0] - C[k] * dC[0]) * inv / C[0]);
+    }
+    if constexpr (MT > 0) {
+        if (sites && F <= REACH) {
+            AxisCoef<MT> ac;
+            ac.load(blk);
+#pragma unroll
+            for (int j = 0; j < REACH; ++j) {
+                if (j < F) {
+                    const SiteVals v = ac.values(j);
+                    sites[j] = v.m;
+                    sites[REACH + j] = v.dmu;
+                    sites[2 * REACH + j] = v.dR;
+                }
+            }
+        }
     }
 }
 
-__global__ void decode_route_kernel(const float *__restrict__ p, long long atoms, AxisCfg out_ax,
-                                    AxisCfg in_ax, CoordCfg cc, float *__restrict__ table,
-                                    int words, long long *__restrict__ keys,
-                                    int *__restrict__ routing, unsigned *__restrict__ status) {
-    long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (a >= atoms) return;
-    float4 row = reinterpret_cast<const float4 *>(p)[a];
-    float *rec = table + a * (long long)words;
-    int *irec = reinterpret_cast<int *>(rec);
-    unsigned bad = 0;
+__device__ inline void write_axis_block(float *blk, const Route &r, double R, const AxisCfg &ax,
+                                        const ProfileTab &tab, float *sites) {
+    if (ax.modes == 8)
+        write_axis_block_t<8>(blk, r, R, ax, tab, sites);
+    else
+        write_axis_block_t<0>(blk, r, R, ax, tab, nullptr);
+}
+
+struct Decoded {
+    double amp, r_out, r_in, ch0, ch1;
+    int flags;
+    unsigned bad;
+};
+
+// Physical amplitude, radii and chain-rule factors of one atom row.
+__device__ inline Decoded decode_atom(float4 row, const CoordCfg &cc, const AxisCfg &out_ax,
+                                      const AxisCfg &in_ax) {
+    Decoded d = {0, 0, 0, 0, 0, 0, 0u};
     if (!(isfinite(row.x) && isfinite(row.y) && isfinite(row.z) && isfinite(row.w)))
-        bad |= TCST_STATUS_NONFINITE;
-    double amp = 0, r_out = 0, r_in = 0, ch0 = 0, ch1 = 0;
-    int flags = 0;
-    if (!bad && cc.kind == TCST_RATIONAL) {
+        d.bad |= TCST_STATUS_NONFINITE;
+    if (!d.bad && cc.kind == TCST_RATIONAL) {
         // _backends/torch/parameterizations/rational_radius.py:6-38.
-        double av = row.x, q = row.y;
-        if (q < 0 || q > 1 || fabs(av) > cc.amax) bad |= TCST_STATUS_BOUNDS;
-        double ratio = ddiv(av, 0.3);
-        double denom = dadd(1.0, dmul(3.0, dmul(ratio, ratio)));
-        double lower = dadd(cc.rmin, ddiv(dsub(cc.rbirth, cc.rmin), denom));
-        double log_lower = log(lower), log_high = log(cc.rmax);
-        double raw = exp(dadd(dmul(dsub(1.0, q), log_lower), dmul(q, log_high)));
-        double value = q == 0 ? lower : (q == 1 ? cc.rmax : raw);
+        const double av = row.x, q = row.y;
+        if (q < 0 || q > 1 || fabs(av) > cc.amax) d.bad |= TCST_STATUS_BOUNDS;
+        const double ratio = ddiv(av, 0.3);
+        const double denom = dadd(1.0, dmul(3.0, dmul(ratio, ratio)));
+        const double lower = dadd(cc.rmin, ddiv(dsub(cc.rbirth, cc.rmin), denom));
+        const double log_lower = log(lower), log_high = log(cc.rmax);
+        const double raw = exp(dadd(dmul(dsub(1.0, q), log_lower), dmul(q, log_high)));
+        const double value = q == 0 ? lower : (q == 1 ? cc.rmax : raw);
         float enc = __double2float_rn(value);
         enc = fminf(fmaxf(enc, cc.lo32), cc.hi32);
-        r_out = r_in = double(enc);
-        amp = av;
-        double dlower = -(cc.rbirth - cc.rmin) * (6.0 * av / 0.09) / (denom * denom);
-        ch0 = raw * (1.0 - q) / lower * dlower;
-        ch1 = raw * (log_high - log_lower);
-    } else if (!bad) {
+        d.r_out = d.r_in = double(enc);
+        d.amp = av;
+        const double dlower = -(cc.rbirth - cc.rmin) * (6.0 * av / 0.09) / (denom * denom);
+        d.ch0 = raw * (1.0 - q) / lower * dlower;
+        d.ch1 = raw * (log_high - log_lower);
+    } else if (!d.bad) {
         // _backends/torch/parameterizations/polar_amp_width.py:127-139.
-        double s = row.x, t = row.y;
-        double rs = dadd(dmul(s, s), dmul(t, t));
-        double tiny = 1.1754943508222875e-38; // float32 tiny: the parameter dtype's
-        double safe = fmax(rs, tiny);
-        double rad = sqrt(safe);
-        amp = ddiv(dmul(cc.amax, s), rad);
-        double alpha = fmin(fmax(ddiv(dsub(rs, 1.0), 3.0), 0.0), 1.0);
-        r_out = polar_radius(amp, alpha, cc.ob, cc);
-        r_in = polar_radius(amp, alpha, cc.ib, cc);
+        const double s = row.x, t = row.y;
+        const double rs = dadd(dmul(s, s), dmul(t, t));
+        const double tiny = 1.1754943508222875e-38; // float32 tiny: the parameter dtype's
+        const double rad = sqrt(fmax(rs, tiny));
+        d.amp = ddiv(dmul(cc.amax, s), rad);
+        const double alpha = fmin(fmax(ddiv(dsub(rs, 1.0), 3.0), 0.0), 1.0);
+        d.r_out = polar_radius(d.amp, alpha, cc.ob, cc);
+        d.r_in = polar_radius(d.amp, alpha, cc.ib, cc);
         if (rs > tiny) {
-            double r3 = rad * rad * rad;
-            ch0 = cc.amax * (1.0 / rad - s * s / r3);
-            ch1 = -cc.amax * s * t / r3;
+            const double r3 = rad * rad * rad;
+            d.ch0 = cc.amax * (1.0 / rad - s * s / r3);
+            d.ch1 = -cc.amax * s * t / r3;
         } else {
-            ch0 = cc.amax / rad;
-            ch1 = 0.0;
+            d.ch0 = cc.amax / rad;
         }
-        flags |= 1;
+        d.flags |= 1;
     }
-    if (!bad) {
-        if (!(r_out > 0 && r_out <= out_ax.period / 2 && r_in > 0 && r_in <= in_ax.period / 2))
-            bad |= TCST_STATUS_RADIUS;
-    }
-    float *ob = rec + 4;
-    float *ib = rec + 4 + axis_words(out_ax.modes);
-    if (bad) {
-        atomicOr(status, bad);
-        rec[0] = 0.0f;
-        rec[1] = rec[2] = 0.0f;
-        irec[3] = flags | 2;
-        reinterpret_cast<int *>(ob)[0] = 0;
-        reinterpret_cast<int *>(ob)[1] = 0;
-        reinterpret_cast<int *>(ib)[0] = 0;
-        reinterpret_cast<int *>(ib)[1] = 0;
-        if (keys) keys[a] = -1;
+    if (!d.bad && !(d.r_out > 0 && d.r_out <= out_ax.period / 2 && d.r_in > 0 &&
+                    d.r_in <= in_ax.period / 2))
+        d.bad |= TCST_STATUS_RADIUS;
+    return d;
+}
+
+// Two threads per atom (adjacent lanes): both decode the row; thread 0 routes
+// and profiles the output axis and writes the record header, the output span
+// and the owner key; thread 1 does the input axis.
+__global__ void __launch_bounds__(256) decode_route_kernel(
+    const float *__restrict__ p, AxisCfg out_ax, AxisCfg in_ax, CoordCfg cc,
+    const __grid_constant__ ProfileTab tab_out, const __grid_constant__ ProfileTab tab_in,
+    Table tv, long long *__restrict__ keys, int *__restrict__ routing,
+    unsigned *__restrict__ status) {
+    const long long atoms = tv.atoms;
+    const int words = tv.words;
+    const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long a = tid >> 1;
+    const int side = int(tid & 1); // 0 = output axis, 1 = input axis
+    const bool live = a < atoms;
+    const float4 row = live ? reinterpret_cast<const float4 *>(p)[a] : make_float4(0, 0, 0, 0);
+    const Decoded d = decode_atom(row, cc, out_ax, in_ax);
+    const AxisCfg &ax = side ? in_ax : out_ax;
+    float *rec = const_cast<float *>(tv.rec) + a * (long long)words;
+    float *blk = rec + 4 + (side ? axis_words(out_ax.modes) : 0);
+    int4 *spans = const_cast<int4 *>(tv.spans);
+    float *sites = const_cast<float *>(tv.sites) + a * SITE_FLOATS + side * 3 * REACH;
+    int node = 0, wrapped = 0, foot = 0;
+    if (live && d.bad) {
+        if (side == 0) {
+            atomicOr(status, d.bad);
+            rec[0] = rec[1] = rec[2] = 0.0f;
+            reinterpret_cast<int *>(rec)[3] = d.flags | 2;
+            spans[a] = make_int4(0, 0, 0, 0);
+            tv.bin_of[a] = tv.geom.nbins - 1;
+            if (keys) keys[a] = -1;
+        }
+        reinterpret_cast<int *>(blk)[0] = 0;
+        reinterpret_cast<int *>(blk)[1] = 0;
         if (routing)
-            for (int i = 0; i < 6; ++i) routing[a * 6 + i] = -1;
-        return;
+            for (int i = 0; i < 3; ++i) routing[a * 6 + 3 * side + i] = -1;
+    } else if (live) {
+        const double R = side ? d.r_in : d.r_out;
+        const Route r = route_axis(R, double(side ? row.w : row.z), ax);
+        write_axis_block(blk, r, R, ax, side ? tab_in : tab_out, sites);
+        {
+            const long long first = (long long)r.first_tile * r.tile;
+            const long long wr = first % ax.sites;
+            wrapped = int(wr < 0 ? wr + ax.sites : wr);
+            foot = r.count * r.tile;
+        }
+        const int tc = ax.sites / r.tile;
+        int m = r.first_tile % tc;
+        m += m < 0 ? tc : 0;
+        node = ax.node_offset[2 * r.level + r.count - 2] + m;
+        if (side == 0) {
+            rec[0] = float(d.amp);
+            rec[1] = float(d.ch0);
+            rec[2] = float(d.ch1);
+            reinterpret_cast<int *>(rec)[3] = d.flags;
+        }
+        if (routing) {
+            int *rt = routing + a * 6 + 3 * side;
+            rt[0] = r.level;
+            rt[1] = r.count;
+            rt[2] = r.first_tile;
+        }
     }
-    Route ro = route_axis(r_out, double(row.z), out_ax);
-    Route ri = route_axis(r_in, double(row.w), in_ax);
-    rec[0] = float(amp);
-    rec[1] = float(ch0);
-    rec[2] = float(ch1);
-    irec[3] = flags;
-    write_axis_block(ob, ro, r_out, out_ax);
-    write_axis_block(ib, ri, r_in, in_ax);
-    if (keys) {
-        int tco = out_ax.sites / ro.tile, tci = in_ax.sites / ri.tile;
-        int mo = ro.first_tile % tco;
-        mo += mo < 0 ? tco : 0;
-        int mi = ri.first_tile % tci;
-        mi += mi < 0 ? tci : 0;
-        long long no = out_ax.node_offset[2 * ro.level + ro.count - 2] + mo;
-        long long ni = in_ax.node_offset[2 * ri.level + ri.count - 2] + mi;
-        keys[a] = no * in_ax.node_count + ni;
+    // Owner key no * input_node_count + ni (reference pipeline.cu:75-80); the
+    // output thread also publishes the span pair and the atom's bin.
+    const int other = __shfl_xor_sync(0xffffffffu, node, 1);
+    const int other_wrapped = __shfl_xor_sync(0xffffffffu, wrapped, 1);
+    const int other_foot = __shfl_xor_sync(0xffffffffu, foot, 1);
+    if (live && !d.bad && side == 0) {
+        if (keys) keys[a] = (long long)node * in_ax.node_count + other;
+        const int4 span = make_int4(wrapped, foot, other_wrapped, other_foot);
+        spans[a] = span;
+        tv.bin_of[a] = atom_bin(span, tv.geom);
     }
-    if (routing) {
-        int *rt = routing + a * 6;
-        rt[0] = ro.level;
-        rt[1] = ro.count;
-        rt[2] = ro.first_tile;
-        rt[3] = ri.level;
-        rt[4] = ri.count;
-        rt[5] = ri.first_tile;
+}
+
+// Stable counting sort of the atoms by bin, in three launches:
+//   count:   sort block b counts the bins of its contiguous atom chunk into
+//            counts[bin][b];
+//   scan:    one CTA turns counts (bin-major) into exclusive starts, so
+//            counts[bin][b] is where block b's atoms of that bin begin;
+//   scatter: block b walks its chunk in id order and places every atom after
+//            the earlier atoms of the same bin (warp match + warp-ordered
+//            claims), so each bin lists its atoms in increasing id order.
+constexpr int SORT_THREADS = 1024;
+
+__global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
+    extern __shared__ int hist[];
+    const BinGeom &g = tv.geom;
+    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const long long a0 = blockIdx.x * g.chunk, a1 = min(tv.atoms, a0 + g.chunk);
+    for (long long a = a0 + threadIdx.x; a < a1; a += blockDim.x) atomicAdd(hist + tv.bin_of[a], 1);
+    __syncthreads();
+    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x)
+        tv.counts[(long long)i * g.sort_blocks + blockIdx.x] = hist[i];
+}
+
+__global__ void __launch_bounds__(SORT_THREADS) bin_scan_kernel(Table tv) {
+    __shared__ int part[SORT_THREADS];
+    const BinGeom &g = tv.geom;
+    const long long total = (long long)g.nbins * g.sort_blocks;
+    const int t = threadIdx.x;
+    const long long per = (total + SORT_THREADS - 1) / SORT_THREADS;
+    const long long k0 = t * per, k1 = min(total, k0 + per);
+    int local = 0;
+    for (long long k = k0; k < k1; ++k) local += tv.counts[k];
+    part[t] = local;
+    __syncthreads();
+    for (int off = 1; off < SORT_THREADS; off <<= 1) {
+        const int v = t >= off ? part[t - off] : 0;
+        __syncthreads();
+        part[t] += v;
+        __syncthreads();
+    }
+    int run = part[t] - local;
+    for (long long k = k0; k < k1; ++k) {
+        const int c = tv.counts[k];
+        tv.counts[k] = run;
+        run += c;
+    }
+    __syncthreads();
+    for (int i = t; i < g.nbins; i += SORT_THREADS)
+        tv.offsets[i] = tv.counts[(long long)i * g.sort_blocks];
+    if (t == 0) tv.offsets[g.nbins] = int(tv.atoms);
+}
+
+__global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
+    extern __shared__ int cursor[];
+    const BinGeom &g = tv.geom;
+    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x)
+        cursor[i] = tv.counts[(long long)i * g.sort_blocks + blockIdx.x];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long long a0 = blockIdx.x * g.chunk, a1 = min(tv.atoms, a0 + g.chunk);
+    for (long long base = a0; base < a1; base += SORT_THREADS) {
+        const long long a = base + threadIdx.x;
+        const bool live = a < a1;
+        const int bin = live ? tv.bin_of[a] : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        const int leader = __ffs(peers) - 1;
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        int start = 0;
+        // Warps claim their slots one after another, so earlier ids come first.
+        for (int w = 0; w < SORT_THREADS / 32; ++w) {
+            if (warp == w && live && lane == leader) {
+                start = cursor[bin];
+                cursor[bin] = start + __popc(peers);
+            }
+            __syncthreads();
+        }
+        start = __shfl_sync(0xffffffffu, start, leader);
+        if (live) tv.ids[start + rank] = int(a);
     }
 }
 
@@ -363,7 +515,11 @@ using namespace tcst;
 extern "C" int64_t tcst_atom_table_bytes(int64_t atoms, const tcst_axis *out_axis,
                                          const tcst_axis *in_axis) {
     if (atoms < 0 || !out_axis || !in_axis) return -1;
-    return atoms * int64_t(record_words(out_axis->modes, in_axis->modes)) * 4;
+    // Records, spans, site values, bins and the sort workspace (common.cuh).
+    return table_layout(atoms, record_words(out_axis->modes, in_axis->modes),
+                        out_axis->site_count, in_axis->site_count, out_axis->modes,
+                        in_axis->modes)
+        .total;
 }
 
 extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_axis *out_axis,
@@ -384,17 +540,50 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
         tcst_set_error("tcst_decode_route: invalid atom count or NULL pointer");
         return TCST_ERR_ARGUMENT;
     }
+    if (!atom_table_dev || !status_dev) {
+        tcst_set_error("tcst_decode_route: NULL atom table or status word");
+        return TCST_ERR_ARGUMENT;
+    }
     if (reinterpret_cast<uintptr_t>(p_dev) % 16 || reinterpret_cast<uintptr_t>(atom_table_dev) % 16) {
         tcst_set_error("tcst_decode_route: p and the atom table must be 16-byte aligned");
         return TCST_ERR_ARGUMENT;
     }
-    if (atoms == 0) return TCST_OK;
-    int words = record_words(oa.modes, ia.modes);
-    int threads = 128;
-    long long blocks = (atoms + threads - 1) / threads;
-    decode_route_kernel<<<unsigned(blocks), threads, 0, (cudaStream_t)stream>>>(
-        p_dev, atoms, oa, ia, cc, (float *)atom_table_dev, words, (long long *)owner_keys_dev,
-        routing_dev, status_dev);
+    if (atoms > 0x7fffffffLL) {
+        tcst_set_error("tcst_decode_route: at most 2^31 - 1 atoms");
+        return TCST_ERR_UNSUPPORTED;
+    }
+    const int words = record_words(oa.modes, ia.modes);
+    const Table tv = table_view(atom_table_dev, atoms, words, oa.sites, ia.sites, oa.modes, ia.modes);
+    const BinGeom &g = tv.geom;
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t hist_bytes = size_t(g.nbins) * 4;
+    static bool configured = false;
+    if (!configured) {
+        TCST_CUDA(cudaFuncSetAttribute(bin_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       MAX_BINS * 4));
+        TCST_CUDA(cudaFuncSetAttribute(bin_scatter_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_BINS * 4));
+        configured = true;
+    }
+    if (atoms == 0) {
+        TCST_CUDA(cudaMemsetAsync(tv.offsets, 0, size_t(g.nbins + 1) * 4, st));
+        return TCST_OK;
+    }
+    {
+        const int threads = 256;
+        const long long blocks = (2 * atoms + threads - 1) / threads;
+        ProfileTab to, ti;
+        make_profile_tab(oa.modes, &to);
+        make_profile_tab(ia.modes, &ti);
+        decode_route_kernel<<<unsigned(blocks), threads, 0, st>>>(
+            p_dev, oa, ia, cc, to, ti, tv, (long long *)owner_keys_dev, routing_dev, status_dev);
+        TCST_CUDA(cudaGetLastError());
+        bin_count_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
+        TCST_CUDA(cudaGetLastError());
+    }
+    bin_scan_kernel<<<1, SORT_THREADS, 0, st>>>(tv);
+    TCST_CUDA(cudaGetLastError());
+    bin_scatter_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

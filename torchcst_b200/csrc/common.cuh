@@ -139,6 +139,182 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
     return {m, dR, dmu * blk[3]};
 }
 
+// ---------------------------------------------------------------------------
+// Atom table layout (one buffer per decode call, saved for the backward pass):
+//   records [atoms][words]
+//   spans   [atoms] int4: output first site wrapped, output footprint,
+//                         input first site wrapped, input footprint
+//   sites   [atoms][2 axes][3 values][REACH]: m, dm/dmu, dm/dR of the first
+//           REACH footprint sites of each axis (filled when F <= REACH)
+//   bin_of  [atoms] int: the atom's bin
+//   offsets [nbins + 1] int, ids [atoms] int: atom ids grouped by bin, in
+//           increasing id order inside every bin (stable counting sort)
+//   counts  [nbins][sort_blocks] int: sort workspace
+//
+// Bins. Footprint class c holds atoms whose larger footprint is at most
+// CLASS_REACH[c] sites; within a class, atoms are binned by the TS x TS tile
+// of (output first site, input first site). Bin c * rt * ct + tile_row * ct +
+// tile_col. Everything else (wider footprints, invalid atoms) shares the last
+// bin ("wide"). When the geometry is not binned (mode counts other than 8, or
+// more tiles than the sort handles) there is only the wide bin.
+// ---------------------------------------------------------------------------
+constexpr int REACH = 16;
+constexpr int SITE_FLOATS = 2 * 3 * REACH;
+constexpr int TS = 32;     // bin tile edge and weight tile edge, in sites
+constexpr int NCLASS = 3;  // footprint classes binned by tile
+constexpr int MAX_BINS = 49153;  // per-CTA bin counters must fit in shared memory
+constexpr int SORT_CHUNK = 4096; // atoms per sort block
+
+__host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : c == 1 ? 64 : 128; }
+
+__host__ __device__ inline long long align16(long long x) { return (x + 15) & ~15LL; }
+
+struct BinGeom {
+    int rt, ct;      // tile rows / columns (0 when not binned)
+    int nbins;       // NCLASS * rt * ct + 1, or 1
+    int sort_blocks; // counting-sort blocks
+    long long chunk; // atoms per sort block
+};
+
+__host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in, int modes_out,
+                                            int modes_in) {
+    BinGeom g;
+    g.rt = (n_out + TS - 1) / TS;
+    g.ct = (n_in + TS - 1) / TS;
+    const long long nb = (long long)NCLASS * g.rt * g.ct + 1;
+    if (modes_out != 8 || modes_in != 8 || nb > MAX_BINS) {
+        g.rt = g.ct = 0;
+        g.nbins = 1;
+    } else {
+        g.nbins = int(nb);
+    }
+    long long blocks = (atoms + SORT_CHUNK - 1) / SORT_CHUNK;
+    blocks = blocks < 1 ? 1 : (blocks > 64 ? 64 : blocks);
+    g.sort_blocks = int(blocks);
+    g.chunk = (atoms + blocks - 1) / blocks;
+    return g;
+}
+
+struct TableLayout {
+    long long spans_off, sites_off, binof_off, offsets_off, ids_off, counts_off, total; // bytes
+    BinGeom geom;
+};
+
+__host__ __device__ inline TableLayout table_layout(long long atoms, int words, int n_out,
+                                                   int n_in, int modes_out, int modes_in) {
+    TableLayout t;
+    t.geom = bin_geom(atoms, n_out, n_in, modes_out, modes_in);
+    t.spans_off = align16(atoms * words * 4);
+    t.sites_off = align16(t.spans_off + atoms * 16);
+    t.binof_off = align16(t.sites_off + atoms * SITE_FLOATS * 4);
+    t.offsets_off = align16(t.binof_off + atoms * 4);
+    t.ids_off = align16(t.offsets_off + 4LL * (t.geom.nbins + 1));
+    t.counts_off = align16(t.ids_off + atoms * 4);
+    t.total = align16(t.counts_off + 4LL * t.geom.nbins * t.geom.sort_blocks);
+    return t;
+}
+
+// Device pointers into one atom table.
+struct Table {
+    const float *rec;
+    int words;
+    long long atoms;
+    const int4 *spans;
+    const float *sites;
+    int *bin_of, *offsets, *ids, *counts;
+    BinGeom geom;
+};
+
+__host__ __device__ inline Table table_view(const void *base, long long atoms, int words,
+                                            int n_out, int n_in, int modes_out, int modes_in) {
+    const TableLayout l = table_layout(atoms, words, n_out, n_in, modes_out, modes_in);
+    char *b = static_cast<char *>(const_cast<void *>(base));
+    Table t;
+    t.rec = reinterpret_cast<const float *>(b);
+    t.words = words;
+    t.atoms = atoms;
+    t.spans = reinterpret_cast<const int4 *>(b + l.spans_off);
+    t.sites = reinterpret_cast<const float *>(b + l.sites_off);
+    t.bin_of = reinterpret_cast<int *>(b + l.binof_off);
+    t.offsets = reinterpret_cast<int *>(b + l.offsets_off);
+    t.ids = reinterpret_cast<int *>(b + l.ids_off);
+    t.counts = reinterpret_cast<int *>(b + l.counts_off);
+    t.geom = l.geom;
+    return t;
+}
+
+// Bin of an atom from its spans (invalid atoms have footprint 0).
+__device__ __forceinline__ int atom_bin(int4 span, const BinGeom &g) {
+    const int wide = g.nbins - 1;
+    if (g.rt == 0 || span.y <= 0 || span.w <= 0) return wide;
+    const int f = max(span.y, span.w);
+    int c = 0;
+    while (c < NCLASS && f > class_reach(c)) ++c;
+    if (c == NCLASS) return wide;
+    return (c * g.rt + span.x / TS) * g.ct + span.z / TS;
+}
+
+// Per-axis profile of one atom held in registers (M known at compile time).
+template <int M> struct AxisCoef {
+    int first, F;
+    float phase0, omega;
+    float c[M + 1], dc[M + 1];
+    __device__ __forceinline__ void load(const float *blk) {
+        first = reinterpret_cast<const int *>(blk)[0];
+        F = reinterpret_cast<const int *>(blk)[1];
+        phase0 = blk[2];
+        omega = blk[3];
+#pragma unroll
+        for (int k = 0; k <= M; ++k) {
+            c[k] = blk[4 + k];
+            dc[k] = blk[5 + M + k];
+        }
+    }
+    // Header and mass coefficients only (dcoef left unset).
+    __device__ __forceinline__ void load_mass(const float *blk) {
+        first = reinterpret_cast<const int *>(blk)[0];
+        F = reinterpret_cast<const int *>(blk)[1];
+        phase0 = blk[2];
+        omega = blk[3];
+#pragma unroll
+        for (int k = 0; k <= M; ++k) c[k] = blk[4 + k];
+    }
+    __device__ __forceinline__ float mass(int j) const {
+        const float t = phase0 + 2.0f * float(j) / float(F);
+        float s1, c1;
+        sincospif(t, &s1, &c1);
+        float acc = c[0], cprev = 1.0f, ccur = c1;
+#pragma unroll
+        for (int k = 1; k <= M; ++k) {
+            acc = fmaf(c[k], ccur, acc);
+            const float cn = fmaf(2.0f * c1, ccur, -cprev);
+            cprev = ccur;
+            ccur = cn;
+        }
+        return acc;
+    }
+    __device__ __forceinline__ SiteVals values(int j) const {
+        const float t = phase0 + 2.0f * float(j) / float(F);
+        float s1, c1;
+        sincospif(t, &s1, &c1);
+        float m = c[0], dR = dc[0], dmu = 0.0f;
+        float cprev = 1.0f, ccur = c1, sprev = 0.0f, scur = s1;
+#pragma unroll
+        for (int k = 1; k <= M; ++k) {
+            m = fmaf(c[k], ccur, m);
+            dR = fmaf(dc[k], ccur, dR);
+            dmu = fmaf(float(k) * c[k], scur, dmu);
+            const float cn = fmaf(2.0f * c1, ccur, -cprev);
+            const float sn = fmaf(2.0f * c1, scur, -sprev);
+            cprev = ccur;
+            ccur = cn;
+            sprev = scur;
+            scur = sn;
+        }
+        return {m, dR, dmu * omega};
+    }
+};
+
 __host__ int make_axis(const tcst_axis *in, AxisCfg *out, char *err, int errlen);
 __host__ int make_coords(const tcst_coordinates *in, const AxisCfg &out_ax,
                          const AxisCfg &in_ax, CoordCfg *out, char *err, int errlen);

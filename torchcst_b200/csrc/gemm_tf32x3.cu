@@ -377,6 +377,16 @@ static int launch(int M, int N, int K, const CUtensorMap *maps, int kps, int spl
     return TCST_OK;
 }
 
+// C = 0 for an empty contraction (K == 0): no operand is read.
+__global__ void zero_fill_kernel(float *__restrict__ C, long long M, long long N, long long ldc,
+                                 long long split_stride, int splits) {
+    long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    long long per = M * N;
+    if (idx >= per * splits) return;
+    long long s = idx / per, r = (idx % per) / N, c = idx % N;
+    C[s * split_stride + r * ldc + c] = 0.0f;
+}
+
 } // namespace gemm
 } // namespace tcst
 
@@ -394,9 +404,19 @@ extern "C" int tcst_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float *a_
         return TCST_ERR_ARGUMENT;
     }
     if (M == 0 || N == 0) return TCST_OK;
-    if (!a_hi_dev || !a_lo_dev || !b_hi_dev || !b_lo_dev || !c_dev || ldc < N ||
-        (split_k > 1 && split_stride < M * ldc)) {
-        tcst_set_error("tcst_gemm_tf32x3: NULL operand or invalid output layout");
+    if (!c_dev || ldc < N || (split_k > 1 && split_stride < M * ldc)) {
+        tcst_set_error("tcst_gemm_tf32x3: NULL output or invalid output layout");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (K == 0) {
+        long long total = M * N * split_k;
+        zero_fill_kernel<<<unsigned((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+            c_dev, M, N, ldc, split_stride, split_k);
+        TCST_CUDA(cudaGetLastError());
+        return TCST_OK;
+    }
+    if (!a_hi_dev || !a_lo_dev || !b_hi_dev || !b_lo_dev) {
+        tcst_set_error("tcst_gemm_tf32x3: NULL operand");
         return TCST_ERR_ARGUMENT;
     }
     const long long a_inner = a_mn_major ? M : K, a_outer = a_mn_major ? K : M;

@@ -31,7 +31,7 @@ class _CellMassLinear(torch.autograd.Function):
         atoms = p.shape[0]
         table = R.decode_route(plan, p, ws.status)
         layer._maybe_check(ws)
-        _, w_hi, w_lo, ldw = R.assemble_weight(plan, table, atoms, ws.acc)
+        _, w_hi, w_lo, ldw = R.assemble_weight(plan, table, atoms, ws)
         x_hi, x_lo, ldx = R.split_tf32(x)
         rows = x.shape[0]
         y = torch.empty(rows, plan.n_out, dtype=torch.float32, device=x.device)
@@ -220,7 +220,7 @@ class CSTLinear(nn.Module):
         ws = self._workspace(p.device)
         table = R.decode_route(self._plan, p, ws.status)
         self._maybe_check(ws)
-        w, _, _, _ = R.assemble_weight(self._plan, table, p.shape[0], ws.acc, dense=True,
+        w, _, _, _ = R.assemble_weight(self._plan, table, p.shape[0], ws, dense=True,
                                        split=False)
         return w
 

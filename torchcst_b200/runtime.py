@@ -89,13 +89,21 @@ class Plan:
 
 
 class Workspace:
-    """Persistent per-device scratch of one layer: the int64 weight accumulator
-    (kept all-zero between calls by the native finalize pass) and the status word."""
+    """Persistent per-device scratch of one layer: the weight assembly's
+    fixed-point plane for wide atoms and the status word."""
 
     def __init__(self, plan: Plan, device):
+        self.plan = plan
         self.device = torch.device(device)
-        self.acc = torch.zeros(plan.n_out * plan.n_in, dtype=torch.int64, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._scratch = None
+
+    def scratch(self, atoms: int):
+        need = int(N.load().tcst_weight_scratch_bytes(atoms, ctypes.byref(self.plan.out_axis),
+                                                       ctypes.byref(self.plan.in_axis)))
+        if self._scratch is None or self._scratch.numel() * 4 < need:
+            self._scratch = torch.empty((need + 15) // 16 * 4, dtype=torch.int32, device=self.device)
+        return self._scratch
 
 
 def decode_route(plan: Plan, p, status, *, owner_keys=None, routing=None):
@@ -108,8 +116,9 @@ def decode_route(plan: Plan, p, status, *, owner_keys=None, routing=None):
     return table
 
 
-def assemble_weight(plan: Plan, table, atoms, acc, *, dense=False, split=True):
-    dev = acc.device
+def assemble_weight(plan: Plan, table, atoms, ws: Workspace, *, dense=False, split=True):
+    dev = ws.device
+    scratch = ws.scratch(atoms)
     ld = pad4(plan.n_in)
     w = torch.empty(plan.n_out, plan.n_in, dtype=torch.float32, device=dev) if dense else None
     hi = lo = None
@@ -117,8 +126,8 @@ def assemble_weight(plan: Plan, table, atoms, acc, *, dense=False, split=True):
         hi = torch.empty(plan.n_out, ld, dtype=torch.float32, device=dev)
         lo = torch.empty(plan.n_out, ld, dtype=torch.float32, device=dev)
     N.call("tcst_assemble_weight", _vp(table), atoms, ctypes.byref(plan.out_axis),
-           ctypes.byref(plan.in_axis), _vp(acc), _vp(w), plan.n_in, _vp(hi), _vp(lo), ld,
-           _stream(dev))
+           ctypes.byref(plan.in_axis), _vp(scratch), scratch.numel() * 4, _vp(w), plan.n_in,
+           _vp(hi), _vp(lo), ld, _stream(dev))
     return w, hi, lo, ld
 
 

@@ -3,11 +3,12 @@
 Computes exactly what ``y = layer(x); ((y - t)**2).mean().backward();
 optimizer.step()`` computes, without autograd bookkeeping: the MSE upstream
 gradient is produced directly as TF32 split planes by the loss kernel, every
-buffer is allocated once, and the step is a fixed sequence of ten native
-launches on the current stream:
+buffer is allocated once, and the step is a fixed sequence of native launches
+on the current stream:
 
-    decode/route -> weight scatter -> weight finalize -> split X -> GEMM Y
-    -> MSE dY -> GEMM dX -> GEMM dW (split-K) -> pullback -> optimizer
+    decode/route -> bin sort (count, scan, scatter) -> weight (clear wide plane,
+    wide atoms, tile gather) -> split X -> GEMM Y -> MSE dY -> GEMM dX ->
+    GEMM dW (split-K) -> pullback (three footprint classes, wide) -> optimizer
 
 With ``process_group`` set (data parallel, rows sharded across ranks, atoms
 replicated), the atom gradient is all-reduced (sum) before the optimizer so
@@ -28,7 +29,7 @@ from .spec import PolarRadius
 
 
 class MSETrainStep:
-    LAUNCHES_PER_STEP = 10
+    LAUNCHES_PER_STEP = 16  # kernels; the wide-plane clear is one memset node besides
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
                  process_group=None, world_rows=None):
@@ -44,6 +45,7 @@ class MSETrainStep:
         self.atoms = A
         f32 = torch.float32
         self.table = torch.empty(max(plan.table_bytes(A) // 4, 1), dtype=f32, device=dev)
+        self.scratch = self.ws.scratch(A)
         self.ldw = R.pad4(plan.n_in)
         self.w_hi = torch.empty(plan.n_out, self.ldw, dtype=f32, device=dev)
         self.w_lo = torch.empty_like(self.w_hi)
@@ -78,7 +80,8 @@ class MSETrainStep:
         A, rows = self.atoms, self.rows
         N.check(lib.tcst_decode_route(vp(p), A, oa, ia, ctypes.byref(plan.coords), vp(self.table),
                                       None, None, vp(ws.status), st), "decode")
-        N.check(lib.tcst_assemble_weight(vp(self.table), A, oa, ia, vp(ws.acc), None, plan.n_in,
+        N.check(lib.tcst_assemble_weight(vp(self.table), A, oa, ia, vp(self.scratch),
+                                         self.scratch.numel() * 4, None, plan.n_in,
                                          vp(self.w_hi), vp(self.w_lo), self.ldw, st), "weight")
         N.check(lib.tcst_split_tf32(vp(x), rows, plan.n_in, x.stride(0), vp(self.x_hi),
                                     vp(self.x_lo), self.ldx, st), "split")
