@@ -176,9 +176,11 @@ int tcst_gemm_tf32x3(int64_t M, int64_t N, int64_t K,
  * d amp, d mu_out, d mu_in and d R reduced over each atom footprint in a fixed
  * order, then the rational (a, q) or Polar (s, t) chain. Replaces the autograd
  * backward of radius_cell_mass.factors through integrated_cells,
- * density_coefficients and physical_parameters. grad_dev is [atoms][4]. */
+ * density_coefficients and physical_parameters. grad_dev is [atoms][4].
+ * With split > 1 the partials are first summed in place into G_0 (the other
+ * partials are left as they were). */
 int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
-                  const tcst_axis *in_axis, const float *g_dev, int64_t ldg,
+                  const tcst_axis *in_axis, float *g_dev, int64_t ldg,
                   int32_t split, int64_t split_stride, float *grad_dev, void *stream);
 
 /* Fused CSTAdamW step on [atoms][4] rows, in place: AdamW moments and proposal,

@@ -145,22 +145,45 @@ def _align16(x):
     return (x + 15) // 16 * 16
 
 
+def _reach(c):
+    return 16 if c == 0 else 64 << (c - 1)
+
+
+def _edge(c):
+    return 32 if c < 3 else _reach(c) // 2
+
+
+def _bin_geom(out_axis, in_axis):
+    """Classes, tiles per axis and first bin of each class, restating the device
+    bin geometry (fine classes on 32-site tiles, coarse ones on reach/2)."""
+    no, ni = out_axis.site_count, in_axis.site_count
+    tr, tc, base, nb, c = [], [], [], 0, 0
+    while True:
+        e = _edge(c)
+        tr.append(-(-no // e))
+        tc.append(-(-ni // e))
+        base.append(nb)
+        nb += tr[-1] * tc[-1]
+        c += 1
+        if _reach(c - 1) >= 2 * max(no, ni):
+            break
+    if out_axis.modes != 8 or in_axis.modes != 8 or nb + 1 > 49153:
+        return dict(nclass=0, nbins=2)
+    return dict(nclass=c, tr=tr, tc=tc, base=base, nbins=nb + 1)
+
+
 def _table_sections(out_axis, in_axis, atoms):
     """Byte offsets of the atom table sections, restating the device layout
     (records, spans, site values, bin_of, offsets, ids)."""
     aw = lambda m: 4 + 2 * (m + 1)
     words = (4 + aw(out_axis.modes) + aw(in_axis.modes) + 3) // 4 * 4
-    rt, ct = -(-out_axis.site_count // 32), -(-in_axis.site_count // 32)
-    nbins = 3 * rt * ct + 1
-    if out_axis.modes != 8 or in_axis.modes != 8 or nbins > 49153:
-        rt = ct = 0
-        nbins = 1
+    geo = _bin_geom(out_axis, in_axis)
     spans = _align16(atoms * words * 4)
     sites = _align16(spans + atoms * 16)
     binof = _align16(sites + atoms * 96 * 4)
     offsets = _align16(binof + atoms * 4)
-    ids = _align16(offsets + 4 * (nbins + 1))
-    return dict(spans=spans, binof=binof, offsets=offsets, ids=ids, rt=rt, ct=ct, nbins=nbins)
+    ids = _align16(offsets + 4 * (geo["nbins"] + 1))
+    return dict(spans=spans, binof=binof, offsets=offsets, ids=ids, geo=geo)
 
 
 @pytest.mark.parametrize("name", ["config1", "hierarchy", "config3", "config5s", "config2"])
@@ -173,9 +196,11 @@ def test_bins_are_stable_and_complete(R, name):
     raw = table.view(torch.int32).cpu().numpy()
     A = d["p0"].shape[0]
     sec = _table_sections(out_axis, in_axis, A)
+    geo = sec["geo"]
+    nb = geo["nbins"]
     spans = raw[sec["spans"] // 4: sec["spans"] // 4 + 4 * A].reshape(A, 4)
     bin_of = raw[sec["binof"] // 4: sec["binof"] // 4 + A]
-    offsets = raw[sec["offsets"] // 4: sec["offsets"] // 4 + sec["nbins"] + 1]
+    offsets = raw[sec["offsets"] // 4: sec["offsets"] // 4 + nb + 1]
     ids = raw[sec["ids"] // 4: sec["ids"] // 4 + A]
     # Spans: wrapped first sites and footprints of both axes, from the golden routing.
     for side, (axis, col) in enumerate([(out_axis, 0), (in_axis, 2)]):
@@ -184,14 +209,19 @@ def test_bins_are_stable_and_complete(R, name):
         np.testing.assert_array_equal(spans[:, col], (d[f"route_{key}_first_tile"] * tile)
                                       % axis.site_count)
         np.testing.assert_array_equal(spans[:, col + 1], d[f"route_{key}_count"] * tile)
-    # Expected bin: footprint class x first-site tile, wide otherwise.
+    # Expected bin: class (smallest reach covering the larger footprint) x tile.
     f = np.maximum(spans[:, 1], spans[:, 3])
-    cls = np.select([f <= 16, f <= 64, f <= 128], [0, 1, 2], 3)
-    rt, ct, nb = sec["rt"], sec["ct"], sec["nbins"]
-    if rt:
-        want = np.where(cls < 3, (cls * rt + spans[:, 0] // 32) * ct + spans[:, 2] // 32, nb - 1)
+    if geo["nclass"]:
+        cls = np.zeros(A, np.int64)
+        while (f > np.vectorize(_reach)(cls)).any():
+            cls += f > np.vectorize(_reach)(cls)
+        e = np.vectorize(_edge)(cls)
+        base = np.asarray(geo["base"])[cls]
+        tcs = np.asarray(geo["tc"])[cls]
+        want = base + (spans[:, 0] // e) * tcs + spans[:, 2] // e
     else:
-        want = np.full(A, nb - 1)
+        want = np.zeros(A, np.int64)
+    want = np.where(f > 0, want, nb - 1)
     np.testing.assert_array_equal(bin_of, want)
     np.testing.assert_array_equal(offsets, np.concatenate([[0], np.cumsum(np.bincount(want, minlength=nb))]))
     # Stable: ids grouped by bin, increasing inside every bin.

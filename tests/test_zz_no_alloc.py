@@ -4,10 +4,12 @@ Callers that cannot hand the library device memory (for example a plugin whose
 host framework owns every device allocation) use tcst_assemble_weight_static,
 whose scratch is an array built into the library. This test calls it
 through the C ABI twice in a row and checks each result against
-tcst_assemble_weight run with caller-provided scratch. The fixed-point
-accumulation is exact, so the outputs must agree bit for bit (tighter than the
-1e-4 tolerance the other parity tests use). It must pass in a fresh process
-and after the rest of the suite, which is why it sits in the last test file.
+tcst_assemble_weight run with caller-provided scratch. Both run the same
+kernels in the same fixed order, so the outputs must agree bit for bit
+(tighter than the 1e-4 tolerance the other parity tests use). The cases cover
+every footprint class, including the mid-size classes whose masses live in the
+scratch. It must pass in a fresh process and after the rest of the suite,
+which is why it sits in the last test file.
 """
 
 import ctypes
@@ -39,7 +41,8 @@ def _planes(plan, dev):
     return w, hi, lo, ld
 
 
-@pytest.mark.parametrize("case,n_out,n_in,radius_max", [("config2", 1024, 1024, 512.0),
+@pytest.mark.parametrize("case,n_out,n_in,radius_max", [("config5s", 512, 512, 256.0),
+                                                        ("config4s", 1024, 256, 128.0),
                                                         ("config1", 8, 16, 4.0)])
 def test_static_weight_matches_caller_scratch(case, n_out, n_in, radius_max):
     if not torch.cuda.is_available():
@@ -83,11 +86,10 @@ def test_static_weight_rejects_oversized_layers():
     limit = lib.tcst_static_weight_scratch_bytes()
     assert limit == 32 << 20
     axis = N.Axis(1024, 1, 2, 8, 1.0, 0.0)
-    wide = N.Axis(8192, 1, 2, 8, 1.0, 0.0)
-    atoms = 65536
-    assert lib.tcst_weight_scratch_bytes(atoms, ctypes.byref(axis), ctypes.byref(axis)) <= limit
-    assert lib.tcst_weight_scratch_bytes(atoms, ctypes.byref(wide), ctypes.byref(axis)) > limit
-    rc = lib.tcst_assemble_weight_static(None, atoms, ctypes.byref(wide), ctypes.byref(axis),
+    fits, too_many = 32768, 65536
+    assert lib.tcst_weight_scratch_bytes(fits, ctypes.byref(axis), ctypes.byref(axis)) <= limit
+    assert lib.tcst_weight_scratch_bytes(too_many, ctypes.byref(axis), ctypes.byref(axis)) > limit
+    rc = lib.tcst_assemble_weight_static(None, too_many, ctypes.byref(axis), ctypes.byref(axis),
                                          None, 0, None, None, 0, None)
     assert rc == 3
     assert b"more than the built-in" in lib.tcst_last_error()

@@ -396,12 +396,14 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
 
 // Stable counting sort of the atoms by bin, in three launches:
 //   count:   sort block b counts the bins of its contiguous atom chunk into
-//            counts[bin][b];
-//   scan:    one CTA turns counts (bin-major) into exclusive starts, so
-//            counts[bin][b] is where block b's atoms of that bin begin;
-//   scatter: block b walks its chunk in id order and places every atom after
-//            the earlier atoms of the same bin (warp match + warp-ordered
-//            claims), so each bin lists its atoms in increasing id order.
+//            counts[b][bin];
+//   column:  one thread per bin turns its column into exclusive prefixes over
+//            the blocks (counts[b][bin] = atoms of that bin in blocks < b) and
+//            leaves the bin's total in counts[blocks][bin];
+//   scatter: every block scans the bin totals into bin starts (block 0 also
+//            stores them as the offsets), then walks its chunk in id order and
+//            places each atom after the earlier atoms of its bin (warp match +
+//            warp-ordered claims), so every bin lists its atoms in id order.
 constexpr int SORT_THREADS = 1024;
 
 __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
@@ -412,49 +414,70 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
     const long long a0 = blockIdx.x * g.chunk, a1 = min(tv.atoms, a0 + g.chunk);
     for (long long a = a0 + threadIdx.x; a < a1; a += blockDim.x) atomicAdd(hist + tv.bin_of[a], 1);
     __syncthreads();
-    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x)
-        tv.counts[(long long)i * g.sort_blocks + blockIdx.x] = hist[i];
+    int *row = tv.counts + (long long)blockIdx.x * g.nbins;
+    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x) row[i] = hist[i];
 }
 
-__global__ void __launch_bounds__(SORT_THREADS) bin_scan_kernel(Table tv) {
-    __shared__ int part[SORT_THREADS];
+__global__ void __launch_bounds__(256) bin_column_kernel(Table tv) {
     const BinGeom &g = tv.geom;
-    const long long total = (long long)g.nbins * g.sort_blocks;
-    const int t = threadIdx.x;
-    const long long per = (total + SORT_THREADS - 1) / SORT_THREADS;
-    const long long k0 = t * per, k1 = min(total, k0 + per);
-    int local = 0;
-    for (long long k = k0; k < k1; ++k) local += tv.counts[k];
-    part[t] = local;
-    __syncthreads();
-    for (int off = 1; off < SORT_THREADS; off <<= 1) {
-        const int v = t >= off ? part[t - off] : 0;
-        __syncthreads();
-        part[t] += v;
-        __syncthreads();
+    const int bin = blockIdx.x * blockDim.x + threadIdx.x;
+    if (bin >= g.nbins) return;
+    int run = 0;
+    for (int b = 0; b < g.sort_blocks; ++b) {
+        int *c = tv.counts + (long long)b * g.nbins + bin;
+        const int v = *c;
+        *c = run;
+        run += v;
     }
-    int run = part[t] - local;
-    for (long long k = k0; k < k1; ++k) {
-        const int c = tv.counts[k];
-        tv.counts[k] = run;
-        run += c;
-    }
-    __syncthreads();
-    for (int i = t; i < g.nbins; i += SORT_THREADS)
-        tv.offsets[i] = tv.counts[(long long)i * g.sort_blocks];
-    if (t == 0) tv.offsets[g.nbins] = int(tv.atoms);
+    tv.counts[(long long)g.sort_blocks * g.nbins + bin] = run;
 }
 
 __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
     extern __shared__ int cursor[];
+    __shared__ int wsum[SORT_THREADS / 32];
     const BinGeom &g = tv.geom;
-    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x)
-        cursor[i] = tv.counts[(long long)i * g.sort_blocks + blockIdx.x];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    // Bin starts: exclusive scan of the totals, each thread over a contiguous run.
+    const int *total = tv.counts + (long long)g.sort_blocks * g.nbins;
+    const int per = (g.nbins + SORT_THREADS - 1) / SORT_THREADS;
+    const int i0 = t * per;
+    int local = 0;
+    for (int k = 0; k < per; ++k)
+        if (i0 + k < g.nbins) local += total[i0 + k];
+    int inc = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) wsum[warp] = inc;
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (warp == 0) {
+        const int w = wsum[lane];
+        int winc = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, winc, o);
+            if (lane >= o) winc += y;
+        }
+        wsum[lane] = winc - w;
+    }
+    __syncthreads();
+    int run = wsum[warp] + inc - local;
+    const int *mine = tv.counts + (long long)blockIdx.x * g.nbins;
+    for (int k = 0; k < per; ++k) {
+        const int i = i0 + k;
+        if (i < g.nbins) {
+            if (blockIdx.x == 0) tv.offsets[i] = run;
+            cursor[i] = run + mine[i];
+            run += total[i];
+        }
+    }
+    if (blockIdx.x == 0 && t == 0) tv.offsets[g.nbins] = int(tv.atoms);
+    __syncthreads();
     const long long a0 = blockIdx.x * g.chunk, a1 = min(tv.atoms, a0 + g.chunk);
     for (long long base = a0; base < a1; base += SORT_THREADS) {
-        const long long a = base + threadIdx.x;
+        const long long a = base + t;
         const bool live = a < a1;
         const int bin = live ? tv.bin_of[a] : -1;
         const unsigned peers = __match_any_sync(0xffffffffu, bin);
@@ -581,7 +604,7 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
         bin_count_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
         TCST_CUDA(cudaGetLastError());
     }
-    bin_scan_kernel<<<1, SORT_THREADS, 0, st>>>(tv);
+    bin_column_kernel<<<unsigned((g.nbins + 255) / 256), 256, 0, st>>>(tv);
     TCST_CUDA(cudaGetLastError());
     bin_scatter_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
     TCST_CUDA(cudaGetLastError());

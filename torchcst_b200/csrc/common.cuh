@@ -149,44 +149,63 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
 //   bin_of  [atoms] int: the atom's bin
 //   offsets [nbins + 1] int, ids [atoms] int: atom ids grouped by bin, in
 //           increasing id order inside every bin (stable counting sort)
-//   counts  [nbins][sort_blocks] int: sort workspace
+//   counts  [sort_blocks + 1][nbins] int: sort workspace
 //
-// Bins. Footprint class c holds atoms whose larger footprint is at most
-// CLASS_REACH[c] sites; within a class, atoms are binned by the TS x TS tile
-// of (output first site, input first site). Bin c * rt * ct + tile_row * ct +
-// tile_col. Everything else (wider footprints, invalid atoms) shares the last
-// bin ("wide"). When the geometry is not binned (mode counts other than 8, or
-// more tiles than the sort handles) there is only the wide bin.
+// Bins. An atom's class is the smallest c whose reach class_reach(c) covers
+// its larger footprint max(F_out, F_in). Classes 0..NFINE-1 (reach 16, 64, 128)
+// are binned by the TS x TS tile of (output first site, input first site);
+// coarser classes (reach 256, 512, ... up to twice the larger axis, the widest
+// footprint routing produces) by tiles of edge reach / 2. Bins are numbered
+// class by class, tiles row-major, and invalid atoms take the last bin. When
+// the geometry is not binned (mode counts other than 8, or more bins than the
+// sort handles) every valid atom is in class-free bin 0.
 // ---------------------------------------------------------------------------
 constexpr int REACH = 16;
 constexpr int SITE_FLOATS = 2 * 3 * REACH;
-constexpr int TS = 32;     // bin tile edge and weight tile edge, in sites
-constexpr int NCLASS = 3;  // footprint classes binned by tile
-constexpr int MAX_BINS = 49153;  // per-CTA bin counters must fit in shared memory
-constexpr int SORT_CHUNK = 4096; // atoms per sort block
+constexpr int TS = 32;          // fine bin tile edge and weight tile edge, in sites
+constexpr int NFINE = 3;        // classes binned by TS tiles
+constexpr int MAX_CLASSES = 16;
+constexpr int MAX_BINS = 49153; // per-CTA bin counters must fit in shared memory
+constexpr int SORT_CHUNK = 1024; // atoms per sort block (at most 64 blocks)
+constexpr int CACHE_SITES = 128; // masses cached per axis for classes 1..NFINE-1
 
-__host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : c == 1 ? 64 : 128; }
+__host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : 64 << (c - 1); }
+__host__ __device__ constexpr int class_edge(int c) { return c < NFINE ? TS : class_reach(c) / 2; }
 
 __host__ __device__ inline long long align16(long long x) { return (x + 15) & ~15LL; }
 
 struct BinGeom {
-    int rt, ct;      // tile rows / columns (0 when not binned)
-    int nbins;       // NCLASS * rt * ct + 1, or 1
-    int sort_blocks; // counting-sort blocks
-    long long chunk; // atoms per sort block
+    int nclass;                   // 0 when not binned
+    int tr[MAX_CLASSES], tc[MAX_CLASSES]; // tiles per axis of each class
+    int base[MAX_CLASSES + 1];    // first bin of each class; base[nclass] = first bin past them
+    int nbins;                    // base[nclass] + 1 (invalid bin)
+    int sort_blocks;              // counting-sort blocks
+    long long chunk;              // atoms per sort block
 };
 
 __host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in, int modes_out,
                                             int modes_in) {
     BinGeom g;
-    g.rt = (n_out + TS - 1) / TS;
-    g.ct = (n_in + TS - 1) / TS;
-    const long long nb = (long long)NCLASS * g.rt * g.ct + 1;
-    if (modes_out != 8 || modes_in != 8 || nb > MAX_BINS) {
-        g.rt = g.ct = 0;
-        g.nbins = 1;
+    const int nmax = n_out > n_in ? n_out : n_in;
+    int nc = 0;
+    long long nb = 0;
+    while (nc < MAX_CLASSES) {
+        const int e = class_edge(nc);
+        g.tr[nc] = (n_out + e - 1) / e;
+        g.tc[nc] = (n_in + e - 1) / e;
+        g.base[nc] = int(nb < 0x7fffffff ? nb : 0x7fffffff);
+        nb += (long long)g.tr[nc] * g.tc[nc];
+        ++nc;
+        if (class_reach(nc - 1) >= 2 * nmax) break;
+    }
+    if (modes_out != 8 || modes_in != 8 || nb + 1 > MAX_BINS || class_reach(nc - 1) < 2 * nmax) {
+        g.nclass = 0;
+        g.base[0] = 0;
+        g.nbins = 2; // bin 0: every valid atom; bin 1: invalid atoms
     } else {
-        g.nbins = int(nb);
+        g.nclass = nc;
+        g.base[nc] = int(nb);
+        g.nbins = int(nb) + 1;
     }
     long long blocks = (atoms + SORT_CHUNK - 1) / SORT_CHUNK;
     blocks = blocks < 1 ? 1 : (blocks > 64 ? 64 : blocks);
@@ -210,7 +229,7 @@ __host__ __device__ inline TableLayout table_layout(long long atoms, int words, 
     t.offsets_off = align16(t.binof_off + atoms * 4);
     t.ids_off = align16(t.offsets_off + 4LL * (t.geom.nbins + 1));
     t.counts_off = align16(t.ids_off + atoms * 4);
-    t.total = align16(t.counts_off + 4LL * t.geom.nbins * t.geom.sort_blocks);
+    t.total = align16(t.counts_off + 4LL * t.geom.nbins * (t.geom.sort_blocks + 1));
     return t;
 }
 
@@ -243,15 +262,21 @@ __host__ __device__ inline Table table_view(const void *base, long long atoms, i
     return t;
 }
 
+__host__ __device__ inline int atom_class(int4 span) {
+    const int f = span.y > span.w ? span.y : span.w;
+    int c = 0;
+    while (class_reach(c) < f) ++c;
+    return c;
+}
+
 // Bin of an atom from its spans (invalid atoms have footprint 0).
 __device__ __forceinline__ int atom_bin(int4 span, const BinGeom &g) {
-    const int wide = g.nbins - 1;
-    if (g.rt == 0 || span.y <= 0 || span.w <= 0) return wide;
-    const int f = max(span.y, span.w);
-    int c = 0;
-    while (c < NCLASS && f > class_reach(c)) ++c;
-    if (c == NCLASS) return wide;
-    return (c * g.rt + span.x / TS) * g.ct + span.z / TS;
+    const int invalid = g.nbins - 1;
+    if (span.y <= 0 || span.w <= 0) return invalid;
+    if (g.nclass == 0) return 0;
+    const int c = atom_class(span);
+    const int e = class_edge(c);
+    return g.base[c] + (span.x / e) * g.tc[c] + span.z / e;
 }
 
 // Per-axis profile of one atom held in registers (M known at compile time).

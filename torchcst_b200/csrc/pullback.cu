@@ -16,9 +16,10 @@
 //                                 table's site buffer;
 //   classes 1, 2 (<= 64, <= 128): one warp per atom, lanes over input sites,
 //                                 output-site values in per-warp shared memory.
-// Wide-bin atoms: one warp per atom reads G from global memory. Every atom is
-// reduced by one thread or one warp with a fixed xor tree, so the gradient is
-// bitwise reproducible.
+// Coarser classes (and every atom of an unbinned geometry): one CTA per atom
+// walks the footprint in chunks, G from global memory. Every atom is reduced by
+// one thread, one warp (fixed xor tree) or one CTA (fixed tree), so the
+// gradient is bitwise reproducible.
 
 #include <algorithm>
 
@@ -40,19 +41,65 @@ __device__ __forceinline__ float4 chain(const float *rec, float s_amp, float s_m
     return make_float4(fmaf(d_r, ch0, s_amp), d_r * ch1, amp * s_mo, amp * s_mi);
 }
 
-// G window [wr x wc] at (R0, C0) with rows/columns wrapped modulo no / ni.
-__device__ __forceinline__ void stage_window(float *gw, int wr, int wc, int pitch, int R0, int C0,
-                                             int no, int ni, const float *__restrict__ g,
-                                             long long ldg, int split, long long split_stride) {
-    for (int i = threadIdx.x; i < wr * wc; i += blockDim.x) {
-        const int rl = i / wc, cl = i - rl * wc;
-        int row = R0 + rl, col = C0 + cl;
-        while (row >= no) row -= no;
-        while (col >= ni) col -= ni;
-        const float *gp = g + (long long)row * ldg + col;
+// G_0 += G_1 + ... + G_{split-1}, in place (rows of ni valid columns).
+__global__ void g_reduce_kernel(float *__restrict__ g, int no, int ni, long long ldg, int split,
+                                long long split_stride) {
+    const long long total = (long long)no * ni;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / ni, c = i - r * ni;
+        float *gp = g + r * ldg + c;
         float v = gp[0];
         for (int s = 1; s < split; ++s) v += gp[s * split_stride];
-        gw[rl * pitch + cl] = v;
+        gp[0] = v;
+    }
+}
+
+__global__ void g_reduce4_kernel(float4 *__restrict__ g, int no, int ni4, long long ldg4,
+                                 int split, long long split_stride4) {
+    const long long total = (long long)no * ni4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / ni4, c = i - r * ni4;
+        float4 *gp = g + r * ldg4 + c;
+        float4 v = gp[0];
+        for (int s = 1; s < split; ++s) {
+            const float4 w = gp[s * split_stride4];
+            v.x += w.x, v.y += w.y, v.z += w.z, v.w += w.w;
+        }
+        gp[0] = v;
+    }
+}
+
+// G window [W x W] at (R0, C0) with rows/columns wrapped modulo no / ni;
+// four independent loads in flight per thread.
+template <int W, int PITCH>
+__device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, int ni,
+                                             const float *__restrict__ g, long long ldg, int split,
+                                             long long split_stride) {
+    constexpr int N = W * W;
+    for (int i0 = threadIdx.x; i0 < N; i0 += 4 * blockDim.x) {
+        float v[4];
+        int dst[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = i0 + u * blockDim.x;
+            dst[u] = -1;
+            v[u] = 0.f;
+            if (i < N) {
+                const int rl = i / W, cl = i - rl * W;
+                int row = R0 + rl, col = C0 + cl;
+                while (row >= no) row -= no;
+                while (col >= ni) col -= ni;
+                const float *gp = g + (long long)row * ldg + col;
+                v[u] = gp[0];
+                for (int s = 1; s < split; ++s) v[u] += gp[s * split_stride];
+                dst[u] = rl * PITCH + cl;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (dst[u] >= 0) gw[dst[u]] = v[u];
     }
 }
 
@@ -62,13 +109,13 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     long long split_stride, float4 *__restrict__ grad) {
     constexpr int W = TS + REACH - 1;
     __shared__ float gw[W * W];
-    const int ct = tv.geom.ct;
+    const int ct = tv.geom.tc[0];
     const int tr = blockIdx.x / ct, tc = blockIdx.x - tr * ct;
-    const int bin = blockIdx.x; // class 0 bins come first, row-major by tile
+    const int bin = tv.geom.base[0] + blockIdx.x; // class 0 bins, row-major by tile
     const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
     if (begin == end) return;
     const int R0 = tr * TS, C0 = tc * TS;
-    stage_window(gw, W, W, W, R0, C0, no, ni, g, ldg, split, split_stride);
+    stage_window<W, W>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
     __syncthreads();
     for (int k = begin + threadIdx.x; k < end; k += blockDim.x) {
         const long long a = tv.ids[k];
@@ -119,15 +166,16 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     extern __shared__ float sm[];
     float *gw = sm;
     const BinGeom &geo = tv.geom;
-    const int rc2 = (geo.ct + 1) / 2;
+    const int nr = geo.tr[cls], nc = geo.tc[cls];
+    const int rc2 = (nc + 1) / 2;
     const int ir = blockIdx.x / rc2, ic = blockIdx.x - ir * rc2;
     int rb[4], re[4], total = 0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         const int tr = 2 * ir + (q >> 1), tc = 2 * ic + (q & 1);
         rb[q] = re[q] = 0;
-        if (tr < geo.rt && tc < geo.ct) {
-            const int bin = (cls * geo.rt + tr) * geo.ct + tc;
+        if (tr < nr && tc < nc) {
+            const int bin = geo.base[cls] + tr * nc + tc;
             rb[q] = tv.offsets[bin];
             re[q] = tv.offsets[bin + 1];
         }
@@ -135,7 +183,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     }
     if (total == 0) return;
     const int R0 = 2 * ir * TS, C0 = 2 * ic * TS;
-    stage_window(gw, W, W, PITCH, R0, C0, no, ni, g, ldg, split, split_stride);
+    stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float *rowv = sm + W * PITCH + warp * 3 * RC; // m, dm/dmu, dm/dR of the output sites
@@ -184,6 +232,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
 #pragma unroll
         for (int j = 0; j < Q; ++j) h0[j] = h1[j] = h2[j] = 0.f;
         const float *g0 = gw + (span.x - R0) * PITCH;
+#pragma unroll 4
         for (int r = 0; r < fo; ++r) {
             const float m = rowv[r], dm = rowv[RC + r], dr = rowv[2 * RC + r];
             const float *grow = g0 + r * PITCH;
@@ -219,61 +268,85 @@ template <int RC> constexpr size_t class_smem() {
     return size_t(2 * TS + RC - 1) * (2 * TS + RC) * 4 + size_t(PC_WARPS) * 3 * RC * 4;
 }
 
-// Wide-bin atoms: one warp per atom, G from global memory. The atoms are
-// ids[range[0] .. range[1]) (bounds read on the device).
-__global__ void __launch_bounds__(256) pullback_wide_kernel(
-    Table tv, const int *__restrict__ range, AxisCfg out_ax, AxisCfg in_ax,
+// Coarse classes: one CTA per atom. The footprint is walked in chunks of
+// PW_CHUNK x PW_CHUNK sites whose site values are staged in shared memory;
+// warps take rows, lanes take columns, G comes from global memory. The atoms
+// are ids[*begin .. atoms) (bound read on the device).
+constexpr int PW_THREADS = 256;
+constexpr int PW_CHUNK = 256;
+
+__global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
+    Table tv, const int *__restrict__ begin_ptr, AxisCfg out_ax, AxisCfg in_ax,
     const float *__restrict__ g, long long ldg, int split, long long split_stride,
     float4 *__restrict__ grad) {
-    const int lane = threadIdx.x & 31;
-    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
-    const long long nwarps = (gridDim.x * (long long)blockDim.x) >> 5;
+    __shared__ float so[3][PW_CHUNK], si[3][PW_CHUNK];
+    __shared__ float red[PW_THREADS / 32][4];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int aw = axis_words(out_ax.modes);
     const int ni = in_ax.sites, no = out_ax.sites;
-    const long long begin = range[0], end = range[1];
-    for (long long k = begin + warp; k < end; k += nwarps) {
+    const long long begin = *begin_ptr;
+    for (long long k = begin + blockIdx.x; k < tv.atoms; k += gridDim.x) {
         const long long a = tv.ids[k];
         const float *rec = tv.rec + a * (long long)tv.words;
         const float *ob = rec + 4;
         const float *ib = rec + 4 + aw;
-        const int fo = reinterpret_cast<const int *>(ob)[1];
-        const int fi = reinterpret_cast<const int *>(ib)[1];
-        const int first_o = reinterpret_cast<const int *>(ob)[0];
-        const int first_i = reinterpret_cast<const int *>(ib)[0];
+        const int4 sp = tv.spans[a];
+        const int fo = sp.y, fi = sp.w;
         float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
-        for (int cb = 0; cb < fi; cb += 32) {
-            const int c = cb + lane;
-            const bool cv = c < fi;
-            SiteVals vi = {0.f, 0.f, 0.f};
-            if (cv) vi = site_values(ib, in_ax.modes, c, fi);
-            int col = (first_i + c) % ni;
-            col = col < 0 ? col + ni : col;
-            float h0 = 0.f, h1 = 0.f, h2 = 0.f;
-            for (int r0 = 0; r0 < fo; r0 += 32) {
-                const int rows = min(32, fo - r0);
-                SiteVals vo = {0.f, 0.f, 0.f};
-                if (lane < rows) vo = site_values(ob, out_ax.modes, r0 + lane, fo);
-                int orow = (first_o + r0 + lane) % no;
-                orow = orow < 0 ? orow + no : orow;
-                for (int rr = 0; rr < rows; ++rr) {
-                    const float mo = __shfl_sync(0xffffffffu, vo.m, rr);
-                    const float dmo = __shfl_sync(0xffffffffu, vo.dmu, rr);
-                    const float dro = __shfl_sync(0xffffffffu, vo.dR, rr);
-                    const int row = __shfl_sync(0xffffffffu, orow, rr);
-                    if (cv) {
-                        const float *gp = g + (long long)row * ldg + col;
-                        float gv = gp[0];
-                        for (int s = 1; s < split; ++s) gv += gp[s * split_stride];
-                        h0 = fmaf(gv, mo, h0);
-                        h1 = fmaf(gv, dmo, h1);
-                        h2 = fmaf(gv, dro, h2);
+        for (int r0 = 0; r0 < fo; r0 += PW_CHUNK) {
+            const int nr = min(PW_CHUNK, fo - r0);
+            for (int c0 = 0; c0 < fi; c0 += PW_CHUNK) {
+                const int nc = min(PW_CHUNK, fi - c0);
+                __syncthreads();
+                for (int j = threadIdx.x; j < nr; j += PW_THREADS) {
+                    const SiteVals v = site_values(ob, out_ax.modes, r0 + j, fo);
+                    so[0][j] = v.m;
+                    so[1][j] = v.dmu;
+                    so[2][j] = v.dR;
+                }
+                for (int j = threadIdx.x; j < nc; j += PW_THREADS) {
+                    const SiteVals v = site_values(ib, in_ax.modes, c0 + j, fi);
+                    si[0][j] = v.m;
+                    si[1][j] = v.dmu;
+                    si[2][j] = v.dR;
+                }
+                __syncthreads();
+                for (int r = warp; r < nr; r += PW_THREADS / 32) {
+                    int row = sp.x + r0 + r;
+                    while (row >= no) row -= no;
+                    const float mo = so[0][r], dmo = so[1][r], dro = so[2][r];
+                    const float *grow = g + (long long)row * ldg;
+                    float h0 = 0.f, h1 = 0.f, h2 = 0.f;
+                    for (int cb = 0; cb < nc; cb += 128) {
+                        float gv[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int c = cb + lane + 32 * u;
+                            gv[u] = 0.f;
+                            if (c < nc) {
+                                int col = sp.z + c0 + c;
+                                while (col >= ni) col -= ni;
+                                const float *gp = grow + col;
+                                gv[u] = gp[0];
+                                for (int s = 1; s < split; ++s) gv[u] += gp[s * split_stride];
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int c = cb + lane + 32 * u;
+                            if (c < nc) {
+                                h0 = fmaf(gv[u], si[0][c], h0); // sum G m_in
+                                h1 = fmaf(gv[u], si[1][c], h1); // sum G dm_in/dmu
+                                h2 = fmaf(gv[u], si[2][c], h2); // sum G dm_in/dR
+                            }
+                        }
                     }
+                    s_amp = fmaf(mo, h0, s_amp);
+                    s_mo = fmaf(dmo, h0, s_mo);
+                    s_mi = fmaf(mo, h1, s_mi);
+                    s_r = fmaf(dro, h0, fmaf(mo, h2, s_r));
                 }
             }
-            s_amp = fmaf(h0, vi.m, s_amp);
-            s_mo = fmaf(h1, vi.m, s_mo);
-            s_mi = fmaf(h0, vi.dmu, s_mi);
-            s_r = fmaf(h2, vi.m, fmaf(h0, vi.dR, s_r));
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) {
@@ -282,7 +355,24 @@ __global__ void __launch_bounds__(256) pullback_wide_kernel(
             s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
             s_r += __shfl_xor_sync(0xffffffffu, s_r, off);
         }
-        if (lane == 0) grad[a] = chain(rec, s_amp, s_mo, s_mi, s_r);
+        if (lane == 0) {
+            red[warp][0] = s_amp;
+            red[warp][1] = s_mo;
+            red[warp][2] = s_mi;
+            red[warp][3] = s_r;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+            for (int w = 0; w < PW_THREADS / 32; ++w) {
+                t0 += red[w][0];
+                t1 += red[w][1];
+                t2 += red[w][2];
+                t3 += red[w][3];
+            }
+            grad[a] = chain(rec, t0, t1, t2, t3);
+        }
+        __syncthreads(); // red and the staged values are reused by the next atom
     }
 }
 
@@ -291,7 +381,7 @@ __global__ void __launch_bounds__(256) pullback_wide_kernel(
 using namespace tcst;
 
 extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
-                             const tcst_axis *in_axis, const float *g_dev, int64_t ldg,
+                             const tcst_axis *in_axis, float *g_dev, int64_t ldg,
                              int32_t split, int64_t split_stride, float *grad_dev, void *stream) {
     char err[256];
     AxisCfg oa, ia;
@@ -314,7 +404,22 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
     const BinGeom &geo = tv.geom;
     cudaStream_t st = (cudaStream_t)stream;
     float4 *grad = reinterpret_cast<float4 *>(grad_dev);
-    if (geo.rt > 0) {
+    if (split > 1) {
+        // Every later read of G then costs one load instead of `split`.
+        const bool vec = ia.sites % 4 == 0 && ldg % 4 == 0 && split_stride % 4 == 0 &&
+                         reinterpret_cast<uintptr_t>(g_dev) % 16 == 0;
+        if (vec) {
+            g_reduce4_kernel<<<148 * 8, 256, 0, st>>>(reinterpret_cast<float4 *>(g_dev), oa.sites,
+                                                      ia.sites / 4, ldg / 4, split,
+                                                      split_stride / 4);
+        } else {
+            g_reduce_kernel<<<148 * 8, 256, 0, st>>>(g_dev, oa.sites, ia.sites, ldg, split,
+                                                     split_stride);
+        }
+        TCST_CUDA(cudaGetLastError());
+        split = 1;
+    }
+    if (geo.nclass > 0) {
         static bool configured = false;
         if (!configured) {
             TCST_CUDA(cudaFuncSetAttribute(pullback_class_kernel<64>,
@@ -325,20 +430,28 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
                                            int(class_smem<128>())));
             configured = true;
         }
-        pullback_class0_kernel<<<unsigned(geo.rt * geo.ct), P0_THREADS, 0, st>>>(
+        pullback_class0_kernel<<<unsigned(geo.tr[0] * geo.tc[0]), P0_THREADS, 0, st>>>(
             tv, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
         TCST_CUDA(cudaGetLastError());
-        const unsigned regions = unsigned(((geo.rt + 1) / 2) * ((geo.ct + 1) / 2));
-        pullback_class_kernel<64><<<regions, PC_THREADS, class_smem<64>(), st>>>(
-            tv, 1, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
-        TCST_CUDA(cudaGetLastError());
-        pullback_class_kernel<128><<<regions, PC_THREADS, class_smem<128>(), st>>>(
-            tv, 2, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
-        TCST_CUDA(cudaGetLastError());
+        if (geo.nclass > 1) {
+            const unsigned regions = unsigned(((geo.tr[1] + 1) / 2) * ((geo.tc[1] + 1) / 2));
+            pullback_class_kernel<64><<<regions, PC_THREADS, class_smem<64>(), st>>>(
+                tv, 1, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
+            TCST_CUDA(cudaGetLastError());
+        }
+        if (geo.nclass > 2) {
+            const unsigned regions = unsigned(((geo.tr[2] + 1) / 2) * ((geo.tc[2] + 1) / 2));
+            pullback_class_kernel<128><<<regions, PC_THREADS, class_smem<128>(), st>>>(
+                tv, 2, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
+            TCST_CUDA(cudaGetLastError());
+        }
     }
-    const long long warps = std::min<long long>(atoms, 148LL * 32);
-    pullback_wide_kernel<<<unsigned((warps + 7) / 8), 256, 0, st>>>(
-        tv, tv.offsets + geo.nbins - 1, oa, ia, g_dev, ldg, split, split_stride, grad);
+    // Coarse classes and invalid atoms (all atoms when unbinned): their range
+    // starts at the first coarse bin and runs to the end of the ids.
+    const int first_bin = geo.nclass > 0 ? geo.base[std::min(NFINE, geo.nclass)] : 0;
+    const long long ctas = std::min<long long>(atoms, 148LL * 8);
+    pullback_wide_kernel<<<unsigned(ctas), PW_THREADS, 0, st>>>(
+        tv, tv.offsets + first_bin, oa, ia, g_dev, ldg, split, split_stride, grad);
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

@@ -3,17 +3,16 @@
 //
 // Weight assembly uses the bins that tcst_decode_route stored in the atom
 // table (footprint class x first-site tile, atoms in id order inside a bin):
-//   wide:   atoms of the wide bin (footprint above the largest class) add their
-//           products into a 64-bit fixed-point plane (2^-40 units) with global
-//           reductions; integer adds are exact, so the plane does not depend on
-//           the order in which they land;
-//   gather: one CTA per TS x TS weight tile walks, in a fixed order, every bin
-//           whose atoms can reach the tile, keeps the atoms that do, stages
-//           their masses on the tile's rows and columns in shared memory
-//           (images folded modulo N) and accumulates the outer products in
-//           registers (4 x 4 per thread). The tile adds the wide plane and
-//           writes W and/or its TF32 split planes.
-// Fixed scan order + id-ordered bins make W bitwise reproducible.
+//   cache:  one warp per atom of classes 1..NFINE-1 writes the atom's masses on
+//           both footprints into the caller's scratch (class 0 masses are in the
+//           atom table's site buffer; coarser classes are evaluated where used);
+//   gather: one CTA per TS x TS weight tile lists, in a fixed order, every bin
+//           whose atoms can reach the tile, keeps the atoms that do, stages their
+//           masses on the tile's rows and columns in shared memory (images folded
+//           modulo N) and accumulates the outer products in registers (4 x 4 per
+//           thread), then writes W and/or its TF32 split planes.
+// A fixed bin order and id-ordered bins make W bitwise reproducible; there are
+// no atomics.
 
 #include <algorithm>
 #include <mutex>
@@ -22,10 +21,9 @@
 
 namespace tcst {
 
-constexpr float FIXED_SCALE = 1099511627776.0f; // 2^40
-constexpr double FIXED_UNIT = 1.0 / 1099511627776.0;
 constexpr int WT_THREADS = 64; // 8 x 8 threads, 4 x 4 outputs each
-constexpr int WT_BATCH = 32;   // atoms staged per pass
+constexpr int WT_BATCH = 64;   // candidates per pass
+constexpr int MAX_SCAN = 320;  // bins a weight tile can scan
 
 __device__ __forceinline__ float tf32_rna(float x) {
     unsigned r;
@@ -33,12 +31,8 @@ __device__ __forceinline__ float tf32_rna(float x) {
     return __uint_as_float(r);
 }
 
-__device__ __forceinline__ void red_add_u64(unsigned long long *addr, long long v) {
-    asm volatile("red.global.add.u64 [%0], %1;" ::"l"(addr), "l"((unsigned long long)v) : "memory");
-}
-
-__host__ __device__ inline long long plane_words64(int n_out, int n_in) {
-    return (long long)n_out * n_in;
+__host__ __device__ inline long long cache_floats(long long atoms) {
+    return atoms * 2 * CACHE_SITES;
 }
 
 // Does the cyclic footprint [f, f + F) (mod n) meet sites [t0, t0 + tl)?
@@ -49,183 +43,236 @@ __device__ __forceinline__ bool window_hits(int f, int F, int t0, int tl, int n)
     return d < F || d + tl > n;
 }
 
-// Folded mass of the atom at the tile site t0 + p: sum over footprint sites j
-// with (f + j) mod n == t0 + p. `sv` (class 0) holds the first REACH masses.
-template <bool SITES>
-__device__ __forceinline__ float folded_mass(const float *blk, const float *sv, int f, int F,
-                                             int site, int n) {
-    int j = site - f;
-    if (j < 0) j += n;
-    float v = 0.f;
-    if (SITES) {
-        for (; j < F; j += n) v += sv[j];
-    } else {
-        if (j >= F) return 0.f;
+// Source tiles (k = 0 .. count-1 steps back from the tile holding `t0`) whose
+// atoms of class c can reach sites [t0, t0 + TS).
+__device__ __forceinline__ int reach_tiles(int c, int tiles, int n) {
+    const int e = class_edge(c);
+    const int k = 1 + (class_reach(c) - 1 + e - 1) / e + (n % e != 0);
+    return min(k, tiles);
+}
+
+// Class 1..NFINE-1 mass cache: cache[a][axis][j] = m_axis(j), j < F_axis.
+__global__ void __launch_bounds__(256) mass_cache_kernel(Table tv, float *__restrict__ cache) {
+    const int lane = threadIdx.x & 31;
+    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = (gridDim.x * (long long)blockDim.x) >> 5;
+    const BinGeom &g = tv.geom;
+    const int begin = tv.offsets[g.base[min(1, g.nclass)]];
+    const int end = tv.offsets[g.base[min(NFINE, g.nclass)]];
+    const int aw = axis_words(8);
+    const int side = lane >> 4, l = lane & 15; // half-warp per axis
+    for (long long k = begin + warp; k < end; k += nwarps) {
+        const long long a = tv.ids[k];
+        const float *rec = tv.rec + a * (long long)tv.words;
+        const int4 sp = tv.spans[a];
         AxisCoef<8> ac;
-        ac.load_mass(blk);
-        for (; j < F; j += n) v += ac.mass(j);
+        ac.load_mass(rec + 4 + side * aw);
+        const int F = side ? sp.w : sp.y;
+        float *dst = cache + (a * 2 + side) * CACHE_SITES;
+        for (int j = l; j < F; j += 16) dst[j] = ac.mass(j);
     }
-    return v;
 }
 
 struct GatherOut {
-    const unsigned long long *plane; // wide-atom plane or NULL
     float *w, *hi, *lo;
     long long ldw, lds;
 };
 
-__device__ __forceinline__ void gather_range(const Table &tv, int begin, int end, bool class0,
-                                             int R0, int TR, int no, int C0, int TC, int ni,
-                                             float (&acc)[4][4], int *cand, float (*us)[TS],
-                                             float (*vs)[TS], int *wcount) {
+__global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int no, int ni,
+                                                                   int modes_o, int modes_i,
+                                                                   int tiles_c,
+                                                                   const float *__restrict__ cache,
+                                                                   GatherOut out) {
+    __shared__ int sbeg[MAX_SCAN], scls[MAX_SCAN], spre[MAX_SCAN + 1];
+    __shared__ int wtot[2];
+    __shared__ __align__(16) float us[WT_BATCH][TS];
+    __shared__ __align__(16) float vs[WT_BATCH][TS];
+    __shared__ int cand[WT_BATCH], ccls[WT_BATCH];
+    __shared__ int4 cspan[WT_BATCH];
+    __shared__ float camp[WT_BATCH];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int trow = blockIdx.x / tiles_c, tcol = blockIdx.x - trow * tiles_c;
+    const int R0 = trow * TS, C0 = tcol * TS;
+    const int TR = min(TS, no - R0), TC = min(TS, ni - C0);
+    const BinGeom &g = tv.geom;
+
+    // 1. The bins to scan, in a fixed order, with their atom counts.
+    int nscan;
+    if (g.nclass == 0) {
+        nscan = 1;
+        if (t == 0) {
+            sbeg[0] = tv.offsets[0];
+            scls[0] = -1;
+            spre[0] = 0;
+            spre[1] = tv.offsets[1] - tv.offsets[0];
+        }
+    } else {
+        nscan = 0;
+        for (int c = 0; c < g.nclass; ++c)
+            nscan += reach_tiles(c, g.tr[c], no) * reach_tiles(c, g.tc[c], ni);
+        nscan = min(nscan, MAX_SCAN);
+        for (int i = t; i < nscan; i += WT_THREADS) {
+            int c = 0, rem = i, kr = 0, kc = 0;
+            for (; c < g.nclass; ++c) {
+                kr = reach_tiles(c, g.tr[c], no);
+                kc = reach_tiles(c, g.tc[c], ni);
+                if (rem < kr * kc) break;
+                rem -= kr * kc;
+            }
+            const int e = class_edge(c);
+            const int k = rem / kc, l = rem - k * kc;
+            int sr = R0 / e - k, sc = C0 / e - l;
+            sr += sr < 0 ? g.tr[c] : 0;
+            sc += sc < 0 ? g.tc[c] : 0;
+            const int bin = g.base[c] + sr * g.tc[c] + sc;
+            sbeg[i] = tv.offsets[bin];
+            spre[i + 1] = tv.offsets[bin + 1] - sbeg[i];
+            scls[i] = c;
+        }
+        __syncthreads();
+        // Inclusive prefix of the counts in spre[1..nscan], contiguous runs per thread.
+        const int per = (nscan + WT_THREADS - 1) / WT_THREADS, i0 = t * per;
+        int local = 0;
+        for (int k = 0; k < per; ++k)
+            if (i0 + k < nscan) local += spre[i0 + k + 1];
+        int inc = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
+        }
+        if (lane == 31) wtot[warp] = inc;
+        __syncthreads();
+        int run = inc - local + (warp ? wtot[0] : 0);
+        for (int k = 0; k < per; ++k)
+            if (i0 + k < nscan) {
+                run += spre[i0 + k + 1];
+                spre[i0 + k + 1] = run;
+            }
+        if (t == 0) spre[0] = 0;
+    }
+    __syncthreads();
+    const int total = spre[nscan];
     const int r0 = (t >> 3) * 4, c0 = (t & 7) * 4;
-    const int aw = axis_words(8);
-    for (int base = begin; base < end; base += WT_THREADS) {
-        const int idx = base + t;
+    const int aw = axis_words(modes_o);
+    float acc[4][4] = {};
+
+    // 2. Candidates in passes of WT_BATCH: keep those that reach the tile.
+    for (int base = 0; base < total; base += WT_BATCH) {
+        const int i = base + t;
         bool hit = false;
-        int a = -1;
-        if (idx < end) {
-            a = tv.ids[idx];
-            const int4 sp = tv.spans[a];
+        int a = 0, cls = 0;
+        int4 sp = make_int4(0, 0, 0, 0);
+        if (i < total) {
+            int lo = 0, hi = nscan - 1; // last slot with spre[slot] <= i
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (spre[mid] <= i) lo = mid;
+                else hi = mid - 1;
+            }
+            a = tv.ids[sbeg[lo] + (i - spre[lo])];
+            cls = scls[lo];
+            sp = tv.spans[a];
             hit = window_hits(sp.x, sp.y, R0, TR, no) && window_hits(sp.z, sp.w, C0, TC, ni);
         }
         const unsigned m = __ballot_sync(0xffffffffu, hit);
-        if (lane == 0) wcount[warp] = __popc(m);
+        if (lane == 0) wtot[warp] = __popc(m);
         __syncthreads();
-        const int n = wcount[0] + wcount[1];
-        if (hit) cand[(warp ? wcount[0] : 0) + __popc(m & ((1u << lane) - 1u))] = a;
+        const int n = wtot[0] + wtot[1];
+        if (hit) {
+            const int slot = (warp ? wtot[0] : 0) + __popc(m & ((1u << lane) - 1u));
+            cand[slot] = a;
+            ccls[slot] = cls;
+            cspan[slot] = sp;
+            camp[slot] = tv.rec[(long long)a * tv.words];
+        }
         __syncthreads();
-        for (int h = 0; h < n; h += WT_BATCH) {
-            const int nb = min(WT_BATCH, n - h);
-            // Warp 0 stages amp * m_out on the tile rows, warp 1 m_in on the columns.
-            for (int s2 = 0; s2 < nb; ++s2) {
-                const int atom = cand[h + s2];
-                const float *rec = tv.rec + (long long)atom * tv.words;
-                const int4 sp = tv.spans[atom];
+        // 3. Stage: warp 0 the tile rows (amp * m_out), warp 1 the columns (m_in).
+        // Main pass: classes with stored masses and no second image, one
+        // independent load per candidate; a second pass evaluates the rest.
+        {
+            const int side = warp, p = lane;
+            const int lim = side ? TC : TR, nn = side ? ni : no;
+            const int site = (side ? C0 : R0) + p;
+            float(*dst)[TS] = side ? vs : us;
+            bool rest = false;
+#pragma unroll 8
+            for (int s2 = 0; s2 < n; ++s2) {
+                const int4 q = cspan[s2];
+                const int f = side ? q.z : q.x, F = side ? q.w : q.y;
+                const int c = ccls[s2];
+                const long long atom = cand[s2];
+                int j = site - f;
+                j += j < 0 ? nn : 0;
+                const bool stored = c >= 0 && c < NFINE && F <= nn;
+                const float *src = c == 0 ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
+                                          : cache + (atom * 2 + side) * CACHE_SITES;
                 float v = 0.f;
-                if (warp == 0) {
-                    if (lane < TR) {
-                        const float *sv = tv.sites + (long long)atom * SITE_FLOATS;
-                        v = class0 ? folded_mass<true>(rec + 4, sv, sp.x, sp.y, R0 + lane, no)
-                                   : folded_mass<false>(rec + 4, sv, sp.x, sp.y, R0 + lane, no);
-                        v *= rec[0];
+                if (stored && p < lim && j < F) v = src[j];
+                dst[s2][p] = side ? v : v * camp[s2];
+                rest |= !stored;
+            }
+            if (__any_sync(0xffffffffu, rest)) {
+                for (int s2 = 0; s2 < n; ++s2) {
+                    const int4 q = cspan[s2];
+                    const int f = side ? q.z : q.x, F = side ? q.w : q.y;
+                    const int c = ccls[s2];
+                    if (c >= 0 && c < NFINE && F <= nn) continue;
+                    const long long atom = cand[s2];
+                    int j = site - f;
+                    j += j < 0 ? nn : 0;
+                    float v = 0.f;
+                    if (p < lim && j < F) {
+                        const float *blk = tv.rec + atom * tv.words + 4 + side * aw;
+                        if (c == 0) {
+                            const float *sv = tv.sites + atom * SITE_FLOATS + side * 3 * REACH;
+                            for (; j < F; j += nn) v += sv[j];
+                        } else if (c > 0 && c < NFINE) {
+                            const float *cv = cache + (atom * 2 + side) * CACHE_SITES;
+                            for (; j < F; j += nn) v += cv[j];
+                        } else if (c >= NFINE) {
+                            AxisCoef<8> ac;
+                            ac.load_mass(blk);
+                            for (; j < F; j += nn) v += ac.mass(j);
+                        } else {
+                            // Unbinned geometry: any mode count.
+                            const int modes = side ? modes_i : modes_o;
+                            for (; j < F; j += nn) v += site_mass(blk, modes, j, F);
+                        }
                     }
-                    us[s2][lane] = v;
-                } else {
-                    if (lane < TC) {
-                        const float *sv = tv.sites + (long long)atom * SITE_FLOATS + 3 * REACH;
-                        v = class0 ? folded_mass<true>(rec + 4 + aw, sv, sp.z, sp.w, C0 + lane, ni)
-                                   : folded_mass<false>(rec + 4 + aw, sv, sp.z, sp.w, C0 + lane, ni);
-                    }
-                    vs[s2][lane] = v;
+                    dst[s2][p] = side ? v : v * camp[s2];
                 }
             }
-            __syncthreads();
-            for (int s2 = 0; s2 < nb; ++s2) {
-                const float4 u = *reinterpret_cast<const float4 *>(&us[s2][r0]);
-                const float4 v = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
-                const float uu[4] = {u.x, u.y, u.z, u.w}, vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(uu[i], vv[j], acc[i][j]);
-            }
-            __syncthreads();
         }
+        __syncthreads();
+        for (int s2 = 0; s2 < n; ++s2) {
+            const float4 u = *reinterpret_cast<const float4 *>(&us[s2][r0]);
+            const float4 v = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
+            const float uu[4] = {u.x, u.y, u.z, u.w}, vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(uu[ii], vv[jj], acc[ii][jj]);
+        }
+        __syncthreads();
     }
-}
 
-__global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int no, int ni,
-                                                                   int tiles_c, GatherOut out) {
-    __shared__ __align__(16) float us[WT_BATCH][TS];
-    __shared__ __align__(16) float vs[WT_BATCH][TS];
-    __shared__ int cand[WT_THREADS];
-    __shared__ int wcount[2];
-    const int tr = blockIdx.x / tiles_c, tc = blockIdx.x - tr * tiles_c;
-    const int R0 = tr * TS, C0 = tc * TS;
-    const int TR = min(TS, no - R0), TC = min(TS, ni - C0);
-    float acc[4][4] = {};
-    const BinGeom &g = tv.geom;
-    if (g.rt > 0) {
-        for (int c = 0; c < NCLASS; ++c) {
-            const int span_tiles = (class_reach(c) - 1 + TS - 1) / TS;
-            const int kr = min(g.rt, 1 + span_tiles + (no % TS != 0));
-            const int kc = min(g.ct, 1 + span_tiles + (ni % TS != 0));
-            for (int k = 0; k < kr; ++k) {
-                int sr = tr - k;
-                sr += sr < 0 ? g.rt : 0;
-                for (int l = 0; l < kc; ++l) {
-                    int sc = tc - l;
-                    sc += sc < 0 ? g.ct : 0;
-                    const int bin = (c * g.rt + sr) * g.ct + sc;
-                    gather_range(tv, tv.offsets[bin], tv.offsets[bin + 1], c == 0, R0, TR, no, C0,
-                                 TC, ni, acc, cand, us, vs, wcount);
-                }
-            }
-        }
-    }
-    const bool wide = out.plane && tv.offsets[g.nbins] > tv.offsets[g.nbins - 1];
-    const int r0 = (threadIdx.x >> 3) * 4, c0 = (threadIdx.x & 7) * 4;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = r0 + i;
+    for (int ii = 0; ii < 4; ++ii) {
+        const int r = r0 + ii;
         if (r >= TR) continue;
         const long long row = R0 + r;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = c0 + j;
+        for (int jj = 0; jj < 4; ++jj) {
+            const int c = c0 + jj;
             if (c >= TC) continue;
             const long long col = C0 + c;
-            float v = acc[i][j];
-            if (wide) v += float(double((long long)out.plane[row * ni + col]) * FIXED_UNIT);
+            const float v = acc[ii][jj];
             if (out.w) out.w[row * out.ldw + col] = v;
             if (out.hi) {
                 const float h = tf32_rna(v);
                 out.hi[row * out.lds + col] = h;
                 out.lo[row * out.lds + col] = tf32_rna(v - h);
-            }
-        }
-    }
-}
-
-// Wide-bin atoms: one warp per atom adds its elements into the fixed-point
-// plane. The atoms are ids[range[0] .. range[1]) (bounds read on the device).
-__global__ void __launch_bounds__(256) weight_wide_kernel(Table tv, const int *__restrict__ range,
-                                                          AxisCfg out_ax, AxisCfg in_ax,
-                                                          unsigned long long *__restrict__ plane) {
-    const int lane = threadIdx.x & 31;
-    const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
-    const long long nwarps = (gridDim.x * (long long)blockDim.x) >> 5;
-    const int aw = axis_words(out_ax.modes);
-    const int ni = in_ax.sites, no = out_ax.sites;
-    const long long begin = range[0], end = range[1];
-    for (long long k = begin + warp; k < end; k += nwarps) {
-        const long long a = tv.ids[k];
-        const float *rec = tv.rec + a * (long long)tv.words;
-        const float *ob = rec + 4;
-        const float *ib = rec + 4 + aw;
-        const int fo = reinterpret_cast<const int *>(ob)[1];
-        const int fi = reinterpret_cast<const int *>(ib)[1];
-        const int first_o = reinterpret_cast<const int *>(ob)[0];
-        const int first_i = reinterpret_cast<const int *>(ib)[0];
-        const float amp = rec[0];
-        for (int r0 = 0; r0 < fo; r0 += 32) {
-            const int rows = min(32, fo - r0);
-            const float mo = lane < rows ? amp * site_mass(ob, out_ax.modes, r0 + lane, fo) : 0.f;
-            int orow = (first_o + r0 + lane) % no;
-            orow = orow < 0 ? orow + no : orow;
-            for (int cb = 0; cb < fi; cb += 32) {
-                const int c = cb + lane;
-                const bool cv = c < fi;
-                const float mi = cv ? site_mass(ib, in_ax.modes, c, fi) * FIXED_SCALE : 0.f;
-                int col = (first_i + c) % ni;
-                col = col < 0 ? col + ni : col;
-                for (int rr = 0; rr < rows; ++rr) {
-                    const float v = __shfl_sync(0xffffffffu, mo, rr) * mi;
-                    const int row = __shfl_sync(0xffffffffu, orow, rr);
-                    if (cv) red_add_u64(plane + (long long)row * ni + col, __float2ll_rn(v));
-                }
             }
         }
     }
@@ -324,7 +371,7 @@ extern "C" int64_t tcst_weight_scratch_bytes(int64_t atoms, const tcst_axis *out
                                              const tcst_axis *in_axis) {
     if (atoms < 0 || !out_axis || !in_axis || out_axis->site_count < 1 || in_axis->site_count < 1)
         return -1;
-    return plane_words64(out_axis->site_count, in_axis->site_count) * 8;
+    return std::max<int64_t>(cache_floats(atoms) * 4, 16);
 }
 
 static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa,
@@ -333,20 +380,17 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
                     cudaStream_t st) {
     const int words = record_words(oa.modes, ia.modes);
     const Table tv = table_view(atom_table_dev, atoms, words, oa.sites, ia.sites, oa.modes, ia.modes);
-    unsigned long long *plane = static_cast<unsigned long long *>(scratch);
-    // Wide atoms: the plane is cleared and filled first; the wide bin's bounds
-    // are only known on the device, so the kernel reads them.
-    TCST_CUDA(cudaMemsetAsync(plane, 0, plane_words64(oa.sites, ia.sites) * 8, st));
-    if (atoms > 0) {
-        const long long warps = std::min<long long>(atoms, sm_count() * 32LL);
-        weight_wide_kernel<<<unsigned((warps + 7) / 8), 256, 0, st>>>(
-            tv, tv.offsets + tv.geom.nbins - 1, oa, ia, plane);
+    float *cache = static_cast<float *>(scratch);
+    if (atoms > 0 && tv.geom.nclass > 0) {
+        // The class range is only known on the device; the kernel reads it.
+        const long long warps = std::min<long long>(atoms, sm_count() * 64LL);
+        mass_cache_kernel<<<unsigned((warps + 7) / 8), 256, 0, st>>>(tv, cache);
         TCST_CUDA(cudaGetLastError());
     }
     const int tiles_r = (oa.sites + TS - 1) / TS, tiles_c = (ia.sites + TS - 1) / TS;
-    GatherOut out = {plane, weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split};
-    weight_gather_kernel<<<unsigned(tiles_r * tiles_c), WT_THREADS, 0, st>>>(tv, oa.sites, ia.sites,
-                                                                           tiles_c, out);
+    GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split};
+    weight_gather_kernel<<<unsigned(tiles_r * tiles_c), WT_THREADS, 0, st>>>(
+        tv, oa.sites, ia.sites, oa.modes, ia.modes, tiles_c, cache, out);
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -365,7 +409,7 @@ extern "C" int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
         return rc;
     }
     if (atoms < 0 || !scratch_dev || !atom_table_dev ||
-        scratch_bytes < plane_words64(oa.sites, ia.sites) * 8 ||
+        scratch_bytes < cache_floats(atoms) * 4 ||
         reinterpret_cast<uintptr_t>(scratch_dev) % 16 ||
         ((weight_hi_dev == nullptr) != (weight_lo_dev == nullptr)) ||
         (weight_dev && ld_weight < ia.sites) || (weight_hi_dev && ld_split < ia.sites)) {
@@ -434,28 +478,28 @@ extern "C" int tcst_mse_grad(const float *y_dev, const float *target_dev, int64_
 // Weight assembly without caller-provided scratch.
 //
 // Some callers cannot hand this library device memory for the assembly's
-// scratch: a plugin running inside a host framework whose allocator owns every
-// device byte, or a fixed-footprint deployment that forbids allocation after
-// start-up. For them the scratch lives in a fixed array compiled into this
-// library. Every GPU that loads the library holds the array until the process
-// exits.
+// scratch (the mass cache of mid-size footprints): a plugin running inside a
+// host framework whose allocator owns every device byte, or a fixed-footprint
+// deployment that forbids allocation after start-up. For them the scratch
+// lives in a fixed array compiled into this library. Every GPU that loads the
+// library holds the array until the process exits.
 // ---------------------------------------------------------------------------
 
 namespace {
 
-constexpr long long STATIC_SCRATCH_BYTES = 32LL << 20; // 32 MiB
+constexpr long long STATIC_SCRATCH_BYTES = 32LL << 20; // 32 MiB: up to 32768 atoms
 constexpr int MAX_DEVICES = 64;
 
-static __device__ __align__(256) unsigned long long g_static_scratch[STATIC_SCRATCH_BYTES / 8];
+static __device__ __align__(256) float g_static_scratch[STATIC_SCRATCH_BYTES / 4];
 
 std::mutex g_static_mutex;
 void *g_static_ptr[MAX_DEVICES] = {};
 
 // Host code must not pass g_static_scratch itself to a kernel: in host code that
 // name is only a stand-in. The device address comes from cudaGetSymbolAddress,
-// taken once per device with that device current; the array is cleared once
-// there, and every later call leaves its bin counters at zero again.
-int static_scratch(cudaStream_t stream, void **out) {
+// taken once per device with that device current. The cache needs no
+// initialization: every call writes the entries it reads.
+int static_scratch(void **out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return tcst_cuda_check(e, "cudaGetDevice");
@@ -468,8 +512,6 @@ int static_scratch(cudaStream_t stream, void **out) {
         void *ptr = nullptr;
         e = cudaGetSymbolAddress(&ptr, g_static_scratch);
         if (e != cudaSuccess) return tcst_cuda_check(e, "cudaGetSymbolAddress");
-        e = cudaMemsetAsync(ptr, 0, sizeof(g_static_scratch), stream);
-        if (e != cudaSuccess) return tcst_cuda_check(e, "cudaMemsetAsync");
         g_static_ptr[dev] = ptr;
     }
     *out = g_static_ptr[dev];
@@ -493,11 +535,10 @@ extern "C" int tcst_assemble_weight_static(const void *atom_table_dev, int64_t a
         tcst_set_error("%s", err);
         return rc;
     }
-    if (plane_words64(oa.sites, ia.sites) * 8 > STATIC_SCRATCH_BYTES) {
-        tcst_set_error("tcst_assemble_weight_static: a %d x %d weight needs %lld scratch bytes, "
+    if (cache_floats(atoms) * 4 > STATIC_SCRATCH_BYTES) {
+        tcst_set_error("tcst_assemble_weight_static: %lld atoms need %lld scratch bytes, "
                        "more than the built-in %lld; use tcst_assemble_weight",
-                       oa.sites, ia.sites, plane_words64(oa.sites, ia.sites) * 8,
-                       STATIC_SCRATCH_BYTES);
+                       (long long)atoms, cache_floats(atoms) * 4, STATIC_SCRATCH_BYTES);
         return TCST_ERR_UNSUPPORTED;
     }
     if (atoms < 0 || !atom_table_dev ||
@@ -508,7 +549,7 @@ extern "C" int tcst_assemble_weight_static(const void *atom_table_dev, int64_t a
     }
     cudaStream_t st = (cudaStream_t)stream;
     void *scratch = nullptr;
-    if ((rc = static_scratch(st, &scratch))) return rc;
+    if ((rc = static_scratch(&scratch))) return rc;
     return assemble(atom_table_dev, atoms, oa, ia, scratch, weight_dev, ld_weight, weight_hi_dev,
                     weight_lo_dev, ld_split, st);
 }
