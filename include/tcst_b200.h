@@ -192,6 +192,14 @@ int tcst_optimizer_step(float *p_dev, const float *grad_dev, float *exp_avg_dev,
                         float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
                         const tcst_adamw *params, void *stream);
 
+/* The same step with the tcst_adamw scalars in device memory (16-byte aligned),
+ * read when the kernel runs, so a captured CUDA graph can replay the step while
+ * the host refreshes the bias corrections between replays. No reference
+ * counterpart: the reference's optimizer reads its scalars on the host. */
+int tcst_optimizer_step_device(float *p_dev, const float *grad_dev, float *exp_avg_dev,
+                               float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
+                               const tcst_adamw *params_dev, void *stream);
+
 /* MSE upstream gradient dY = (Y - T) * scale split into TF32 hi/lo planes, plus
  * per-block partial sums of (Y - T)^2 in loss_partial_dev[blocks] (double).
  * Returns the number of partial blocks through *blocks (nullable). */

@@ -1,0 +1,83 @@
+"""The fused MSE train step: eager launches, CUDA-graph replays and the drop-in
+autograd API take the same step.
+
+Eager and replayed steps run the same kernels on the same buffers, so atoms and
+optimizer moments must agree bit for bit. The autograd path forms dY with torch
+ops instead of the fused loss kernel, so it agrees to float32 rounding.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from tests.golden_cases import load
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(seed=0):
+    from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
+    d = load("config5s")
+    grid = chart_presets.regular_grid(512, geometry="flat_torus")
+    layer = CSTLinear(charts=(grid, grid), atoms=torch.as_tensor(d["p0"]), device="cuda",
+                      validate="off",
+                      kernel=kernels.product(kernels.cell_mass(ChebyshevSpec(modes=8)),
+                                             coordinates=kernels.rational_radius(radius_max=256.0)))
+    opt = CSTAdamW(layer.parameters(), model=layer, lr=1e-3,
+                   field_lrs={"amplitude": 2.4e-3, "radius_fraction": 9.6e-3})
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    xs = [torch.randn(256, 512, device="cuda", generator=g) for _ in range(2)]
+    ts = [torch.randn(256, 512, device="cuda", generator=g) for _ in range(2)]
+    return layer, opt, xs, ts
+
+
+def _state(layer, opt):
+    p = layer.atoms.p
+    st = opt.state[p]
+    return [p.detach().clone(), st["exp_avg"].clone(), st["exp_avg_sq"].clone()]
+
+
+def test_graph_replay_matches_eager_steps():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from torchcst_b200.train import MSETrainStep
+    runs = []
+    for graphs in (False, True):
+        layer, opt, xs, ts = _setup()
+        step = MSETrainStep(layer, opt, 256)
+        losses = [float(step(xs[0], ts[0]))]
+        if graphs:
+            step.capture(list(zip(xs, ts)))
+        for i in range(1, 5):
+            losses.append(float(step(xs[i % 2], ts[i % 2])))
+        torch.cuda.synchronize()
+        runs.append((losses, _state(layer, opt), int(opt.state[layer.atoms.p]["step"])))
+        step.release()
+    (l0, s0, n0), (l1, s1, n1) = runs
+    assert n0 == n1 == 5
+    assert l0 == l1
+    for a, b in zip(s0, s1):
+        assert torch.equal(a, b)
+
+
+def test_fused_step_matches_autograd_api():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from torchcst_b200.train import MSETrainStep
+    layer, opt, xs, ts = _setup()
+    step = MSETrainStep(layer, opt, 256)
+    fused_loss = float(step(xs[0], ts[0]))
+    fused = _state(layer, opt)
+
+    layer2, opt2, _, _ = _setup()
+    y = layer2(xs[0])
+    loss = (y - ts[0]).square().mean()
+    loss.backward()
+    opt2.step()
+    api = _state(layer2, opt2)
+    api_loss = float(loss.detach())
+    assert abs(fused_loss - api_loss) <= 1e-6 * abs(api_loss)
+    # Same update up to float32 rounding of dY (torch ops vs the fused loss kernel).
+    for a, b in zip(fused, api):
+        a, b = a.cpu().numpy().astype(np.float64), b.cpu().numpy().astype(np.float64)
+        assert np.abs(a - b).max() <= 1e-4 * max(np.abs(b).max(), 1e-30)

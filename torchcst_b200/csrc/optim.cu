@@ -40,11 +40,9 @@ __device__ __forceinline__ float torus(float x, float period) {
     return mod;
 }
 
-__global__ void optimizer_kernel(float4 *__restrict__ p, const float4 *__restrict__ grad,
-                                 float4 *__restrict__ m, float4 *__restrict__ v,
-                                 long long atoms, int kind, tcst_adamw h) {
-    long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (a >= atoms) return;
+__device__ __forceinline__ void step_row(long long a, float4 *__restrict__ p,
+                                         const float4 *__restrict__ grad, float4 *__restrict__ m,
+                                         float4 *__restrict__ v, int kind, const tcst_adamw &h) {
     float4 prev = p[a], g = grad[a], mm = m[a], vv = v[a];
     float4 pt;
     pt.x = adam_one(prev.x, g.x, mm.x, vv.x, h);
@@ -111,6 +109,25 @@ __global__ void optimizer_kernel(float4 *__restrict__ p, const float4 *__restric
     p[a] = out;
 }
 
+__global__ void optimizer_kernel(float4 *__restrict__ p, const float4 *__restrict__ grad,
+                                 float4 *__restrict__ m, float4 *__restrict__ v,
+                                 long long atoms, int kind, tcst_adamw h) {
+    const long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (a < atoms) step_row(a, p, grad, m, v, kind, h);
+}
+
+// Same step with the scalars read from device memory when the kernel runs.
+__global__ void optimizer_dev_kernel(float4 *__restrict__ p, const float4 *__restrict__ grad,
+                                     float4 *__restrict__ m, float4 *__restrict__ v,
+                                     long long atoms, int kind,
+                                     const tcst_adamw *__restrict__ hp) {
+    __shared__ tcst_adamw h;
+    if (threadIdx.x == 0) h = *hp;
+    __syncthreads();
+    const long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (a < atoms) step_row(a, p, grad, m, v, kind, h);
+}
+
 } // namespace tcst
 
 using namespace tcst;
@@ -133,6 +150,29 @@ extern "C" int tcst_optimizer_step(float *p_dev, const float *grad_dev, float *e
     optimizer_kernel<<<unsigned((atoms + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
         (float4 *)p_dev, (const float4 *)grad_dev, (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev,
         atoms, kind, *params);
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+extern "C" int tcst_optimizer_step_device(float *p_dev, const float *grad_dev, float *exp_avg_dev,
+                                          float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
+                                          const tcst_adamw *params_dev, void *stream) {
+    if (atoms < 0 || !params_dev || (kind != TCST_RATIONAL && kind != TCST_POLAR) ||
+        (atoms && (!p_dev || !grad_dev || !exp_avg_dev || !exp_avg_sq_dev))) {
+        tcst_set_error("tcst_optimizer_step_device: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(p_dev) | reinterpret_cast<uintptr_t>(grad_dev) |
+         reinterpret_cast<uintptr_t>(exp_avg_dev) | reinterpret_cast<uintptr_t>(exp_avg_sq_dev) |
+         reinterpret_cast<uintptr_t>(params_dev)) %
+        16) {
+        tcst_set_error("tcst_optimizer_step_device: pointers must be 16-byte aligned");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (atoms == 0) return TCST_OK;
+    optimizer_dev_kernel<<<unsigned((atoms + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        (float4 *)p_dev, (const float4 *)grad_dev, (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev,
+        atoms, kind, params_dev);
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

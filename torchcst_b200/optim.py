@@ -16,6 +16,7 @@ from __future__ import annotations
 import ctypes
 import math
 
+import numpy as np
 import torch
 from torch.optim import AdamW
 
@@ -28,7 +29,8 @@ REFERENCE = "_cst_field_lr_reference"
 
 
 def _f32(x) -> float:
-    return float(torch.tensor(x, dtype=torch.float32))
+    """Round a Python float to float32 (round to nearest even), as torch.tensor does."""
+    return float(np.float32(x))
 
 
 class CSTAdamW(AdamW):
@@ -76,14 +78,29 @@ class CSTAdamW(AdamW):
     def _native_params(self, site: CSTLinear, group, step: int) -> N.AdamW:
         lr = group["lr"]
         beta1, beta2 = group["betas"]
-        h = N.AdamW()
-        h.lerp_weight = _f32(1 - beta1)
-        h.beta2 = _f32(beta2)
-        h.one_minus_beta2 = _f32(1 - beta2)
+        key = (id(site), lr, beta1, beta2, group["eps"], group["weight_decay"],
+               tuple(sorted((group.get("field_lrs") or {}).items())), group.get(REFERENCE))
+        cache = self.__dict__.setdefault("_params_cache", {})
+        base = cache.get(key)
+        if base is None:
+            if len(cache) >= 64:  # learning-rate schedules create a key per rate
+                cache.clear()
+            base = cache[key] = self._step_free_params(site, group)
+        h = N.AdamW.from_buffer_copy(base)
         bc1 = 1 - beta1 ** step
         bc2 = 1 - beta2 ** step
         h.neg_step_size = _f32(-(lr / bc1))
         h.bias2_sqrt = _f32(bc2 ** 0.5)
+        return h
+
+    def _step_free_params(self, site: CSTLinear, group) -> N.AdamW:
+        """Every tcst_adamw field except the two bias corrections."""
+        lr = group["lr"]
+        beta1, beta2 = group["betas"]
+        h = N.AdamW()
+        h.lerp_weight = _f32(1 - beta1)
+        h.beta2 = _f32(beta2)
+        h.one_minus_beta2 = _f32(1 - beta2)
         h.eps = _f32(group["eps"])
         wd = group["weight_decay"]
         h.has_decay = int(wd != 0)
@@ -121,6 +138,31 @@ class CSTAdamW(AdamW):
             h.polar_decay = float(torch.exp(-4.0 * rr * torch.tensor(lr, dtype=p32)))
             h.polar_energy_step = _f32(lr) if coords.activity_mode == "time_energy" else 0.0
         return h
+
+    def site_step(self, p):
+        """Advance the step count of atom parameter ``p`` exactly as :meth:`step`
+        does and return ``(params, state, kind)`` for ``tcst_optimizer_step*``, or
+        ``None`` when the group's learning rate is 0 (no update)."""
+        site = self._sites.get(id(p))
+        if site is None:
+            raise ValueError("not an atom parameter of a managed CSTLinear")
+        group = next(g for g in self.param_groups if any(q is p for q in g["params"]))
+        if group.get("amsgrad") or group.get("maximize"):
+            raise NotImplementedError("amsgrad/maximize are not implemented for atom groups")
+        lr = group["lr"]
+        if type(lr) not in (int, float) or not math.isfinite(lr) or lr < 0:
+            raise ValueError("CST learning rates must be finite nonnegative Python scalars")
+        state = self.state[p]
+        if not state:
+            state["step"] = torch.tensor(0.0, dtype=torch.float32)
+            state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+        state["step"] += 1
+        if lr == 0:
+            return None
+        h = self._native_params(site, group, int(state["step"].item()))
+        kind = N.TCST_POLAR if isinstance(site.kernel.coordinates, PolarRadius) else N.TCST_RATIONAL
+        return h, state, kind
 
     @torch.no_grad()
     def step(self, closure=None):

@@ -6,13 +6,19 @@ gradient is produced directly as TF32 split planes by the loss kernel, every
 buffer is allocated once, and the step is a fixed sequence of native launches
 on the current stream:
 
-    decode/route -> bin sort (count, scan, scatter) -> weight (clear wide plane,
-    wide atoms, tile gather) -> split X -> GEMM Y -> MSE dY -> GEMM dX ->
-    GEMM dW (split-K) -> pullback (three footprint classes, wide) -> optimizer
+    decode/route -> bin sort (count, column prefix, scatter) -> weight (mass
+    cache, tile gather) -> split X -> GEMM Y -> MSE dY -> GEMM dX -> GEMM dW
+    (split-K) -> pullback (split-K sum, three footprint classes, wide atoms) ->
+    optimizer
+
+The optimizer reads its per-step scalars (bias corrections) from device memory,
+refreshed from a pinned host ring before each step, so :meth:`capture` can
+record the whole sequence as one CUDA graph per input buffer pair and replay it
+with the host doing only the scalar refresh.
 
 With ``process_group`` set (data parallel, rows sharded across ranks, atoms
 replicated), the atom gradient is all-reduced (sum) before the optimizer so
-every rank applies the identical update.
+every rank applies the identical update; such steps are not captured.
 """
 
 from __future__ import annotations
@@ -25,11 +31,11 @@ from . import _native as N
 from . import runtime as R
 from .linear import CSTLinear
 from .optim import CSTAdamW
-from .spec import PolarRadius
 
 
 class MSETrainStep:
-    LAUNCHES_PER_STEP = 16  # kernels; the wide-plane clear is one memset node besides
+    LAUNCHES_PER_STEP = 18  # kernels; plus one host-to-device copy of the optimizer scalars
+    RING = 64
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
                  process_group=None, world_rows=None):
@@ -65,13 +71,33 @@ class MSETrainStep:
         self.partial = torch.empty(1024, dtype=torch.float64, device=dev)
         total_rows = self.rows if world_rows is None else int(world_rows)
         self.scale = float(torch.tensor(2.0 / (total_rows * plan.n_out), dtype=f32))
-        self.kind = N.TCST_POLAR if isinstance(layer.kernel.coordinates, PolarRadius) else N.TCST_RATIONAL
         self.nblocks = ctypes.c_int32(0)
-        self._x = None
+        nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
+        self.params_dev = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        self._ring = torch.zeros(self.RING, nbytes, dtype=torch.uint8).pin_memory()
+        self._ring_events = [None] * self.RING
+        self._slot = 0
+        self._state = None
+        self._kind = None
+        self._graphs = {}
 
-    def __call__(self, x, target):
-        """Run one step on device tensors x [rows, in], target [rows, out]; returns the
-        loss as a 0-d float64 device tensor (no host synchronization)."""
+    # -- pieces --------------------------------------------------------------------
+
+    def _upload(self, h):
+        """Copy the step's optimizer scalars to the device through the pinned ring."""
+        slot = self._slot
+        ev = self._ring_events[slot]
+        if ev is not None:
+            ev.synchronize()  # the copy that last read this slot has run
+        ctypes.memmove(self._ring[slot].data_ptr(), ctypes.addressof(h), ctypes.sizeof(h))
+        self.params_dev.copy_(self._ring[slot], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._ring_events[slot] = ev
+        self._slot = (slot + 1) % self.RING
+
+    def _launch(self, x, target, optimize=True):
+        """Enqueue the step's kernels on the current stream; returns the loss."""
         plan, ws, vp = self.plan, self.ws, R._vp
         p = self.layer.atoms.p
         st = R._stream(p.device)
@@ -105,6 +131,57 @@ class MSETrainStep:
                                   self.gstride, vp(self.grad), st), "pullback")
         if self.pg is not None:
             torch.distributed.all_reduce(self.grad, group=self.pg)
-        p.grad = self.grad
-        self.opt.step()
+        if optimize:
+            state = self._state
+            N.check(lib.tcst_optimizer_step_device(
+                vp(p), vp(self.grad), vp(state["exp_avg"]), vp(state["exp_avg_sq"]), A,
+                self._kind, vp(self.params_dev), st), "optimizer")
         return self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
+
+    def _advance(self):
+        """Host side of one optimizer step: step count and scalars to the device.
+        Returns False when the learning rate is 0 (the step leaves p unchanged)."""
+        p = self.layer.atoms.p
+        out = self.opt.site_step(p)
+        p.grad = self.grad
+        if out is None:
+            return False
+        h, self._state, self._kind = out
+        self._upload(h)
+        return True
+
+    # -- public --------------------------------------------------------------------
+
+    def __call__(self, x, target):
+        """Run one step on device tensors x [rows, in], target [rows, out]; returns the
+        loss as a 0-d float64 device tensor (no host synchronization)."""
+        optimize = self._advance()
+        key = (x.data_ptr(), target.data_ptr())
+        graph = self._graphs.get(key) if optimize else None
+        if graph is not None:
+            graph[0].replay()
+            return graph[1]
+        return self._launch(x, target, optimize)
+
+    def capture(self, pairs):
+        """Record one CUDA graph per (x, target) buffer pair; later calls with those
+        buffers replay it. Needs one eager step first (one-time kernel setup) and
+        no process group."""
+        if self.pg is not None:
+            raise ValueError("steps with a process group are not captured")
+        if self._state is None:
+            raise RuntimeError("run one eager step before capturing")
+        torch.cuda.synchronize()
+        for x, target in pairs:
+            key = (x.data_ptr(), target.data_ptr())
+            if key in self._graphs:
+                continue
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                loss = self._launch(x, target, True)
+            self._graphs[key] = (graph, loss)
+        torch.cuda.synchronize()
+
+    def release(self):
+        """Drop the captured graphs."""
+        self._graphs.clear()
