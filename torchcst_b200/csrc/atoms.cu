@@ -210,19 +210,19 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
     sincospi(R / P, &sa, &ca);
     const double y = -0.25 * ca * ca;
     const double dy = 0.5 * ca * sa * (PI / P); // dy/dR
-    double C[CAP + 1], dC[CAP + 1];
-#pragma unroll
-    for (int k = 0; k <= CAP; ++k) {
-        if (k > M) break;
+    // C_k and dC_k/dR one k at a time (Horner in y), so few doubles stay live.
+    auto coef = [&](int k, double &c, double &d) {
         const double *w = tab.w + k * (M + 1);
-        double v = w[M], d = 0.0;
+        double v = w[M], dv = 0.0;
         for (int s2 = M - 1; s2 >= 0; --s2) {
-            d = fma(d, y, v);
+            dv = fma(dv, y, v);
             v = fma(v, y, w[s2]);
         }
-        C[k] = v;
-        dC[k] = d * dy;
-    }
+        c = v;
+        d = dv * dy;
+    };
+    double C0, dC0;
+    coef(0, C0, dC0);
     const long long first = (long long)r.first_tile * r.tile;
     const int F = r.count * r.tile;
     int *iblk = reinterpret_cast<int *>(blk);
@@ -230,16 +230,28 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
     iblk[1] = F;
     blk[2] = float(2.0 * (double(first) * ax.spacing - r.local) / P);
     blk[3] = float(2.0 * PI / P);
-    const double inv = 1.0 / (P * C[0]);
-#pragma unroll
-    for (int k = 0; k <= CAP; ++k) {
-        if (k > M) break;
-        const double x = double(k) * ax.spacing / P;
-        const double sinc = k == 0 ? 1.0 : sinpi(x) / (PI * x);
+    const double inv = 1.0 / (P * C0);
+    // sin(pi k x1) for k = 0..M by the Chebyshev recurrence
+    // sin((k+1)a) = 2 cos(a) sin(k a) - sin((k-1)a), from one sincospi.
+    const double x1 = ax.spacing / P;
+    double s1, c1;
+    sincospi(x1, &s1, &c1);
+    double sprev = 0.0, scur = s1;
+#pragma unroll 1
+    for (int k = 0; k <= M; ++k) {
+        double Ck = C0, dCk = dC0, sinc = 1.0;
+        if (k > 0) {
+            coef(k, Ck, dCk);
+            sinc = scur / (PI * double(k) * x1);
+            const double sn = 2.0 * c1 * scur - sprev;
+            sprev = scur;
+            scur = sn;
+        }
         const double wk = (k == 0 ? 1.0 : 2.0) * ax.spacing * sinc;
-        blk[4 + k] = float(wk * C[k] * inv);
-        blk[5 + M + k] = float(wk * (dC[k] * C[0] - C[k] * dC[0]) * inv / C[0]);
+        blk[4 + k] = float(wk * Ck * inv);
+        blk[5 + M + k] = float(wk * (dCk * C0 - Ck * dC0) * inv / C0);
     }
+    (void)CAP;
     if constexpr (MT > 0) {
         if (sites && F <= REACH) {
             AxisCoef<MT> ac;
@@ -418,18 +430,25 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
     for (int i = threadIdx.x; i < g.nbins; i += blockDim.x) row[i] = hist[i];
 }
 
-__global__ void __launch_bounds__(256) bin_column_kernel(Table tv) {
+__global__ void __launch_bounds__(64) bin_column_kernel(Table tv) {
     const BinGeom &g = tv.geom;
     const int bin = blockIdx.x * blockDim.x + threadIdx.x;
     if (bin >= g.nbins) return;
     int run = 0;
-    for (int b = 0; b < g.sort_blocks; ++b) {
-        int *c = tv.counts + (long long)b * g.nbins + bin;
-        const int v = *c;
-        *c = run;
-        run += v;
+    int *col = tv.counts + bin;
+    // Sixteen independent loads in flight, then their prefixes.
+    for (int b0 = 0; b0 < g.sort_blocks; b0 += 16) {
+        int v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+            v[u] = b0 + u < g.sort_blocks ? col[(long long)(b0 + u) * g.nbins] : 0;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            if (b0 + u < g.sort_blocks) col[(long long)(b0 + u) * g.nbins] = run;
+            run += v[u];
+        }
     }
-    tv.counts[(long long)g.sort_blocks * g.nbins + bin] = run;
+    col[(long long)g.sort_blocks * g.nbins] = run;
 }
 
 __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
@@ -604,7 +623,7 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
         bin_count_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
         TCST_CUDA(cudaGetLastError());
     }
-    bin_column_kernel<<<unsigned((g.nbins + 255) / 256), 256, 0, st>>>(tv);
+    bin_column_kernel<<<unsigned((g.nbins + 63) / 64), 64, 0, st>>>(tv);
     TCST_CUDA(cudaGetLastError());
     bin_scatter_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
     TCST_CUDA(cudaGetLastError());
