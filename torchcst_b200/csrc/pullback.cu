@@ -27,7 +27,7 @@
 
 namespace tcst {
 
-constexpr int P0_THREADS = 128;
+constexpr int P0_THREADS = 64;
 constexpr int PC_THREADS = 256;
 constexpr int PC_WARPS = PC_THREADS / 32;
 
@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     constexpr int W = 2 * TS + RC - 1;
     constexpr int PITCH = W + 1;
     constexpr int Q = RC / 32;
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     float *gw = sm;
     const BinGeom &geo = tv.geom;
     const int nr = geo.tr[cls], nc = geo.tc[cls];
@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float *rowv = sm + W * PITCH + warp * 3 * RC; // m, dm/dmu, dm/dR of the output sites
+    float4 *rowv = reinterpret_cast<float4 *>(sm + W * PITCH) + warp * RC; // (m, dm/dmu, dm/dR, 0)
     const int aw = axis_words(8);
     for (int item = warp; item < total; item += PC_WARPS) {
         int k = item, q = 0;
@@ -203,9 +203,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
             ao.load(rec + 4);
             for (int r = lane; r < fo; r += 32) {
                 const SiteVals v = ao.values(r);
-                rowv[r] = v.m;
-                rowv[RC + r] = v.dmu;
-                rowv[2 * RC + r] = v.dR;
+                rowv[r] = make_float4(v.m, v.dmu, v.dR, 0.f);
             }
         }
         float mi[Q], dmi[Q], dri[Q];
@@ -215,15 +213,15 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
             ai.load(rec + 4 + aw);
 #pragma unroll
             for (int j = 0; j < Q; ++j) {
+                // Lanes past the footprint read a valid window column with zero weights.
                 const int c = lane + 32 * j;
                 mi[j] = dmi[j] = dri[j] = 0.f;
-                cl[j] = -1;
+                cl[j] = min(span.z - C0 + c, W - 1);
                 if (c < fi) {
                     const SiteVals v = ai.values(c);
                     mi[j] = v.m;
                     dmi[j] = v.dmu;
                     dri[j] = v.dR;
-                    cl[j] = span.z - C0 + c;
                 }
             }
         }
@@ -233,15 +231,18 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
         for (int j = 0; j < Q; ++j) h0[j] = h1[j] = h2[j] = 0.f;
         const float *g0 = gw + (span.x - R0) * PITCH;
 #pragma unroll 4
+        const int nq = (fi + 31) >> 5; // column slots in use (warp-uniform)
         for (int r = 0; r < fo; ++r) {
-            const float m = rowv[r], dm = rowv[RC + r], dr = rowv[2 * RC + r];
+            const float4 rv = rowv[r];
             const float *grow = g0 + r * PITCH;
 #pragma unroll
             for (int j = 0; j < Q; ++j) {
-                const float gv = cl[j] >= 0 ? grow[cl[j]] : 0.f;
-                h0[j] = fmaf(gv, m, h0[j]);
-                h1[j] = fmaf(gv, dm, h1[j]);
-                h2[j] = fmaf(gv, dr, h2[j]);
+                if (j < nq) {
+                    const float gv = grow[cl[j]];
+                    h0[j] = fmaf(gv, rv.x, h0[j]);
+                    h1[j] = fmaf(gv, rv.y, h1[j]);
+                    h2[j] = fmaf(gv, rv.z, h2[j]);
+                }
             }
         }
         float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
 }
 
 template <int RC> constexpr size_t class_smem() {
-    return size_t(2 * TS + RC - 1) * (2 * TS + RC) * 4 + size_t(PC_WARPS) * 3 * RC * 4;
+    return size_t(2 * TS + RC - 1) * (2 * TS + RC) * 4 + size_t(PC_WARPS) * RC * 16;
 }
 
 // Coarse classes: one CTA per atom. The footprint is walked in chunks of

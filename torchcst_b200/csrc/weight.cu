@@ -9,7 +9,7 @@
 //   gather: one CTA per TS x TS weight tile lists, in a fixed order, every bin
 //           whose atoms can reach the tile, keeps the atoms that do, stages their
 //           masses on the tile's rows and columns in shared memory (images folded
-//           modulo N) and accumulates the outer products in registers (4 x 4 per
+//           modulo N) and accumulates the outer products in registers (2 x 4 per
 //           thread), then writes W and/or its TF32 split planes.
 // A fixed bin order and id-ordered bins make W bitwise reproducible; there are
 // no atomics.
@@ -21,8 +21,8 @@
 
 namespace tcst {
 
-constexpr int WT_THREADS = 64; // 8 x 8 threads, 4 x 4 outputs each
-constexpr int WT_BATCH = 64;   // candidates per pass
+constexpr int WT_THREADS = 128; // 16 x 8 threads, 2 x 4 outputs each
+constexpr int WT_STAGE = 64;          // hits staged per sub-pass
 constexpr int MAX_SCAN = 320;  // bins a weight tile can scan
 
 __device__ __forceinline__ float tf32_rna(float x) {
@@ -84,12 +84,12 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
                                                                    const float *__restrict__ cache,
                                                                    GatherOut out) {
     __shared__ int sbeg[MAX_SCAN], scls[MAX_SCAN], spre[MAX_SCAN + 1];
-    __shared__ int wtot[2];
-    __shared__ __align__(16) float us[WT_BATCH][TS];
-    __shared__ __align__(16) float vs[WT_BATCH][TS];
-    __shared__ int cand[WT_BATCH], ccls[WT_BATCH];
-    __shared__ int4 cspan[WT_BATCH];
-    __shared__ float camp[WT_BATCH];
+    __shared__ int wtot[WT_THREADS / 32];
+    __shared__ __align__(16) float us[WT_STAGE][TS];
+    __shared__ __align__(16) float vs[WT_STAGE][TS];
+    __shared__ int cand[WT_THREADS], ccls[WT_THREADS];
+    __shared__ int4 cspan[WT_THREADS];
+    __shared__ float camp[WT_THREADS];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int trow = blockIdx.x / tiles_c, tcol = blockIdx.x - trow * tiles_c;
     const int R0 = trow * TS, C0 = tcol * TS;
@@ -143,7 +143,8 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
         }
         if (lane == 31) wtot[warp] = inc;
         __syncthreads();
-        int run = inc - local + (warp ? wtot[0] : 0);
+        int run = inc - local;
+        for (int w = 0; w < warp; ++w) run += wtot[w];
         for (int k = 0; k < per; ++k)
             if (i0 + k < nscan) {
                 run += spre[i0 + k + 1];
@@ -153,12 +154,12 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
     }
     __syncthreads();
     const int total = spre[nscan];
-    const int r0 = (t >> 3) * 4, c0 = (t & 7) * 4;
+    const int r0 = (t >> 3) * 2, c0 = (t & 7) * 4;
     const int aw = axis_words(modes_o);
-    float acc[4][4] = {};
+    float acc[2][4] = {};
 
-    // 2. Candidates in passes of WT_BATCH: keep those that reach the tile.
-    for (int base = 0; base < total; base += WT_BATCH) {
+    // 2. Candidates in passes of one per thread: keep those that reach the tile.
+    for (int base = 0; base < total; base += WT_THREADS) {
         const int i = base + t;
         bool hit = false;
         int a = 0, cls = 0;
@@ -178,87 +179,97 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
         const unsigned m = __ballot_sync(0xffffffffu, hit);
         if (lane == 0) wtot[warp] = __popc(m);
         __syncthreads();
-        const int n = wtot[0] + wtot[1];
+        int n = 0, before = 0;
+#pragma unroll
+        for (int w = 0; w < WT_THREADS / 32; ++w) {
+            before += w < warp ? wtot[w] : 0;
+            n += wtot[w];
+        }
         if (hit) {
-            const int slot = (warp ? wtot[0] : 0) + __popc(m & ((1u << lane) - 1u));
+            const int slot = before + __popc(m & ((1u << lane) - 1u));
             cand[slot] = a;
             ccls[slot] = cls;
             cspan[slot] = sp;
             camp[slot] = tv.rec[(long long)a * tv.words];
         }
         __syncthreads();
-        // 3. Stage: warp 0 the tile rows (amp * m_out), warp 1 the columns (m_in).
-        // Main pass: classes with stored masses and no second image, one
-        // independent load per candidate; a second pass evaluates the rest.
-        {
-            const int side = warp, p = lane;
-            const int lim = side ? TC : TR, nn = side ? ni : no;
-            const int site = (side ? C0 : R0) + p;
-            float(*dst)[TS] = side ? vs : us;
-            bool rest = false;
+        for (int h0 = 0; h0 < n; h0 += WT_STAGE) {
+            const int nb = min(WT_STAGE, n - h0);
+            // 3. Stage: odd warps the tile columns (m_in), even warps the rows
+            // (amp * m_out); warps 0-1 take even hits, warps 2-3 odd ones.
+            // Main pass: classes with stored masses and no second image, one
+            // independent load per candidate; a second pass evaluates the rest.
+            {
+                const int side = warp & 1, p = lane, half = warp >> 1;
+                const int lim = side ? TC : TR, nn = side ? ni : no;
+                const int site = (side ? C0 : R0) + p;
+                float(*dst)[TS] = side ? vs : us;
+                bool rest = false;
 #pragma unroll 8
-            for (int s2 = 0; s2 < n; ++s2) {
-                const int4 q = cspan[s2];
-                const int f = side ? q.z : q.x, F = side ? q.w : q.y;
-                const int c = ccls[s2];
-                const long long atom = cand[s2];
-                int j = site - f;
-                j += j < 0 ? nn : 0;
-                const bool stored = c >= 0 && c < NFINE && F <= nn;
-                const float *src = c == 0 ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
-                                          : cache + (atom * 2 + side) * CACHE_SITES;
-                float v = 0.f;
-                if (stored && p < lim && j < F) v = src[j];
-                dst[s2][p] = side ? v : v * camp[s2];
-                rest |= !stored;
-            }
-            if (__any_sync(0xffffffffu, rest)) {
-                for (int s2 = 0; s2 < n; ++s2) {
-                    const int4 q = cspan[s2];
+                for (int s2 = half; s2 < nb; s2 += 2) {
+                    const int4 q = cspan[h0 + s2];
                     const int f = side ? q.z : q.x, F = side ? q.w : q.y;
-                    const int c = ccls[s2];
-                    if (c >= 0 && c < NFINE && F <= nn) continue;
-                    const long long atom = cand[s2];
+                    const int c = ccls[h0 + s2];
+                    const long long atom = cand[h0 + s2];
                     int j = site - f;
                     j += j < 0 ? nn : 0;
+                    const bool stored = c >= 0 && c < NFINE && F <= nn;
+                    const float *src = c == 0 ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
+                                              : cache + (atom * 2 + side) * CACHE_SITES;
                     float v = 0.f;
-                    if (p < lim && j < F) {
-                        const float *blk = tv.rec + atom * tv.words + 4 + side * aw;
-                        if (c == 0) {
-                            const float *sv = tv.sites + atom * SITE_FLOATS + side * 3 * REACH;
-                            for (; j < F; j += nn) v += sv[j];
-                        } else if (c > 0 && c < NFINE) {
-                            const float *cv = cache + (atom * 2 + side) * CACHE_SITES;
-                            for (; j < F; j += nn) v += cv[j];
-                        } else if (c >= NFINE) {
-                            AxisCoef<8> ac;
-                            ac.load_mass(blk);
-                            for (; j < F; j += nn) v += ac.mass(j);
-                        } else {
-                            // Unbinned geometry: any mode count.
-                            const int modes = side ? modes_i : modes_o;
-                            for (; j < F; j += nn) v += site_mass(blk, modes, j, F);
+                    if (stored && p < lim && j < F) v = src[j];
+                    dst[s2][p] = side ? v : v * camp[h0 + s2];
+                    rest |= !stored;
+                }
+                if (__any_sync(0xffffffffu, rest)) {
+                    for (int s2 = half; s2 < nb; s2 += 2) {
+                        const int4 q = cspan[h0 + s2];
+                        const int f = side ? q.z : q.x, F = side ? q.w : q.y;
+                        const int c = ccls[h0 + s2];
+                        if (c >= 0 && c < NFINE && F <= nn) continue;
+                        const long long atom = cand[h0 + s2];
+                        int j = site - f;
+                        j += j < 0 ? nn : 0;
+                        float v = 0.f;
+                        if (p < lim && j < F) {
+                            const float *blk = tv.rec + atom * tv.words + 4 + side * aw;
+                            if (c == 0) {
+                                const float *sv = tv.sites + atom * SITE_FLOATS + side * 3 * REACH;
+                                for (; j < F; j += nn) v += sv[j];
+                            } else if (c > 0 && c < NFINE) {
+                                const float *cv = cache + (atom * 2 + side) * CACHE_SITES;
+                                for (; j < F; j += nn) v += cv[j];
+                            } else if (c >= NFINE) {
+                                AxisCoef<8> ac;
+                                ac.load_mass(blk);
+                                for (; j < F; j += nn) v += ac.mass(j);
+                            } else {
+                                // Unbinned geometry: any mode count.
+                                const int modes = side ? modes_i : modes_o;
+                                for (; j < F; j += nn) v += site_mass(blk, modes, j, F);
+                            }
                         }
+                        dst[s2][p] = side ? v : v * camp[h0 + s2];
                     }
-                    dst[s2][p] = side ? v : v * camp[s2];
                 }
             }
-        }
-        __syncthreads();
-        for (int s2 = 0; s2 < n; ++s2) {
-            const float4 u = *reinterpret_cast<const float4 *>(&us[s2][r0]);
-            const float4 v = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
-            const float uu[4] = {u.x, u.y, u.z, u.w}, vv[4] = {v.x, v.y, v.z, v.w};
+            __syncthreads();
+#pragma unroll 4
+            for (int s2 = 0; s2 < nb; ++s2) {
+                const float2 u = *reinterpret_cast<const float2 *>(&us[s2][r0]);
+                const float4 v = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
+                const float uu[2] = {u.x, u.y}, vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int ii = 0; ii < 4; ++ii)
+                for (int ii = 0; ii < 2; ++ii)
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(uu[ii], vv[jj], acc[ii][jj]);
+                    for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(uu[ii], vv[jj], acc[ii][jj]);
+            }
+            __syncthreads();
         }
-        __syncthreads();
     }
 
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
+    for (int ii = 0; ii < 2; ++ii) {
         const int r = r0 + ii;
         if (r >= TR) continue;
         const long long row = R0 + r;
