@@ -287,11 +287,11 @@ def main():
     for i in range(args.warmup):
         step(xs[i % nbuf], ts[i % nbuf])
     torch.cuda.synchronize()
-    graphs = pg is None
-    if graphs:
-        # One CUDA graph per input buffer pair; the host then only refreshes the
-        # optimizer scalars and replays.
-        step.capture(list(zip(xs, ts)))
+    graphs = True
+    # One CUDA graph per input buffer pair (plus the optimizer graph when data
+    # parallel); the host then only refreshes the optimizer scalars, replays and,
+    # with several ranks, issues the gradient all-reduce between the graphs.
+    step.capture(list(zip(xs, ts)))
     if pg is not None:
         dist.barrier()
     # Clock samples bracket the timed region: the sampler starts first and the GPU

@@ -17,8 +17,11 @@ record the whole sequence as one CUDA graph per input buffer pair and replay it
 with the host doing only the scalar refresh.
 
 With ``process_group`` set (data parallel, rows sharded across ranks, atoms
-replicated), the atom gradient is all-reduced (sum) before the optimizer so
-every rank applies the identical update; such steps are not captured.
+replicated), the loss is scaled by the global row count and the atom gradient
+is all-reduced (sum) before the optimizer, so every rank applies the identical
+update. Captured steps then replay two graphs per step, the gradient and the
+optimizer, with the all-reduce issued between them; neither graph holds a
+collective.
 """
 
 from __future__ import annotations
@@ -31,6 +34,20 @@ from . import _native as N
 from . import runtime as R
 from .linear import CSTLinear
 from .optim import CSTAdamW
+
+
+def dp_loss_scale(rows: int, n_out: int, world_rows: int | None = None) -> float:
+    """float32 dY scale of the mean-squared error over ``world_rows`` rows (all
+    ranks) of ``n_out`` outputs; ``rows`` when there is no process group."""
+    total = rows if world_rows is None else int(world_rows)
+    return float(torch.tensor(2.0 / (total * n_out), dtype=torch.float32))
+
+
+def dp_reduce_gradient(grad: torch.Tensor, process_group=None) -> torch.Tensor:
+    """Sum the per-rank atom gradients in place (no-op without a group)."""
+    if process_group is not None:
+        torch.distributed.all_reduce(grad, group=process_group)
+    return grad
 
 
 class MSETrainStep:
@@ -69,8 +86,7 @@ class MSETrainStep:
         self.g = torch.empty(self.split * self.gstride, dtype=f32, device=dev)
         self.grad = torch.empty(A, 4, dtype=f32, device=dev)
         self.partial = torch.empty(1024, dtype=torch.float64, device=dev)
-        total_rows = self.rows if world_rows is None else int(world_rows)
-        self.scale = float(torch.tensor(2.0 / (total_rows * plan.n_out), dtype=f32))
+        self.scale = dp_loss_scale(self.rows, plan.n_out, world_rows)
         self.nblocks = ctypes.c_int32(0)
         nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
         self.params_dev = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
@@ -80,6 +96,7 @@ class MSETrainStep:
         self._state = None
         self._kind = None
         self._graphs = {}
+        self._opt_graph = None
 
     # -- pieces --------------------------------------------------------------------
 
@@ -97,7 +114,24 @@ class MSETrainStep:
         self._slot = (slot + 1) % self.RING
 
     def _launch(self, x, target, optimize=True):
-        """Enqueue the step's kernels on the current stream; returns the loss."""
+        """Enqueue the step's kernels (and the gradient all-reduce) on the current
+        stream; returns the loss."""
+        loss = self._launch_grad(x, target)
+        dp_reduce_gradient(self.grad, self.pg)
+        if optimize:
+            self._launch_opt()
+        return loss
+
+    def _launch_opt(self):
+        p = self.layer.atoms.p
+        state = self._state
+        vp = R._vp
+        N.check(N.load().tcst_optimizer_step_device(
+            vp(p), vp(self.grad), vp(state["exp_avg"]), vp(state["exp_avg_sq"]), self.atoms,
+            self._kind, vp(self.params_dev), R._stream(p.device)), "optimizer")
+
+    def _launch_grad(self, x, target):
+        """Forward and backward kernels up to this rank's atom gradient."""
         plan, ws, vp = self.plan, self.ws, R._vp
         p = self.layer.atoms.p
         st = R._stream(p.device)
@@ -129,13 +163,6 @@ class MSETrainStep:
                                      vp(ws.status), st), "gemm dw")
         N.check(lib.tcst_pullback(vp(self.table), A, oa, ia, vp(self.g), self.ldg, self.split,
                                   self.gstride, vp(self.grad), st), "pullback")
-        if self.pg is not None:
-            torch.distributed.all_reduce(self.grad, group=self.pg)
-        if optimize:
-            state = self._state
-            N.check(lib.tcst_optimizer_step_device(
-                vp(p), vp(self.grad), vp(state["exp_avg"]), vp(state["exp_avg_sq"]), A,
-                self._kind, vp(self.params_dev), st), "optimizer")
         return self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
 
     def _advance(self):
@@ -160,15 +187,17 @@ class MSETrainStep:
         graph = self._graphs.get(key) if optimize else None
         if graph is not None:
             graph[0].replay()
+            if self.pg is not None:
+                dp_reduce_gradient(self.grad, self.pg)
+                self._opt_graph.replay()
             return graph[1]
         return self._launch(x, target, optimize)
 
     def capture(self, pairs):
         """Record one CUDA graph per (x, target) buffer pair; later calls with those
-        buffers replay it. Needs one eager step first (one-time kernel setup) and
-        no process group."""
-        if self.pg is not None:
-            raise ValueError("steps with a process group are not captured")
+        buffers replay it. Needs one eager step first (one-time kernel setup). With
+        a process group the optimizer is a second graph and the all-reduce runs
+        between the two."""
         if self._state is None:
             raise RuntimeError("run one eager step before capturing")
         torch.cuda.synchronize()
@@ -178,10 +207,17 @@ class MSETrainStep:
                 continue
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                loss = self._launch(x, target, True)
+                loss = self._launch_grad(x, target)
+                if self.pg is None:
+                    self._launch_opt()
             self._graphs[key] = (graph, loss)
+        if self.pg is not None and self._opt_graph is None:
+            self._opt_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self._opt_graph):
+                self._launch_opt()
         torch.cuda.synchronize()
 
     def release(self):
         """Drop the captured graphs."""
         self._graphs.clear()
+        self._opt_graph = None
