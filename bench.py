@@ -184,7 +184,7 @@ def breakdown(lib, step, x, t):
         # brackets kernel time only, not host gaps.
         torch.cuda.synchronize()
         torch.cuda._sleep(50_000_000)
-        step._launch(x, t, optimize=False)
+        step._launch_grad(x, t)
         torch.cuda.synchronize()
     finally:
         for n in names:
@@ -295,9 +295,9 @@ def main():
     if pg is not None:
         dist.barrier()
     # Clock samples bracket the timed region: the sampler starts first and the GPU
-    # keeps running the same step until at least two samples landed on each side.
-    # Those extra steps train the model (atoms widen as q grows), so the atoms and
-    # the optimizer state are restored before the timed steps.
+    # keeps running the step's kernels until at least two samples landed on each
+    # side. The timed steps start from the state the warm-up left (saved here and
+    # restored after the diagnostics below).
     p = layer.atoms.p
     saved_p = p.detach().clone()
     saved_state = {k: (v.clone() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()}
@@ -305,8 +305,10 @@ def main():
     sampler.start()
     t_wait = time.perf_counter()
     i_pre = 0
+    # The GPU runs the step's gradient kernels (no collective, no update; the
+    # count differs between ranks) until the sampler has rows before the region.
     while len(sampler.rows) < 2 and time.perf_counter() - t_wait < 5.0:
-        step(xs[i_pre % nbuf], ts[i_pre % nbuf])
+        step._launch_grad(xs[i_pre % nbuf], ts[i_pre % nbuf])
         i_pre += 1
         torch.cuda.synchronize()
     with torch.no_grad():
@@ -342,7 +344,7 @@ def main():
     t_wait = time.perf_counter()
     i_post = 0
     while len(sampler.rows) < n_before + 2 and time.perf_counter() - t_wait < 5.0:
-        step(xs[i_post % nbuf], ts[i_post % nbuf])
+        step._launch_grad(xs[i_post % nbuf], ts[i_post % nbuf])
         i_post += 1
         torch.cuda.synchronize()
     clocks = sampler.stop()
@@ -361,7 +363,7 @@ def main():
     torch.cuda._sleep(100_000_000)
     timed.on = True
     for i in range(3):
-        step._launch(xs[i % nbuf], ts[i % nbuf], optimize=False)
+        step._launch_grad(xs[i % nbuf], ts[i % nbuf])
     timed.on = False
     torch.cuda.synchronize()
     gemm_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in gemm_events)
@@ -453,7 +455,8 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}",
+            "data": "synthetic", "config": dict(CONFIG, global_batch=ROWS * world,
+                                                rows_per_rank=ROWS, parallelism=f"dp{world}",
                                                 l2="rotating inputs, 10 x 32 MiB buffers > L2"),
             "e2e": {"value": e2e_value, "unit": "steps/s",
                     "h2d_bytes_per_step": 2 * ROWS * N_IO * 4, "d2h_bytes_per_step": 4,
