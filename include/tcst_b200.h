@@ -101,8 +101,9 @@ const char *tcst_version(void);
 const char *tcst_last_error(void);
 
 /* Bytes of the atom table written by tcst_decode_route: per-atom records,
- * output footprint spans and the output-band bins used by the weight assembly
- * and the pullback. */
+ * footprint spans, the site values of narrow footprints, and the atoms sorted
+ * into footprint-class x first-site-tile bins (in id order inside each bin)
+ * that the weight assembly and the pullback walk. */
 int64_t tcst_atom_table_bytes(int64_t atoms, const tcst_axis *out_axis,
                               const tcst_axis *in_axis);
 
@@ -122,12 +123,11 @@ int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_axis *out_ax
 
 /* Assemble the dense weight W = sum_a amp_a m_out,a (x) m_in,a (images folded
  * modulo N) from the atom table. Replaces the W side of factors/weight
- * (radius_cell_mass.py:225-263). Uses the output-band bins that
- * tcst_decode_route stored in the atom table; each band is accumulated in
- * 64-bit fixed point and the overlapping band partials are merged, so W is
- * bitwise independent of atom order. scratch_dev is 16-byte aligned and
- * tcst_weight_scratch_bytes() long (3 x 8 x N_out x N_in bytes of band
- * partials); its contents need no initialization. Any of
+ * (radius_cell_mass.py:225-263). Each 32 x 32 tile of W gathers, in a fixed
+ * order, the bins whose atoms can reach it, so W is bitwise reproducible.
+ * scratch_dev is 16-byte aligned and tcst_weight_scratch_bytes() long
+ * (2 x 128 floats per atom: the masses of mid-size footprints, written and read
+ * within the call); its contents need no initialization. Any of
  * weight_dev / hi / lo may be NULL; hi+lo is the two-term TF32 split consumed by
  * tcst_gemm_tf32x3. */
 int64_t tcst_weight_scratch_bytes(int64_t atoms, const tcst_axis *out_axis,
@@ -143,13 +143,12 @@ int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
  * inside a host framework whose allocator owns the device, or a fixed-footprint
  * deployment): the scratch is a fixed array built into this library,
  * tcst_static_weight_scratch_bytes() = 32 MiB, which every GPU that loads the
- * library holds until exit. That covers a 1024 x 1024 weight with up to a
- * million atoms; a layer whose tcst_weight_scratch_bytes() exceeds it is
- * rejected with TCST_ERR_UNSUPPORTED. The first call on a device looks up the array's device
- * address and clears it on `stream`; make that first call before any stream
- * capture. Every call shares the one array and leaves its counters at zero;
- * calls that overlap on the GPU (same device, different streams) race. Nothing
- * is allocated. */
+ * library holds until exit. That covers up to 32,768 atoms (1 KiB each); a
+ * layer whose tcst_weight_scratch_bytes() exceeds it is rejected with
+ * TCST_ERR_UNSUPPORTED. The first call on a device looks up the array's device
+ * address; make that first call before any stream capture. Every call shares
+ * the one array; calls that overlap on the GPU (same device, different streams)
+ * race. Nothing is allocated. */
 int tcst_assemble_weight_static(const void *atom_table_dev, int64_t atoms,
                                 const tcst_axis *out_axis, const tcst_axis *in_axis,
                                 float *weight_dev, int64_t ld_weight, float *weight_hi_dev,
