@@ -1,0 +1,101 @@
+"""The torchcst backend plugin against the real reference package (CPU).
+
+Registers the B200 Algorithm into torchcst's own registry, round-trips its
+ExecutionPlan through JSON, checks that torchcst declarations convert to the
+same native plan this package builds from its own declarations, and that a
+reference CSTLinear routed to the plugin reports the missing sm_100 device
+instead of running elsewhere. Needs the reference source tree; skipped where it
+is absent (it is never present on the GPU box).
+"""
+
+import os
+import sys
+
+import pytest
+import torch
+
+REF_SRC = "/root/reference/src"
+
+
+@pytest.fixture(scope="module")
+def tc():
+    if not os.path.isdir(REF_SRC):
+        pytest.skip("reference source tree not present")
+    if REF_SRC not in sys.path:
+        sys.path.insert(0, REF_SRC)
+    try:
+        import torchcst
+    except Exception as exc:  # pragma: no cover - depends on the container
+        pytest.skip(f"torchcst not importable: {exc}")
+    return torchcst
+
+
+def _native_bytes(plan):
+    import ctypes
+    return (bytes(memoryview(plan.out_axis)), bytes(memoryview(plan.in_axis)),
+            bytes(ctypes.string_at(ctypes.addressof(plan.coords), ctypes.sizeof(plan.coords))))
+
+
+def test_register_plan_round_trip_and_duplicates(tc):
+    from torchcst._backends.dispatch.select import FixedSelector
+    from torchcst_b200 import plugin
+    registry, plan = plugin.register()
+    assert registry.loads_plan(registry.dumps_plan(plan)) == plan
+    assert registry.validate_plan(plan).id == plugin.ALGORITHM_ID
+    with pytest.raises(ValueError):
+        registry.register(plugin.algorithm())
+    FixedSelector(plan, registry=registry)
+    with pytest.raises(ValueError):
+        registry.validate_plan(plugin.plan(plugin.B200Recipe(validate="maybe")))
+
+
+def _reference_layer(tc, n_out, n_in, coords, base_in=1, merge=2, atoms=16, seed=0):
+    from torchcst import ChebyshevSpec, CSTLinear, chart_presets, kernels
+    k = kernels.product(kernels.cell_mass(ChebyshevSpec(modes=8), merge_factor=merge),
+                        kernels.cell_mass(ChebyshevSpec(modes=8), base_tile_sites=base_in,
+                                          merge_factor=merge),
+                        coordinates=coords)
+    torch.manual_seed(seed)
+    return CSTLinear(charts=(chart_presets.regular_grid(n_out, geometry="flat_torus"),
+                             chart_presets.regular_grid(n_in, geometry="flat_torus")),
+                     atoms=atoms, kernel=k)
+
+
+def test_declarations_convert_to_the_same_native_plan(tc):
+    from torchcst import kernels as rk
+    from torchcst.kernels.parameterizations.base import RadiusBounds as RB
+    from torchcst_b200 import kernels, plugin
+    from torchcst_b200 import runtime as R
+    from torchcst_b200.spec import (CellMass, ChebyshevSpec, RadiusBounds, RegularGrid,
+                                    radius_cell_mass_axes)
+    cases = [
+        ((8, 16, 1, 2), rk.rational_radius(radius_max=4.0, radius_fraction=0.0),
+         kernels.rational_radius(radius_max=4.0)),
+        ((1024, 1024, 1, 2), rk.rational_radius(radius_max=512.0, radius_fraction=0.0),
+         kernels.rational_radius(radius_max=512.0)),
+        ((1024, 784, 49, 2),
+         rk.polar(amplitude_max=1.0, w_c=0.3, bounds=RB(minimum=0.5, birth=4.0, maximum=50.0,
+                                                         upper_floor=1.0)),
+         kernels.polar(amplitude_max=1.0, w_c=0.3,
+                       bounds=RadiusBounds(minimum=0.5, birth=4.0, maximum=50.0,
+                                           upper_floor=1.0))),
+    ]
+    for (n_out, n_in, base_in, merge), ref_coords, own_coords in cases:
+        layer = _reference_layer(tc, n_out, n_in, ref_coords, base_in, merge)
+        axes, spec = plugin.spec_from_reference(layer.cst_charts(), layer.kernel.declaration())
+        own_kernel = kernels.product(CellMass(ChebyshevSpec(8), 1, merge),
+                                     CellMass(ChebyshevSpec(8), base_in, merge),
+                                     coordinates=own_coords)
+        own_axes = radius_cell_mass_axes((RegularGrid(n_out), RegularGrid(n_in)), own_kernel)
+        assert axes == own_axes
+        assert _native_bytes(R.Plan.make(axes, spec)) == \
+            _native_bytes(R.Plan.make(own_axes, own_kernel))
+
+
+def test_reference_layer_routed_to_the_plugin_needs_sm100(tc):
+    from torchcst import kernels as rk
+    from torchcst_b200 import plugin
+    layer = _reference_layer(tc, 8, 16, rk.rational_radius(radius_max=4.0, radius_fraction=0.0))
+    layer.selector = plugin.selector()
+    with pytest.raises(Exception, match="sm_100"):
+        layer(torch.randn(4, 16))
