@@ -71,18 +71,46 @@ __global__ void g_reduce4_kernel(float4 *__restrict__ g, int no, int ni4, long l
     }
 }
 
-// G window [W x W] at (R0, C0) with rows/columns wrapped modulo no / ni;
-// four independent loads in flight per thread.
+// G window [W x W] at (R0, C0) with rows/columns wrapped modulo no / ni.
+// Interior windows (no column wrap, 16-byte aligned rows) move float4s, four
+// in flight per thread; windows that wrap past the last column use scalars.
 template <int W, int PITCH>
 __device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, int ni,
                                              const float *__restrict__ g, long long ldg, int split,
                                              long long split_stride) {
-    constexpr int N = W * W;
-    for (int i0 = threadIdx.x; i0 < N; i0 += 4 * blockDim.x) {
-        float v[4];
-        int dst[4];
+    constexpr int W4 = (W + 3) / 4; // float4 columns per row (PITCH >= 4 * W4)
+    static_assert(PITCH >= 4 * W4 && PITCH % 4 == 0, "window pitch");
+    const bool vec = split == 1 && C0 + 4 * W4 <= ni && ldg % 4 == 0 && C0 % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(g) & 15) == 0;
+    if (vec) {
+        constexpr int N4 = W * W4;
+        for (int i0 = threadIdx.x; i0 < N4; i0 += 4 * blockDim.x) {
+            float4 v[4];
+            int dst[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * blockDim.x;
+                dst[u] = -1;
+                if (i < N4) {
+                    const int rl = i / W4, c4 = i - rl * W4;
+                    int row = R0 + rl;
+                    while (row >= no) row -= no;
+                    v[u] = *reinterpret_cast<const float4 *>(g + (long long)row * ldg + C0 + 4 * c4);
+                    dst[u] = rl * PITCH + 4 * c4;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (dst[u] >= 0) *reinterpret_cast<float4 *>(gw + dst[u]) = v[u];
+        }
+        return;
+    }
+    constexpr int N = W * W;
+    for (int i0 = threadIdx.x; i0 < N; i0 += 8 * blockDim.x) {
+        float v[8];
+        int dst[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
             const int i = i0 + u * blockDim.x;
             dst[u] = -1;
             v[u] = 0.f;
@@ -98,7 +126,7 @@ __device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, 
             }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < 8; ++u)
             if (dst[u] >= 0) gw[dst[u]] = v[u];
     }
 }
@@ -108,14 +136,15 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     Table tv, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, float4 *__restrict__ grad) {
     constexpr int W = TS + REACH - 1;
-    __shared__ float gw[W * W];
+    constexpr int PITCH = W + 1;
+    __shared__ __align__(16) float gw[W * PITCH];
     const int ct = tv.geom.tc[0];
     const int tr = blockIdx.x / ct, tc = blockIdx.x - tr * ct;
     const int bin = tv.geom.base[0] + blockIdx.x; // class 0 bins, row-major by tile
     const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
     if (begin == end) return;
     const int R0 = tr * TS, C0 = tc * TS;
-    stage_window<W, W>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
+    stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
     __syncthreads();
     for (int k = begin + threadIdx.x; k < end; k += blockDim.x) {
         const long long a = tv.ids[k];
@@ -135,11 +164,11 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
 #pragma unroll
         for (int c = 0; c < REACH; ++c)
             if (c >= fi) im[c] = idmu[c] = idr[c] = 0.f;
-        const float *g0 = gw + (span.x - R0) * W + (span.z - C0);
+        const float *g0 = gw + (span.x - R0) * PITCH + (span.z - C0);
         float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
         for (int r = 0; r < fo; ++r) {
             const float rm = sv[r], rdmu = sv[REACH + r], rdr = sv[2 * REACH + r];
-            const float *grow = g0 + r * W;
+            const float *grow = g0 + r * PITCH;
 #pragma unroll
             for (int c = 0; c < REACH; ++c) {
                 const float gv = c < fi ? grow[c] : 0.f;
