@@ -161,8 +161,8 @@ def cpu_reference(steps, warmup, sample_rows=512, log=None):
 def breakdown(lib, step, x, t):
     """Per-launch CUDA-event times of one step (diagnostic, stderr)."""
     import torch
-    names = ["tcst_decode_route", "tcst_assemble_weight", "tcst_split_tf32", "tcst_gemm_tf32x3",
-             "tcst_mse_grad", "tcst_pullback"]
+    names = ["tcst_decode_route", "tcst_assemble_weight", "tcst_absmax", "tcst_split_f16",
+             "tcst_gemm_f16x3", "tcst_mse_grad_f32", "tcst_pullback"]
     originals = {n: getattr(lib, n) for n in names}
     records = []
 
@@ -263,7 +263,7 @@ def main():
     # GEMM timing hooks: events around the three GEMM launches of every step.
     lib = _native.load()
     gemm_events = []
-    orig_gemm = lib.tcst_gemm_tf32x3
+    orig_gemm = lib.tcst_gemm_f16x3
 
     class Timed:
         def __init__(self):
@@ -282,7 +282,7 @@ def main():
             return rc
 
     timed = Timed()
-    lib.tcst_gemm_tf32x3 = timed
+    lib.tcst_gemm_f16x3 = timed
 
     for i in range(args.warmup):
         step(xs[i % nbuf], ts[i % nbuf])
@@ -442,14 +442,14 @@ def main():
     peak_src = "measured" if "bf16_tflops" in peaks else "fallback"
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
     roofline = {
-        "bound": "tensor", "kernel": "tcst gemm_tf32x3_kernel (Y, dX, dW launches)",
+        "bound": "tensor", "kernel": "tcst gemm_x3_kernel<F16> (Y, dX, dW launches)",
         "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
         "peak_source": f"bf16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
         "traffic": None,
         "note": "achieved = algorithmic fp32 GEMM flops 2*M*N*K per launch / CUDA-event time; "
-                "each flop costs 3 TF32 tensor products (hi*hi+hi*lo+lo*hi) and TF32 issues at "
-                "half the bf16 rate, so 3xTF32 caps frac at 1/6",
-        "frac_of_3xtf32_ceiling": achieved * 6.0 / bf16,
+                "each flop costs 3 f16 tensor products (hi*hi+hi*lo+lo*hi) at the bf16 rate, "
+                "so the three-product split caps frac at 1/3",
+        "frac_of_3x_ceiling": achieved * 3.0 / bf16,
         "gemm_share_of_step": (gemm_ms / 3) / ms_per_step if ms_per_step > 0 else None,
     }
     line = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world,

@@ -171,6 +171,37 @@ int tcst_gemm_tf32x3(int64_t M, int64_t N, int64_t K,
                      float *c_dev, int64_t ldc, int32_t split_k, int64_t split_stride,
                      uint32_t *status_dev, void *stream);
 
+/* The same three-product contraction on f16 split planes (kind::f16 at twice
+ * the TF32 rate, half the operand bytes). Planes come from tcst_split_f16
+ * (element type IEEE half, leading dimensions multiples of 8); a_scale_dev /
+ * b_scale_dev point at the per-tensor power-of-two scales that split stored,
+ * and the epilogue multiplies by 1 / (s_A s_B) (exact). Otherwise as
+ * tcst_gemm_tf32x3. */
+int tcst_gemm_f16x3(int64_t M, int64_t N, int64_t K, const void *a_hi_dev, const void *a_lo_dev,
+                    int64_t lda, int32_t a_mn_major, const float *a_scale_dev,
+                    const void *b_hi_dev, const void *b_lo_dev, int64_t ldb,
+                    int32_t b_mn_major, const float *b_scale_dev, float *c_dev, int64_t ldc,
+                    int32_t split_k, int64_t split_stride, uint32_t *status_dev, void *stream);
+
+/* *amax_dev = max(*amax_dev, max |x|) over a [rows][cols] float32 view (start
+ * it at 0). */
+int tcst_absmax(const float *x_dev, int64_t rows, int64_t cols, int64_t ld, float *amax_dev,
+                void *stream);
+
+/* F16 split for tcst_gemm_f16x3: s = 2^k with max |s x| in [2^14, 2^15) from
+ * *amax_dev (s = 1 when it is 0 or not finite), hi = rn_f16(s x),
+ * lo = rn_f16(s x - hi); s is stored in *scale_dev. */
+int tcst_split_f16(const float *x_dev, int64_t rows, int64_t cols, int64_t ld_x,
+                   const float *amax_dev, void *hi_dev, void *lo_dev, int64_t ld_out,
+                   float *scale_dev, void *stream);
+
+/* MSE upstream gradient in float32: dY = (Y - T) * scale (dy_dev may equal y_dev
+ * with ld_out == ld), per-block sums of (Y - T)^2 as tcst_mse_grad, and
+ * max |dY| folded into *amax_dev (nullable) for the f16 split. */
+int tcst_mse_grad_f32(const float *y_dev, const float *target_dev, int64_t rows, int64_t cols,
+                      int64_t ld, float scale, float *dy_dev, int64_t ld_out,
+                      double *loss_partial_dev, int32_t *blocks, float *amax_dev, void *stream);
+
 /* Atom-parameter gradient from G = sum_s G_s = dY^T X ([N_out][ldg] per split):
  * d amp, d mu_out, d mu_in and d R reduced over each atom footprint in a fixed
  * order, then the rational (a, q) or Polar (s, t) chain. Replaces the autograd

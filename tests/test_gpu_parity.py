@@ -80,6 +80,53 @@ def test_gemm_tf32x3(R, a_mn, b_mn, shape, split):
     assert err < 1e-5, err
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("shape,split", [((256, 512, 256), 1), ((130, 300, 70), 1),
+                                         ((128, 256, 1000), 3), ((8, 16, 4), 1),
+                                         ((300, 520, 1030), 2)])
+@pytest.mark.parametrize("scales", [(1.0, 1.0), (1e-7, 3e4)])
+def test_gemm_f16x3(R, a_mn, b_mn, shape, split, scales):
+    """Three-product f16 split with per-tensor power-of-two scales: the same
+    11-bit significands as 3xTF32, so the same 1e-5 bound, for operands many
+    decades apart in magnitude."""
+    M, N, K = shape
+    g = torch.Generator().manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, generator=g) * scales[0]
+    B = torch.randn(N, K, generator=g) * scales[1]
+    ref = A.double() @ B.double().T
+    a_store = (A.T if a_mn else A).contiguous().cuda()
+    b_store = (B.T if b_mn else B).contiguous().cuda()
+    a = R.F16Split(*a_store.shape, "cuda").fill(a_store)
+    b = R.F16Split(*b_store.shape, "cuda").fill(b_store)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ldc = R.pad4(N)
+    c = torch.full((split, M, ldc), float("nan"), device="cuda")
+    R.gemm_f16(M, N, K, a, a_mn, b, b_mn, c, ldc, status, split_k=split, split_stride=M * ldc)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    out = c[:, :, :N].sum(0).double().cpu()
+    err = float((out - ref).abs().max() / ref.abs().max())
+    assert err < 1e-5, err
+
+
+def test_f16_split_scale_and_exactness(R):
+    """s is a power of two putting max |s x| in [2^14, 2^15); hi + lo keeps
+    22 significant bits of s x."""
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(64, 100, generator=g) * 1e-3).cuda()
+    sp = R.F16Split(64, 100, "cuda").fill(x)
+    torch.cuda.synchronize()
+    amax, s = float(sp.amax[0]), float(sp.scale[0])
+    assert amax == float(x.abs().max())
+    assert s == 2.0 ** round(np.log2(s))
+    assert 2 ** 14 <= amax * s < 2 ** 15
+    recon = (sp.hi[:, :100].double() + sp.lo[:, :100].double()).cpu() / s
+    xd = x.double().cpu()
+    # lo rounds at 2^-11 of itself, or at the f16 subnormal step 2^-24 below 2^-14.
+    bound = xd.abs() * 2.0 ** -21 + 2.0 ** -24 / s
+    assert bool(((recon - xd).abs() <= bound).all())
+
+
 # -- routing ------------------------------------------------------------------------
 
 

@@ -1,7 +1,13 @@
-// C = A B^T on Blackwell tensor cores (tcgen05.mma kind::tf32, TMEM accumulator)
-// with float32 accuracy from the three-product TF32 split:
+// C = A B^T on Blackwell tensor cores (tcgen05.mma, TMEM accumulator) with
+// float32 accuracy from a three-product split:
 //     C ~= A_hi B_hi + A_hi B_lo + A_lo B_hi,
-// where X_hi = rn_tf32(X) and X_lo = rn_tf32(X - X_hi) are produced upstream.
+// in one of two element formats, both with 11-bit significands:
+//   TF32: X_hi = rn_tf32(X), X_lo = rn_tf32(X - X_hi)           (kind::tf32)
+//   F16:  X_hi = rn_f16(s X), X_lo = rn_f16(s X - X_hi), with a per-tensor
+//         power-of-two s that puts max |s X| in [2^14, 2^15)     (kind::f16)
+// The F16 products run at twice the TF32 rate on half the operand bytes; the
+// epilogue multiplies by 1 / (s_A s_B), which is exact. Splits are produced
+// upstream (tcst_split_tf32, tcst_split_f16).
 //
 // One CTA computes one 128 x BN output tile of one split-K slice:
 //   warp 0       TMA producer: four 2-D tiled bulk tensor loads per stage
@@ -11,9 +17,10 @@
 //                stage into one fp32 accumulator of BN TMEM columns; a
 //                tcgen05.commit frees the stage, a final one signals the epilogue;
 //   warps 2..5   epilogue: tcgen05.ld 32 columns at a time, fp32 stores.
-// K-major operands are staged as [rows][32] float rows (128-byte swizzle,
-// 16-byte units); MN-major operands as 32-element strips of [32 k][32] (4 KiB
-// each, 128-byte swizzle with 32-byte units, the MN-major tf32 layout). Every mbarrier wait is bounded: on expiry the kernel raises
+// K-major operands are staged as rows of 128 bytes (BK elements, 128-byte
+// swizzle, 16-byte units); MN-major operands as strips of 128 bytes of MN by BK
+// k-rows (TF32: 128-byte swizzle with 32-byte units, the MN-major tf32 layout;
+// F16: plain 128-byte swizzle). Every mbarrier wait is bounded: on expiry the kernel raises
 // TCST_STATUS_TIMEOUT in the status word and unwinds without touching TMEM
 // again except to free it.
 
@@ -28,13 +35,27 @@ namespace tcst {
 namespace gemm {
 
 constexpr int BM = 128;
-constexpr int BK = 32; // fp32 elements per 128-byte swizzle row
 constexpr int THREADS = 192;
 constexpr unsigned WAIT_LIMIT = 1u << 22; // a few seconds of try_wait polling
 
-template <int BN, int STAGES> struct Layout {
-    static constexpr int A_BYTES = BM * BK * 4;
-    static constexpr int B_BYTES = BN * BK * 4;
+// Element formats. ESIZE bytes per element; BK elements per 128-byte row; one
+// MMA consumes KSTEP elements of K (32 bytes).
+struct TF32 {
+    static constexpr int ESIZE = 4, BK = 32, KSTEP = 8;
+    static constexpr unsigned AB_FORMAT = 2; // instruction-descriptor A/B format
+    static constexpr unsigned MN_LAYOUT = 1; // 128-byte swizzle, 32-byte units
+    static constexpr unsigned MN_SBO = 512;
+};
+struct F16 {
+    static constexpr int ESIZE = 2, BK = 64, KSTEP = 16;
+    static constexpr unsigned AB_FORMAT = 0;
+    static constexpr unsigned MN_LAYOUT = 2; // 128-byte swizzle, 16-byte units
+    static constexpr unsigned MN_SBO = 1024;
+};
+
+template <class P, int BN, int STAGES> struct Layout {
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
     static constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024; // + barriers + alignment slack
@@ -96,13 +117,22 @@ __device__ __forceinline__ uint64_t smem_desc(unsigned addr, unsigned lbo, unsig
     return d;
 }
 
-__device__ __forceinline__ void mma_tf32(unsigned tmem_d, uint64_t a, uint64_t b, unsigned idesc,
-                                         unsigned accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+template <class P>
+__device__ __forceinline__ void mma(unsigned tmem_d, uint64_t a, uint64_t b, unsigned idesc,
+                                    unsigned accumulate) {
+    if constexpr (P::ESIZE == 4) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+            "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+    }
 }
 
 __device__ __forceinline__ void mma_commit(unsigned bar) {
@@ -111,30 +141,38 @@ __device__ __forceinline__ void mma_commit(unsigned bar) {
                  : "memory");
 }
 
-// Staged operand geometry. K-major: [rows][32] fp32 rows of 128 bytes, 16-byte
-// swizzle units over 8-row (1024-byte) groups. MN-major: 32-element MN strips of
-// [32 k][32] (4 KiB, strip stride = LBO), 32-byte swizzle units over 4-row
-// (512-byte) groups (= SBO).
-template <bool MN> struct OperandGeom {
-    // Byte offset of k-step kk (8 fp32 of K) inside one staged operand.
-    static __device__ __forceinline__ unsigned kstep(int kk) { return MN ? kk * 1024u : kk * 32u; }
-    static __device__ __forceinline__ unsigned lbo() { return MN ? 4096u : 16u; }
-    static __device__ __forceinline__ unsigned sbo() { return MN ? 512u : 1024u; }
-    static __device__ __forceinline__ unsigned layout() { return MN ? 1u : 2u; }
+// Staged operand geometry. K-major: rows of 128 bytes (BK elements), 16-byte
+// swizzle units over 8-row (1024-byte) groups; a k-step is 32 bytes along the
+// row. MN-major: strips of 128 bytes of MN (32 TF32 or 64 F16 elements) by BK
+// k-rows (BK * 128 bytes, strip stride = LBO); swizzle groups of 4 rows (TF32,
+// 32-byte units) or 8 rows (F16) are SBO apart; a k-step is KSTEP rows.
+template <class P, bool MN> struct OperandGeom {
+    static constexpr unsigned STRIP = P::BK * 128u;
+    static constexpr int STRIP_ELEMS = 128 / P::ESIZE;
+    static __device__ __forceinline__ unsigned kstep(int kk) {
+        return MN ? kk * unsigned(P::KSTEP) * 128u : kk * 32u;
+    }
+    static __device__ __forceinline__ unsigned lbo() { return MN ? STRIP : 16u; }
+    static __device__ __forceinline__ unsigned sbo() { return MN ? P::MN_SBO : 1024u; }
+    static __device__ __forceinline__ unsigned layout() { return MN ? P::MN_LAYOUT : 2u; }
     static __device__ __forceinline__ uint64_t desc(unsigned addr) {
         return smem_desc(addr, lbo(), sbo(), layout());
     }
 };
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
+template <class P, int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a_hi,
-                       const __grid_constant__ CUtensorMap map_a_lo,
-                       const __grid_constant__ CUtensorMap map_b_hi,
-                       const __grid_constant__ CUtensorMap map_b_lo, int M, int N, int K,
-                       int k_per_split, float *__restrict__ C, long long ldc,
-                       long long split_stride, unsigned *__restrict__ status) {
-    using L = Layout<BN, STAGES>;
+    gemm_x3_kernel(const __grid_constant__ CUtensorMap map_a_hi,
+                   const __grid_constant__ CUtensorMap map_a_lo,
+                   const __grid_constant__ CUtensorMap map_b_hi,
+                   const __grid_constant__ CUtensorMap map_b_lo, int M, int N, int K,
+                   int k_per_split, float *__restrict__ C, long long ldc, long long split_stride,
+                   const float *__restrict__ scale_a, const float *__restrict__ scale_b,
+                   unsigned *__restrict__ status) {
+    using L = Layout<P, BN, STAGES>;
+    constexpr int BK = P::BK;
+    using GA = OperandGeom<P, A_MN>;
+    using GB = OperandGeom<P, B_MN>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -197,9 +235,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tma_load_2d(a_lo, &map_a_lo, full_bar(s), k0, tile_m * BM);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < BM / 32; ++j) {
-                        tma_load_2d(a_hi + j * 4096, &map_a_hi, full_bar(s), tile_m * BM + 32 * j, k0);
-                        tma_load_2d(a_lo + j * 4096, &map_a_lo, full_bar(s), tile_m * BM + 32 * j, k0);
+                    for (int j = 0; j < BM / GA::STRIP_ELEMS; ++j) {
+                        const int m0 = tile_m * BM + GA::STRIP_ELEMS * j;
+                        tma_load_2d(a_hi + j * GA::STRIP, &map_a_hi, full_bar(s), m0, k0);
+                        tma_load_2d(a_lo + j * GA::STRIP, &map_a_lo, full_bar(s), m0, k0);
                     }
                 }
                 if (!B_MN) {
@@ -207,19 +246,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tma_load_2d(b_lo, &map_b_lo, full_bar(s), k0, tile_n * BN);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < BN / 32; ++j) {
-                        tma_load_2d(b_hi + j * 4096, &map_b_hi, full_bar(s), tile_n * BN + 32 * j, k0);
-                        tma_load_2d(b_lo + j * 4096, &map_b_lo, full_bar(s), tile_n * BN + 32 * j, k0);
+                    for (int j = 0; j < BN / GB::STRIP_ELEMS; ++j) {
+                        const int n0 = tile_n * BN + GB::STRIP_ELEMS * j;
+                        tma_load_2d(b_hi + j * GB::STRIP, &map_b_hi, full_bar(s), n0, k0);
+                        tma_load_2d(b_lo + j * GB::STRIP, &map_b_lo, full_bar(s), n0, k0);
                     }
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // Instruction descriptor: f32 accumulate, tf32 A/B, majors, N>>3, M>>4.
-            const unsigned idesc = (1u << 4) | (2u << 7) | (2u << 10) | (unsigned(A_MN) << 15) |
-                                   (unsigned(B_MN) << 16) | (unsigned(BN >> 3) << 17) |
-                                   (unsigned(BM >> 4) << 24);
+            // Instruction descriptor: f32 accumulate, A/B format, majors, N>>3, M>>4.
+            const unsigned idesc = (1u << 4) | (P::AB_FORMAT << 7) | (P::AB_FORMAT << 10) |
+                                   (unsigned(A_MN) << 15) | (unsigned(B_MN) << 16) |
+                                   (unsigned(BN >> 3) << 17) | (unsigned(BM >> 4) << 24);
             int issued = 0;
             for (int kb = 0; kb < num_kb; ++kb) {
                 const int s = kb % STAGES;
@@ -234,16 +274,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const unsigned a_hi = st, a_lo = st + L::A_BYTES;
                 const unsigned b_hi = a_lo + L::A_BYTES, b_lo = b_hi + L::B_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    const unsigned ao = OperandGeom<A_MN>::kstep(kk);
-                    const unsigned bo = OperandGeom<B_MN>::kstep(kk);
-                    const uint64_t dah = OperandGeom<A_MN>::desc(a_hi + ao);
-                    const uint64_t dal = OperandGeom<A_MN>::desc(a_lo + ao);
-                    const uint64_t dbh = OperandGeom<B_MN>::desc(b_hi + bo);
-                    const uint64_t dbl = OperandGeom<B_MN>::desc(b_lo + bo);
-                    mma_tf32(tmem_base, dah, dbh, idesc, issued ? 1u : 0u);
-                    mma_tf32(tmem_base, dah, dbl, idesc, 1u);
-                    mma_tf32(tmem_base, dal, dbh, idesc, 1u);
+                for (int kk = 0; kk < BK / P::KSTEP; ++kk) {
+                    const unsigned ao = GA::kstep(kk);
+                    const unsigned bo = GB::kstep(kk);
+                    const uint64_t dah = GA::desc(a_hi + ao);
+                    const uint64_t dal = GA::desc(a_lo + ao);
+                    const uint64_t dbh = GB::desc(b_hi + bo);
+                    const uint64_t dbl = GB::desc(b_lo + bo);
+                    mma<P>(tmem_base, dah, dbh, idesc, issued ? 1u : 0u);
+                    mma<P>(tmem_base, dah, dbl, idesc, 1u);
+                    mma<P>(tmem_base, dal, dbh, idesc, 1u);
                     issued = 1;
                 }
                 mma_commit(empty_bar(s));
@@ -263,6 +303,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (ready && !*abort_flag) {
             const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+            // 1 / (s_A s_B): a power of two, so the product is exact.
+            const float inv = (scale_a && scale_b) ? 1.0f / (*scale_a * *scale_b) : 1.0f;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 unsigned r[32];
@@ -290,13 +332,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (vec && col0 + 32 <= N) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4 *>(dst + j) =
-                                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                            *reinterpret_cast<float4 *>(dst + j) = make_float4(
+                                __uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
+                                __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
-                            if (col0 + j < N) dst[j] = __uint_as_float(r[j]);
+                            if (col0 + j < N) dst[j] = __uint_as_float(r[j]) * inv;
                     }
                 }
             }
@@ -333,10 +375,11 @@ static EncodeFn encode_fn() {
     return fn;
 }
 
-// 2-D fp32 map over a row-major [outer][inner] array with leading dimension ld,
-// box {32, box_outer}, zero fill outside the array; 128-byte swizzle with 16-byte
-// units for K-major operands, 32-byte units for MN-major ones.
-static int make_map(CUtensorMap *map, const float *base, long long inner, long long outer,
+// 2-D map over a row-major [outer][inner] array with leading dimension ld
+// (elements), box {128 bytes of inner, box_outer}, zero fill outside the array;
+// 128-byte swizzle (MN-major TF32: with 32-byte units).
+template <class P>
+static int make_map(CUtensorMap *map, const void *base, long long inner, long long outer,
                     long long ld, int box_outer, bool mn_major) {
     EncodeFn fn = encode_fn();
     if (!fn) {
@@ -344,36 +387,21 @@ static int make_map(CUtensorMap *map, const float *base, long long inner, long l
         return TCST_ERR_CUDA;
     }
     cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
-    cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
-    cuuint32_t box[2] = {32u, cuuint32_t(box_outer)};
+    cuuint64_t strides[1] = {cuuint64_t(ld) * P::ESIZE};
+    cuuint32_t box[2] = {cuuint32_t(128 / P::ESIZE), cuuint32_t(box_outer)};
     cuuint32_t estr[2] = {1u, 1u};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUtensorMapDataType dt =
+        P::ESIZE == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUtensorMapSwizzle sw = (mn_major && P::ESIZE == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                              : CU_TENSOR_MAP_SWIZZLE_128B;
+    CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         tcst_set_error("cuTensorMapEncodeTiled failed (%d) for inner=%lld outer=%lld ld=%lld",
                        int(r), inner, outer, ld);
         return TCST_ERR_CUDA;
     }
-    return TCST_OK;
-}
-
-template <int BN, int STAGES, bool A_MN, bool B_MN>
-static int launch(int M, int N, int K, const CUtensorMap *maps, int kps, int splits, float *C,
-                  long long ldc, long long sstride, unsigned *status, cudaStream_t stream) {
-    using L = Layout<BN, STAGES>;
-    auto kern = gemm_tf32x3_kernel<BN, STAGES, A_MN, B_MN>;
-    static bool configured = false;
-    if (!configured) {
-        TCST_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       L::SMEM_BYTES));
-        configured = true;
-    }
-    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, splits);
-    kern<<<grid, THREADS, L::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], M, N, K, kps,
-                                                   C, ldc, sstride, status);
-    TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
 
@@ -387,6 +415,93 @@ __global__ void zero_fill_kernel(float *__restrict__ C, long long M, long long N
     C[s * split_stride + r * ldc + c] = 0.0f;
 }
 
+template <class P, int BN, int STAGES, bool A_MN, bool B_MN>
+static int launch(int M, int N, int K, const CUtensorMap *maps, int kps, int splits, float *C,
+                  long long ldc, long long sstride, const float *sa, const float *sb,
+                  unsigned *status, cudaStream_t stream) {
+    using L = Layout<P, BN, STAGES>;
+    auto kern = gemm_x3_kernel<P, BN, STAGES, A_MN, B_MN>;
+    static bool configured = false;
+    if (!configured) {
+        TCST_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       L::SMEM_BYTES));
+        configured = true;
+    }
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, splits);
+    kern<<<grid, THREADS, L::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], M, N, K, kps,
+                                                   C, ldc, sstride, sa, sb, status);
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+// Shared host path of both formats.
+template <class P>
+static int gemm_x3(const char *name, int64_t M, int64_t N, int64_t K, const void *a_hi_dev,
+                   const void *a_lo_dev, int64_t lda, int32_t a_mn_major, const void *b_hi_dev,
+                   const void *b_lo_dev, int64_t ldb, int32_t b_mn_major, float *c_dev,
+                   int64_t ldc, int32_t split_k, int64_t split_stride, const float *sa,
+                   const float *sb, uint32_t *status_dev, void *stream) {
+    if (M < 0 || N < 0 || K < 0 || split_k < 1 || !status_dev || M > INT32_MAX ||
+        N > INT32_MAX || K > INT32_MAX) {
+        tcst_set_error("%s: invalid sizes", name);
+        return TCST_ERR_ARGUMENT;
+    }
+    if (M == 0 || N == 0) return TCST_OK;
+    if (!c_dev || ldc < N || (split_k > 1 && split_stride < M * ldc)) {
+        tcst_set_error("%s: NULL output or invalid output layout", name);
+        return TCST_ERR_ARGUMENT;
+    }
+    if (K == 0) {
+        long long total = M * N * split_k;
+        zero_fill_kernel<<<unsigned((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+            c_dev, M, N, ldc, split_stride, split_k);
+        TCST_CUDA(cudaGetLastError());
+        return TCST_OK;
+    }
+    if (!a_hi_dev || !a_lo_dev || !b_hi_dev || !b_lo_dev) {
+        tcst_set_error("%s: NULL operand", name);
+        return TCST_ERR_ARGUMENT;
+    }
+    const long long a_inner = a_mn_major ? M : K, a_outer = a_mn_major ? K : M;
+    const long long b_inner = b_mn_major ? N : K, b_outer = b_mn_major ? K : N;
+    const int align = 16 / P::ESIZE; // elements per 16 bytes
+    if (lda < a_inner || ldb < b_inner || lda % align || ldb % align ||
+        ((reinterpret_cast<uintptr_t>(a_hi_dev) | reinterpret_cast<uintptr_t>(a_lo_dev) |
+          reinterpret_cast<uintptr_t>(b_hi_dev) | reinterpret_cast<uintptr_t>(b_lo_dev)) & 15)) {
+        tcst_set_error("%s: operands need 16-byte aligned bases and rows", name);
+        return TCST_ERR_ARGUMENT;
+    }
+    constexpr int BN = 256;
+    constexpr int STAGES = 2;
+    constexpr int BK = P::BK;
+    CUtensorMap maps[4];
+    int rc;
+    const int a_box = a_mn_major ? BK : BM;
+    const int b_box = b_mn_major ? BK : BN;
+    if ((rc = make_map<P>(&maps[0], a_hi_dev, a_inner, a_outer, lda, a_box, a_mn_major)) ||
+        (rc = make_map<P>(&maps[1], a_lo_dev, a_inner, a_outer, lda, a_box, a_mn_major)) ||
+        (rc = make_map<P>(&maps[2], b_hi_dev, b_inner, b_outer, ldb, b_box, b_mn_major)) ||
+        (rc = make_map<P>(&maps[3], b_lo_dev, b_inner, b_outer, ldb, b_box, b_mn_major)))
+        return rc;
+    // Split K into whole BK blocks.
+    long long kb_total = (K + BK - 1) / BK;
+    long long kb_per = (kb_total + split_k - 1) / split_k;
+    int kps = int(kb_per * BK);
+    cudaStream_t st = (cudaStream_t)stream;
+    unsigned *status = status_dev;
+    if (!a_mn_major && !b_mn_major)
+        return launch<P, BN, STAGES, false, false>(int(M), int(N), int(K), maps, kps, split_k,
+                                                   c_dev, ldc, split_stride, sa, sb, status, st);
+    if (!a_mn_major && b_mn_major)
+        return launch<P, BN, STAGES, false, true>(int(M), int(N), int(K), maps, kps, split_k,
+                                                  c_dev, ldc, split_stride, sa, sb, status, st);
+    if (a_mn_major && !b_mn_major)
+        return launch<P, BN, STAGES, true, false>(int(M), int(N), int(K), maps, kps, split_k,
+                                                  c_dev, ldc, split_stride, sa, sb, status, st);
+    return launch<P, BN, STAGES, true, true>(int(M), int(N), int(K), maps, kps, split_k, c_dev,
+                                             ldc, split_stride, sa, sb, status, st);
+}
+
 } // namespace gemm
 } // namespace tcst
 
@@ -398,61 +513,23 @@ extern "C" int tcst_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float *a_
                                 const float *b_hi_dev, const float *b_lo_dev, int64_t ldb,
                                 int32_t b_mn_major, float *c_dev, int64_t ldc, int32_t split_k,
                                 int64_t split_stride, uint32_t *status_dev, void *stream) {
-    if (M < 0 || N < 0 || K < 0 || split_k < 1 || !status_dev || M > INT32_MAX ||
-        N > INT32_MAX || K > INT32_MAX) {
-        tcst_set_error("tcst_gemm_tf32x3: invalid sizes");
+    return gemm_x3<TF32>("tcst_gemm_tf32x3", M, N, K, a_hi_dev, a_lo_dev, lda, a_mn_major,
+                         b_hi_dev, b_lo_dev, ldb, b_mn_major, c_dev, ldc, split_k, split_stride,
+                         nullptr, nullptr, status_dev, stream);
+}
+
+extern "C" int tcst_gemm_f16x3(int64_t M, int64_t N, int64_t K, const void *a_hi_dev,
+                               const void *a_lo_dev, int64_t lda, int32_t a_mn_major,
+                               const float *a_scale_dev, const void *b_hi_dev,
+                               const void *b_lo_dev, int64_t ldb, int32_t b_mn_major,
+                               const float *b_scale_dev, float *c_dev, int64_t ldc,
+                               int32_t split_k, int64_t split_stride, uint32_t *status_dev,
+                               void *stream) {
+    if (M > 0 && N > 0 && K > 0 && (!a_scale_dev || !b_scale_dev)) {
+        tcst_set_error("tcst_gemm_f16x3: NULL operand scale");
         return TCST_ERR_ARGUMENT;
     }
-    if (M == 0 || N == 0) return TCST_OK;
-    if (!c_dev || ldc < N || (split_k > 1 && split_stride < M * ldc)) {
-        tcst_set_error("tcst_gemm_tf32x3: NULL output or invalid output layout");
-        return TCST_ERR_ARGUMENT;
-    }
-    if (K == 0) {
-        long long total = M * N * split_k;
-        zero_fill_kernel<<<unsigned((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-            c_dev, M, N, ldc, split_stride, split_k);
-        TCST_CUDA(cudaGetLastError());
-        return TCST_OK;
-    }
-    if (!a_hi_dev || !a_lo_dev || !b_hi_dev || !b_lo_dev) {
-        tcst_set_error("tcst_gemm_tf32x3: NULL operand");
-        return TCST_ERR_ARGUMENT;
-    }
-    const long long a_inner = a_mn_major ? M : K, a_outer = a_mn_major ? K : M;
-    const long long b_inner = b_mn_major ? N : K, b_outer = b_mn_major ? K : N;
-    if (lda < a_inner || ldb < b_inner || lda % 4 || ldb % 4 ||
-        ((reinterpret_cast<uintptr_t>(a_hi_dev) | reinterpret_cast<uintptr_t>(a_lo_dev) |
-          reinterpret_cast<uintptr_t>(b_hi_dev) | reinterpret_cast<uintptr_t>(b_lo_dev)) & 15)) {
-        tcst_set_error("tcst_gemm_tf32x3: operands need 16-byte aligned bases and ld %% 4 == 0");
-        return TCST_ERR_ARGUMENT;
-    }
-    constexpr int BN = 256;
-    constexpr int STAGES = 2;
-    CUtensorMap maps[4];
-    int rc;
-    const int a_box = a_mn_major ? BK : BM;
-    const int b_box = b_mn_major ? BK : BN;
-    if ((rc = make_map(&maps[0], a_hi_dev, a_inner, a_outer, lda, a_box, a_mn_major)) ||
-        (rc = make_map(&maps[1], a_lo_dev, a_inner, a_outer, lda, a_box, a_mn_major)) ||
-        (rc = make_map(&maps[2], b_hi_dev, b_inner, b_outer, ldb, b_box, b_mn_major)) ||
-        (rc = make_map(&maps[3], b_lo_dev, b_inner, b_outer, ldb, b_box, b_mn_major)))
-        return rc;
-    // Split K into whole BK blocks.
-    long long kb_total = (K + BK - 1) / BK;
-    long long kb_per = (kb_total + split_k - 1) / split_k;
-    int kps = int(kb_per * BK);
-    cudaStream_t st = (cudaStream_t)stream;
-    unsigned *status = status_dev;
-    if (!a_mn_major && !b_mn_major)
-        return launch<BN, STAGES, false, false>(int(M), int(N), int(K), maps, kps, split_k, c_dev, ldc,
-                                                split_stride, status, st);
-    if (!a_mn_major && b_mn_major)
-        return launch<BN, STAGES, false, true>(int(M), int(N), int(K), maps, kps, split_k, c_dev, ldc,
-                                               split_stride, status, st);
-    if (a_mn_major && !b_mn_major)
-        return launch<BN, STAGES, true, false>(int(M), int(N), int(K), maps, kps, split_k, c_dev, ldc,
-                                               split_stride, status, st);
-    return launch<BN, STAGES, true, true>(int(M), int(N), int(K), maps, kps, split_k, c_dev, ldc,
-                                          split_stride, status, st);
+    return gemm_x3<F16>("tcst_gemm_f16x3", M, N, K, a_hi_dev, a_lo_dev, lda, a_mn_major,
+                        b_hi_dev, b_lo_dev, ldb, b_mn_major, c_dev, ldc, split_k, split_stride,
+                        a_scale_dev, b_scale_dev, status_dev, stream);
 }

@@ -17,6 +17,8 @@
 #include <algorithm>
 #include <mutex>
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace tcst {
@@ -316,6 +318,150 @@ __global__ void split4_kernel(const float4 *__restrict__ x, long long rows, int 
     lo[r * ldo4 + c] = l;
 }
 
+// Per-tensor power-of-two scale of the F16 split: max |s X| lands in
+// [2^14, 2^15), inside the f16 range with the hi rounding included.
+__device__ __forceinline__ float f16_scale(float amax) {
+    if (!(amax > 0.f) || !(amax < 3.0e38f)) return 1.f;
+    int e;
+    frexpf(amax, &e); // amax = m 2^e, m in [0.5, 1)
+    const int k = max(-120, min(120, 15 - e));
+    return ldexpf(1.f, k);
+}
+
+__device__ __forceinline__ void atomic_max_abs(float *amax, float v) {
+    // Non-negative floats order like their bit patterns.
+    atomicMax(reinterpret_cast<unsigned *>(amax), __float_as_uint(v));
+}
+
+// Block-wide max of m (blockDim.x <= 1024, a multiple of 32), then one atomic
+// per block: same-address atomics serialize, so keep them few.
+__device__ __forceinline__ void block_max_to(float *amax, float m) {
+    __shared__ float wmax[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        m = threadIdx.x < (blockDim.x >> 5) ? wmax[threadIdx.x] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (threadIdx.x == 0 && m > 0.f) atomic_max_abs(amax, m);
+    }
+}
+
+// max |x| over a [rows][cols] view into *amax (which must start at 0 or lower).
+__global__ void __launch_bounds__(1024) absmax_kernel(const float *__restrict__ x, long long rows,
+                                                     int cols, long long ld, int vec,
+                                                     float *__restrict__ amax) {
+    float m = 0.f;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    if (vec) {
+        const int c4 = cols / 4;
+        const long long total = rows * c4;
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
+            const long long r = i / c4;
+            const float4 v = reinterpret_cast<const float4 *>(x + r * ld)[i - r * c4];
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        const long long total = rows * cols;
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
+            const long long r = i / cols;
+            m = fmaxf(m, fabsf(x[r * ld + (i - r * cols)]));
+        }
+    }
+    block_max_to(amax, m);
+}
+
+// F16 split: hi = rn_f16(s x), lo = rn_f16(s x - hi); s from *amax. Block 0
+// stores s for the GEMM epilogue.
+__global__ void __launch_bounds__(256) split_f16_kernel(const float *__restrict__ x,
+                                                        long long rows, int cols, long long ldx,
+                                                        int vec, const float *__restrict__ amax,
+                                                        __half *__restrict__ hi,
+                                                        __half *__restrict__ lo, long long ldo,
+                                                        float *__restrict__ scale_out) {
+    const float s = f16_scale(*amax);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    if (vec) {
+        const int c4 = cols / 4;
+        const long long total = rows * c4;
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
+            const long long r = i / c4;
+            const int c = int(i - r * c4);
+            const float4 v = reinterpret_cast<const float4 *>(x + r * ldx)[c];
+            const float a[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
+            __half h[4], l[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                h[j] = __float2half_rn(a[j]);
+                l[j] = __float2half_rn(a[j] - __half2float(h[j]));
+            }
+            uint2 hp, lp;
+            hp.x = uint32_t(__half_as_ushort(h[0])) | (uint32_t(__half_as_ushort(h[1])) << 16);
+            hp.y = uint32_t(__half_as_ushort(h[2])) | (uint32_t(__half_as_ushort(h[3])) << 16);
+            lp.x = uint32_t(__half_as_ushort(l[0])) | (uint32_t(__half_as_ushort(l[1])) << 16);
+            lp.y = uint32_t(__half_as_ushort(l[2])) | (uint32_t(__half_as_ushort(l[3])) << 16);
+            reinterpret_cast<uint2 *>(hi + r * ldo)[c] = hp;
+            reinterpret_cast<uint2 *>(lo + r * ldo)[c] = lp;
+        }
+    } else {
+        const long long total = rows * cols;
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
+            const long long r = i / cols;
+            const int c = int(i - r * cols);
+            const float a = x[r * ldx + c] * s;
+            const __half h = __float2half_rn(a);
+            hi[r * ldo + c] = h;
+            lo[r * ldo + c] = __float2half_rn(a - __half2float(h));
+        }
+    }
+}
+
+// MSE upstream gradient in float32: dY = (Y - T) * scale (dY may overwrite Y),
+// per-block sums of (Y - T)^2 in double (fixed tree) and max |dY| into *amax.
+__global__ void __launch_bounds__(256) mse_f32_kernel(const float *y, const float *__restrict__ t,
+                                                      long long rows, int cols, long long ld,
+                                                      float scale, float *dy, long long ldo,
+                                                      double *__restrict__ partial, int vec,
+                                                      float *__restrict__ amax) {
+    __shared__ double red[256];
+    double acc = 0;
+    float m = 0.f;
+    for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+        if (vec) {
+            const float4 *yr = reinterpret_cast<const float4 *>(y + r * ld);
+            const float4 *tr = reinterpret_cast<const float4 *>(t + r * ld);
+            float4 *dr = reinterpret_cast<float4 *>(dy + r * ldo);
+            for (int c = threadIdx.x; c < cols / 4; c += blockDim.x) {
+                const float4 a = yr[c], b = tr[c];
+                const float d0 = a.x - b.x, d1 = a.y - b.y, d2 = a.z - b.z, d3 = a.w - b.w;
+                acc += double(d0) * d0 + double(d1) * d1 + double(d2) * d2 + double(d3) * d3;
+                const float4 g = make_float4(d0 * scale, d1 * scale, d2 * scale, d3 * scale);
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(g.x), fabsf(g.y)), fmaxf(fabsf(g.z), fabsf(g.w))));
+                dr[c] = g;
+            }
+        } else {
+            for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+                const float d = y[r * ld + c] - t[r * ld + c];
+                acc += double(d) * double(d);
+                const float g = d * scale;
+                m = fmaxf(m, fabsf(g));
+                dy[r * ldo + c] = g;
+            }
+        }
+    }
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int s2 = 128; s2 > 0; s2 >>= 1) {
+        if (threadIdx.x < s2) red[threadIdx.x] += red[threadIdx.x + s2];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) partial[blockIdx.x] = red[0];
+    if (amax) block_max_to(amax, m);
+}
+
 // MSE upstream gradient: dY = (Y - T) * scale, split into TF32 planes; per-block
 // sums of (Y - T)^2 in double (fixed reduction tree, deterministic). Each CTA
 // owns whole rows; vector path when rows are 16-byte aligned multiples of 4.
@@ -459,6 +605,73 @@ extern "C" int tcst_split_tf32(const float *x_dev, int64_t rows, int64_t cols, i
         dim3 grid(unsigned((cols + 255) / 256), unsigned(rows));
         split_kernel<<<grid, 256, 0, st>>>(x_dev, int(cols), ld_x, hi_dev, lo_dev, ld_out);
     }
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+extern "C" int tcst_absmax(const float *x_dev, int64_t rows, int64_t cols, int64_t ld,
+                           float *amax_dev, void *stream) {
+    if (rows < 0 || cols < 0 || !amax_dev || (rows * cols && (!x_dev || ld < cols))) {
+        tcst_set_error("tcst_absmax: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (rows * cols == 0) return TCST_OK;
+    const int vec = cols % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(x_dev) & 15) == 0;
+    const long long work = vec ? rows * (cols / 4) : rows * cols;
+    const long long blocks = std::min<long long>((work + 1023) / 1024, sm_count() * 2LL);
+    absmax_kernel<<<unsigned(blocks), 1024, 0, (cudaStream_t)stream>>>(x_dev, rows, int(cols), ld,
+                                                                        vec, amax_dev);
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+extern "C" int tcst_split_f16(const float *x_dev, int64_t rows, int64_t cols, int64_t ld_x,
+                              const float *amax_dev, void *hi_dev, void *lo_dev, int64_t ld_out,
+                              float *scale_dev, void *stream) {
+    if (rows < 0 || cols < 0 || !amax_dev || !scale_dev) {
+        tcst_set_error("tcst_split_f16: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (rows * cols == 0) return TCST_OK;
+    if (ld_x < cols || ld_out < cols || !x_dev || !hi_dev || !lo_dev) {
+        tcst_set_error("tcst_split_f16: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    const int vec = cols % 4 == 0 && ld_x % 4 == 0 && ld_out % 4 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(x_dev) & 15) |
+                     (reinterpret_cast<uintptr_t>(hi_dev) & 7) |
+                     (reinterpret_cast<uintptr_t>(lo_dev) & 7)) == 0;
+    const long long work = vec ? rows * (cols / 4) : rows * cols;
+    const long long blocks = std::min<long long>((work + 255) / 256, sm_count() * 16LL);
+    split_f16_kernel<<<unsigned(blocks), 256, 0, (cudaStream_t)stream>>>(
+        x_dev, rows, int(cols), ld_x, vec, amax_dev, (__half *)hi_dev, (__half *)lo_dev, ld_out,
+        scale_dev);
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+extern "C" int tcst_mse_grad_f32(const float *y_dev, const float *target_dev, int64_t rows,
+                                 int64_t cols, int64_t ld, float scale, float *dy_dev,
+                                 int64_t ld_out, double *loss_partial_dev, int32_t *blocks,
+                                 float *amax_dev, void *stream) {
+    const int nblocks = sm_count() * 4;
+    if (blocks) *blocks = nblocks;
+    if (rows < 0 || cols < 1 || ld < cols || ld_out < cols || !loss_partial_dev ||
+        (rows && (!y_dev || !target_dev || !dy_dev))) {
+        tcst_set_error("tcst_mse_grad_f32: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (dy_dev == y_dev && ld_out != ld) {
+        tcst_set_error("tcst_mse_grad_f32: dY may overwrite Y only with the same leading dimension");
+        return TCST_ERR_ARGUMENT;
+    }
+    const int vec =
+        cols % 4 == 0 && ld % 4 == 0 && ld_out % 4 == 0 &&
+        ((reinterpret_cast<uintptr_t>(y_dev) | reinterpret_cast<uintptr_t>(target_dev) |
+          reinterpret_cast<uintptr_t>(dy_dev)) % 16) == 0;
+    mse_f32_kernel<<<nblocks, 256, 0, (cudaStream_t)stream>>>(y_dev, target_dev, rows, int(cols), ld,
+                                                              scale, dy_dev, ld_out,
+                                                              loss_partial_dev, vec, amax_dev);
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

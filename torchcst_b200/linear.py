@@ -22,47 +22,59 @@ from .spec import KernelSpec, PolarRadius, RationalRadius, RegularGrid, radius_c
 
 
 class _CellMassLinear(torch.autograd.Function):
-    """Y = X W^T with W assembled from atoms; backward gives dX and p.grad."""
+    """Y = X W^T with W assembled from atoms; backward gives dX and p.grad.
+
+    X, W and dY enter the tensor cores as f16 hi/lo planes with per-tensor
+    power-of-two scales (three products, float32-accurate; see
+    ``tcst_gemm_f16x3``)."""
 
     @staticmethod
     def forward(ctx, x, p, layer):
         ws = layer._workspace(x.device)
         plan = layer._plan
         atoms = p.shape[0]
+        dev = x.device
         table = R.decode_route(plan, p, ws.status)
         layer._maybe_check(ws)
-        _, w_hi, w_lo, ldw = R.assemble_weight(plan, table, atoms, ws)
-        x_hi, x_lo, ldx = R.split_tf32(x)
+        w, _, _, _ = R.assemble_weight(plan, table, atoms, ws, dense=True, split=False)
+        w16 = R.F16Split(plan.n_out, plan.n_in, dev).fill(w)
         rows = x.shape[0]
-        y = torch.empty(rows, plan.n_out, dtype=torch.float32, device=x.device)
-        R.gemm(rows, plan.n_out, plan.n_in, (x_hi, x_lo), ldx, False, (w_hi, w_lo), ldw, False,
-               y, plan.n_out, ws.status)
-        ctx.save_for_backward(x_hi, x_lo, w_hi, w_lo, table)
-        ctx.meta = (layer, ldx, ldw, rows, atoms)
+        x16 = R.F16Split(rows, plan.n_in, dev)
+        if rows:
+            x16.fill(x)
+        y = torch.empty(rows, plan.n_out, dtype=torch.float32, device=dev)
+        R.gemm_f16(rows, plan.n_out, plan.n_in, x16, False, w16, False, y, plan.n_out, ws.status)
+        ctx.save_for_backward(table)
+        ctx.splits = (x16, w16)
+        ctx.meta = (layer, rows, atoms)
         return y
 
     @staticmethod
     @once_differentiable
     def backward(ctx, dy):
-        x_hi, x_lo, w_hi, w_lo, table = ctx.saved_tensors
-        layer, ldx, ldw, rows, atoms = ctx.meta
+        (table,) = ctx.saved_tensors
+        x16, w16 = ctx.splits
+        layer, rows, atoms = ctx.meta
         plan = layer._plan
         ws = layer._workspace(dy.device)
         dy = dy.contiguous()
-        dy_hi, dy_lo, ldy = R.split_tf32(dy)
+        dy16 = R.F16Split(rows, plan.n_out, dy.device)
+        if rows:
+            dy16.fill(dy)
         dx = grad = None
         if ctx.needs_input_grad[0]:
             dx = torch.empty(rows, plan.n_in, dtype=torch.float32, device=dy.device)
-            R.gemm(rows, plan.n_in, plan.n_out, (dy_hi, dy_lo), ldy, False, (w_hi, w_lo), ldw,
-                   True, dx, plan.n_in, ws.status)
+            R.gemm_f16(rows, plan.n_in, plan.n_out, dy16, False, w16, True, dx, plan.n_in,
+                       ws.status)
         if ctx.needs_input_grad[1]:
             split = R.weight_split_k(plan, rows)
             ldg = R.pad4(plan.n_in)
             stride = plan.n_out * ldg
             g = torch.empty(split * stride, dtype=torch.float32, device=dy.device)
-            R.gemm(plan.n_out, plan.n_in, rows, (dy_hi, dy_lo), ldy, True, (x_hi, x_lo), ldx, True,
-                   g, ldg, ws.status, split_k=split, split_stride=stride)
+            R.gemm_f16(plan.n_out, plan.n_in, rows, dy16, True, x16, True, g, ldg, ws.status,
+                       split_k=split, split_stride=stride)
             grad = R.pullback(plan, table, atoms, g, ldg, split, stride, dy.device)
+        ctx.splits = None
         return dx, grad, None
 
 

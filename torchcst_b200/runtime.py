@@ -147,6 +147,47 @@ def split_tf32(x):
     return hi, lo, ld
 
 
+def pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+class F16Split:
+    """F16 hi/lo planes of one float32 matrix plus its device-side absmax and
+    power-of-two scale (own storage, or views into a caller's buffers)."""
+
+    def __init__(self, rows, cols, device, *, amax=None, scale=None):
+        self.rows, self.cols, self.ld = rows, cols, pad8(cols)
+        self.hi = torch.empty(rows, self.ld, dtype=torch.float16, device=device)
+        self.lo = torch.empty_like(self.hi)
+        if amax is None:
+            words = torch.zeros(2, dtype=torch.float32, device=device)
+            amax, scale = words[0:1], words[1:2]
+        self.amax, self.scale = amax, scale
+
+    @property
+    def scale_ptr(self):
+        return self.scale.data_ptr()
+
+    def fill(self, x, *, amax_ready=False):
+        """Split float32 x [rows][cols] (strided rows); with ``amax_ready`` the
+        caller already folded max |x| into a zeroed ``self.amax``."""
+        st = _stream(x.device)
+        if not amax_ready:
+            self.amax.zero_()
+            N.call("tcst_absmax", _vp(x), self.rows, self.cols, x.stride(0), _vp(self.amax), st)
+        N.call("tcst_split_f16", _vp(x), self.rows, self.cols, x.stride(0), _vp(self.amax),
+               _vp(self.hi), _vp(self.lo), self.ld, _vp(self.scale), st)
+        return self
+
+
+def gemm_f16(M, N_, K, a: F16Split, a_mn, b: F16Split, b_mn, c, ldc, status, *, split_k=1,
+             split_stride=0):
+    N.call("tcst_gemm_f16x3", M, N_, K, _vp(a.hi), _vp(a.lo), a.ld, int(a_mn),
+           ctypes.c_void_p(a.scale_ptr), _vp(b.hi), _vp(b.lo), b.ld, int(b_mn),
+           ctypes.c_void_p(b.scale_ptr), _vp(c), ldc, split_k, split_stride, _vp(status),
+           _stream(c.device))
+
+
 def gemm(M, N_, K, a, lda, a_mn, b, ldb, b_mn, c, ldc, status, *, split_k=1, split_stride=0):
     """C[s] = A B^T over a K slice s (three-product TF32 split on tcgen05)."""
     N.call("tcst_gemm_tf32x3", M, N_, K, _vp(a[0]), _vp(a[1]), lda, int(a_mn), _vp(b[0]),

@@ -7,7 +7,8 @@ buffer is allocated once, and the step is a fixed sequence of native launches
 on the current stream:
 
     decode/route -> bin sort (count, column prefix, scatter) -> weight (mass
-    cache, tile gather) -> split X -> GEMM Y -> MSE dY -> GEMM dX -> GEMM dW
+    cache, tile gather) -> f16 splits of W and X (absmax, split) -> GEMM Y ->
+    MSE dY (float32, with absmax) -> f16 split of dY -> GEMM dX -> GEMM dW
     (split-K) -> pullback (split-K sum, three footprint classes, wide atoms) ->
     optimizer
 
@@ -51,7 +52,7 @@ def dp_reduce_gradient(grad: torch.Tensor, process_group=None) -> torch.Tensor:
 
 
 class MSETrainStep:
-    LAUNCHES_PER_STEP = 18  # kernels; plus one host-to-device copy of the optimizer scalars
+    LAUNCHES_PER_STEP = 22  # kernels; plus one absmax clear and one scalar copy
     RING = 64
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
@@ -69,16 +70,17 @@ class MSETrainStep:
         f32 = torch.float32
         self.table = torch.empty(max(plan.table_bytes(A) // 4, 1), dtype=f32, device=dev)
         self.scratch = self.ws.scratch(A)
-        self.ldw = R.pad4(plan.n_in)
-        self.w_hi = torch.empty(plan.n_out, self.ldw, dtype=f32, device=dev)
-        self.w_lo = torch.empty_like(self.w_hi)
-        self.ldx = R.pad4(plan.n_in)
-        self.x_hi = torch.empty(self.rows, self.ldx, dtype=f32, device=dev)
-        self.x_lo = torch.empty_like(self.x_hi)
-        self.y = torch.empty(self.rows, plan.n_out, dtype=f32, device=dev)
-        self.ldy = R.pad4(plan.n_out)
-        self.dy_hi = torch.empty(self.rows, self.ldy, dtype=f32, device=dev)
-        self.dy_lo = torch.empty_like(self.dy_hi)
+        self.w = torch.empty(plan.n_out, plan.n_in, dtype=f32, device=dev)
+        # absmax words (zeroed together each step) and scales of the W, X, dY splits
+        self.amax = torch.zeros(3, dtype=f32, device=dev)
+        self.scales = torch.ones(3, dtype=f32, device=dev)
+        self.w16 = R.F16Split(plan.n_out, plan.n_in, dev, amax=self.amax[0:1],
+                              scale=self.scales[0:1])
+        self.x16 = R.F16Split(self.rows, plan.n_in, dev, amax=self.amax[1:2],
+                              scale=self.scales[1:2])
+        self.dy16 = R.F16Split(self.rows, plan.n_out, dev, amax=self.amax[2:3],
+                               scale=self.scales[2:3])
+        self.y = torch.empty(self.rows, plan.n_out, dtype=f32, device=dev)  # Y, then dY
         self.dx = torch.empty(self.rows, plan.n_in, dtype=f32, device=dev) if need_dx else None
         self.split = R.weight_split_k(plan, self.rows)
         self.ldg = R.pad4(plan.n_in)
@@ -141,26 +143,32 @@ class MSETrainStep:
         N.check(lib.tcst_decode_route(vp(p), A, oa, ia, ctypes.byref(plan.coords), vp(self.table),
                                       None, None, vp(ws.status), st), "decode")
         N.check(lib.tcst_assemble_weight(vp(self.table), A, oa, ia, vp(self.scratch),
-                                         self.scratch.numel() * 4, None, plan.n_in,
-                                         vp(self.w_hi), vp(self.w_lo), self.ldw, st), "weight")
-        N.check(lib.tcst_split_tf32(vp(x), rows, plan.n_in, x.stride(0), vp(self.x_hi),
-                                    vp(self.x_lo), self.ldx, st), "split")
-        N.check(lib.tcst_gemm_tf32x3(rows, plan.n_out, plan.n_in, vp(self.x_hi), vp(self.x_lo),
-                                     self.ldx, 0, vp(self.w_hi), vp(self.w_lo), self.ldw, 0,
-                                     vp(self.y), plan.n_out, 1, 0, vp(ws.status), st), "gemm y")
-        N.check(lib.tcst_mse_grad(vp(self.y), vp(target), rows, plan.n_out, plan.n_out,
-                                  ctypes.c_float(self.scale), vp(self.dy_hi), vp(self.dy_lo),
-                                  self.ldy, vp(self.partial), ctypes.byref(self.nblocks), st),
-                "mse")
+                                         self.scratch.numel() * 4, vp(self.w), plan.n_in, None,
+                                         None, plan.n_in, st), "weight")
+        self.amax.zero_()
+        w16, x16, dy16 = self.w16, self.x16, self.dy16
+        for sp, src, ld in ((w16, self.w, plan.n_in), (x16, x, x.stride(0))):
+            N.check(lib.tcst_absmax(vp(src), sp.rows, sp.cols, ld, vp(sp.amax), st), "absmax")
+            N.check(lib.tcst_split_f16(vp(src), sp.rows, sp.cols, ld, vp(sp.amax), vp(sp.hi),
+                                       vp(sp.lo), sp.ld, vp(sp.scale), st), "split")
+
+        def gemm(M, N_, K, a, a_mn, b, b_mn, c, ldc, split=1, sstride=0, what="gemm"):
+            N.check(lib.tcst_gemm_f16x3(M, N_, K, vp(a.hi), vp(a.lo), a.ld, a_mn, vp(a.scale),
+                                        vp(b.hi), vp(b.lo), b.ld, b_mn, vp(b.scale), vp(c), ldc,
+                                        split, sstride, vp(ws.status), st), what)
+
+        gemm(rows, plan.n_out, plan.n_in, x16, 0, w16, 0, self.y, plan.n_out, what="gemm y")
+        N.check(lib.tcst_mse_grad_f32(vp(self.y), vp(target), rows, plan.n_out, plan.n_out,
+                                      ctypes.c_float(self.scale), vp(self.y), plan.n_out,
+                                      vp(self.partial), ctypes.byref(self.nblocks),
+                                      vp(dy16.amax), st), "mse")
+        N.check(lib.tcst_split_f16(vp(self.y), rows, plan.n_out, plan.n_out, vp(dy16.amax),
+                                   vp(dy16.hi), vp(dy16.lo), dy16.ld, vp(dy16.scale), st),
+                "split dy")
         if self.need_dx:
-            N.check(lib.tcst_gemm_tf32x3(rows, plan.n_in, plan.n_out, vp(self.dy_hi),
-                                         vp(self.dy_lo), self.ldy, 0, vp(self.w_hi),
-                                         vp(self.w_lo), self.ldw, 1, vp(self.dx), plan.n_in, 1, 0,
-                                         vp(ws.status), st), "gemm dx")
-        N.check(lib.tcst_gemm_tf32x3(plan.n_out, plan.n_in, rows, vp(self.dy_hi), vp(self.dy_lo),
-                                     self.ldy, 1, vp(self.x_hi), vp(self.x_lo), self.ldx, 1,
-                                     vp(self.g), self.ldg, self.split, self.gstride,
-                                     vp(ws.status), st), "gemm dw")
+            gemm(rows, plan.n_in, plan.n_out, dy16, 0, w16, 1, self.dx, plan.n_in, what="gemm dx")
+        gemm(plan.n_out, plan.n_in, rows, dy16, 1, x16, 1, self.g, self.ldg, self.split,
+             self.gstride, what="gemm dw")
         N.check(lib.tcst_pullback(vp(self.table), A, oa, ia, vp(self.g), self.ldg, self.split,
                                   self.gstride, vp(self.grad), st), "pullback")
         return self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
