@@ -27,7 +27,7 @@
 
 namespace tcst {
 
-constexpr int P0_THREADS = 64;
+constexpr int P0_THREADS = 256;
 constexpr int PC_THREADS = 256;
 constexpr int PC_WARPS = PC_THREADS / 32;
 
@@ -131,7 +131,68 @@ __device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, 
     }
 }
 
-// Class 0: one CTA per first-site tile, one thread per atom.
+// Rows [r_lo, r_hi) x columns [c_lo, c_hi) of the G window at (R0, C0) (window
+// coordinates, pitch PITCH); float4s when the rectangle's columns do not wrap.
+template <int PITCH>
+__device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_lo, int c_hi,
+                                           int R0, int C0, int no, int ni,
+                                           const float *__restrict__ g, long long ldg) {
+    c_lo &= ~3;
+    const int nr = r_hi - r_lo, n4 = (c_hi - c_lo + 3) >> 2;
+    if (nr <= 0 || n4 <= 0) return;
+    const bool vec = C0 + c_lo + 4 * n4 <= ni && c_lo + 4 * n4 <= PITCH && ldg % 4 == 0 &&
+                     C0 % 4 == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0;
+    if (vec) {
+        const int n = nr * n4;
+        for (int i0 = threadIdx.x; i0 < n; i0 += 4 * blockDim.x) {
+            float4 v[4];
+            int dst[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * blockDim.x;
+                dst[u] = -1;
+                if (i < n) {
+                    const int rr = i / n4, c4 = i - rr * n4;
+                    int row = R0 + r_lo + rr;
+                    while (row >= no) row -= no;
+                    v[u] = *reinterpret_cast<const float4 *>(g + (long long)row * ldg + C0 + c_lo +
+                                                             4 * c4);
+                    dst[u] = (r_lo + rr) * PITCH + c_lo + 4 * c4;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (dst[u] >= 0) *reinterpret_cast<float4 *>(gw + dst[u]) = v[u];
+        }
+        return;
+    }
+    const int nc = c_hi - c_lo, n = nr * nc;
+    for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
+        float v[8];
+        int dst[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * blockDim.x;
+            dst[u] = -1;
+            if (i < n) {
+                const int rr = i / nc, cc = i - rr * nc;
+                int row = R0 + r_lo + rr, col = C0 + c_lo + cc;
+                while (row >= no) row -= no;
+                while (col >= ni) col -= ni;
+                v[u] = g[(long long)row * ldg + col];
+                dst[u] = (r_lo + rr) * PITCH + c_lo + cc;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (dst[u] >= 0) gw[dst[u]] = v[u];
+    }
+}
+
+// Class 0: one CTA per first-site tile; four threads per atom, each owning
+// four of the (at most 16) input sites; the output-site values of the atom are
+// spread over the quad and shuffled per row; the quad sums its four partials in
+// a fixed xor order.
 __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     Table tv, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, float4 *__restrict__ grad) {
@@ -146,41 +207,60 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     const int R0 = tr * TS, C0 = tc * TS;
     stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
     __syncthreads();
-    for (int k = begin + threadIdx.x; k < end; k += blockDim.x) {
-        const long long a = tv.ids[k];
-        const int4 span = tv.spans[a];
-        const float *sv = tv.sites + a * SITE_FLOATS;
-        const float4 *iv = reinterpret_cast<const float4 *>(sv + 3 * REACH);
-        float im[REACH], idmu[REACH], idr[REACH];
-#pragma unroll
-        for (int q = 0; q < REACH / 4; ++q) {
-            const float4 m4 = iv[q], u4 = iv[REACH / 4 + q], r4 = iv[REACH / 2 + q];
-            im[4 * q] = m4.x, im[4 * q + 1] = m4.y, im[4 * q + 2] = m4.z, im[4 * q + 3] = m4.w;
-            idmu[4 * q] = u4.x, idmu[4 * q + 1] = u4.y, idmu[4 * q + 2] = u4.z,
-            idmu[4 * q + 3] = u4.w;
-            idr[4 * q] = r4.x, idr[4 * q + 1] = r4.y, idr[4 * q + 2] = r4.z, idr[4 * q + 3] = r4.w;
+    const int lane = threadIdx.x & 31, q = lane & 3;
+    const int quads = blockDim.x >> 2;
+    for (int k0 = begin; k0 < end; k0 += quads) {
+        const int k = k0 + (threadIdx.x >> 2);
+        const bool live = k < end;
+        long long a = 0;
+        int4 span = make_int4(0, 0, 0, 0);
+        float4 om = make_float4(0, 0, 0, 0), od = om, orr = om, im = om, id = om, ir = om;
+        if (live) {
+            a = tv.ids[k];
+            span = tv.spans[a];
+            const float4 *sv = reinterpret_cast<const float4 *>(tv.sites + a * SITE_FLOATS);
+            om = sv[q], od = sv[4 + q], orr = sv[8 + q];   // output rows 4q .. 4q+3
+            im = sv[12 + q], id = sv[16 + q], ir = sv[20 + q]; // input columns 4q .. 4q+3
         }
         const int fo = span.y, fi = span.w;
+        float cm[4] = {im.x, im.y, im.z, im.w}, cd[4] = {id.x, id.y, id.z, id.w},
+              cr[4] = {ir.x, ir.y, ir.z, ir.w};
 #pragma unroll
-        for (int c = 0; c < REACH; ++c)
-            if (c >= fi) im[c] = idmu[c] = idr[c] = 0.f;
-        const float *g0 = gw + (span.x - R0) * PITCH + (span.z - C0);
+        for (int j = 0; j < 4; ++j)
+            if (4 * q + j >= fi) cm[j] = cd[j] = cr[j] = 0.f;
+        const float *g0 = gw + (live ? (span.x - R0) * PITCH + (span.z - C0) + 4 * q : 0);
         float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
-        for (int r = 0; r < fo; ++r) {
-            const float rm = sv[r], rdmu = sv[REACH + r], rdr = sv[2 * REACH + r];
-            const float *grow = g0 + r * PITCH;
+        const int base = lane & ~3;
 #pragma unroll
-            for (int c = 0; c < REACH; ++c) {
-                const float gv = c < fi ? grow[c] : 0.f;
-                const float t = gv * im[c];
-                const float u = gv * rm;
-                s_amp = fmaf(t, rm, s_amp);
-                s_mo = fmaf(t, rdmu, s_mo);
-                s_mi = fmaf(u, idmu[c], s_mi);
-                s_r = fmaf(t, rdr, fmaf(u, idr[c], s_r));
+        for (int r = 0; r < REACH; ++r) {
+            const float vm = (r & 3) == 0 ? om.x : (r & 3) == 1 ? om.y : (r & 3) == 2 ? om.z : om.w;
+            const float vd = (r & 3) == 0 ? od.x : (r & 3) == 1 ? od.y : (r & 3) == 2 ? od.z : od.w;
+            const float vr = (r & 3) == 0 ? orr.x : (r & 3) == 1 ? orr.y : (r & 3) == 2 ? orr.z : orr.w;
+            const float rm = __shfl_sync(0xffffffffu, vm, base | (r >> 2));
+            const float rdmu = __shfl_sync(0xffffffffu, vd, base | (r >> 2));
+            const float rdr = __shfl_sync(0xffffffffu, vr, base | (r >> 2));
+            if (r < fo) {
+                const float *grow = g0 + r * PITCH;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float gv = grow[j];
+                    const float t = gv * cm[j];
+                    const float u = gv * rm;
+                    s_amp = fmaf(t, rm, s_amp);
+                    s_mo = fmaf(t, rdmu, s_mo);
+                    s_mi = fmaf(u, cd[j], s_mi);
+                    s_r = fmaf(t, rdr, fmaf(u, cr[j], s_r));
+                }
             }
         }
-        grad[a] = chain(tv.rec + a * (long long)tv.words, s_amp, s_mo, s_mi, s_r);
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+            s_amp += __shfl_xor_sync(0xffffffffu, s_amp, off);
+            s_mo += __shfl_xor_sync(0xffffffffu, s_mo, off);
+            s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
+            s_r += __shfl_xor_sync(0xffffffffu, s_r, off);
+        }
+        if (live && q == 0) grad[a] = chain(tv.rec + a * (long long)tv.words, s_amp, s_mo, s_mi, s_r);
     }
 }
 
@@ -212,7 +292,37 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     }
     if (total == 0) return;
     const int R0 = 2 * ir * TS, C0 = 2 * ic * TS;
-    stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
+    // Stage only the bounding box of the region's footprints.
+    __shared__ int box[4]; // row lo, row hi, col lo, col hi (window coordinates)
+    if (threadIdx.x == 0) box[0] = box[2] = W, box[1] = box[3] = 0;
+    __syncthreads();
+    {
+        int rlo = W, rhi = 0, clo = W, chi = 0;
+        for (int item = threadIdx.x; item < total; item += blockDim.x) {
+            int k = item, q = 0;
+            while (k >= re[q] - rb[q]) {
+                k -= re[q] - rb[q];
+                ++q;
+            }
+            const int4 sp = tv.spans[tv.ids[rb[q] + k]];
+            rlo = min(rlo, sp.x - R0);
+            rhi = max(rhi, sp.x - R0 + sp.y);
+            clo = min(clo, sp.z - C0);
+            chi = max(chi, sp.z - C0 + sp.w);
+        }
+        if (rhi > rlo) {
+            atomicMin(&box[0], rlo);
+            atomicMax(&box[1], min(rhi, W));
+            atomicMin(&box[2], clo);
+            atomicMax(&box[3], min(chi, W));
+        }
+    }
+    __syncthreads();
+    if (split == 1) {
+        stage_rect<PITCH>(gw, box[0], box[1], box[2], box[3], R0, C0, no, ni, g, ldg);
+    } else {
+        stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
+    }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float4 *rowv = reinterpret_cast<float4 *>(sm + W * PITCH) + warp * RC; // (m, dm/dmu, dm/dR, 0)
@@ -242,10 +352,11 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
             ai.load(rec + 4 + aw);
 #pragma unroll
             for (int j = 0; j < Q; ++j) {
-                // Lanes past the footprint read a valid window column with zero weights.
+                // Lanes past the footprint re-read the footprint's last (staged)
+                // column with zero weights.
                 const int c = lane + 32 * j;
                 mi[j] = dmi[j] = dri[j] = 0.f;
-                cl[j] = min(span.z - C0 + c, W - 1);
+                cl[j] = span.z - C0 + min(c, max(fi, 1) - 1);
                 if (c < fi) {
                     const SiteVals v = ai.values(c);
                     mi[j] = v.m;

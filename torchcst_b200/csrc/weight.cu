@@ -350,31 +350,49 @@ __device__ __forceinline__ void block_max_to(float *amax, float m) {
 }
 
 // max |x| over a [rows][cols] view into *amax (which must start at 0 or lower).
-__global__ void __launch_bounds__(1024) absmax_kernel(const float *__restrict__ x, long long rows,
+// Blocks take four rows at a time (four independent loads in flight per
+// thread), threads the row's float4s (or floats).
+constexpr int ROWS_PER_PASS = 4;
+
+__global__ void __launch_bounds__(256) absmax_kernel(const float *__restrict__ x, long long rows,
                                                      int cols, long long ld, int vec,
                                                      float *__restrict__ amax) {
     float m = 0.f;
-    const long long stride = (long long)gridDim.x * blockDim.x;
-    if (vec) {
-        const int c4 = cols / 4;
-        const long long total = rows * c4;
-        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
-            const long long r = i / c4;
-            const float4 v = reinterpret_cast<const float4 *>(x + r * ld)[i - r * c4];
-            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        }
-    } else {
-        const long long total = rows * cols;
-        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
-            const long long r = i / cols;
-            m = fmaxf(m, fabsf(x[r * ld + (i - r * cols)]));
+    const int n = vec ? cols / 4 : cols;
+    for (long long r0 = blockIdx.x * (long long)ROWS_PER_PASS; r0 < rows;
+         r0 += (long long)gridDim.x * ROWS_PER_PASS) {
+        for (int c = threadIdx.x; c < n; c += blockDim.x) {
+            if (vec) {
+                float4 v[ROWS_PER_PASS];
+#pragma unroll
+                for (int u = 0; u < ROWS_PER_PASS; ++u)
+                    v[u] = r0 + u < rows ? reinterpret_cast<const float4 *>(x + (r0 + u) * ld)[c]
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int u = 0; u < ROWS_PER_PASS; ++u)
+                    m = fmaxf(m, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)),
+                                       fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+            } else {
+                float v[ROWS_PER_PASS];
+#pragma unroll
+                for (int u = 0; u < ROWS_PER_PASS; ++u)
+                    v[u] = r0 + u < rows ? x[(r0 + u) * ld + c] : 0.f;
+#pragma unroll
+                for (int u = 0; u < ROWS_PER_PASS; ++u) m = fmaxf(m, fabsf(v[u]));
+            }
         }
     }
     block_max_to(amax, m);
 }
 
+__device__ __forceinline__ void split2(float a0, float a1, __half2 &h, __half2 &l) {
+    h = __float22half2_rn(make_float2(a0, a1));
+    const float2 b = __half22float2(h);
+    l = __float22half2_rn(make_float2(a0 - b.x, a1 - b.y));
+}
+
 // F16 split: hi = rn_f16(s x), lo = rn_f16(s x - hi); s from *amax. Block 0
-// stores s for the GEMM epilogue.
+// stores s for the GEMM epilogue. Four rows per pass, as absmax_kernel.
 __global__ void __launch_bounds__(256) split_f16_kernel(const float *__restrict__ x,
                                                         long long rows, int cols, long long ldx,
                                                         int vec, const float *__restrict__ amax,
@@ -383,38 +401,39 @@ __global__ void __launch_bounds__(256) split_f16_kernel(const float *__restrict_
                                                         float *__restrict__ scale_out) {
     const float s = f16_scale(*amax);
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
-    const long long stride = (long long)gridDim.x * blockDim.x;
-    if (vec) {
-        const int c4 = cols / 4;
-        const long long total = rows * c4;
-        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
-            const long long r = i / c4;
-            const int c = int(i - r * c4);
-            const float4 v = reinterpret_cast<const float4 *>(x + r * ldx)[c];
-            const float a[4] = {v.x * s, v.y * s, v.z * s, v.w * s};
-            __half h[4], l[4];
+    const int n = vec ? cols / 4 : cols;
+    for (long long r0 = blockIdx.x * (long long)ROWS_PER_PASS; r0 < rows;
+         r0 += (long long)gridDim.x * ROWS_PER_PASS) {
+        for (int c = threadIdx.x; c < n; c += blockDim.x) {
+            if (vec) {
+                float4 v[ROWS_PER_PASS];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                h[j] = __float2half_rn(a[j]);
-                l[j] = __float2half_rn(a[j] - __half2float(h[j]));
+                for (int u = 0; u < ROWS_PER_PASS; ++u)
+                    if (r0 + u < rows) v[u] = reinterpret_cast<const float4 *>(x + (r0 + u) * ldx)[c];
+#pragma unroll
+                for (int u = 0; u < ROWS_PER_PASS; ++u) {
+                    if (r0 + u >= rows) continue;
+                    __half2 h0, l0, h1, l1;
+                    split2(v[u].x * s, v[u].y * s, h0, l0);
+                    split2(v[u].z * s, v[u].w * s, h1, l1);
+                    uint2 hp, lp;
+                    hp.x = *reinterpret_cast<unsigned *>(&h0);
+                    hp.y = *reinterpret_cast<unsigned *>(&h1);
+                    lp.x = *reinterpret_cast<unsigned *>(&l0);
+                    lp.y = *reinterpret_cast<unsigned *>(&l1);
+                    reinterpret_cast<uint2 *>(hi + (r0 + u) * ldo)[c] = hp;
+                    reinterpret_cast<uint2 *>(lo + (r0 + u) * ldo)[c] = lp;
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < ROWS_PER_PASS; ++u) {
+                    if (r0 + u >= rows) continue;
+                    const float a = x[(r0 + u) * ldx + c] * s;
+                    const __half h = __float2half_rn(a);
+                    hi[(r0 + u) * ldo + c] = h;
+                    lo[(r0 + u) * ldo + c] = __float2half_rn(a - __half2float(h));
+                }
             }
-            uint2 hp, lp;
-            hp.x = uint32_t(__half_as_ushort(h[0])) | (uint32_t(__half_as_ushort(h[1])) << 16);
-            hp.y = uint32_t(__half_as_ushort(h[2])) | (uint32_t(__half_as_ushort(h[3])) << 16);
-            lp.x = uint32_t(__half_as_ushort(l[0])) | (uint32_t(__half_as_ushort(l[1])) << 16);
-            lp.y = uint32_t(__half_as_ushort(l[2])) | (uint32_t(__half_as_ushort(l[3])) << 16);
-            reinterpret_cast<uint2 *>(hi + r * ldo)[c] = hp;
-            reinterpret_cast<uint2 *>(lo + r * ldo)[c] = lp;
-        }
-    } else {
-        const long long total = rows * cols;
-        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += stride) {
-            const long long r = i / cols;
-            const int c = int(i - r * cols);
-            const float a = x[r * ldx + c] * s;
-            const __half h = __float2half_rn(a);
-            hi[r * ldo + c] = h;
-            lo[r * ldo + c] = __float2half_rn(a - __half2float(h));
         }
     }
 }
@@ -617,10 +636,10 @@ extern "C" int tcst_absmax(const float *x_dev, int64_t rows, int64_t cols, int64
     }
     if (rows * cols == 0) return TCST_OK;
     const int vec = cols % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(x_dev) & 15) == 0;
-    const long long work = vec ? rows * (cols / 4) : rows * cols;
-    const long long blocks = std::min<long long>((work + 1023) / 1024, sm_count() * 2LL);
-    absmax_kernel<<<unsigned(blocks), 1024, 0, (cudaStream_t)stream>>>(x_dev, rows, int(cols), ld,
-                                                                        vec, amax_dev);
+    const long long blocks =
+        std::min<long long>((rows + ROWS_PER_PASS - 1) / ROWS_PER_PASS, sm_count() * 8LL);
+    absmax_kernel<<<unsigned(blocks), 256, 0, (cudaStream_t)stream>>>(x_dev, rows, int(cols), ld,
+                                                                       vec, amax_dev);
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -641,8 +660,8 @@ extern "C" int tcst_split_f16(const float *x_dev, int64_t rows, int64_t cols, in
                     ((reinterpret_cast<uintptr_t>(x_dev) & 15) |
                      (reinterpret_cast<uintptr_t>(hi_dev) & 7) |
                      (reinterpret_cast<uintptr_t>(lo_dev) & 7)) == 0;
-    const long long work = vec ? rows * (cols / 4) : rows * cols;
-    const long long blocks = std::min<long long>((work + 255) / 256, sm_count() * 16LL);
+    const long long blocks =
+        std::min<long long>((rows + ROWS_PER_PASS - 1) / ROWS_PER_PASS, sm_count() * 8LL);
     split_f16_kernel<<<unsigned(blocks), 256, 0, (cudaStream_t)stream>>>(
         x_dev, rows, int(cols), ld_x, vec, amax_dev, (__half *)hi_dev, (__half *)lo_dev, ld_out,
         scale_dev);
