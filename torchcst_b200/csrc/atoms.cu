@@ -339,6 +339,7 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
     const __grid_constant__ ProfileTab tab_out, const __grid_constant__ ProfileTab tab_in,
     Table tv, long long *__restrict__ keys, int *__restrict__ routing,
     unsigned *__restrict__ status) {
+    pdl_wait();
     const long long atoms = tv.atoms;
     const int words = tv.words;
     const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -419,6 +420,7 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
 constexpr int SORT_THREADS = 1024;
 
 __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
+    pdl_wait();
     extern __shared__ int hist[];
     const BinGeom &g = tv.geom;
     for (int i = threadIdx.x; i < g.nbins; i += blockDim.x) hist[i] = 0;
@@ -431,6 +433,7 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
 }
 
 __global__ void __launch_bounds__(64) bin_column_kernel(Table tv) {
+    pdl_wait();
     const BinGeom &g = tv.geom;
     const int bin = blockIdx.x * blockDim.x + threadIdx.x;
     if (bin >= g.nbins) return;
@@ -452,6 +455,7 @@ __global__ void __launch_bounds__(64) bin_column_kernel(Table tv) {
 }
 
 __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
+    pdl_wait();
     extern __shared__ int cursor[];
     __shared__ int wsum[SORT_THREADS / 32];
     const BinGeom &g = tv.geom;
@@ -541,6 +545,7 @@ __device__ double axis_energy(const float *blk, int modes, int n) {
 
 __global__ void energy_kernel(const float *__restrict__ table, int words, long long atoms,
                               AxisCfg out_ax, AxisCfg in_ax, double *__restrict__ energy) {
+    pdl_wait();
     long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (a >= atoms) return;
     const float *rec = table + a * (long long)words;
@@ -617,15 +622,15 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
         ProfileTab to, ti;
         make_profile_tab(oa.modes, &to);
         make_profile_tab(ia.modes, &ti);
-        decode_route_kernel<<<unsigned(blocks), threads, 0, st>>>(
-            p_dev, oa, ia, cc, to, ti, tv, (long long *)owner_keys_dev, routing_dev, status_dev);
+        TCST_CUDA(launch_pdl(decode_route_kernel, dim3(unsigned(blocks)), dim3(threads), 0, st, 
+            p_dev, oa, ia, cc, to, ti, tv, (long long *)owner_keys_dev, routing_dev, status_dev));
         TCST_CUDA(cudaGetLastError());
-        bin_count_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
+        TCST_CUDA(launch_pdl(bin_count_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv));
         TCST_CUDA(cudaGetLastError());
     }
-    bin_column_kernel<<<unsigned((g.nbins + 63) / 64), 64, 0, st>>>(tv);
+    TCST_CUDA(launch_pdl(bin_column_kernel, dim3(unsigned((g.nbins + 63) / 64)), dim3(64), 0, st, tv));
     TCST_CUDA(cudaGetLastError());
-    bin_scatter_kernel<<<unsigned(g.sort_blocks), SORT_THREADS, hist_bytes, st>>>(tv);
+    TCST_CUDA(launch_pdl(bin_scatter_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -647,8 +652,8 @@ extern "C" int tcst_atom_energies(const void *atom_table_dev, int64_t atoms,
     }
     if (atoms == 0) return TCST_OK;
     int words = record_words(oa.modes, ia.modes);
-    energy_kernel<<<unsigned((atoms + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
-        (const float *)atom_table_dev, words, atoms, oa, ia, energy_dev);
+    TCST_CUDA(launch_pdl(energy_kernel, dim3(unsigned((atoms + 127) / 128)), dim3(128), 0, (cudaStream_t)stream, 
+        (const float *)atom_table_dev, words, atoms, oa, ia, energy_dev));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

@@ -20,6 +20,8 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
+
 #include <cuda_runtime.h>
 
 #include "../../include/tcst_b200.h"
@@ -343,6 +345,33 @@ template <int M> struct AxisCoef {
 __host__ int make_axis(const tcst_axis *in, AxisCfg *out, char *err, int errlen);
 __host__ int make_coords(const tcst_coordinates *in, const AxisCfg &out_ax,
                          const AxisCfg &in_ax, CoordCfg *out, char *err, int errlen);
+
+} // namespace tcst
+
+namespace tcst {
+
+// Programmatic dependent launch: every kernel of this library is launched with
+// programmatic stream serialization, so its blocks may become resident while
+// the previous kernel on the stream drains; each kernel calls pdl_wait() before
+// it touches memory that a predecessor writes (griddepcontrol.wait returns
+// once the predecessor grid has completed and its writes are visible).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 } // namespace tcst
 

@@ -213,6 +213,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const unsigned tmem_base = *tmem_slot;
+    pdl_wait(); // operands and C come from earlier kernels; the setup above does not
 
     if (warp == 0) {
         if (lane == 0) {
@@ -408,6 +409,7 @@ static int make_map(CUtensorMap *map, const void *base, long long inner, long lo
 // C = 0 for an empty contraction (K == 0): no operand is read.
 __global__ void zero_fill_kernel(float *__restrict__ C, long long M, long long N, long long ldc,
                                  long long split_stride, int splits) {
+    pdl_wait();
     long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     long long per = M * N;
     if (idx >= per * splits) return;
@@ -428,8 +430,8 @@ static int launch(int M, int N, int K, const CUtensorMap *maps, int kps, int spl
         configured = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, splits);
-    kern<<<grid, THREADS, L::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3], M, N, K, kps,
-                                                   C, ldc, sstride, sa, sb, status);
+    TCST_CUDA(launch_pdl(kern, dim3(grid), dim3(THREADS), L::SMEM_BYTES, stream, maps[0], maps[1], maps[2], maps[3], M, N, K, kps,
+                                                   C, ldc, sstride, sa, sb, status));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -453,8 +455,8 @@ static int gemm_x3(const char *name, int64_t M, int64_t N, int64_t K, const void
     }
     if (K == 0) {
         long long total = M * N * split_k;
-        zero_fill_kernel<<<unsigned((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-            c_dev, M, N, ldc, split_stride, split_k);
+        TCST_CUDA(launch_pdl(zero_fill_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, 
+            c_dev, M, N, ldc, split_stride, split_k));
         TCST_CUDA(cudaGetLastError());
         return TCST_OK;
     }

@@ -112,6 +112,7 @@ __device__ __forceinline__ void step_row(long long a, float4 *__restrict__ p,
 __global__ void optimizer_kernel(float4 *__restrict__ p, const float4 *__restrict__ grad,
                                  float4 *__restrict__ m, float4 *__restrict__ v,
                                  long long atoms, int kind, tcst_adamw h) {
+    pdl_wait();
     const long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (a < atoms) step_row(a, p, grad, m, v, kind, h);
 }
@@ -121,6 +122,7 @@ __global__ void optimizer_dev_kernel(float4 *__restrict__ p, const float4 *__res
                                      float4 *__restrict__ m, float4 *__restrict__ v,
                                      long long atoms, int kind,
                                      const tcst_adamw *__restrict__ hp) {
+    pdl_wait();
     __shared__ tcst_adamw h;
     if (threadIdx.x == 0) h = *hp;
     __syncthreads();
@@ -147,9 +149,9 @@ extern "C" int tcst_optimizer_step(float *p_dev, const float *grad_dev, float *e
         return TCST_ERR_ARGUMENT;
     }
     if (atoms == 0) return TCST_OK;
-    optimizer_kernel<<<unsigned((atoms + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+    TCST_CUDA(launch_pdl(optimizer_kernel, dim3(unsigned((atoms + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, 
         (float4 *)p_dev, (const float4 *)grad_dev, (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev,
-        atoms, kind, *params);
+        atoms, kind, *params));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -170,9 +172,9 @@ extern "C" int tcst_optimizer_step_device(float *p_dev, const float *grad_dev, f
         return TCST_ERR_ARGUMENT;
     }
     if (atoms == 0) return TCST_OK;
-    optimizer_dev_kernel<<<unsigned((atoms + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+    TCST_CUDA(launch_pdl(optimizer_dev_kernel, dim3(unsigned((atoms + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, 
         (float4 *)p_dev, (const float4 *)grad_dev, (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev,
-        atoms, kind, params_dev);
+        atoms, kind, params_dev));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

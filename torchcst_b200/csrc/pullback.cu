@@ -44,6 +44,7 @@ __device__ __forceinline__ float4 chain(const float *rec, float s_amp, float s_m
 // G_0 += G_1 + ... + G_{split-1}, in place (rows of ni valid columns).
 __global__ void g_reduce_kernel(float *__restrict__ g, int no, int ni, long long ldg, int split,
                                 long long split_stride) {
+    pdl_wait();
     const long long total = (long long)no * ni;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
@@ -57,6 +58,7 @@ __global__ void g_reduce_kernel(float *__restrict__ g, int no, int ni, long long
 
 __global__ void g_reduce4_kernel(float4 *__restrict__ g, int no, int ni4, long long ldg4,
                                  int split, long long split_stride4) {
+    pdl_wait();
     const long long total = (long long)no * ni4;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
@@ -196,6 +198,7 @@ __device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_
 __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     Table tv, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, float4 *__restrict__ grad) {
+    pdl_wait();
     constexpr int W = TS + REACH - 1;
     constexpr int PITCH = W + 1;
     __shared__ __align__(16) float gw[W * PITCH];
@@ -269,6 +272,7 @@ template <int RC>
 __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     Table tv, int cls, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, float4 *__restrict__ grad) {
+    pdl_wait();
     constexpr int W = 2 * TS + RC - 1;
     constexpr int PITCH = W + 1;
     constexpr int Q = RC / 32;
@@ -420,6 +424,7 @@ __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
     Table tv, const int *__restrict__ begin_ptr, AxisCfg out_ax, AxisCfg in_ax,
     const float *__restrict__ g, long long ldg, int split, long long split_stride,
     float4 *__restrict__ grad) {
+    pdl_wait();
     __shared__ float so[3][PW_CHUNK], si[3][PW_CHUNK];
     __shared__ float red[PW_THREADS / 32][4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -550,12 +555,12 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
         const bool vec = ia.sites % 4 == 0 && ldg % 4 == 0 && split_stride % 4 == 0 &&
                          reinterpret_cast<uintptr_t>(g_dev) % 16 == 0;
         if (vec) {
-            g_reduce4_kernel<<<148 * 8, 256, 0, st>>>(reinterpret_cast<float4 *>(g_dev), oa.sites,
+            TCST_CUDA(launch_pdl(g_reduce4_kernel, dim3(148 * 8), dim3(256), 0, st, reinterpret_cast<float4 *>(g_dev), oa.sites,
                                                       ia.sites / 4, ldg / 4, split,
-                                                      split_stride / 4);
+                                                      split_stride / 4));
         } else {
-            g_reduce_kernel<<<148 * 8, 256, 0, st>>>(g_dev, oa.sites, ia.sites, ldg, split,
-                                                     split_stride);
+            TCST_CUDA(launch_pdl(g_reduce_kernel, dim3(148 * 8), dim3(256), 0, st, g_dev, oa.sites, ia.sites, ldg, split,
+                                                     split_stride));
         }
         TCST_CUDA(cudaGetLastError());
         split = 1;
@@ -571,19 +576,19 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
                                            int(class_smem<128>())));
             configured = true;
         }
-        pullback_class0_kernel<<<unsigned(geo.tr[0] * geo.tc[0]), P0_THREADS, 0, st>>>(
-            tv, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
+        TCST_CUDA(launch_pdl(pullback_class0_kernel, dim3(unsigned(geo.tr[0] * geo.tc[0])), dim3(P0_THREADS), 0, st, 
+            tv, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
         TCST_CUDA(cudaGetLastError());
         if (geo.nclass > 1) {
             const unsigned regions = unsigned(((geo.tr[1] + 1) / 2) * ((geo.tc[1] + 1) / 2));
-            pullback_class_kernel<64><<<regions, PC_THREADS, class_smem<64>(), st>>>(
-                tv, 1, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
+            TCST_CUDA(launch_pdl(pullback_class_kernel<64>, dim3(regions), dim3(PC_THREADS), class_smem<64>(), st, 
+                tv, 1, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
             TCST_CUDA(cudaGetLastError());
         }
         if (geo.nclass > 2) {
             const unsigned regions = unsigned(((geo.tr[2] + 1) / 2) * ((geo.tc[2] + 1) / 2));
-            pullback_class_kernel<128><<<regions, PC_THREADS, class_smem<128>(), st>>>(
-                tv, 2, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad);
+            TCST_CUDA(launch_pdl(pullback_class_kernel<128>, dim3(regions), dim3(PC_THREADS), class_smem<128>(), st, 
+                tv, 2, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
             TCST_CUDA(cudaGetLastError());
         }
     }
@@ -591,8 +596,8 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
     // starts at the first coarse bin and runs to the end of the ids.
     const int first_bin = geo.nclass > 0 ? geo.base[std::min(NFINE, geo.nclass)] : 0;
     const long long ctas = std::min<long long>(atoms, 148LL * 8);
-    pullback_wide_kernel<<<unsigned(ctas), PW_THREADS, 0, st>>>(
-        tv, tv.offsets + first_bin, oa, ia, g_dev, ldg, split, split_stride, grad);
+    TCST_CUDA(launch_pdl(pullback_wide_kernel, dim3(unsigned(ctas)), dim3(PW_THREADS), 0, st, 
+        tv, tv.offsets + first_bin, oa, ia, g_dev, ldg, split, split_stride, grad));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

@@ -55,6 +55,7 @@ __device__ __forceinline__ int reach_tiles(int c, int tiles, int n) {
 
 // Class 1..NFINE-1 mass cache: cache[a][axis][j] = m_axis(j), j < F_axis.
 __global__ void __launch_bounds__(256) mass_cache_kernel(Table tv, float *__restrict__ cache) {
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = (gridDim.x * (long long)blockDim.x) >> 5;
@@ -85,6 +86,7 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
                                                                    int tiles_c,
                                                                    const float *__restrict__ cache,
                                                                    GatherOut out) {
+    pdl_wait();
     __shared__ int sbeg[MAX_SCAN], scls[MAX_SCAN], spre[MAX_SCAN + 1];
     __shared__ int wtot[WT_THREADS / 32];
     __shared__ __align__(16) float us[WT_STAGE][TS];
@@ -293,6 +295,7 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
 
 __global__ void split_kernel(const float *__restrict__ x, int cols, long long ldx,
                              float *__restrict__ hi, float *__restrict__ lo, long long ldo) {
+    pdl_wait();
     const long long r = blockIdx.y;
     for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x) {
         const float v = x[r * ldx + c];
@@ -306,6 +309,7 @@ __global__ void split_kernel(const float *__restrict__ x, int cols, long long ld
 __global__ void split4_kernel(const float4 *__restrict__ x, long long rows, int cols4,
                               long long ldx4, float4 *__restrict__ hi, float4 *__restrict__ lo,
                               long long ldo4) {
+    pdl_wait();
     long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (idx >= rows * cols4) return;
     long long r = idx / cols4;
@@ -357,6 +361,7 @@ constexpr int ROWS_PER_PASS = 4;
 __global__ void __launch_bounds__(256) absmax_kernel(const float *__restrict__ x, long long rows,
                                                      int cols, long long ld, int vec,
                                                      float *__restrict__ amax) {
+    pdl_wait();
     float m = 0.f;
     const int n = vec ? cols / 4 : cols;
     for (long long r0 = blockIdx.x * (long long)ROWS_PER_PASS; r0 < rows;
@@ -399,6 +404,7 @@ __global__ void __launch_bounds__(256) split_f16_kernel(const float *__restrict_
                                                         __half *__restrict__ hi,
                                                         __half *__restrict__ lo, long long ldo,
                                                         float *__restrict__ scale_out) {
+    pdl_wait();
     const float s = f16_scale(*amax);
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
     const int n = vec ? cols / 4 : cols;
@@ -445,6 +451,7 @@ __global__ void __launch_bounds__(256) mse_f32_kernel(const float *y, const floa
                                                       float scale, float *dy, long long ldo,
                                                       double *__restrict__ partial, int vec,
                                                       float *__restrict__ amax) {
+    pdl_wait();
     __shared__ double red[256];
     double acc = 0;
     float m = 0.f;
@@ -490,6 +497,7 @@ __global__ void __launch_bounds__(256) mse_kernel(const float *__restrict__ y,
                                                   float *__restrict__ hi, float *__restrict__ lo,
                                                   long long ldo, double *__restrict__ partial,
                                                   int vec) {
+    pdl_wait();
     __shared__ double red[256];
     double acc = 0;
     for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -560,13 +568,13 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
     if (atoms > 0 && tv.geom.nclass > 0) {
         // The class range is only known on the device; the kernel reads it.
         const long long warps = std::min<long long>(atoms, sm_count() * 64LL);
-        mass_cache_kernel<<<unsigned((warps + 7) / 8), 256, 0, st>>>(tv, cache);
+        TCST_CUDA(launch_pdl(mass_cache_kernel, dim3(unsigned((warps + 7) / 8)), dim3(256), 0, st, tv, cache));
         TCST_CUDA(cudaGetLastError());
     }
     const int tiles_r = (oa.sites + TS - 1) / TS, tiles_c = (ia.sites + TS - 1) / TS;
     GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split};
-    weight_gather_kernel<<<unsigned(tiles_r * tiles_c), WT_THREADS, 0, st>>>(
-        tv, oa.sites, ia.sites, oa.modes, ia.modes, tiles_c, cache, out);
+    TCST_CUDA(launch_pdl(weight_gather_kernel, dim3(unsigned(tiles_r * tiles_c)), dim3(WT_THREADS), 0, st, 
+        tv, oa.sites, ia.sites, oa.modes, ia.modes, tiles_c, cache, out));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -613,16 +621,16 @@ extern "C" int tcst_split_tf32(const float *x_dev, int64_t rows, int64_t cols, i
                 reinterpret_cast<uintptr_t>(lo_dev)) % 16 == 0;
     if (vec) {
         long long total = rows * (cols / 4);
-        split4_kernel<<<unsigned((total + 255) / 256), 256, 0, st>>>(
+        TCST_CUDA(launch_pdl(split4_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, st, 
             (const float4 *)x_dev, rows, int(cols / 4), ld_x / 4, (float4 *)hi_dev,
-            (float4 *)lo_dev, ld_out / 4);
+            (float4 *)lo_dev, ld_out / 4));
     } else {
         if (rows > 65535) {
             tcst_set_error("tcst_split_tf32: unaligned rows limited to 65535");
             return TCST_ERR_UNSUPPORTED;
         }
         dim3 grid(unsigned((cols + 255) / 256), unsigned(rows));
-        split_kernel<<<grid, 256, 0, st>>>(x_dev, int(cols), ld_x, hi_dev, lo_dev, ld_out);
+        TCST_CUDA(launch_pdl(split_kernel, dim3(grid), dim3(256), 0, st, x_dev, int(cols), ld_x, hi_dev, lo_dev, ld_out));
     }
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
@@ -638,8 +646,8 @@ extern "C" int tcst_absmax(const float *x_dev, int64_t rows, int64_t cols, int64
     const int vec = cols % 4 == 0 && ld % 4 == 0 && (reinterpret_cast<uintptr_t>(x_dev) & 15) == 0;
     const long long blocks =
         std::min<long long>((rows + ROWS_PER_PASS - 1) / ROWS_PER_PASS, sm_count() * 8LL);
-    absmax_kernel<<<unsigned(blocks), 256, 0, (cudaStream_t)stream>>>(x_dev, rows, int(cols), ld,
-                                                                       vec, amax_dev);
+    TCST_CUDA(launch_pdl(absmax_kernel, dim3(unsigned(blocks)), dim3(256), 0, (cudaStream_t)stream, x_dev, rows, int(cols), ld,
+                                                                       vec, amax_dev));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -662,9 +670,9 @@ extern "C" int tcst_split_f16(const float *x_dev, int64_t rows, int64_t cols, in
                      (reinterpret_cast<uintptr_t>(lo_dev) & 7)) == 0;
     const long long blocks =
         std::min<long long>((rows + ROWS_PER_PASS - 1) / ROWS_PER_PASS, sm_count() * 8LL);
-    split_f16_kernel<<<unsigned(blocks), 256, 0, (cudaStream_t)stream>>>(
+    TCST_CUDA(launch_pdl(split_f16_kernel, dim3(unsigned(blocks)), dim3(256), 0, (cudaStream_t)stream, 
         x_dev, rows, int(cols), ld_x, vec, amax_dev, (__half *)hi_dev, (__half *)lo_dev, ld_out,
-        scale_dev);
+        scale_dev));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -688,9 +696,9 @@ extern "C" int tcst_mse_grad_f32(const float *y_dev, const float *target_dev, in
         cols % 4 == 0 && ld % 4 == 0 && ld_out % 4 == 0 &&
         ((reinterpret_cast<uintptr_t>(y_dev) | reinterpret_cast<uintptr_t>(target_dev) |
           reinterpret_cast<uintptr_t>(dy_dev)) % 16) == 0;
-    mse_f32_kernel<<<nblocks, 256, 0, (cudaStream_t)stream>>>(y_dev, target_dev, rows, int(cols), ld,
+    TCST_CUDA(launch_pdl(mse_f32_kernel, dim3(nblocks), dim3(256), 0, (cudaStream_t)stream, y_dev, target_dev, rows, int(cols), ld,
                                                               scale, dy_dev, ld_out,
-                                                              loss_partial_dev, vec, amax_dev);
+                                                              loss_partial_dev, vec, amax_dev));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -710,9 +718,9 @@ extern "C" int tcst_mse_grad(const float *y_dev, const float *target_dev, int64_
         cols % 4 == 0 && ld % 4 == 0 && ld_out % 4 == 0 &&
         ((reinterpret_cast<uintptr_t>(y_dev) | reinterpret_cast<uintptr_t>(target_dev) |
           reinterpret_cast<uintptr_t>(dy_hi_dev) | reinterpret_cast<uintptr_t>(dy_lo_dev)) % 16) == 0;
-    mse_kernel<<<nblocks, 256, 0, (cudaStream_t)stream>>>(y_dev, target_dev, rows, int(cols), ld,
+    TCST_CUDA(launch_pdl(mse_kernel, dim3(nblocks), dim3(256), 0, (cudaStream_t)stream, y_dev, target_dev, rows, int(cols), ld,
                                                           scale, dy_hi_dev, dy_lo_dev, ld_out,
-                                                          loss_partial_dev, vec);
+                                                          loss_partial_dev, vec));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

@@ -99,6 +99,9 @@ class MSETrainStep:
         self._kind = None
         self._graphs = {}
         self._opt_graph = None
+        # Side stream for the branches that do not depend on the main chain
+        # (X split during weight assembly; dX GEMM during dW GEMM + pullback).
+        self._side = torch.cuda.Stream(dev)
 
     # -- pieces --------------------------------------------------------------------
 
@@ -136,27 +139,35 @@ class MSETrainStep:
         """Forward and backward kernels up to this rank's atom gradient."""
         plan, ws, vp = self.plan, self.ws, R._vp
         p = self.layer.atoms.p
-        st = R._stream(p.device)
+        main = torch.cuda.current_stream(p.device)
+        side = self._side
+        st, st2 = main.cuda_stream, side.cuda_stream
         oa, ia = ctypes.byref(plan.out_axis), ctypes.byref(plan.in_axis)
         lib = N.load()
         A, rows = self.atoms, self.rows
+        w16, x16, dy16 = self.w16, self.x16, self.dy16
+
+        def split(sp, src, ld, stream):
+            N.check(lib.tcst_absmax(vp(src), sp.rows, sp.cols, ld, vp(sp.amax), stream), "absmax")
+            N.check(lib.tcst_split_f16(vp(src), sp.rows, sp.cols, ld, vp(sp.amax), vp(sp.hi),
+                                       vp(sp.lo), sp.ld, vp(sp.scale), stream), "split")
+
+        def gemm(M, N_, K, a, a_mn, b, b_mn, c, ldc, split=1, sstride=0, what="gemm",
+                 stream=st):
+            N.check(lib.tcst_gemm_f16x3(M, N_, K, vp(a.hi), vp(a.lo), a.ld, a_mn, vp(a.scale),
+                                        vp(b.hi), vp(b.lo), b.ld, b_mn, vp(b.scale), vp(c), ldc,
+                                        split, sstride, vp(ws.status), stream), what)
+
+        self.amax.zero_()
+        side.wait_stream(main)  # X split runs beside decode and weight assembly
+        split(x16, x, x.stride(0), st2)
         N.check(lib.tcst_decode_route(vp(p), A, oa, ia, ctypes.byref(plan.coords), vp(self.table),
                                       None, None, vp(ws.status), st), "decode")
         N.check(lib.tcst_assemble_weight(vp(self.table), A, oa, ia, vp(self.scratch),
                                          self.scratch.numel() * 4, vp(self.w), plan.n_in, None,
                                          None, plan.n_in, st), "weight")
-        self.amax.zero_()
-        w16, x16, dy16 = self.w16, self.x16, self.dy16
-        for sp, src, ld in ((w16, self.w, plan.n_in), (x16, x, x.stride(0))):
-            N.check(lib.tcst_absmax(vp(src), sp.rows, sp.cols, ld, vp(sp.amax), st), "absmax")
-            N.check(lib.tcst_split_f16(vp(src), sp.rows, sp.cols, ld, vp(sp.amax), vp(sp.hi),
-                                       vp(sp.lo), sp.ld, vp(sp.scale), st), "split")
-
-        def gemm(M, N_, K, a, a_mn, b, b_mn, c, ldc, split=1, sstride=0, what="gemm"):
-            N.check(lib.tcst_gemm_f16x3(M, N_, K, vp(a.hi), vp(a.lo), a.ld, a_mn, vp(a.scale),
-                                        vp(b.hi), vp(b.lo), b.ld, b_mn, vp(b.scale), vp(c), ldc,
-                                        split, sstride, vp(ws.status), st), what)
-
+        split(w16, self.w, plan.n_in, st)
+        main.wait_stream(side)
         gemm(rows, plan.n_out, plan.n_in, x16, 0, w16, 0, self.y, plan.n_out, what="gemm y")
         N.check(lib.tcst_mse_grad_f32(vp(self.y), vp(target), rows, plan.n_out, plan.n_out,
                                       ctypes.c_float(self.scale), vp(self.y), plan.n_out,
@@ -165,13 +176,17 @@ class MSETrainStep:
         N.check(lib.tcst_split_f16(vp(self.y), rows, plan.n_out, plan.n_out, vp(dy16.amax),
                                    vp(dy16.hi), vp(dy16.lo), dy16.ld, vp(dy16.scale), st),
                 "split dy")
-        if self.need_dx:
-            gemm(rows, plan.n_in, plan.n_out, dy16, 0, w16, 1, self.dx, plan.n_in, what="gemm dx")
+        if self.need_dx:  # dX beside dW and the pullback
+            side.wait_stream(main)
+            gemm(rows, plan.n_in, plan.n_out, dy16, 0, w16, 1, self.dx, plan.n_in, what="gemm dx",
+                 stream=st2)
         gemm(plan.n_out, plan.n_in, rows, dy16, 1, x16, 1, self.g, self.ldg, self.split,
              self.gstride, what="gemm dw")
         N.check(lib.tcst_pullback(vp(self.table), A, oa, ia, vp(self.g), self.ldg, self.split,
                                   self.gstride, vp(self.grad), st), "pullback")
-        return self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
+        loss = self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
+        main.wait_stream(side)
+        return loss
 
     def _advance(self):
         """Host side of one optimizer step: step count and scalars to the device.
