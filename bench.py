@@ -216,6 +216,124 @@ def run_reference_arm(args):
     return 0
 
 
+EXTRA = {
+    3: {"metric": "train steps/s (fwd+bwd+CSTAdamW), Polar 784->1024 + ReLU + Linear(1024,10), B=256",
+        "config": {"workload": "config3: CSTLinear 784->1024 Polar cell mass (atoms 16384, M=8, "
+                               "input base tile 49), ReLU, dense 1024->10, cross-entropy, "
+                               "CSTAdamW lr 1e-3 on all parameters",
+                   "global_batch": 256, "atoms": 16384}},
+    4: {"metric": "train steps/s (fwd+bwd+CSTAdamW), FFN pair 2048->8192->2048, 8192 tokens",
+        "config": {"workload": "config4: CSTLinear 2048->8192, GELU, CSTLinear 8192->2048, "
+                               "32768 atoms each, rational radius radius_max=1024 q=0.25, "
+                               "xavier_normal_ gain 1, MSE, CSTAdamW lr 1e-3",
+                   "global_batch": 8192, "atoms": 65536}},
+}
+
+
+def run_extra_config(args):
+    """Configs 3 and 4 through the drop-in autograd API (layer(s), torch loss,
+    CSTAdamW), timed over exactly --steps steps with CUDA events; e2e adds the
+    pinned host-to-device copy of each step's inputs and the loss read-back."""
+    import torch
+    import torch.nn.functional as F
+    from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
+    from torchcst_b200.init import xavier_normal_
+    from torchcst_b200.spec import RadiusBounds
+
+    world, rank, local = dist_info()
+    if world > 1:
+        raise SystemExit("configs 3 and 4 run on one GPU")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    grid = lambda n: chart_presets.regular_grid(n, geometry="flat_torus")
+    cheb = ChebyshevSpec(modes=8)
+    if args.config == 3:
+        b = RadiusBounds(minimum=0.5, birth=4.0, maximum=50.0, upper_floor=1.0)
+        kernel = kernels.product(kernels.cell_mass(cheb), kernels.cell_mass(cheb, base_tile_sites=49),
+                                 coordinates=kernels.polar(amplitude_max=1.0, w_c=0.3, bounds=b))
+        layer = CSTLinear(charts=(grid(1024), grid(784)), atoms=16384, kernel=kernel, device=dev,
+                          validate="off")
+        model = torch.nn.Sequential(layer, torch.nn.ReLU(), torch.nn.Linear(1024, 10).to(dev))
+        rows = 256
+
+        def batch():
+            img = torch.zeros(rows, 28, 28, device=dev)
+            crop = torch.rand(rows, 20, 20, device=dev, generator=gen)
+            keep = torch.rand(rows, 20, 20, device=dev, generator=gen) < 0.37  # ~19% of 784
+            img[:, 4:24, 4:24] = crop * keep
+            return img.reshape(rows, 784), torch.randint(0, 10, (rows,), device=dev,
+                                                         generator=gen)
+
+        loss_fn = F.cross_entropy
+    else:
+        kernel = kernels.product(kernels.cell_mass(cheb), coordinates=kernels.rational_radius(
+            radius_max=1024.0, radius_fraction=0.25))
+        l1 = CSTLinear(charts=(grid(8192), grid(2048)), atoms=32768, kernel=kernel, device=dev,
+                       validate="off")
+        l2 = CSTLinear(charts=(grid(2048), grid(8192)), atoms=32768, kernel=kernel, device=dev,
+                       validate="off")
+        xavier_normal_(l1, gain=1.0, q=0.25)
+        xavier_normal_(l2, gain=1.0, q=0.25)
+        model = torch.nn.Sequential(l1, torch.nn.GELU(), l2)
+        rows = 8192
+
+        def batch():
+            return (torch.randn(rows, 2048, device=dev, generator=gen),
+                    torch.randn(rows, 2048, device=dev, generator=gen))
+
+        loss_fn = F.mse_loss
+    opt = CSTAdamW(model.parameters(), model=model, lr=1e-3)
+    data = [batch() for _ in range(2)]
+
+    def step(x, y):
+        opt.zero_grad(set_to_none=True)
+        loss = loss_fn(model(x), y)
+        loss.backward()
+        opt.step()
+        return loss
+
+    for i in range(args.warmup):
+        step(*data[i % 2])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        loss = step(*data[i % 2])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # e2e: inputs from pinned host memory every step, loss read back.
+    host = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in data]
+    dx = [torch.empty_like(x) for x, _ in data]
+    dy = [torch.empty_like(y) for _, y in data]
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(args.steps):
+        b = i % 2
+        dx[b].copy_(host[b][0], non_blocking=True)
+        dy[b].copy_(host[b][1], non_blocking=True)
+        lo = step(dx[b], dy[b])
+        loss_host.copy_(lo.detach().reshape(1), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    h2d = sum(t.numel() * t.element_size() for t in host[0])
+    spec = EXTRA[args.config]
+    line = {"metric": spec["metric"], "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": dict(spec["config"], parallelism="dp1"),
+            "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4, "api": "model(x); loss.backward(); CSTAdamW.step()"},
+            "loss": float(loss.detach())}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -227,7 +345,12 @@ def main():
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="print per-launch CUDA-event times of one step to stderr")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="2: the headline config (default); 3, 4: the other named shapes on one "
+                         "GPU through the drop-in API")
     args = ap.parse_args()
+    if args.config != 2 and args.impl != "reference":
+        return run_extra_config(args)
     if args.impl == "reference":
         return run_reference_arm(args)
 

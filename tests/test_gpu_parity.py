@@ -214,7 +214,7 @@ def _bin_geom(out_axis, in_axis):
         c += 1
         if _reach(c - 1) >= 2 * max(no, ni):
             break
-    if out_axis.modes != 8 or in_axis.modes != 8 or nb + 1 > 49153:
+    if out_axis.modes != 8 or in_axis.modes != 8 or nb + 1 > 98304:
         return dict(nclass=0, nbins=2)
     return dict(nclass=c, tr=tr, tc=tc, base=base, nbins=nb + 1)
 

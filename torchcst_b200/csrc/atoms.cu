@@ -419,17 +419,26 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
 //            warp-ordered claims), so every bin lists its atoms in id order.
 constexpr int SORT_THREADS = 1024;
 
+// Per-block bin counters are 16-bit (a block holds at most 65,535 atoms), two
+// to a shared-memory word, so the shared histogram covers MAX_BINS bins.
+__device__ __forceinline__ unsigned half_add(unsigned *words, int bin, unsigned n) {
+    const int shift = (bin & 1) * 16;
+    return (atomicAdd(words + (bin >> 1), n << shift) >> shift) & 0xFFFFu;
+}
+
 __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
     pdl_wait();
-    extern __shared__ int hist[];
+    extern __shared__ unsigned hist[];
     const BinGeom &g = tv.geom;
-    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x) hist[i] = 0;
+    const int words = (g.nbins + 1) >> 1;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const long long a0 = blockIdx.x * g.chunk, a1 = min(tv.atoms, a0 + g.chunk);
-    for (long long a = a0 + threadIdx.x; a < a1; a += blockDim.x) atomicAdd(hist + tv.bin_of[a], 1);
+    for (long long a = a0 + threadIdx.x; a < a1; a += blockDim.x) half_add(hist, tv.bin_of[a], 1);
     __syncthreads();
     int *row = tv.counts + (long long)blockIdx.x * g.nbins;
-    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x) row[i] = hist[i];
+    for (int i = threadIdx.x; i < g.nbins; i += blockDim.x)
+        row[i] = int((hist[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu);
 }
 
 __global__ void __launch_bounds__(64) bin_column_kernel(Table tv) {
@@ -456,7 +465,7 @@ __global__ void __launch_bounds__(64) bin_column_kernel(Table tv) {
 
 __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
     pdl_wait();
-    extern __shared__ int cursor[];
+    extern __shared__ unsigned cursor[]; // 16-bit claims made so far, per bin
     __shared__ int wsum[SORT_THREADS / 32];
     const BinGeom &g = tv.geom;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -487,16 +496,18 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
     }
     __syncthreads();
     int run = wsum[warp] + inc - local;
-    const int *mine = tv.counts + (long long)blockIdx.x * g.nbins;
+    // This block's start in every bin replaces its column prefix in place.
+    int *mine = tv.counts + (long long)blockIdx.x * g.nbins;
     for (int k = 0; k < per; ++k) {
         const int i = i0 + k;
         if (i < g.nbins) {
             if (blockIdx.x == 0) tv.offsets[i] = run;
-            cursor[i] = run + mine[i];
+            mine[i] += run;
             run += total[i];
         }
     }
     if (blockIdx.x == 0 && t == 0) tv.offsets[g.nbins] = int(tv.atoms);
+    for (int i = t; i < (g.nbins + 1) >> 1; i += SORT_THREADS) cursor[i] = 0;
     __syncthreads();
     const long long a0 = blockIdx.x * g.chunk, a1 = min(tv.atoms, a0 + g.chunk);
     for (long long base = a0; base < a1; base += SORT_THREADS) {
@@ -506,13 +517,12 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
         const unsigned peers = __match_any_sync(0xffffffffu, bin);
         const int leader = __ffs(peers) - 1;
         const int rank = __popc(peers & ((1u << lane) - 1u));
+        const int bin_base = live ? mine[bin] : 0; // loaded before the ordered claims
         int start = 0;
         // Warps claim their slots one after another, so earlier ids come first.
         for (int w = 0; w < SORT_THREADS / 32; ++w) {
-            if (warp == w && live && lane == leader) {
-                start = cursor[bin];
-                cursor[bin] = start + __popc(peers);
-            }
+            if (warp == w && live && lane == leader)
+                start = bin_base + int(half_add(cursor, bin, unsigned(__popc(peers))));
             __syncthreads();
         }
         start = __shfl_sync(0xffffffffu, start, leader);
@@ -603,13 +613,13 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
     const Table tv = table_view(atom_table_dev, atoms, words, oa.sites, ia.sites, oa.modes, ia.modes);
     const BinGeom &g = tv.geom;
     cudaStream_t st = (cudaStream_t)stream;
-    const size_t hist_bytes = size_t(g.nbins) * 4;
+    const size_t hist_bytes = size_t((g.nbins + 1) >> 1) * 4;
     static bool configured = false;
     if (!configured) {
         TCST_CUDA(cudaFuncSetAttribute(bin_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       MAX_BINS * 4));
+                                       MAX_BINS * 2));
         TCST_CUDA(cudaFuncSetAttribute(bin_scatter_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_BINS * 4));
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_BINS * 2));
         configured = true;
     }
     if (atoms == 0) {

@@ -167,8 +167,8 @@ constexpr int SITE_FLOATS = 2 * 3 * REACH;
 constexpr int TS = 32;          // fine bin tile edge and weight tile edge, in sites
 constexpr int NFINE = 3;        // classes binned by TS tiles
 constexpr int MAX_CLASSES = 16;
-constexpr int MAX_BINS = 49153; // per-CTA bin counters must fit in shared memory
-constexpr int SORT_CHUNK = 1024; // atoms per sort block (at most 64 blocks)
+constexpr int MAX_BINS = 98304;  // 16-bit per-CTA bin counters fit in shared memory
+constexpr int SORT_CHUNK = 1024; // atoms per sort block (64 blocks, more for > 4M atoms)
 constexpr int CACHE_SITES = 128; // masses cached per axis for classes 1..NFINE-1
 
 __host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : 64 << (c - 1); }
@@ -209,8 +209,12 @@ __host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in
         g.base[nc] = int(nb);
         g.nbins = int(nb) + 1;
     }
+    // At most 64 blocks, but never more than 65,535 atoms per block (16-bit counters).
     long long blocks = (atoms + SORT_CHUNK - 1) / SORT_CHUNK;
-    blocks = blocks < 1 ? 1 : (blocks > 64 ? 64 : blocks);
+    const long long at_least = (atoms + 65534) / 65535;
+    blocks = blocks > 64 ? 64 : blocks;
+    blocks = blocks < at_least ? at_least : blocks;
+    blocks = blocks < 1 ? 1 : blocks;
     g.sort_blocks = int(blocks);
     g.chunk = (atoms + blocks - 1) / blocks;
     return g;
