@@ -237,19 +237,21 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
     double s1, c1;
     sincospi(x1, &s1, &c1);
     double sprev = 0.0, scur = s1;
+    // Reciprocals once: sinc_k = sin(pi k x1) / (pi k x1).
+    const double inv_pix = 1.0 / (PI * x1), inv_c0 = 1.0 / C0;
 #pragma unroll 1
     for (int k = 0; k <= M; ++k) {
         double Ck = C0, dCk = dC0, sinc = 1.0;
         if (k > 0) {
             coef(k, Ck, dCk);
-            sinc = scur / (PI * double(k) * x1);
+            sinc = scur * inv_pix * (1.0 / double(k));
             const double sn = 2.0 * c1 * scur - sprev;
             sprev = scur;
             scur = sn;
         }
         const double wk = (k == 0 ? 1.0 : 2.0) * ax.spacing * sinc;
         blk[4 + k] = float(wk * Ck * inv);
-        blk[5 + M + k] = float(wk * (dCk * C0 - Ck * dC0) * inv / C0);
+        blk[5 + M + k] = float(wk * (dCk * C0 - Ck * dC0) * inv * inv_c0);
     }
     (void)CAP;
     if constexpr (MT > 0) {
@@ -334,7 +336,7 @@ __device__ inline Decoded decode_atom(float4 row, const CoordCfg &cc, const Axis
 // Two threads per atom (adjacent lanes): both decode the row; thread 0 routes
 // and profiles the output axis and writes the record header, the output span
 // and the owner key; thread 1 does the input axis.
-__global__ void __launch_bounds__(256) decode_route_kernel(
+__global__ void __launch_bounds__(256, 4) decode_route_kernel(
     const float *__restrict__ p, AxisCfg out_ax, AxisCfg in_ax, CoordCfg cc,
     const __grid_constant__ ProfileTab tab_out, const __grid_constant__ ProfileTab tab_in,
     Table tv, long long *__restrict__ keys, int *__restrict__ routing,
