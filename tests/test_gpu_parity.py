@@ -222,7 +222,7 @@ def _bin_geom(out_axis, in_axis):
 def _table_sections(out_axis, in_axis, atoms):
     """Byte offsets of the atom table sections, restating the device layout
     (records, spans, site values, bin_of, offsets, ids)."""
-    aw = lambda m: 4 + 2 * (m + 1)
+    aw = lambda m: (4 + 2 * (m + 1) + 3) // 4 * 4
     words = (4 + aw(out_axis.modes) + aw(in_axis.modes) + 3) // 4 * 4
     geo = _bin_geom(out_axis, in_axis)
     spans = _align16(atoms * words * 4)

@@ -225,11 +225,6 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
     coef(0, C0, dC0);
     const long long first = (long long)r.first_tile * r.tile;
     const int F = r.count * r.tile;
-    int *iblk = reinterpret_cast<int *>(blk);
-    iblk[0] = int(first);
-    iblk[1] = F;
-    blk[2] = float(2.0 * (double(first) * ax.spacing - r.local) / P);
-    blk[3] = float(2.0 * PI / P);
     const double inv = 1.0 / (P * C0);
     // sin(pi k x1) for k = 0..M by the Chebyshev recurrence
     // sin((k+1)a) = 2 cos(a) sin(k a) - sin((k-1)a), from one sincospi.
@@ -239,36 +234,80 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
     double sprev = 0.0, scur = s1;
     // Reciprocals once: sinc_k = sin(pi k x1) / (pi k x1).
     const double inv_pix = 1.0 / (PI * x1), inv_c0 = 1.0 / C0;
-#pragma unroll 1
-    for (int k = 0; k <= M; ++k) {
-        double Ck = C0, dCk = dC0, sinc = 1.0;
-        if (k > 0) {
-            coef(k, Ck, dCk);
-            sinc = scur * inv_pix * (1.0 / double(k));
-            const double sn = 2.0 * c1 * scur - sprev;
-            sprev = scur;
-            scur = sn;
-        }
-        const double wk = (k == 0 ? 1.0 : 2.0) * ax.spacing * sinc;
-        blk[4 + k] = float(wk * Ck * inv);
-        blk[5 + M + k] = float(wk * (dCk * C0 - Ck * dC0) * inv * inv_c0);
-    }
-    (void)CAP;
+    const float phase0 = float(2.0 * (double(first) * ax.spacing - r.local) / P);
+    const float omega = float(2.0 * PI / P);
     if constexpr (MT > 0) {
+        // Whole block in registers, then float4 stores (the block is 16-byte aligned).
+        float w[24];
+        w[0] = __int_as_float(int(first));
+        w[1] = __int_as_float(F);
+        w[2] = phase0;
+        w[3] = omega;
+#pragma unroll
+        for (int k = 0; k <= MT; ++k) {
+            double Ck = C0, dCk = dC0, sinc = 1.0;
+            if (k > 0) {
+                coef(k, Ck, dCk);
+                sinc = scur * inv_pix * (1.0 / double(k));
+                const double sn = 2.0 * c1 * scur - sprev;
+                sprev = scur;
+                scur = sn;
+            }
+            const double wk = (k == 0 ? 1.0 : 2.0) * ax.spacing * sinc;
+            w[4 + k] = float(wk * Ck * inv);
+            w[5 + MT + k] = float(wk * (dCk * C0 - Ck * dC0) * inv * inv_c0);
+        }
+#pragma unroll
+        for (int k = 6 + 2 * MT; k < 24; ++k) w[k] = 0.f;
+        float4 *b4 = reinterpret_cast<float4 *>(blk);
+#pragma unroll
+        for (int q = 0; q < 6; ++q) b4[q] = make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         if (sites && F <= REACH) {
             AxisCoef<MT> ac;
-            ac.load(blk);
 #pragma unroll
-            for (int j = 0; j < REACH; ++j) {
-                if (j < F) {
-                    const SiteVals v = ac.values(j);
-                    sites[j] = v.m;
-                    sites[REACH + j] = v.dmu;
-                    sites[2 * REACH + j] = v.dR;
+            for (int k = 0; k <= MT; ++k) {
+                ac.c[k] = w[4 + k];
+                ac.dc[k] = w[5 + MT + k];
+            }
+            ac.first = int(first);
+            ac.F = F;
+            ac.phase0 = phase0;
+            ac.omega = omega;
+            float4 *s4 = reinterpret_cast<float4 *>(sites);
+#pragma unroll
+            for (int q = 0; q < REACH / 4; ++q) {
+                if (4 * q < F) {
+                    SiteVals v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) v[u] = ac.values(4 * q + u);
+                    s4[q] = make_float4(v[0].m, v[1].m, v[2].m, v[3].m);
+                    s4[REACH / 4 + q] = make_float4(v[0].dmu, v[1].dmu, v[2].dmu, v[3].dmu);
+                    s4[REACH / 2 + q] = make_float4(v[0].dR, v[1].dR, v[2].dR, v[3].dR);
                 }
             }
         }
+    } else {
+        int *iblk = reinterpret_cast<int *>(blk);
+        iblk[0] = int(first);
+        iblk[1] = F;
+        blk[2] = phase0;
+        blk[3] = omega;
+#pragma unroll 1
+        for (int k = 0; k <= M; ++k) {
+            double Ck = C0, dCk = dC0, sinc = 1.0;
+            if (k > 0) {
+                coef(k, Ck, dCk);
+                sinc = scur * inv_pix * (1.0 / double(k));
+                const double sn = 2.0 * c1 * scur - sprev;
+                sprev = scur;
+                scur = sn;
+            }
+            const double wk = (k == 0 ? 1.0 : 2.0) * ax.spacing * sinc;
+            blk[4 + k] = float(wk * Ck * inv);
+            blk[5 + M + k] = float(wk * (dCk * C0 - Ck * dC0) * inv * inv_c0);
+        }
     }
+    (void)CAP;
 }
 
 __device__ inline void write_axis_block(float *blk, const Route &r, double R, const AxisCfg &ax,
@@ -419,7 +458,7 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
 //            stores them as the offsets), then walks its chunk in id order and
 //            places each atom after the earlier atoms of its bin (warp match +
 //            warp-ordered claims), so every bin lists its atoms in id order.
-constexpr int SORT_THREADS = 1024;
+constexpr int SORT_THREADS = 512;
 
 // Per-block bin counters are 16-bit (a block holds at most 65,535 atoms), two
 // to a shared-memory word, so the shared histogram covers MAX_BINS bins.
@@ -487,14 +526,15 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
     if (lane == 31) wsum[warp] = inc;
     __syncthreads();
     if (warp == 0) {
-        const int w = wsum[lane];
+        constexpr int NW = SORT_THREADS / 32;
+        const int w = lane < NW ? wsum[lane] : 0;
         int winc = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, winc, o);
             if (lane >= o) winc += y;
         }
-        wsum[lane] = winc - w;
+        if (lane < NW) wsum[lane] = winc - w;
     }
     __syncthreads();
     int run = wsum[warp] + inc - local;

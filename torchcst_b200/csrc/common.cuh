@@ -48,7 +48,8 @@ struct CoordCfg {
     double ob[4], ib[4];
 };
 
-__host__ __device__ inline int axis_words(int modes) { return 4 + 2 * (modes + 1); }
+// Axis blocks are padded to 16 bytes so both start aligned and store as float4s.
+__host__ __device__ inline int axis_words(int modes) { return (4 + 2 * (modes + 1) + 3) & ~3; }
 __host__ __device__ inline int record_words(int modes_out, int modes_in) {
     int w = 4 + axis_words(modes_out) + axis_words(modes_in);
     return (w + 3) & ~3;
@@ -168,7 +169,7 @@ constexpr int TS = 32;          // fine bin tile edge and weight tile edge, in s
 constexpr int NFINE = 3;        // classes binned by TS tiles
 constexpr int MAX_CLASSES = 16;
 constexpr int MAX_BINS = 98304;  // 16-bit per-CTA bin counters fit in shared memory
-constexpr int SORT_CHUNK = 1024; // atoms per sort block (64 blocks, more for > 4M atoms)
+constexpr int SORT_CHUNK = 512;  // atoms per sort block (128 blocks, more for > 8M atoms)
 constexpr int CACHE_SITES = 128; // masses cached per axis for classes 1..NFINE-1
 
 __host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : 64 << (c - 1); }
@@ -209,10 +210,10 @@ __host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in
         g.base[nc] = int(nb);
         g.nbins = int(nb) + 1;
     }
-    // At most 64 blocks, but never more than 65,535 atoms per block (16-bit counters).
+    // At most 128 blocks, but never more than 65,535 atoms per block (16-bit counters).
     long long blocks = (atoms + SORT_CHUNK - 1) / SORT_CHUNK;
     const long long at_least = (atoms + 65534) / 65535;
-    blocks = blocks > 64 ? 64 : blocks;
+    blocks = blocks > 128 ? 128 : blocks;
     blocks = blocks < at_least ? at_least : blocks;
     blocks = blocks < 1 ? 1 : blocks;
     g.sort_blocks = int(blocks);
