@@ -138,6 +138,16 @@ int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
                          int64_t ld_weight, float *weight_hi_dev, float *weight_lo_dev,
                          int64_t ld_split, void *stream);
 
+/* Weight assembly for the f16 three-product GEMM: W (float32, required) as
+ * tcst_assemble_weight, max |W| folded into *amax_dev (start it at 0) while the
+ * tiles are written, then the f16 split of tcst_split_f16 into hi/lo with its
+ * power-of-two scale in *scale_dev. */
+int tcst_assemble_weight_f16(const void *atom_table_dev, int64_t atoms,
+                             const tcst_axis *out_axis, const tcst_axis *in_axis,
+                             void *scratch_dev, int64_t scratch_bytes, float *weight_dev,
+                             int64_t ld_weight, float *amax_dev, void *hi_dev, void *lo_dev,
+                             int64_t ld_split, float *scale_dev, void *stream);
+
 /* No counterpart in the reference. The same weight assembly as
  * tcst_assemble_weight for callers that cannot allocate device memory (a plugin
  * inside a host framework whose allocator owns the device, or a fixed-footprint

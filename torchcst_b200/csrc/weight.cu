@@ -76,9 +76,41 @@ __global__ void __launch_bounds__(256) mass_cache_kernel(Table tv, float *__rest
     }
 }
 
+// Per-tensor power-of-two scale of the F16 split: max |s X| lands in
+// [2^14, 2^15), inside the f16 range with the hi rounding included.
+__device__ __forceinline__ float f16_scale(float amax) {
+    if (!(amax > 0.f) || !(amax < 3.0e38f)) return 1.f;
+    int e;
+    frexpf(amax, &e); // amax = m 2^e, m in [0.5, 1)
+    const int k = max(-120, min(120, 15 - e));
+    return ldexpf(1.f, k);
+}
+
+__device__ __forceinline__ void atomic_max_abs(float *amax, float v) {
+    // Non-negative floats order like their bit patterns.
+    atomicMax(reinterpret_cast<unsigned *>(amax), __float_as_uint(v));
+}
+
+// Block-wide max of m (blockDim.x <= 1024, a multiple of 32), then one atomic
+// per block: same-address atomics serialize, so keep them few.
+__device__ __forceinline__ void block_max_to(float *amax, float m) {
+    __shared__ float wmax[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        m = threadIdx.x < (blockDim.x >> 5) ? wmax[threadIdx.x] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (threadIdx.x == 0 && m > 0.f) atomic_max_abs(amax, m);
+    }
+}
+
 struct GatherOut {
     float *w, *hi, *lo;
     long long ldw, lds;
+    float *amax; // nullable: max |W| folded in, one atomic per tile
 };
 
 __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int no, int ni,
@@ -94,6 +126,7 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
     __shared__ int cand[WT_THREADS], ccls[WT_THREADS];
     __shared__ int4 cspan[WT_THREADS];
     __shared__ float camp[WT_THREADS];
+    __shared__ unsigned rmask[WT_STAGE]; // tile rows each staged atom covers
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int trow = blockIdx.x / tiles_c, tcol = blockIdx.x - trow * tiles_c;
     const int R0 = trow * TS, C0 = tcol * TS;
@@ -221,9 +254,15 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
                     const float *src = c == 0 ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
                                               : cache + (atom * 2 + side) * CACHE_SITES;
                     float v = 0.f;
-                    if (stored && p < lim && j < F) v = src[j];
+                    const bool inside = p < lim && j < F;
+                    if (stored && inside) v = src[j];
                     dst[s2][p] = side ? v : v * camp[h0 + s2];
                     rest |= !stored;
+                    if (side == 0) {
+                        // With F > N every tile row is covered by some image.
+                        const unsigned m = __ballot_sync(0xffffffffu, inside || (p < lim && F > nn));
+                        if (p == 0) rmask[s2] = m;
+                    }
                 }
                 if (__any_sync(0xffffffffu, rest)) {
                     for (int s2 = half; s2 < nb; s2 += 2) {
@@ -258,8 +297,11 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
                 }
             }
             __syncthreads();
+            // Each warp owns tile rows 8w .. 8w+7 and skips atoms that miss them.
+            const unsigned wrows = 0xFFu << (8 * warp);
 #pragma unroll 4
             for (int s2 = 0; s2 < nb; ++s2) {
+                if (!(rmask[s2] & wrows)) continue;
                 const float2 u = *reinterpret_cast<const float2 *>(&us[s2][r0]);
                 const float4 v = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
                 const float uu[2] = {u.x, u.y}, vv[4] = {v.x, v.y, v.z, v.w};
@@ -272,6 +314,7 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
         }
     }
 
+    float vmax = 0.f;
 #pragma unroll
     for (int ii = 0; ii < 2; ++ii) {
         const int r = r0 + ii;
@@ -283,6 +326,7 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
             if (c >= TC) continue;
             const long long col = C0 + c;
             const float v = acc[ii][jj];
+            vmax = fmaxf(vmax, fabsf(v));
             if (out.w) out.w[row * out.ldw + col] = v;
             if (out.hi) {
                 const float h = tf32_rna(v);
@@ -291,6 +335,7 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
             }
         }
     }
+    if (out.amax) block_max_to(out.amax, vmax);
 }
 
 __global__ void split_kernel(const float *__restrict__ x, int cols, long long ldx,
@@ -320,37 +365,6 @@ __global__ void split4_kernel(const float4 *__restrict__ x, long long rows, int 
                            tf32_rna(v.w - h.w));
     hi[r * ldo4 + c] = h;
     lo[r * ldo4 + c] = l;
-}
-
-// Per-tensor power-of-two scale of the F16 split: max |s X| lands in
-// [2^14, 2^15), inside the f16 range with the hi rounding included.
-__device__ __forceinline__ float f16_scale(float amax) {
-    if (!(amax > 0.f) || !(amax < 3.0e38f)) return 1.f;
-    int e;
-    frexpf(amax, &e); // amax = m 2^e, m in [0.5, 1)
-    const int k = max(-120, min(120, 15 - e));
-    return ldexpf(1.f, k);
-}
-
-__device__ __forceinline__ void atomic_max_abs(float *amax, float v) {
-    // Non-negative floats order like their bit patterns.
-    atomicMax(reinterpret_cast<unsigned *>(amax), __float_as_uint(v));
-}
-
-// Block-wide max of m (blockDim.x <= 1024, a multiple of 32), then one atomic
-// per block: same-address atomics serialize, so keep them few.
-__device__ __forceinline__ void block_max_to(float *amax, float m) {
-    __shared__ float wmax[32];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        m = threadIdx.x < (blockDim.x >> 5) ? wmax[threadIdx.x] : 0.f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (threadIdx.x == 0 && m > 0.f) atomic_max_abs(amax, m);
-    }
 }
 
 // max |x| over a [rows][cols] view into *amax (which must start at 0 or lower).
@@ -561,7 +575,7 @@ extern "C" int64_t tcst_weight_scratch_bytes(int64_t atoms, const tcst_axis *out
 static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa,
                     const AxisCfg &ia, void *scratch, float *weight_dev, int64_t ld_weight,
                     float *weight_hi_dev, float *weight_lo_dev, int64_t ld_split,
-                    cudaStream_t st) {
+                    cudaStream_t st, float *amax_dev = nullptr) {
     const int words = record_words(oa.modes, ia.modes);
     const Table tv = table_view(atom_table_dev, atoms, words, oa.sites, ia.sites, oa.modes, ia.modes);
     float *cache = static_cast<float *>(scratch);
@@ -572,7 +586,7 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
         TCST_CUDA(cudaGetLastError());
     }
     const int tiles_r = (oa.sites + TS - 1) / TS, tiles_c = (ia.sites + TS - 1) / TS;
-    GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split};
+    GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split, amax_dev};
     TCST_CUDA(launch_pdl(weight_gather_kernel, dim3(unsigned(tiles_r * tiles_c)), dim3(WT_THREADS), 0, st, 
         tv, oa.sites, ia.sites, oa.modes, ia.modes, tiles_c, cache, out));
     TCST_CUDA(cudaGetLastError());
@@ -602,6 +616,35 @@ extern "C" int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
     }
     return assemble(atom_table_dev, atoms, oa, ia, scratch_dev, weight_dev, ld_weight,
                     weight_hi_dev, weight_lo_dev, ld_split, (cudaStream_t)stream);
+}
+
+extern "C" int tcst_assemble_weight_f16(const void *atom_table_dev, int64_t atoms,
+                                        const tcst_axis *out_axis, const tcst_axis *in_axis,
+                                        void *scratch_dev, int64_t scratch_bytes,
+                                        float *weight_dev, int64_t ld_weight, float *amax_dev,
+                                        void *hi_dev, void *lo_dev, int64_t ld_split,
+                                        float *scale_dev, void *stream) {
+    char err[256];
+    AxisCfg oa, ia;
+    int rc;
+    if ((rc = make_axis(out_axis, &oa, err, sizeof(err))) ||
+        (rc = make_axis(in_axis, &ia, err, sizeof(err)))) {
+        tcst_set_error("%s", err);
+        return rc;
+    }
+    if (atoms < 0 || !scratch_dev || !atom_table_dev || !weight_dev || !amax_dev || !hi_dev ||
+        !lo_dev || !scale_dev || scratch_bytes < cache_floats(atoms) * 4 ||
+        reinterpret_cast<uintptr_t>(scratch_dev) % 16 || ld_weight < ia.sites ||
+        ld_split < ia.sites) {
+        tcst_set_error("tcst_assemble_weight_f16: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    if ((rc = assemble(atom_table_dev, atoms, oa, ia, scratch_dev, weight_dev, ld_weight, nullptr,
+                       nullptr, 0, st, amax_dev)))
+        return rc;
+    return tcst_split_f16(weight_dev, oa.sites, ia.sites, ld_weight, amax_dev, hi_dev, lo_dev,
+                          ld_split, scale_dev, stream);
 }
 
 extern "C" int tcst_split_tf32(const float *x_dev, int64_t rows, int64_t cols, int64_t ld_x,

@@ -36,8 +36,7 @@ class _CellMassLinear(torch.autograd.Function):
         dev = x.device
         table = R.decode_route(plan, p, ws.status)
         layer._maybe_check(ws)
-        w, _, _, _ = R.assemble_weight(plan, table, atoms, ws, dense=True, split=False)
-        w16 = R.F16Split(plan.n_out, plan.n_in, dev).fill(w)
+        w16 = R.assemble_weight_f16(plan, table, atoms, ws)
         rows = x.shape[0]
         x16 = R.F16Split(rows, plan.n_in, dev)
         if rows:

@@ -131,6 +131,19 @@ def assemble_weight(plan: Plan, table, atoms, ws: Workspace, *, dense=False, spl
     return w, hi, lo, ld
 
 
+def assemble_weight_f16(plan: Plan, table, atoms, ws: Workspace):
+    """W assembled straight into f16 split planes (with max |W| and its scale)."""
+    dev = ws.device
+    scratch = ws.scratch(atoms)
+    w = torch.empty(plan.n_out, plan.n_in, dtype=torch.float32, device=dev)
+    sp = F16Split(plan.n_out, plan.n_in, dev)
+    sp.amax.zero_()
+    N.call("tcst_assemble_weight_f16", _vp(table), atoms, ctypes.byref(plan.out_axis),
+           ctypes.byref(plan.in_axis), _vp(scratch), scratch.numel() * 4, _vp(w), plan.n_in,
+           _vp(sp.amax), _vp(sp.hi), _vp(sp.lo), sp.ld, _vp(sp.scale), _stream(dev))
+    return sp
+
+
 def split_tf32(x):
     """Two-term TF32 split of a 2-D float32 CUDA tensor into padded planes."""
     require_cuda(x)

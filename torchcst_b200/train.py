@@ -7,7 +7,7 @@ buffer is allocated once, and the step is a fixed sequence of native launches
 on the current stream:
 
     decode/route -> bin sort (count, column prefix, scatter) -> weight (mass
-    cache, tile gather) -> f16 splits of W and X (absmax, split) -> GEMM Y ->
+    cache, tile gather with max |W|, f16 split) | f16 split of X -> GEMM Y ->
     MSE dY (float32, with absmax) -> f16 split of dY -> GEMM dX -> GEMM dW
     (split-K) -> pullback (split-K sum, three footprint classes, wide atoms) ->
     optimizer
@@ -52,7 +52,7 @@ def dp_reduce_gradient(grad: torch.Tensor, process_group=None) -> torch.Tensor:
 
 
 class MSETrainStep:
-    LAUNCHES_PER_STEP = 22  # kernels; plus one absmax clear and one scalar copy
+    LAUNCHES_PER_STEP = 21  # kernels; plus one absmax clear and one scalar copy
     RING = 64
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
@@ -163,10 +163,10 @@ class MSETrainStep:
         split(x16, x, x.stride(0), st2)
         N.check(lib.tcst_decode_route(vp(p), A, oa, ia, ctypes.byref(plan.coords), vp(self.table),
                                       None, None, vp(ws.status), st), "decode")
-        N.check(lib.tcst_assemble_weight(vp(self.table), A, oa, ia, vp(self.scratch),
-                                         self.scratch.numel() * 4, vp(self.w), plan.n_in, None,
-                                         None, plan.n_in, st), "weight")
-        split(w16, self.w, plan.n_in, st)
+        N.check(lib.tcst_assemble_weight_f16(vp(self.table), A, oa, ia, vp(self.scratch),
+                                             self.scratch.numel() * 4, vp(self.w), plan.n_in,
+                                             vp(w16.amax), vp(w16.hi), vp(w16.lo), w16.ld,
+                                             vp(w16.scale), st), "weight")
         main.wait_stream(side)
         gemm(rows, plan.n_out, plan.n_in, x16, 0, w16, 0, self.y, plan.n_out, what="gemm y")
         N.check(lib.tcst_mse_grad_f32(vp(self.y), vp(target), rows, plan.n_out, plan.n_out,
@@ -176,15 +176,18 @@ class MSETrainStep:
         N.check(lib.tcst_split_f16(vp(self.y), rows, plan.n_out, plan.n_out, vp(dy16.amax),
                                    vp(dy16.hi), vp(dy16.lo), dy16.ld, vp(dy16.scale), st),
                 "split dy")
-        if self.need_dx:  # dX beside dW and the pullback
-            side.wait_stream(main)
+        side.wait_stream(main)  # dX and the loss reduction beside dW and the pullback
+        if self.need_dx:
             gemm(rows, plan.n_in, plan.n_out, dy16, 0, w16, 1, self.dx, plan.n_in, what="gemm dx",
                  stream=st2)
+        with torch.cuda.stream(side):
+            loss = self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
+        if not torch.cuda.is_current_stream_capturing():
+            loss.record_stream(main)  # made on the side stream, read on the main one
         gemm(plan.n_out, plan.n_in, rows, dy16, 1, x16, 1, self.g, self.ldg, self.split,
              self.gstride, what="gemm dw")
         N.check(lib.tcst_pullback(vp(self.table), A, oa, ia, vp(self.g), self.ldg, self.split,
                                   self.gstride, vp(self.grad), st), "pullback")
-        loss = self.partial[: self.nblocks.value].sum() / (rows * plan.n_out)
         main.wait_stream(side)
         return loss
 
