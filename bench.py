@@ -38,6 +38,9 @@ CONFIG = {"workload": "config2: CSTLinear 1024->1024, 65536 atoms, rational radi
                       "radius_max=512 q=0 He init, M=8 cell masses, MSE, CSTAdamW field_lrs",
           "global_batch": 4096, "n_in": 1024, "n_out": 1024, "atoms": 65536}
 ROWS, N_IO, ATOMS = 4096, 1024, 65536
+# DRAM bytes per GEMM launch at this workload (ncu, mean of Y, dX and dW:
+# 20.997 + 21.078 + 33.589 MB): the operand planes read once.
+GEMM_TRAFFIC = 25.22e6
 FIELD_LRS = {"amplitude": 2.4e-3, "radius_fraction": 9.6e-3}
 
 
@@ -568,7 +571,10 @@ def main():
         "bound": "tensor", "kernel": "tcst gemm_x3_kernel<F16> (Y, dX, dW launches)",
         "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
         "peak_source": f"bf16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
-        "traffic": None,
+        "traffic": GEMM_TRAFFIC,
+        "traffic_note": "bytes per launch, mean of the Y, dX and dW launches: ncu "
+                        "dram__bytes_read.sum + dram__bytes_write.sum "
+                        "(profiles/gemm_f16x3_config2.md)",
         "note": "achieved = algorithmic fp32 GEMM flops 2*M*N*K per launch / CUDA-event time; "
                 "each flop costs 3 f16 tensor products (hi*hi+hi*lo+lo*hi) at the bf16 rate, "
                 "so the three-product split caps frac at 1/3",
