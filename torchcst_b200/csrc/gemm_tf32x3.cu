@@ -10,19 +10,19 @@
 // upstream (tcst_split_tf32, tcst_split_f16).
 //
 // One CTA computes one 128 x BN output tile of one split-K slice:
-//   warp 0       TMA producer: four 2-D tiled bulk tensor loads per stage
-//                (A_hi, A_lo, B_hi, B_lo; 128-byte swizzle), completing on the
-//                stage's "full" mbarrier;
-//   warp 1       TMEM allocator and MMA issuer: 3 x (BK / 8) tcgen05.mma per
-//                stage into one fp32 accumulator of BN TMEM columns; a
+//   warp 0       TMA producer: 2-D tiled bulk tensor loads of A_hi, A_lo,
+//                B_hi, B_lo per stage (swizzled), completing on the stage's
+//                "full" mbarrier;
+//   warp 1       TMEM allocator and MMA issuer: 3 x (BK / KSTEP) tcgen05.mma
+//                per stage into one fp32 accumulator of BN TMEM columns; a
 //                tcgen05.commit frees the stage, a final one signals the epilogue;
 //   warps 2..5   epilogue: tcgen05.ld 32 columns at a time, fp32 stores.
-// K-major operands are staged as rows of 128 bytes (BK elements, 128-byte
-// swizzle, 16-byte units); MN-major operands as strips of 128 bytes of MN by BK
-// k-rows (TF32: 128-byte swizzle with 32-byte units, the MN-major tf32 layout;
-// F16: plain 128-byte swizzle). Every mbarrier wait is bounded: on expiry the kernel raises
-// TCST_STATUS_TIMEOUT in the status word and unwinds without touching TMEM
-// again except to free it.
+// K-major operands are staged as swizzled rows of BK elements; MN-major
+// operands as strips of 128 bytes of MN by BK k-rows (TF32: 128-byte swizzle
+// with 32-byte units, the MN-major tf32 layout; F16: 128-byte swizzle, with
+// 64-byte K-major rows and 4 stages). Every mbarrier wait is bounded: on
+// expiry the kernel raises TCST_STATUS_TIMEOUT in the status word and unwinds
+// without touching TMEM again except to free it.
 
 #include <cuda.h>
 
@@ -38,24 +38,41 @@ constexpr int BM = 128;
 constexpr int THREADS = 192;
 constexpr unsigned WAIT_LIMIT = 1u << 22; // a few seconds of try_wait polling
 
-// Element formats. ESIZE bytes per element; BK elements per 128-byte row; one
-// MMA consumes KSTEP elements of K (32 bytes).
+// Staging formats. ESIZE bytes per element; a stage holds BK elements of K;
+// one MMA consumes KSTEP elements of K (32 bytes). K-major operands are staged
+// as rows of K_ROW = BK * ESIZE bytes (the swizzle span); MN-major operands as
+// strips of MN_ROW bytes of MN by BK k-rows. Shared-memory descriptor layout
+// types: 2 = 128-byte swizzle, 1 = 128-byte swizzle with 32-byte units (the
+// MN-major tf32 layout), 4 = 64-byte swizzle; SBO is the distance between
+// 8-row (4-row for type 1) swizzle groups.
 struct TF32 {
-    static constexpr int ESIZE = 4, BK = 32, KSTEP = 8;
+    static constexpr int ESIZE = 4, BK = 32, KSTEP = 8, K_ROW = 128, MN_ROW = 128, STAGES = 2;
     static constexpr unsigned AB_FORMAT = 2; // instruction-descriptor A/B format
-    static constexpr unsigned MN_LAYOUT = 1; // 128-byte swizzle, 32-byte units
-    static constexpr unsigned MN_SBO = 512;
+    static constexpr unsigned K_LAYOUT = 2, K_SBO = 1024;
+    static constexpr unsigned MN_LAYOUT = 1, MN_SBO = 512;
 };
-struct F16 {
-    static constexpr int ESIZE = 2, BK = 64, KSTEP = 16;
+// F16, 64 elements of K per stage: 2 stages of 96 KB (MN-major operands).
+struct F16Wide {
+    static constexpr int ESIZE = 2, BK = 64, KSTEP = 16, K_ROW = 128, MN_ROW = 128, STAGES = 2;
     static constexpr unsigned AB_FORMAT = 0;
-    static constexpr unsigned MN_LAYOUT = 2; // 128-byte swizzle, 16-byte units
-    static constexpr unsigned MN_SBO = 1024;
+    static constexpr unsigned K_LAYOUT = 2, K_SBO = 1024;
+    static constexpr unsigned MN_LAYOUT = 2, MN_SBO = 1024;
+};
+// F16, 32 elements of K per stage: 4 stages of 48 KB, so three fills are in
+// flight while one stage is consumed (the fill latency of a 96 KB stage is
+// about one stage's MMA time, which left the tensor pipe waiting with 2
+// stages). K-major rows are 64 bytes (64-byte swizzle); MN-major strips stay
+// 128 bytes wide. Used when both operands are K-major.
+struct F16 {
+    static constexpr int ESIZE = 2, BK = 32, KSTEP = 16, K_ROW = 64, MN_ROW = 128, STAGES = 4;
+    static constexpr unsigned AB_FORMAT = 0;
+    static constexpr unsigned K_LAYOUT = 4, K_SBO = 512;
+    static constexpr unsigned MN_LAYOUT = 2, MN_SBO = 1024;
 };
 
 template <class P, int BN, int STAGES> struct Layout {
-    static constexpr int A_BYTES = BM * 128;
-    static constexpr int B_BYTES = BN * 128;
+    static constexpr int A_BYTES = BM * P::BK * P::ESIZE;
+    static constexpr int B_BYTES = BN * P::BK * P::ESIZE;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
     static constexpr int SMEM_BYTES = BAR_OFFSET + 256 + 1024; // + barriers + alignment slack
@@ -102,10 +119,8 @@ __device__ __forceinline__ void tma_load_2d(unsigned dst, const CUtensorMap *map
         : "memory");
 }
 
-// UMMA shared-memory matrix descriptor with sm_100 version bits. Layout type 2
-// is the 128-byte swizzle with 16-byte units (K-major operands); layout type 1
-// is the 128-byte swizzle with 32-byte units, the only MN-major layout for
-// 32-bit (tf32) operands.
+// UMMA shared-memory matrix descriptor with sm_100 version bits (layout types
+// as listed with the staging formats above).
 __device__ __forceinline__ uint64_t smem_desc(unsigned addr, unsigned lbo, unsigned sbo,
                                               unsigned layout) {
     uint64_t d = 0;
@@ -141,20 +156,22 @@ __device__ __forceinline__ void mma_commit(unsigned bar) {
                  : "memory");
 }
 
-// Staged operand geometry. K-major: rows of 128 bytes (BK elements), 16-byte
-// swizzle units over 8-row (1024-byte) groups; a k-step is 32 bytes along the
-// row. MN-major: strips of 128 bytes of MN (32 TF32 or 64 F16 elements) by BK
-// k-rows (BK * 128 bytes, strip stride = LBO); swizzle groups of 4 rows (TF32,
-// 32-byte units) or 8 rows (F16) are SBO apart; a k-step is KSTEP rows.
+// Staged operand geometry. K-major: rows of K_ROW bytes (BK elements),
+// swizzled over 8-row groups SBO apart; a k-step is 32 bytes along the row.
+// MN-major: strips of MN_ROW bytes of MN (STRIP_ELEMS elements) by BK k-rows
+// (BK * MN_ROW bytes, strip stride = LBO); swizzle groups of k-rows are SBO
+// apart; a k-step is KSTEP rows.
 template <class P, bool MN> struct OperandGeom {
-    static constexpr unsigned STRIP = P::BK * 128u;
-    static constexpr int STRIP_ELEMS = 128 / P::ESIZE;
+    static constexpr unsigned STRIP = P::BK * unsigned(P::MN_ROW);
+    static constexpr int STRIP_ELEMS = P::MN_ROW / P::ESIZE;
     static __device__ __forceinline__ unsigned kstep(int kk) {
-        return MN ? kk * unsigned(P::KSTEP) * 128u : kk * 32u;
+        return MN ? kk * unsigned(P::KSTEP) * unsigned(P::MN_ROW) : kk * 32u;
     }
     static __device__ __forceinline__ unsigned lbo() { return MN ? STRIP : 16u; }
-    static __device__ __forceinline__ unsigned sbo() { return MN ? P::MN_SBO : 1024u; }
-    static __device__ __forceinline__ unsigned layout() { return MN ? P::MN_LAYOUT : 2u; }
+    static __device__ __forceinline__ unsigned sbo() { return MN ? P::MN_SBO : P::K_SBO; }
+    static __device__ __forceinline__ unsigned layout() {
+        return MN ? P::MN_LAYOUT : P::K_LAYOUT;
+    }
     static __device__ __forceinline__ uint64_t desc(unsigned addr) {
         return smem_desc(addr, lbo(), sbo(), layout());
     }
@@ -377,8 +394,8 @@ static EncodeFn encode_fn() {
 }
 
 // 2-D map over a row-major [outer][inner] array with leading dimension ld
-// (elements), box {128 bytes of inner, box_outer}, zero fill outside the array;
-// 128-byte swizzle (MN-major TF32: with 32-byte units).
+// (elements), box {one staged row of inner, box_outer}, zero fill outside the
+// array; swizzle over that row (MN-major TF32: 128 bytes with 32-byte units).
 template <class P>
 static int make_map(CUtensorMap *map, const void *base, long long inner, long long outer,
                     long long ld, int box_outer, bool mn_major) {
@@ -389,12 +406,14 @@ static int make_map(CUtensorMap *map, const void *base, long long inner, long lo
     }
     cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
     cuuint64_t strides[1] = {cuuint64_t(ld) * P::ESIZE};
-    cuuint32_t box[2] = {cuuint32_t(128 / P::ESIZE), cuuint32_t(box_outer)};
+    const int row = mn_major ? P::MN_ROW : P::K_ROW;
+    cuuint32_t box[2] = {cuuint32_t(row / P::ESIZE), cuuint32_t(box_outer)};
     cuuint32_t estr[2] = {1u, 1u};
     const CUtensorMapDataType dt =
         P::ESIZE == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const CUtensorMapSwizzle sw = (mn_major && P::ESIZE == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
-                                                              : CU_TENSOR_MAP_SWIZZLE_128B;
+    const CUtensorMapSwizzle sw = row == 64                     ? CU_TENSOR_MAP_SWIZZLE_64B
+                                  : (mn_major && P::ESIZE == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                                : CU_TENSOR_MAP_SWIZZLE_128B;
     CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -474,7 +493,7 @@ static int gemm_x3(const char *name, int64_t M, int64_t N, int64_t K, const void
         return TCST_ERR_ARGUMENT;
     }
     constexpr int BN = 256;
-    constexpr int STAGES = 2;
+    constexpr int STAGES = P::STAGES;
     constexpr int BK = P::BK;
     CUtensorMap maps[4];
     int rc;
@@ -531,7 +550,14 @@ extern "C" int tcst_gemm_f16x3(int64_t M, int64_t N, int64_t K, const void *a_hi
         tcst_set_error("tcst_gemm_f16x3: NULL operand scale");
         return TCST_ERR_ARGUMENT;
     }
-    return gemm_x3<F16>("tcst_gemm_f16x3", M, N, K, a_hi_dev, a_lo_dev, lda, a_mn_major,
+    // Four 48 KB stages measured faster when both operands are K-major (Y =
+    // X W^T: 29.5 vs 31.6 us at 4096 x 1024 x 1024); with an MN-major operand
+    // two 96 KB stages are as fast or faster.
+    if (!a_mn_major && !b_mn_major)
+        return gemm_x3<F16>("tcst_gemm_f16x3", M, N, K, a_hi_dev, a_lo_dev, lda, a_mn_major,
+                            b_hi_dev, b_lo_dev, ldb, b_mn_major, c_dev, ldc, split_k,
+                            split_stride, a_scale_dev, b_scale_dev, status_dev, stream);
+    return gemm_x3<F16Wide>("tcst_gemm_f16x3", M, N, K, a_hi_dev, a_lo_dev, lda, a_mn_major,
                         b_hi_dev, b_lo_dev, ldb, b_mn_major, c_dev, ldc, split_k, split_stride,
                         a_scale_dev, b_scale_dev, status_dev, stream);
 }
