@@ -381,6 +381,7 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
     Table tv, long long *__restrict__ keys, int *__restrict__ routing,
     unsigned *__restrict__ status) {
     pdl_wait();
+    if (blockIdx.x == 0 && threadIdx.x == 0) *tv.sync = 0u; // the sort's ticket
     const long long atoms = tv.atoms;
     const int words = tv.words;
     const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -451,13 +452,13 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
 // Stable counting sort of the atoms by bin, in three launches:
 //   count:   sort block b counts the bins of its contiguous atom chunk into
 //            counts[b][bin];
-//   column:  one thread per bin turns its column into exclusive prefixes over
-//            the blocks (counts[b][bin] = atoms of that bin in blocks < b) and
-//            leaves the bin's total in counts[blocks][bin];
-//   scatter: every block scans the bin totals into bin starts (block 0 also
-//            stores them as the offsets), then walks its chunk in id order and
-//            places each atom after the earlier atoms of its bin (warp match +
-//            warp-ordered claims), so every bin lists its atoms in id order.
+//   column:  each bin's column becomes exclusive prefixes over the blocks
+//            (counts[b][bin] = atoms of that bin in blocks < b), its total goes
+//            to counts[blocks][bin], and the last CTA scans the totals into
+//            the bin starts (offsets);
+//   scatter: every block walks its chunk in id order and places each atom
+//            after the earlier atoms of its bin (warp match + warp-ordered
+//            claims), so every bin lists its atoms in id order.
 constexpr int SORT_THREADS = 512;
 
 // Per-block bin counters are 16-bit (a block holds at most 65,535 atoms), two
@@ -482,73 +483,101 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
         row[i] = int((hist[i >> 1] >> ((i & 1) * 16)) & 0xFFFFu);
 }
 
-__global__ void __launch_bounds__(64) bin_column_kernel(Table tv) {
-    pdl_wait();
-    const BinGeom &g = tv.geom;
-    const int bin = blockIdx.x * blockDim.x + threadIdx.x;
-    if (bin >= g.nbins) return;
-    int run = 0;
-    int *col = tv.counts + bin;
-    // Sixteen independent loads in flight, then their prefixes.
-    for (int b0 = 0; b0 < g.sort_blocks; b0 += 16) {
-        int v[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u)
-            v[u] = b0 + u < g.sort_blocks ? col[(long long)(b0 + u) * g.nbins] : 0;
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            if (b0 + u < g.sort_blocks) col[(long long)(b0 + u) * g.nbins] = run;
-            run += v[u];
-        }
-    }
-    col[(long long)g.sort_blocks * g.nbins] = run;
-}
+// Column prefix: counts[b][bin] becomes the number of atoms of `bin` in sort
+// blocks before b (counts[sort_blocks][bin] = the bin's total). A CTA takes 32
+// bins (lanes) and splits the sort blocks into COL_SEGS segments (warps): each
+// warp sums its segment, the segment offsets come from shared memory, then the
+// warp writes its running prefixes. The last CTA to finish (ticket in
+// tv.sync, which the decode reset) scans the totals into the bin starts
+// tv.offsets.
+constexpr int COL_SEGS = 8;
+constexpr int COL_RUN = 16; // segment lengths up to this stay in registers
 
-__global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
+__global__ void __launch_bounds__(COL_SEGS * 32) bin_column_kernel(Table tv) {
     pdl_wait();
-    extern __shared__ unsigned cursor[]; // 16-bit claims made so far, per bin
-    __shared__ int wsum[SORT_THREADS / 32];
+    __shared__ int seg_sum[COL_SEGS][32];
+    __shared__ int wsum[COL_SEGS];
+    __shared__ bool last;
     const BinGeom &g = tv.geom;
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    // Bin starts: exclusive scan of the totals, each thread over a contiguous run.
+    const int t = threadIdx.x, lane = t & 31, seg = t >> 5;
+    const int bin = blockIdx.x * 32 + lane;
+    const int per = (g.sort_blocks + COL_SEGS - 1) / COL_SEGS;
+    const int b_lo = min(seg * per, g.sort_blocks), b_hi = min(b_lo + per, g.sort_blocks);
+    const bool live = bin < g.nbins;
+    int *col = tv.counts + bin;
+    const long long stride = g.nbins;
+    int v[COL_RUN];
+    int sum = 0;
+    if (live && b_hi - b_lo <= COL_RUN) {
+#pragma unroll
+        for (int u = 0; u < COL_RUN; ++u) v[u] = b_lo + u < b_hi ? col[(b_lo + u) * stride] : 0;
+#pragma unroll
+        for (int u = 0; u < COL_RUN; ++u) sum += v[u];
+    } else if (live) {
+        for (int b = b_lo; b < b_hi; ++b) sum += col[b * stride];
+    }
+    seg_sum[seg][lane] = sum;
+    __syncthreads();
+    int run = 0;
+    for (int k = 0; k < seg; ++k) run += seg_sum[k][lane];
+    if (live) {
+        if (b_hi - b_lo <= COL_RUN) {
+#pragma unroll
+            for (int u = 0; u < COL_RUN; ++u)
+                if (b_lo + u < b_hi) {
+                    col[(b_lo + u) * stride] = run;
+                    run += v[u];
+                }
+        } else {
+            for (int b = b_lo; b < b_hi; ++b) {
+                const int c = col[b * stride];
+                col[b * stride] = run;
+                run += c;
+            }
+        }
+        if (seg == COL_SEGS - 1) col[g.sort_blocks * stride] = run;
+    }
+    // Last CTA: bin starts = exclusive scan of the totals.
+    __threadfence();
+    __syncthreads();
+    if (t == 0) last = atomicAdd(tv.sync, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // Totals of other CTAs are read from L2 (__ldcg), past any stale L1 line.
     const int *total = tv.counts + (long long)g.sort_blocks * g.nbins;
-    const int per = (g.nbins + SORT_THREADS - 1) / SORT_THREADS;
-    const int i0 = t * per;
+    const int n = g.nbins, nt = blockDim.x;
+    const int chunk = (n + nt - 1) / nt, i0 = t * chunk;
     int local = 0;
-    for (int k = 0; k < per; ++k)
-        if (i0 + k < g.nbins) local += total[i0 + k];
+    for (int k = 0; k < chunk; ++k)
+        if (i0 + k < n) local += __ldcg(total + i0 + k);
     int inc = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, inc, o);
         if (lane >= o) inc += y;
     }
-    if (lane == 31) wsum[warp] = inc;
+    if (lane == 31) wsum[seg] = inc;
     __syncthreads();
-    if (warp == 0) {
-        constexpr int NW = SORT_THREADS / 32;
-        const int w = lane < NW ? wsum[lane] : 0;
-        int winc = w;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, winc, o);
-            if (lane >= o) winc += y;
+    int base = inc - local;
+    for (int w = 0; w < seg; ++w) base += wsum[w];
+    for (int k = 0; k < chunk; ++k)
+        if (i0 + k < n) {
+            tv.offsets[i0 + k] = base;
+            base += __ldcg(total + i0 + k);
         }
-        if (lane < NW) wsum[lane] = winc - w;
-    }
-    __syncthreads();
-    int run = wsum[warp] + inc - local;
-    // This block's start in every bin replaces its column prefix in place.
-    int *mine = tv.counts + (long long)blockIdx.x * g.nbins;
-    for (int k = 0; k < per; ++k) {
-        const int i = i0 + k;
-        if (i < g.nbins) {
-            if (blockIdx.x == 0) tv.offsets[i] = run;
-            mine[i] += run;
-            run += total[i];
-        }
-    }
-    if (blockIdx.x == 0 && t == 0) tv.offsets[g.nbins] = int(tv.atoms);
+    if (t == 0) tv.offsets[n] = int(tv.atoms);
+}
+
+// Scatter: every sort block places its atoms at bin start + its column prefix
+// + the claims made so far in the block; warps claim one after another, so
+// ids stay in increasing order inside every bin.
+__global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
+    pdl_wait();
+    extern __shared__ unsigned cursor[]; // 16-bit claims made so far, per bin
+    const BinGeom &g = tv.geom;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int *mine = tv.counts + (long long)blockIdx.x * g.nbins;
     for (int i = t; i < (g.nbins + 1) >> 1; i += SORT_THREADS) cursor[i] = 0;
     __syncthreads();
     const long long a0 = blockIdx.x * g.chunk, a1 = min(tv.atoms, a0 + g.chunk);
@@ -559,9 +588,9 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
         const unsigned peers = __match_any_sync(0xffffffffu, bin);
         const int leader = __ffs(peers) - 1;
         const int rank = __popc(peers & ((1u << lane) - 1u));
-        const int bin_base = live ? mine[bin] : 0; // loaded before the ordered claims
+        // Loaded before the ordered claims.
+        const int bin_base = live ? tv.offsets[bin] + mine[bin] : 0;
         int start = 0;
-        // Warps claim their slots one after another, so earlier ids come first.
         for (int w = 0; w < SORT_THREADS / 32; ++w) {
             if (warp == w && live && lane == leader)
                 start = bin_base + int(half_add(cursor, bin, unsigned(__popc(peers))));
@@ -680,7 +709,7 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
         TCST_CUDA(launch_pdl(bin_count_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv));
         TCST_CUDA(cudaGetLastError());
     }
-    TCST_CUDA(launch_pdl(bin_column_kernel, dim3(unsigned((g.nbins + 63) / 64)), dim3(64), 0, st, tv));
+    TCST_CUDA(launch_pdl(bin_column_kernel, dim3(unsigned((g.nbins + 31) / 32)), dim3(COL_SEGS * 32), 0, st, tv));
     TCST_CUDA(cudaGetLastError());
     TCST_CUDA(launch_pdl(bin_scatter_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv));
     TCST_CUDA(cudaGetLastError());

@@ -153,6 +153,7 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
 //   offsets [nbins + 1] int, ids [atoms] int: atom ids grouped by bin, in
 //           increasing id order inside every bin (stable counting sort)
 //   counts  [sort_blocks + 1][nbins] int: sort workspace
+//   sync    one word (+ padding): finished blocks of the sort's column prefix
 //
 // Bins. An atom's class is the smallest c whose reach class_reach(c) covers
 // its larger footprint max(F_out, F_in). Classes 0..NFINE-1 (reach 16, 64, 128)
@@ -222,7 +223,8 @@ __host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in
 }
 
 struct TableLayout {
-    long long spans_off, sites_off, binof_off, offsets_off, ids_off, counts_off, total; // bytes
+    long long spans_off, sites_off, binof_off, offsets_off, ids_off, counts_off, sync_off,
+        total; // bytes
     BinGeom geom;
 };
 
@@ -236,7 +238,8 @@ __host__ __device__ inline TableLayout table_layout(long long atoms, int words, 
     t.offsets_off = align16(t.binof_off + atoms * 4);
     t.ids_off = align16(t.offsets_off + 4LL * (t.geom.nbins + 1));
     t.counts_off = align16(t.ids_off + atoms * 4);
-    t.total = align16(t.counts_off + 4LL * t.geom.nbins * (t.geom.sort_blocks + 1));
+    t.sync_off = align16(t.counts_off + 4LL * t.geom.nbins * (t.geom.sort_blocks + 1));
+    t.total = t.sync_off + 16;
     return t;
 }
 
@@ -248,6 +251,7 @@ struct Table {
     const int4 *spans;
     const float *sites;
     int *bin_of, *offsets, *ids, *counts;
+    unsigned *sync; // blocks of the column prefix that finished (reset by the decode)
     BinGeom geom;
 };
 
@@ -265,6 +269,7 @@ __host__ __device__ inline Table table_view(const void *base, long long atoms, i
     t.offsets = reinterpret_cast<int *>(b + l.offsets_off);
     t.ids = reinterpret_cast<int *>(b + l.ids_off);
     t.counts = reinterpret_cast<int *>(b + l.counts_off);
+    t.sync = reinterpret_cast<unsigned *>(b + l.sync_off);
     t.geom = l.geom;
     return t;
 }
@@ -326,7 +331,10 @@ template <int M> struct AxisCoef {
         return acc;
     }
     __device__ __forceinline__ SiteVals values(int j) const {
-        const float t = phase0 + 2.0f * float(j) / float(F);
+        return values_at(phase0 + 2.0f * float(j) / float(F));
+    }
+    // Values at half-turn phase t.
+    __device__ __forceinline__ SiteVals values_at(float t) const {
         float s1, c1;
         sincospif(t, &s1, &c1);
         float m = c[0], dR = dc[0], dmu = 0.0f;

@@ -14,8 +14,9 @@
 // axes, split-K partials summed while loading), then
 //   class 0 (footprints <= 16):  one thread per atom, site values from the
 //                                 table's site buffer;
-//   classes 1, 2 (<= 64, <= 128): one warp per atom, lanes over input sites,
-//                                 output-site values in per-warp shared memory.
+//   classes 1, 2 (<= 64, <= 128): one CTA per bin, one warp per atom, lanes
+//                                 over input sites, output-site values in
+//                                 per-warp shared memory.
 // Coarser classes (and every atom of an unbinned geometry): one CTA per atom
 // walks the footprint in chunks, G from global memory. Every atom is reduced by
 // one thread, one warp (fixed xor tree) or one CTA (fixed tree), so the
@@ -267,48 +268,38 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     }
 }
 
-// Classes 1 and 2: one CTA per 2 x 2 block of first-site tiles, one warp per atom.
+// Classes 1 and 2: one CTA per bin (first-site tile). The CTA stages the
+// bounding box of its atoms' footprints inside the (TS + RC - 1)-square G
+// window, then each warp takes one atom at a time: output-site values
+// (m, dm/dmu, dm/dR) go to the warp's shared rows, lanes own input sites, and
+// each lane accumulates the three row contractions of its columns before the
+// fixed xor tree. Site phases use a per-atom step 2/F (within an ulp of the
+// forward's phase; the gradient tolerance is far wider).
 template <int RC>
 __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     Table tv, int cls, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, float4 *__restrict__ grad) {
     pdl_wait();
-    constexpr int W = 2 * TS + RC - 1;
+    constexpr int W = TS + RC - 1;
     constexpr int PITCH = W + 1;
     constexpr int Q = RC / 32;
     extern __shared__ __align__(16) float sm[];
     float *gw = sm;
     const BinGeom &geo = tv.geom;
-    const int nr = geo.tr[cls], nc = geo.tc[cls];
-    const int rc2 = (nc + 1) / 2;
-    const int ir = blockIdx.x / rc2, ic = blockIdx.x - ir * rc2;
-    int rb[4], re[4], total = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const int tr = 2 * ir + (q >> 1), tc = 2 * ic + (q & 1);
-        rb[q] = re[q] = 0;
-        if (tr < nr && tc < nc) {
-            const int bin = geo.base[cls] + tr * nc + tc;
-            rb[q] = tv.offsets[bin];
-            re[q] = tv.offsets[bin + 1];
-        }
-        total += re[q] - rb[q];
-    }
-    if (total == 0) return;
-    const int R0 = 2 * ir * TS, C0 = 2 * ic * TS;
-    // Stage only the bounding box of the region's footprints.
+    const int nc = geo.tc[cls];
+    const int tr = blockIdx.x / nc, tc = blockIdx.x - tr * nc;
+    const int bin = geo.base[cls] + blockIdx.x;
+    const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
+    if (begin == end) return;
+    const int R0 = tr * TS, C0 = tc * TS;
+    // Stage only the bounding box of the bin's footprints.
     __shared__ int box[4]; // row lo, row hi, col lo, col hi (window coordinates)
     if (threadIdx.x == 0) box[0] = box[2] = W, box[1] = box[3] = 0;
     __syncthreads();
     {
         int rlo = W, rhi = 0, clo = W, chi = 0;
-        for (int item = threadIdx.x; item < total; item += blockDim.x) {
-            int k = item, q = 0;
-            while (k >= re[q] - rb[q]) {
-                k -= re[q] - rb[q];
-                ++q;
-            }
-            const int4 sp = tv.spans[tv.ids[rb[q] + k]];
+        for (int k = begin + threadIdx.x; k < end; k += blockDim.x) {
+            const int4 sp = tv.spans[tv.ids[k]];
             rlo = min(rlo, sp.x - R0);
             rhi = max(rhi, sp.x - R0 + sp.y);
             clo = min(clo, sp.z - C0);
@@ -331,21 +322,19 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float4 *rowv = reinterpret_cast<float4 *>(sm + W * PITCH) + warp * RC; // (m, dm/dmu, dm/dR, 0)
     const int aw = axis_words(8);
-    for (int item = warp; item < total; item += PC_WARPS) {
-        int k = item, q = 0;
-        while (k >= re[q] - rb[q]) {
-            k -= re[q] - rb[q];
-            ++q;
-        }
-        const long long a = tv.ids[rb[q] + k];
+    long long a_next = begin + warp < end ? tv.ids[begin + warp] : 0;
+    for (int k = begin + warp; k < end; k += PC_WARPS) {
+        const long long a = a_next;
+        if (k + PC_WARPS < end) a_next = tv.ids[k + PC_WARPS];
         const int4 span = tv.spans[a];
         const float *rec = tv.rec + a * (long long)tv.words;
         const int fo = span.y, fi = span.w;
         {
             AxisCoef<8> ao;
             ao.load(rec + 4);
+            const float step = 2.0f / float(fo);
             for (int r = lane; r < fo; r += 32) {
-                const SiteVals v = ao.values(r);
+                const SiteVals v = ao.values_at(fmaf(float(r), step, ao.phase0));
                 rowv[r] = make_float4(v.m, v.dmu, v.dR, 0.f);
             }
         }
@@ -354,6 +343,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
         {
             AxisCoef<8> ai;
             ai.load(rec + 4 + aw);
+            const float step = 2.0f / float(max(fi, 1));
 #pragma unroll
             for (int j = 0; j < Q; ++j) {
                 // Lanes past the footprint re-read the footprint's last (staged)
@@ -362,7 +352,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
                 mi[j] = dmi[j] = dri[j] = 0.f;
                 cl[j] = span.z - C0 + min(c, max(fi, 1) - 1);
                 if (c < fi) {
-                    const SiteVals v = ai.values(c);
+                    const SiteVals v = ai.values_at(fmaf(float(c), step, ai.phase0));
                     mi[j] = v.m;
                     dmi[j] = v.dmu;
                     dri[j] = v.dR;
@@ -374,8 +364,8 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
 #pragma unroll
         for (int j = 0; j < Q; ++j) h0[j] = h1[j] = h2[j] = 0.f;
         const float *g0 = gw + (span.x - R0) * PITCH;
-#pragma unroll 4
         const int nq = (fi + 31) >> 5; // column slots in use (warp-uniform)
+#pragma unroll 4
         for (int r = 0; r < fo; ++r) {
             const float4 rv = rowv[r];
             const float *grow = g0 + r * PITCH;
@@ -408,9 +398,8 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
         __syncwarp();
     }
 }
-
 template <int RC> constexpr size_t class_smem() {
-    return size_t(2 * TS + RC - 1) * (2 * TS + RC) * 4 + size_t(PC_WARPS) * RC * 16;
+    return size_t(TS + RC - 1) * (TS + RC) * 4 + size_t(PC_WARPS) * RC * 16;
 }
 
 // Coarse classes: one CTA per atom. The footprint is walked in chunks of
@@ -580,14 +569,14 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
             tv, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
         TCST_CUDA(cudaGetLastError());
         if (geo.nclass > 1) {
-            const unsigned regions = unsigned(((geo.tr[1] + 1) / 2) * ((geo.tc[1] + 1) / 2));
-            TCST_CUDA(launch_pdl(pullback_class_kernel<64>, dim3(regions), dim3(PC_THREADS), class_smem<64>(), st, 
+            const unsigned bins = unsigned(geo.tr[1] * geo.tc[1]);
+            TCST_CUDA(launch_pdl(pullback_class_kernel<64>, dim3(bins), dim3(PC_THREADS), class_smem<64>(), st, 
                 tv, 1, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
             TCST_CUDA(cudaGetLastError());
         }
         if (geo.nclass > 2) {
-            const unsigned regions = unsigned(((geo.tr[2] + 1) / 2) * ((geo.tc[2] + 1) / 2));
-            TCST_CUDA(launch_pdl(pullback_class_kernel<128>, dim3(regions), dim3(PC_THREADS), class_smem<128>(), st, 
+            const unsigned bins = unsigned(geo.tr[2] * geo.tc[2]);
+            TCST_CUDA(launch_pdl(pullback_class_kernel<128>, dim3(bins), dim3(PC_THREADS), class_smem<128>(), st, 
                 tv, 2, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
             TCST_CUDA(cudaGetLastError());
         }
