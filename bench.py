@@ -230,11 +230,16 @@ EXTRA = {
                                "32768 atoms each, rational radius radius_max=1024 q=0.25, "
                                "xavier_normal_ gain 1, MSE, CSTAdamW lr 1e-3",
                    "global_batch": 8192, "atoms": 65536}},
+    5: {"metric": "train steps/s (fwd+bwd+CSTAdamW), wide layer 8192->8192, 32N atoms",
+        "config": {"workload": "config5: CSTLinear 8192->8192, 262144 atoms, rational radius "
+                               "radius_max=4096, He init (q=0) then q ~ U[0,1] per atom (the "
+                               "variance target no longer holds), MSE, CSTAdamW lr 1e-3",
+                   "global_batch": 16384, "atoms": 262144}},
 }
 
 
 def run_extra_config(args):
-    """Configs 3 and 4 through the drop-in autograd API (layer(s), torch loss,
+    """Configs 3, 4 and 5 through the drop-in autograd API (layer(s), torch loss,
     CSTAdamW), timed over exactly --steps steps with CUDA events; e2e adds the
     pinned host-to-device copy of each step's inputs and the loss read-back."""
     import torch
@@ -245,7 +250,7 @@ def run_extra_config(args):
 
     world, rank, local = dist_info()
     if world > 1:
-        raise SystemExit("configs 3 and 4 run on one GPU")
+        raise SystemExit("configs 3, 4 and 5 run on one GPU")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     torch.manual_seed(0)
@@ -270,6 +275,23 @@ def run_extra_config(args):
                                                          generator=gen)
 
         loss_fn = F.cross_entropy
+    elif args.config == 5:
+        from torchcst_b200.init import kaiming_normal_
+        kernel = kernels.product(kernels.cell_mass(cheb), coordinates=kernels.rational_radius(
+            radius_max=4096.0, radius_fraction=0.0))
+        layer = CSTLinear(charts=(grid(8192), grid(8192)), atoms=262144, kernel=kernel,
+                          device=dev, validate="off")
+        kaiming_normal_(layer, nonlinearity="relu", q=0.0)
+        with torch.no_grad():
+            layer.atoms.p[:, 1].uniform_(0.0, 1.0, generator=gen)
+        model = layer
+        rows = 16384
+
+        def batch():
+            return (torch.randn(rows, 8192, device=dev, generator=gen),
+                    torch.randn(rows, 8192, device=dev, generator=gen))
+
+        loss_fn = F.mse_loss
     else:
         kernel = kernels.product(kernels.cell_mass(cheb), coordinates=kernels.rational_radius(
             radius_max=1024.0, radius_fraction=0.25))
@@ -348,8 +370,8 @@ def main():
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="print per-launch CUDA-event times of one step to stderr")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
-                    help="2: the headline config (default); 3, 4: the other named shapes on one "
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
+                    help="2: the headline config (default); 3, 4, 5: the other named shapes on one "
                          "GPU through the drop-in API")
     args = ap.parse_args()
     if args.config != 2 and args.impl != "reference":

@@ -193,6 +193,20 @@ int tcst_gemm_f16x3(int64_t M, int64_t N, int64_t K, const void *a_hi_dev, const
                     int32_t b_mn_major, const float *b_scale_dev, float *c_dev, int64_t ldc,
                     int32_t split_k, int64_t split_stride, uint32_t *status_dev, void *stream);
 
+/* Y = X W^T as tcst_gemm_f16x3 with both operands K-major and no split,
+ * followed in the epilogue by the MSE gradient of a training step (the
+ * driver-side loss of the reference's examples): writes dY = (Y - T) * scale
+ * to dy_dev (Y itself is not stored), one double sum of (Y - T)^2 per 32 output
+ * rows of a 128 x 256 tile to loss_partial_dev (*partials of them, fixed
+ * order), and folds max |dY| into *amax_dev (nullable) for the f16 split of
+ * dY. K must be positive. */
+int tcst_gemm_f16x3_mse(int64_t M, int64_t N, int64_t K, const void *a_hi_dev,
+                        const void *a_lo_dev, int64_t lda, const float *a_scale_dev,
+                        const void *b_hi_dev, const void *b_lo_dev, int64_t ldb,
+                        const float *b_scale_dev, const float *target_dev, int64_t ld_target,
+                        float scale, float *dy_dev, int64_t ld_dy, double *loss_partial_dev,
+                        int32_t *partials, float *amax_dev, uint32_t *status_dev, void *stream);
+
 /* *amax_dev = max(*amax_dev, max |x|) over a [rows][cols] float32 view (start
  * it at 0). */
 int tcst_absmax(const float *x_dev, int64_t rows, int64_t cols, int64_t ld, float *amax_dev,

@@ -109,6 +109,45 @@ def test_gemm_f16x3(R, a_mn, b_mn, shape, split, scales):
     assert err < 1e-5, err
 
 
+@pytest.mark.parametrize("shape", [(4096, 1024, 1024), (130, 300, 70), (256, 512, 256)])
+def test_gemm_f16x3_mse_epilogue(R, shape):
+    """Forward GEMM with the MSE epilogue: dY = (X W^T - T) * scale, the loss
+    partials sum to sum (X W^T - T)^2, and max |dY| is the max of what it wrote."""
+    from torchcst_b200 import _native as N
+    import ctypes
+    M, Nn, K = shape
+    g = torch.Generator().manual_seed(M + Nn + K)
+    X = torch.randn(M, K, generator=g)
+    W = torch.randn(Nn, K, generator=g) * 0.05
+    T = torch.randn(M, Nn, generator=g)
+    scale = 2.0 / (M * Nn)
+    ref = X.double() @ W.double().T - T.double()
+    x16 = R.F16Split(M, K, "cuda").fill(X.cuda())
+    w16 = R.F16Split(Nn, K, "cuda").fill(W.cuda())
+    Td = T.cuda()
+    dy = torch.full((M, Nn), float("nan"), device="cuda")
+    tiles = -(-Nn // 256) * -(-M // 128)
+    partial = torch.full((4 * tiles,), float("nan"), dtype=torch.float64, device="cuda")
+    amax = torch.zeros(1, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    count = ctypes.c_int32(0)
+    vp = R._vp
+    N.call("tcst_gemm_f16x3_mse", M, Nn, K, vp(x16.hi), vp(x16.lo), x16.ld, vp(x16.scale),
+           vp(w16.hi), vp(w16.lo), w16.ld, vp(w16.scale), vp(Td), Nn, ctypes.c_float(scale),
+           vp(dy), Nn, vp(partial), ctypes.byref(count), vp(amax), vp(status),
+           R._stream(torch.device("cuda")))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert count.value == 4 * tiles
+    out = dy.double().cpu()
+    err = float((out - ref * scale).abs().max() / (ref.abs().max() * scale))
+    assert err < 1e-5, err
+    loss = float(partial.sum())
+    want = float((ref ** 2).sum())
+    assert abs(loss - want) <= 1e-5 * want, (loss, want)
+    assert float(amax.item()) == float(dy.abs().max())
+
+
 def test_f16_split_scale_and_exactness(R):
     """s is a power of two putting max |s x| in [2^14, 2^15); hi + lo keeps
     22 significant bits of s x."""
@@ -216,7 +255,22 @@ def _bin_geom(out_axis, in_axis):
             break
     if out_axis.modes != 8 or in_axis.modes != 8 or nb + 1 > 98304:
         return dict(nclass=0, nbins=2)
-    return dict(nclass=c, tr=tr, tc=tc, base=base, nbins=nb + 1)
+    # Owner-pair level-banks: shared hierarchy, K T > 128, at most 16384 pairs.
+    pairs = {}
+    if (out_axis.base_tile_sites == in_axis.base_tile_sites
+            and out_axis.merge_factor == in_axis.merge_factor
+            and out_axis.spacing == in_axis.spacing and out_axis.merge_factor > 1):
+        t, level = out_axis.base_tile_sites, 0
+        while t <= no and t <= ni:
+            for k in (2, 3):
+                npair = (no // t) * (ni // t)
+                if k * t <= 128 or npair > 16384 or no % t or ni % t or nb + npair + 1 > 98304:
+                    continue
+                pairs[(level, k)] = dict(T=t, ni=ni // t, base=nb)
+                nb += npair
+            t *= out_axis.merge_factor
+            level += 1
+    return dict(nclass=c, tr=tr, tc=tc, base=base, nbins=nb + 1, pairs=pairs)
 
 
 def _table_sections(out_axis, in_axis, atoms):
@@ -266,6 +320,13 @@ def test_bins_are_stable_and_complete(R, name):
         base = np.asarray(geo["base"])[cls]
         tcs = np.asarray(geo["tc"])[cls]
         want = base + (spans[:, 0] // e) * tcs + spans[:, 2] // e
+        # Coarse atoms with the same level and bank on both axes: owner-pair bins.
+        lo, li = d["route_out_level"], d["route_in_level"]
+        ko, ki = d["route_out_count"], d["route_in_count"]
+        for j in np.nonzero((cls >= 3) & (lo == li) & (ko == ki))[0]:
+            pl = geo["pairs"].get((int(lo[j]), int(ko[j])))
+            if pl is not None:
+                want[j] = pl["base"] + (spans[j, 0] // pl["T"]) * pl["ni"] + spans[j, 2] // pl["T"]
     else:
         want = np.zeros(A, np.int64)
     want = np.where(f > 0, want, nb - 1)

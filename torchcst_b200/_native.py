@@ -98,6 +98,9 @@ SIGNATURES = {
                                         P, I64, I32, I64, P, P]),
     "tcst_gemm_f16x3": (ctypes.c_int, [I64, I64, I64, P, P, I64, I32, P, P, P, I64, I32, P, P,
                                        I64, I32, I64, P, P]),
+    "tcst_gemm_f16x3_mse": (ctypes.c_int, [I64, I64, I64, P, P, I64, P, P, P, I64, P, P, I64,
+                                           ctypes.c_float, P, I64, P, ctypes.POINTER(I32), P,
+                                           P, P]),
     "tcst_assemble_weight_f16": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis),
                                                 P, I64, P, I64, P, P, P, I64, P, P]),
     "tcst_absmax": (ctypes.c_int, [P, I64, I64, I64, P, P]),

@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libtcst_b200.so")
-SOURCES = ["atoms.cu", "weight.cu", "gemm_tf32x3.cu", "pullback.cu", "optim.cu"]
+SOURCES = ["atoms.cu", "weight.cu", "pairs.cu", "gemm_tf32x3.cu", "pullback.cu", "optim.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
     float *blk = rec + 4 + (side ? axis_words(out_ax.modes) : 0);
     int4 *spans = const_cast<int4 *>(tv.spans);
     float *sites = const_cast<float *>(tv.sites) + a * SITE_FLOATS + side * 3 * REACH;
-    int node = 0, wrapped = 0, foot = 0;
+    int node = 0, wrapped = 0, foot = 0, lvl = -1, kk = 0;
     if (live && d.bad) {
         if (side == 0) {
             atomicOr(status, d.bad);
@@ -419,6 +419,8 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
             wrapped = int(wr < 0 ? wr + ax.sites : wr);
             foot = r.count * r.tile;
         }
+        lvl = r.level;
+        kk = r.count;
         const int tc = ax.sites / r.tile;
         int m = r.first_tile % tc;
         m += m < 0 ? tc : 0;
@@ -441,11 +443,13 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
     const int other = __shfl_xor_sync(0xffffffffu, node, 1);
     const int other_wrapped = __shfl_xor_sync(0xffffffffu, wrapped, 1);
     const int other_foot = __shfl_xor_sync(0xffffffffu, foot, 1);
+    const int other_lvl = __shfl_xor_sync(0xffffffffu, lvl, 1);
+    const int other_k = __shfl_xor_sync(0xffffffffu, kk, 1);
     if (live && !d.bad && side == 0) {
         if (keys) keys[a] = (long long)node * in_ax.node_count + other;
         const int4 span = make_int4(wrapped, foot, other_wrapped, other_foot);
         spans[a] = span;
-        tv.bin_of[a] = atom_bin(span, tv.geom);
+        tv.bin_of[a] = atom_bin(span, tv.geom, lvl, kk, other_lvl, other_k);
     }
 }
 
@@ -544,13 +548,21 @@ __global__ void __launch_bounds__(COL_SEGS * 32) bin_column_kernel(Table tv) {
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // Totals of other CTAs are read from L2 (__ldcg), past any stale L1 line.
+    // Totals of other CTAs are read from L2 (__ldcg), past any stale L1 line,
+    // COL_RUN at a time so their latencies overlap.
     const int *total = tv.counts + (long long)g.sort_blocks * g.nbins;
     const int n = g.nbins, nt = blockDim.x;
     const int chunk = (n + nt - 1) / nt, i0 = t * chunk;
     int local = 0;
-    for (int k = 0; k < chunk; ++k)
-        if (i0 + k < n) local += __ldcg(total + i0 + k);
+    for (int k0 = 0; k0 < chunk; k0 += COL_RUN) {
+#pragma unroll
+        for (int u = 0; u < COL_RUN; ++u) {
+            const int i = i0 + k0 + u;
+            v[u] = k0 + u < chunk && i < n ? __ldcg(total + i) : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < COL_RUN; ++u) local += v[u];
+    }
     int inc = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -561,11 +573,21 @@ __global__ void __launch_bounds__(COL_SEGS * 32) bin_column_kernel(Table tv) {
     __syncthreads();
     int base = inc - local;
     for (int w = 0; w < seg; ++w) base += wsum[w];
-    for (int k = 0; k < chunk; ++k)
-        if (i0 + k < n) {
-            tv.offsets[i0 + k] = base;
-            base += __ldcg(total + i0 + k);
+    for (int k0 = 0; k0 < chunk; k0 += COL_RUN) {
+#pragma unroll
+        for (int u = 0; u < COL_RUN; ++u) {
+            const int i = i0 + k0 + u;
+            v[u] = k0 + u < chunk && i < n ? __ldcg(total + i) : 0;
         }
+#pragma unroll
+        for (int u = 0; u < COL_RUN; ++u) {
+            const int i = i0 + k0 + u;
+            if (k0 + u < chunk && i < n) {
+                tv.offsets[i] = base;
+                base += v[u];
+            }
+        }
+    }
     if (t == 0) tv.offsets[n] = int(tv.atoms);
 }
 
@@ -643,10 +665,10 @@ using namespace tcst;
 extern "C" int64_t tcst_atom_table_bytes(int64_t atoms, const tcst_axis *out_axis,
                                          const tcst_axis *in_axis) {
     if (atoms < 0 || !out_axis || !in_axis) return -1;
-    // Records, spans, site values, bins and the sort workspace (common.cuh).
+    // Records, spans, site values, bins, the sort workspace and the owner-pair
+    // region (common.cuh).
     return table_layout(atoms, record_words(out_axis->modes, in_axis->modes),
-                        out_axis->site_count, in_axis->site_count, out_axis->modes,
-                        in_axis->modes)
+                        axis_geo(*out_axis), axis_geo(*in_axis))
         .total;
 }
 
@@ -681,7 +703,7 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
         return TCST_ERR_UNSUPPORTED;
     }
     const int words = record_words(oa.modes, ia.modes);
-    const Table tv = table_view(atom_table_dev, atoms, words, oa.sites, ia.sites, oa.modes, ia.modes);
+    const Table tv = table_view(atom_table_dev, atoms, words, axis_geo(oa), axis_geo(ia));
     const BinGeom &g = tv.geom;
     cudaStream_t st = (cudaStream_t)stream;
     const size_t hist_bytes = size_t((g.nbins + 1) >> 1) * 4;

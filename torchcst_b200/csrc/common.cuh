@@ -163,6 +163,19 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
 // class by class, tiles row-major, and invalid atoms take the last bin. When
 // the geometry is not binned (mode counts other than 8, or more bins than the
 // sort handles) every valid atom is in class-free bin 0.
+//
+// Owner pairs. When both axes share the tile hierarchy (base, merge, spacing),
+// a coarse atom whose level and bank (tile T, count K) agree on both axes is
+// binned by its owner pair (T, K, first tile out, first tile in) instead: one
+// "pair level-bank" per (T, K) with K T > 128 and at most PAIR_BIN_CAP pairs,
+// pair bins numbered after the class bins. All atoms of a pair share the
+// footprint, so with the 2M+1 = PF functions phi_f(j) = {1, cos 2 pi k j/F,
+// sin 2 pi k j/F} of the footprint site j, m_a(j) = sum_f alpha_a,f phi_f(j)
+// and the pair's W block is Phi_out C Phi_in^T with
+// C = sum_a amp_a alpha_out,a alpha_in,a^T (PF x PF). A pair with at least
+// PAIR_MIN atoms in a level-bank that has an expansion buffer ("active") takes
+// that path in the weight assembly and the pullback; the atoms of other pairs
+// are treated one by one like any coarse atom.
 // ---------------------------------------------------------------------------
 constexpr int REACH = 16;
 constexpr int SITE_FLOATS = 2 * 3 * REACH;
@@ -172,6 +185,17 @@ constexpr int MAX_CLASSES = 16;
 constexpr int MAX_BINS = 98304;  // 16-bit per-CTA bin counters fit in shared memory
 constexpr int SORT_CHUNK = 512;  // atoms per sort block (128 blocks, more for > 8M atoms)
 constexpr int CACHE_SITES = 128; // masses cached per axis for classes 1..NFINE-1
+constexpr int PF = 17;                // owner-pair basis functions per axis (M = 8)
+constexpr int MAX_PAIR_LB = 32;       // pair level-banks
+constexpr int PAIR_MIN = 4;           // atoms that make an owner pair active
+constexpr int PAIR_BIN_CAP = 16384;   // owner pairs of a level-bank binned as pairs
+constexpr int PAIR_EXPAND_CAP = 4096; // owner pairs of a level-bank with an expansion buffer
+
+// What the bin geometry needs of an axis.
+struct AxisGeo {
+    int sites, base, merge, modes;
+    double spacing;
+};
 
 __host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : 64 << (c - 1); }
 __host__ __device__ constexpr int class_edge(int c) { return c < NFINE ? TS : class_reach(c) / 2; }
@@ -182,14 +206,26 @@ struct BinGeom {
     int nclass;                   // 0 when not binned
     int tr[MAX_CLASSES], tc[MAX_CLASSES]; // tiles per axis of each class
     int base[MAX_CLASSES + 1];    // first bin of each class; base[nclass] = first bin past them
-    int nbins;                    // base[nclass] + 1 (invalid bin)
+    int nbins;                    // last pair bin + 2 (invalid bin)
     int sort_blocks;              // counting-sort blocks
     long long chunk;              // atoms per sort block
+    // Owner-pair level-banks (npl = 0 without a shared hierarchy).
+    int npl;
+    int pl_T[MAX_PAIR_LB], pl_K[MAX_PAIR_LB];   // tile and count
+    int pl_no[MAX_PAIR_LB], pl_ni[MAX_PAIR_LB]; // first tiles per axis (N / T)
+    int pl_base[MAX_PAIR_LB + 1];               // first bin; pl_base[npl] = invalid bin
+    int pl_exp[MAX_PAIR_LB];                    // has an expansion buffer
+    int pl_node[MAX_PAIR_LB];                   // first node flag of the level-bank
+    long long pl_buf[MAX_PAIR_LB];              // float offset of its [no][PF][N_in] buffer
+    int pl_of[2 * MAX_LEVELS];                  // level * 2 + K - 2 -> level-bank or -1
+    int nodes;                                  // node flags
+    long long buf_floats;                       // expansion buffer floats
 };
 
-__host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in, int modes_out,
-                                            int modes_in) {
+__host__ __device__ inline BinGeom bin_geom(long long atoms, const AxisGeo &ao,
+                                            const AxisGeo &ai) {
     BinGeom g;
+    const int n_out = ao.sites, n_in = ai.sites, modes_out = ao.modes, modes_in = ai.modes;
     const int nmax = n_out > n_in ? n_out : n_in;
     int nc = 0;
     long long nb = 0;
@@ -202,13 +238,51 @@ __host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in
         ++nc;
         if (class_reach(nc - 1) >= 2 * nmax) break;
     }
-    if (modes_out != 8 || modes_in != 8 || nb + 1 > MAX_BINS || class_reach(nc - 1) < 2 * nmax) {
+    const long long class_end = nb;
+    g.npl = 0;
+    g.nodes = 0;
+    g.buf_floats = 0;
+    for (int i = 0; i < 2 * MAX_LEVELS; ++i) g.pl_of[i] = -1;
+    const bool binned =
+        modes_out == 8 && modes_in == 8 && nb + 1 <= MAX_BINS && class_reach(nc - 1) >= 2 * nmax;
+    if (binned && ao.base == ai.base && ao.merge == ai.merge && ao.spacing == ai.spacing &&
+        ao.merge > 1 && ao.base > 0) {
+        long long t = ao.base;
+        for (int level = 0; level < MAX_LEVELS && t <= n_out && t <= n_in; ++level) {
+            for (int k = 2; k <= 3 && g.npl < MAX_PAIR_LB; ++k) {
+                const long long no = n_out / t, ni = n_in / t;
+                if (k * t <= class_reach(NFINE - 1) || no * ni > PAIR_BIN_CAP ||
+                    n_out % t || n_in % t || nb + no * ni + 1 > MAX_BINS)
+                    continue;
+                const int l = g.npl++;
+                g.pl_T[l] = int(t);
+                g.pl_K[l] = k;
+                g.pl_no[l] = int(no);
+                g.pl_ni[l] = int(ni);
+                g.pl_base[l] = int(nb);
+                g.pl_exp[l] = no * ni <= PAIR_EXPAND_CAP;
+                g.pl_node[l] = g.nodes;
+                g.pl_buf[l] = g.buf_floats;
+                if (g.pl_exp[l]) {
+                    g.nodes += int(no);
+                    g.buf_floats += no * PF * n_in;
+                }
+                g.pl_of[2 * level + k - 2] = l;
+                nb += no * ni;
+            }
+            t *= ao.merge;
+        }
+    }
+    g.pl_base[g.npl] = int(nb);
+    if (!binned) {
         g.nclass = 0;
+        g.npl = 0;
+        g.pl_base[0] = 1;
         g.base[0] = 0;
         g.nbins = 2; // bin 0: every valid atom; bin 1: invalid atoms
     } else {
         g.nclass = nc;
-        g.base[nc] = int(nb);
+        g.base[nc] = int(class_end);
         g.nbins = int(nb) + 1;
     }
     // At most 128 blocks, but never more than 65,535 atoms per block (16-bit counters).
@@ -224,14 +298,14 @@ __host__ __device__ inline BinGeom bin_geom(long long atoms, int n_out, int n_in
 
 struct TableLayout {
     long long spans_off, sites_off, binof_off, offsets_off, ids_off, counts_off, sync_off,
-        total; // bytes
+        pair_c_off, node_off, buf_off, total; // bytes
     BinGeom geom;
 };
 
-__host__ __device__ inline TableLayout table_layout(long long atoms, int words, int n_out,
-                                                   int n_in, int modes_out, int modes_in) {
+__host__ __device__ inline TableLayout table_layout(long long atoms, int words, const AxisGeo &ao,
+                                                   const AxisGeo &ai) {
     TableLayout t;
-    t.geom = bin_geom(atoms, n_out, n_in, modes_out, modes_in);
+    t.geom = bin_geom(atoms, ao, ai);
     t.spans_off = align16(atoms * words * 4);
     t.sites_off = align16(t.spans_off + atoms * 16);
     t.binof_off = align16(t.sites_off + atoms * SITE_FLOATS * 4);
@@ -239,7 +313,12 @@ __host__ __device__ inline TableLayout table_layout(long long atoms, int words, 
     t.ids_off = align16(t.offsets_off + 4LL * (t.geom.nbins + 1));
     t.counts_off = align16(t.ids_off + atoms * 4);
     t.sync_off = align16(t.counts_off + 4LL * t.geom.nbins * (t.geom.sort_blocks + 1));
-    t.total = t.sync_off + 16;
+    // Owner-pair region: C per pair bin, node flags, expansion buffers.
+    const long long pair_bins = t.geom.npl ? t.geom.pl_base[t.geom.npl] - t.geom.pl_base[0] : 0;
+    t.pair_c_off = t.sync_off + 16;
+    t.node_off = align16(t.pair_c_off + 4LL * PF * PF * pair_bins);
+    t.buf_off = align16(t.node_off + 4LL * t.geom.nodes);
+    t.total = align16(t.buf_off + 4LL * t.geom.buf_floats);
     return t;
 }
 
@@ -252,12 +331,16 @@ struct Table {
     const float *sites;
     int *bin_of, *offsets, *ids, *counts;
     unsigned *sync; // blocks of the column prefix that finished (reset by the decode)
+    float *pair_c;  // [pair bins][PF][PF]: C of active pairs
+    int *node_on;   // [nodes]: output node has an active pair (expansion level-banks)
+    float *pair_buf; // expansion buffers: R = C Phi_in^T summed per output node, then
+                     // the pullback's projections P = Phi_out^T G
     BinGeom geom;
 };
 
 __host__ __device__ inline Table table_view(const void *base, long long atoms, int words,
-                                            int n_out, int n_in, int modes_out, int modes_in) {
-    const TableLayout l = table_layout(atoms, words, n_out, n_in, modes_out, modes_in);
+                                            const AxisGeo &ao, const AxisGeo &ai) {
+    const TableLayout l = table_layout(atoms, words, ao, ai);
     char *b = static_cast<char *>(const_cast<void *>(base));
     Table t;
     t.rec = reinterpret_cast<const float *>(b);
@@ -270,8 +353,25 @@ __host__ __device__ inline Table table_view(const void *base, long long atoms, i
     t.ids = reinterpret_cast<int *>(b + l.ids_off);
     t.counts = reinterpret_cast<int *>(b + l.counts_off);
     t.sync = reinterpret_cast<unsigned *>(b + l.sync_off);
+    t.pair_c = reinterpret_cast<float *>(b + l.pair_c_off);
+    t.node_on = reinterpret_cast<int *>(b + l.node_off);
+    t.pair_buf = reinterpret_cast<float *>(b + l.buf_off);
     t.geom = l.geom;
     return t;
+}
+
+// Level-bank of a pair bin (or -1).
+__host__ __device__ inline int pair_lb(const BinGeom &g, int bin) {
+    if (g.npl == 0 || bin < g.pl_base[0] || bin >= g.pl_base[g.npl]) return -1;
+    int l = 0;
+    while (bin >= g.pl_base[l + 1]) ++l;
+    return l;
+}
+
+// Whether a pair bin takes the owner-pair path.
+__device__ __forceinline__ bool pair_active(const BinGeom &g, const int *offsets, int bin) {
+    const int l = pair_lb(g, bin);
+    return l >= 0 && g.pl_exp[l] && offsets[bin + 1] - offsets[bin] >= PAIR_MIN;
 }
 
 __host__ __device__ inline int atom_class(int4 span) {
@@ -281,12 +381,21 @@ __host__ __device__ inline int atom_class(int4 span) {
     return c;
 }
 
-// Bin of an atom from its spans (invalid atoms have footprint 0).
-__device__ __forceinline__ int atom_bin(int4 span, const BinGeom &g) {
+// Bin of an atom from its spans and its (level, K) on both axes (invalid atoms
+// have footprint 0).
+__device__ __forceinline__ int atom_bin(int4 span, const BinGeom &g, int lvl_o, int k_o,
+                                        int lvl_i, int k_i) {
     const int invalid = g.nbins - 1;
     if (span.y <= 0 || span.w <= 0) return invalid;
     if (g.nclass == 0) return 0;
     const int c = atom_class(span);
+    if (c >= NFINE && lvl_o == lvl_i && k_o == k_i && lvl_o >= 0 && lvl_o < MAX_LEVELS) {
+        const int l = g.pl_of[2 * lvl_o + k_o - 2];
+        if (l >= 0) {
+            const int t = g.pl_T[l];
+            return g.pl_base[l] + (span.x / t) * g.pl_ni[l] + span.z / t;
+        }
+    }
     const int e = class_edge(c);
     return g.base[c] + (span.x / e) * g.tc[c] + span.z / e;
 }
@@ -356,12 +465,33 @@ template <int M> struct AxisCoef {
 };
 
 __host__ int make_axis(const tcst_axis *in, AxisCfg *out, char *err, int errlen);
+
+__host__ __device__ inline AxisGeo axis_geo(const AxisCfg &a) {
+    return AxisGeo{a.sites, a.base, a.merge, a.modes, a.spacing};
+}
+inline AxisGeo axis_geo(const tcst_axis &a) {
+    return AxisGeo{a.site_count, a.base_tile_sites, a.merge_factor, a.modes, a.spacing};
+}
 __host__ int make_coords(const tcst_coordinates *in, const AxisCfg &out_ax,
                          const AxisCfg &in_ax, CoordCfg *out, char *err, int errlen);
 
 } // namespace tcst
 
 namespace tcst {
+
+// Atom gradient from its four footprint sums (s_amp = sum G m_out m_in,
+// s_mo / s_mi with dm/dmu on one axis, s_r = sum G (dm_out/dR m_in +
+// m_out dm_in/dR)): the rational (a, q) chain (rational_radius.py:19-23), the
+// amplitude chain only for Polar rows (radius detached), zero for invalid atoms.
+__device__ __forceinline__ float4 atom_chain(const float *rec, float s_amp, float s_mo,
+                                             float s_mi, float s_r) {
+    const int flags = reinterpret_cast<const int *>(rec)[3];
+    const float amp = rec[0], ch0 = rec[1], ch1 = rec[2];
+    if (flags & 2) return make_float4(0.f, 0.f, 0.f, 0.f);
+    if (flags & 1) return make_float4(s_amp * ch0, s_amp * ch1, amp * s_mo, amp * s_mi);
+    const float d_r = amp * s_r;
+    return make_float4(fmaf(d_r, ch0, s_amp), d_r * ch1, amp * s_mo, amp * s_mi);
+}
 
 // Programmatic dependent launch: every kernel of this library is launched with
 // programmatic stream serialization, so its blocks may become resident while

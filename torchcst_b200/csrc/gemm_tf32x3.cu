@@ -177,6 +177,18 @@ template <class P, bool MN> struct OperandGeom {
     }
 };
 
+// Optional MSE epilogue (Y = X W^T of a training step): instead of Y the
+// kernel writes dY = (Y - T) * scale, one double sum of (Y - T)^2 per
+// epilogue warp into partial[cta * 4 + warp quarter], and max |dY| into amax
+// (non-negative floats order like their bit patterns).
+struct MseEpilogue {
+    const float *target; // nullptr: plain GEMM
+    long long ldt;
+    float scale;
+    double *partial;
+    float *amax;
+};
+
 template <class P, int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_x3_kernel(const __grid_constant__ CUtensorMap map_a_hi,
@@ -185,7 +197,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                    const __grid_constant__ CUtensorMap map_b_lo, int M, int N, int K,
                    int k_per_split, float *__restrict__ C, long long ldc, long long split_stride,
                    const float *__restrict__ scale_a, const float *__restrict__ scale_b,
-                   unsigned *__restrict__ status) {
+                   unsigned *__restrict__ status, MseEpilogue mse) {
     using L = Layout<P, BN, STAGES>;
     constexpr int BK = P::BK;
     using GA = OperandGeom<P, A_MN>;
@@ -319,8 +331,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!ready) atomicOr(status, TCST_STATUS_TIMEOUT);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         }
+        double loss = 0.0;
+        float vmax = 0.f;
         if (ready && !*abort_flag) {
             const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+            const bool vec_t = mse.target && mse.ldt % 4 == 0 &&
+                               (reinterpret_cast<uintptr_t>(mse.target) & 15) == 0;
             // 1 / (s_A s_B): a power of two, so the product is exact.
             const float inv = (scale_a && scale_b) ? 1.0f / (*scale_a * *scale_b) : 1.0f;
 #pragma unroll 1
@@ -344,7 +360,39 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) r[j] = 0u;
                 }
-                if (row < M) {
+                if (row < M && mse.target) {
+                    // dY = (Y - T) * scale in place of Y; sum (Y - T)^2 in double.
+                    const int col0 = tile_n * BN + c0;
+                    float *dst = out + (long long)row * ldc + col0;
+                    const float *tr = mse.target + (long long)row * mse.ldt + col0;
+                    if (vec && vec_t && col0 + 32 <= N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            const float4 t4 = *reinterpret_cast<const float4 *>(tr + j);
+                            const float d0 = __uint_as_float(r[j]) * inv - t4.x;
+                            const float d1 = __uint_as_float(r[j + 1]) * inv - t4.y;
+                            const float d2 = __uint_as_float(r[j + 2]) * inv - t4.z;
+                            const float d3 = __uint_as_float(r[j + 3]) * inv - t4.w;
+                            loss += double(d0) * d0 + double(d1) * d1 + double(d2) * d2 +
+                                    double(d3) * d3;
+                            const float4 g = make_float4(d0 * mse.scale, d1 * mse.scale,
+                                                         d2 * mse.scale, d3 * mse.scale);
+                            vmax = fmaxf(vmax, fmaxf(fmaxf(fabsf(g.x), fabsf(g.y)),
+                                                     fmaxf(fabsf(g.z), fabsf(g.w))));
+                            *reinterpret_cast<float4 *>(dst + j) = g;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < N) {
+                                const float d = __uint_as_float(r[j]) * inv - tr[j];
+                                loss += double(d) * double(d);
+                                const float g = d * mse.scale;
+                                vmax = fmaxf(vmax, fabsf(g));
+                                dst[j] = g;
+                            }
+                    }
+                } else if (row < M) {
                     const int col0 = tile_n * BN + c0;
                     float *dst = out + (long long)row * ldc + col0;
                     if (vec && col0 + 32 <= N) {
@@ -359,6 +407,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                             if (col0 + j < N) dst[j] = __uint_as_float(r[j]) * inv;
                     }
                 }
+            }
+        }
+        if (mse.target) {
+            // One loss partial per epilogue warp (fixed xor tree), one max
+            // atomic per warp.
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                loss += __shfl_xor_sync(0xffffffffu, loss, o);
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+            }
+            if (lane == 0) {
+                mse.partial[(blockIdx.y * (long long)gridDim.x + blockIdx.x) * 4 + quarter] = loss;
+                if (mse.amax && vmax > 0.f)
+                    atomicMax(reinterpret_cast<unsigned *>(mse.amax), __float_as_uint(vmax));
             }
         }
     }
@@ -439,7 +501,7 @@ __global__ void zero_fill_kernel(float *__restrict__ C, long long M, long long N
 template <class P, int BN, int STAGES, bool A_MN, bool B_MN>
 static int launch(int M, int N, int K, const CUtensorMap *maps, int kps, int splits, float *C,
                   long long ldc, long long sstride, const float *sa, const float *sb,
-                  unsigned *status, cudaStream_t stream) {
+                  unsigned *status, cudaStream_t stream, const MseEpilogue &mse) {
     using L = Layout<P, BN, STAGES>;
     auto kern = gemm_x3_kernel<P, BN, STAGES, A_MN, B_MN>;
     static bool configured = false;
@@ -450,7 +512,7 @@ static int launch(int M, int N, int K, const CUtensorMap *maps, int kps, int spl
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, splits);
     TCST_CUDA(launch_pdl(kern, dim3(grid), dim3(THREADS), L::SMEM_BYTES, stream, maps[0], maps[1], maps[2], maps[3], M, N, K, kps,
-                                                   C, ldc, sstride, sa, sb, status));
+                                                   C, ldc, sstride, sa, sb, status, mse));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }
@@ -461,7 +523,8 @@ static int gemm_x3(const char *name, int64_t M, int64_t N, int64_t K, const void
                    const void *a_lo_dev, int64_t lda, int32_t a_mn_major, const void *b_hi_dev,
                    const void *b_lo_dev, int64_t ldb, int32_t b_mn_major, float *c_dev,
                    int64_t ldc, int32_t split_k, int64_t split_stride, const float *sa,
-                   const float *sb, uint32_t *status_dev, void *stream) {
+                   const float *sb, uint32_t *status_dev, void *stream,
+                   const MseEpilogue &mse = MseEpilogue{}) {
     if (M < 0 || N < 0 || K < 0 || split_k < 1 || !status_dev || M > INT32_MAX ||
         N > INT32_MAX || K > INT32_MAX) {
         tcst_set_error("%s: invalid sizes", name);
@@ -512,15 +575,18 @@ static int gemm_x3(const char *name, int64_t M, int64_t N, int64_t K, const void
     unsigned *status = status_dev;
     if (!a_mn_major && !b_mn_major)
         return launch<P, BN, STAGES, false, false>(int(M), int(N), int(K), maps, kps, split_k,
-                                                   c_dev, ldc, split_stride, sa, sb, status, st);
+                                                   c_dev, ldc, split_stride, sa, sb, status, st,
+                                                   mse);
     if (!a_mn_major && b_mn_major)
         return launch<P, BN, STAGES, false, true>(int(M), int(N), int(K), maps, kps, split_k,
-                                                  c_dev, ldc, split_stride, sa, sb, status, st);
+                                                  c_dev, ldc, split_stride, sa, sb, status, st,
+                                                  mse);
     if (a_mn_major && !b_mn_major)
         return launch<P, BN, STAGES, true, false>(int(M), int(N), int(K), maps, kps, split_k,
-                                                  c_dev, ldc, split_stride, sa, sb, status, st);
+                                                  c_dev, ldc, split_stride, sa, sb, status, st,
+                                                  mse);
     return launch<P, BN, STAGES, true, true>(int(M), int(N), int(K), maps, kps, split_k, c_dev,
-                                             ldc, split_stride, sa, sb, status, st);
+                                             ldc, split_stride, sa, sb, status, st, mse);
 }
 
 } // namespace gemm
@@ -560,4 +626,24 @@ extern "C" int tcst_gemm_f16x3(int64_t M, int64_t N, int64_t K, const void *a_hi
     return gemm_x3<F16Wide>("tcst_gemm_f16x3", M, N, K, a_hi_dev, a_lo_dev, lda, a_mn_major,
                         b_hi_dev, b_lo_dev, ldb, b_mn_major, c_dev, ldc, split_k, split_stride,
                         a_scale_dev, b_scale_dev, status_dev, stream);
+}
+
+extern "C" int tcst_gemm_f16x3_mse(int64_t M, int64_t N, int64_t K, const void *a_hi_dev,
+                                   const void *a_lo_dev, int64_t lda, const float *a_scale_dev,
+                                   const void *b_hi_dev, const void *b_lo_dev, int64_t ldb,
+                                   const float *b_scale_dev, const float *target_dev,
+                                   int64_t ld_target, float scale, float *dy_dev, int64_t ld_dy,
+                                   double *loss_partial_dev, int32_t *partials,
+                                   float *amax_dev, uint32_t *status_dev, void *stream) {
+    const int64_t tiles = ((N + 255) / 256) * ((M + BM - 1) / BM);
+    if (partials) *partials = int32_t(tiles * 4);
+    if (M < 0 || N < 0 || K < 1 || !target_dev || ld_target < N || !loss_partial_dev ||
+        !a_scale_dev || !b_scale_dev) {
+        tcst_set_error("tcst_gemm_f16x3_mse: invalid arguments (K must be positive)");
+        return TCST_ERR_ARGUMENT;
+    }
+    const MseEpilogue mse{target_dev, ld_target, scale, loss_partial_dev, amax_dev};
+    return gemm_x3<F16>("tcst_gemm_f16x3_mse", M, N, K, a_hi_dev, a_lo_dev, lda, 0, b_hi_dev,
+                        b_lo_dev, ldb, 0, dy_dev, ld_dy, 1, 0, a_scale_dev, b_scale_dev,
+                        status_dev, stream, mse);
 }

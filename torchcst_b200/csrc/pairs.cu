@@ -1,0 +1,343 @@
+// Owner-pair (Fourier) path for coarse atoms that share an owner pair.
+//
+// All atoms of an owner pair (level-bank (T, K), output first tile a, input
+// first tile b) share their footprints: F = K T sites from a T and from b T on
+// the two axes. On a footprint the profile of an atom is a cosine series in the
+// half-turn phase t_j = phase0 + 2 j / F (common.cuh), so with the PF = 2M + 1
+// functions of the site j
+//     phi_0 = 1, phi_{2k-1} = cos(2 pi k j / F), phi_{2k} = sin(2 pi k j / F)
+// its mass is m(j) = sum_f alpha_f phi_f(j) with
+//     alpha_0 = coef_0, alpha_{2k-1} = coef_k cos(pi k phase0),
+//     alpha_{2k} = -coef_k sin(pi k phase0),
+// and dm/dmu, dm/dR have coefficient vectors of the same form (below). The
+// pair's contribution to W is therefore Phi_out C Phi_in^T with
+//     C = sum_a amp_a alpha_out,a alpha_in,a^T          (PF x PF),
+// and the pullback needs only H = Phi_out^T G Phi_in (PF x PF) per pair: every
+// atom's four gradient sums are bilinear forms of H (this is the wide-atom
+// factorisation of the reference's dense_fourier_weight.cuh and
+// dense_pair_cotangent.cuh, restated). Sites past N fold onto the chart, so
+// Phi is summed over the images of a chart site.
+//
+// Kernels (one launch each, all deterministic):
+//   pair_coef_kernel     C of every active pair bin, atoms in bin (id) order;
+//   pair_expand_kernel   per output node a of an expansion level-bank and
+//                        chunk of input sites: R_a = sum_b C_ab Phi_b^T
+//                        (PF x N_in) over the active partners b in order, and
+//                        the node flag; the weight gather then adds
+//                        Phi_a(rows) R_a(cols) as PF rank-one terms per node;
+//   pair_project_kernel  the pullback's P_a = Phi_a^T G (PF x N_in) per node
+//                        with an active pair, over its footprint rows in order;
+//   pair_grad_kernel     per active pair H_ab = P_a Phi_b, then the gradient
+//                        of each of its atoms.
+
+#include "pairs.cuh"
+
+namespace tcst {
+
+namespace {
+
+constexpr int PC_CHUNK = 32;  // atoms staged per pass of pair_coef_kernel
+constexpr int PX_CHUNK = 256; // input sites per CTA of expand / project
+constexpr int PG_COLS = 64;   // columns staged per pass of pair_grad_kernel
+
+// Coefficient vectors of one axis block: m (alpha), dm/dmu (bmu), dm/dR (br).
+//   dm/dmu(j) = omega sum_k k coef_k sin(pi k t_j)
+//     -> bmu_{2k-1} = omega k coef_k sin(pi k phase0), bmu_{2k} = omega k coef_k cos(pi k phase0)
+//   dm/dR(j) = sum_k dcoef_k cos(pi k t_j) -> br as alpha with dcoef.
+__device__ __forceinline__ void axis_alpha(const float *blk, float *alpha, float *bmu,
+                                           float *br) {
+    const float p0 = blk[2], omega = blk[3];
+    const float *c = blk + 4, *dc = blk + 4 + 9;
+    float s1, c1;
+    sincospif(p0, &s1, &c1);
+    alpha[0] = c[0];
+    if (bmu) bmu[0] = 0.f;
+    if (br) br[0] = dc[0];
+    float cp = 1.f, cc = c1, sp = 0.f, sc = s1;
+#pragma unroll
+    for (int k = 1; k <= 8; ++k) {
+        alpha[2 * k - 1] = c[k] * cc;
+        alpha[2 * k] = -c[k] * sc;
+        if (bmu) {
+            const float w = omega * float(k) * c[k];
+            bmu[2 * k - 1] = w * sc;
+            bmu[2 * k] = w * cc;
+        }
+        if (br) {
+            br[2 * k - 1] = dc[k] * cc;
+            br[2 * k] = -dc[k] * sc;
+        }
+        const float cn = fmaf(2.f * c1, cc, -cp), sn = fmaf(2.f * c1, sc, -sp);
+        cp = cc;
+        cc = cn;
+        sp = sc;
+        sc = sn;
+    }
+}
+
+} // namespace
+
+__global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw) {
+    pdl_wait();
+    const BinGeom &g = tv.geom;
+    const int bin = g.pl_base[0] + blockIdx.x;
+    if (!pair_active(g, tv.offsets, bin)) return;
+    const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
+    __shared__ float sa[PC_CHUNK][2 * PF + 1];
+    const int t = threadIdx.x;
+    const int f = t / PF, gg = t - f * PF;
+    float acc = 0.f;
+    for (int k0 = begin; k0 < end; k0 += PC_CHUNK) {
+        const int n = min(PC_CHUNK, end - k0);
+        if (t < n) {
+            const long long a = tv.ids[k0 + t];
+            const float *rec = tv.rec + a * (long long)tv.words;
+            float ao[PF], ai[PF];
+            axis_alpha(rec + 4, ao, nullptr, nullptr);
+            axis_alpha(rec + 4 + aw, ai, nullptr, nullptr);
+            const float amp = rec[0];
+#pragma unroll
+            for (int e = 0; e < PF; ++e) {
+                sa[t][e] = amp * ao[e];
+                sa[t][PF + e] = ai[e];
+            }
+        }
+        __syncthreads();
+        if (t < PF * PF)
+            for (int j = 0; j < n; ++j) acc = fmaf(sa[j][f], sa[j][PF + gg], acc);
+        __syncthreads();
+    }
+    if (t < PF * PF) tv.pair_c[(long long)blockIdx.x * PF * PF + t] = acc;
+}
+
+// CTA -> (expansion level-bank l, output node a, input chunk ch).
+__device__ __forceinline__ bool expand_cta(const BinGeom &g, int chunks, int &l, int &a,
+                                           int &ch) {
+    int cta = blockIdx.x;
+    for (l = 0; l < g.npl; ++l) {
+        if (!g.pl_exp[l]) continue;
+        const int n = g.pl_no[l] * chunks;
+        if (cta < n) break;
+        cta -= n;
+    }
+    if (l >= g.npl) return false;
+    a = cta / chunks;
+    ch = cta - a * chunks;
+    return true;
+}
+
+__global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_in) {
+    pdl_wait();
+    const BinGeom &g = tv.geom;
+    const int chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
+    int l, a, ch;
+    if (!expand_cta(g, chunks, l, a, ch)) return;
+    const int T = g.pl_T[l], F = g.pl_K[l] * T, nb = g.pl_ni[l];
+    const int i = ch * PX_CHUNK + threadIdx.x;
+    __shared__ float C[PF * PF];
+    float r[PF];
+#pragma unroll
+    for (int f = 0; f < PF; ++f) r[f] = 0.f;
+    bool any = false;
+    for (int b = 0; b < nb; ++b) {
+        const int bin = g.pl_base[l] + a * nb + b;
+        if (tv.offsets[bin + 1] - tv.offsets[bin] < PAIR_MIN) continue; // CTA-uniform
+        any = true;
+        __syncthreads();
+        for (int e = threadIdx.x; e < PF * PF; e += blockDim.x)
+            C[e] = tv.pair_c[(long long)(bin - g.pl_base[0]) * PF * PF + e];
+        __syncthreads();
+        float phi[PF];
+        if (i < n_in && pair_basis(i - b * T, F, n_in, phi)) {
+#pragma unroll
+            for (int f = 0; f < PF; ++f) {
+                float v = r[f];
+#pragma unroll
+                for (int e = 0; e < PF; ++e) v = fmaf(C[f * PF + e], phi[e], v);
+                r[f] = v;
+            }
+        }
+    }
+    if (ch == 0 && threadIdx.x == 0) tv.node_on[g.pl_node[l] + a] = any ? 1 : 0;
+    if (any && i < n_in) {
+        float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in + i;
+#pragma unroll
+        for (int f = 0; f < PF; ++f) out[(long long)f * n_in] = r[f];
+    }
+}
+
+__global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_out, int n_in,
+                                                                const float *__restrict__ gm,
+                                                                long long ldg) {
+    pdl_wait();
+    const BinGeom &g = tv.geom;
+    const int chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
+    int l, a, ch;
+    if (!expand_cta(g, chunks, l, a, ch)) return;
+    if (!tv.node_on[g.pl_node[l] + a]) return;
+    const int T = g.pl_T[l], F = g.pl_K[l] * T;
+    const int i = ch * PX_CHUNK + threadIdx.x;
+    // Distinct chart rows of the footprint: all rows when it wraps onto itself.
+    const int rows = F >= n_out ? n_out : F;
+    const int row0 = F >= n_out ? 0 : a * T;
+    __shared__ float sphi[32][PF + 1];
+    float p[PF];
+#pragma unroll
+    for (int f = 0; f < PF; ++f) p[f] = 0.f;
+    for (int r0 = 0; r0 < rows; r0 += 32) {
+        const int nr = min(32, rows - r0);
+        __syncthreads();
+        if (threadIdx.x < nr) {
+            float phi[PF];
+            int row = row0 + r0 + threadIdx.x;
+            row -= row >= n_out ? n_out : 0;
+            pair_basis(row - a * T, F, n_out, phi);
+#pragma unroll
+            for (int f = 0; f < PF; ++f) sphi[threadIdx.x][f] = phi[f];
+        }
+        __syncthreads();
+        if (i < n_in) {
+            for (int j = 0; j < nr; ++j) {
+                int row = row0 + r0 + j;
+                row -= row >= n_out ? n_out : 0;
+                const float gv = gm[(long long)row * ldg + i];
+#pragma unroll
+                for (int f = 0; f < PF; ++f) p[f] = fmaf(sphi[j][f], gv, p[f]);
+            }
+        }
+    }
+    if (i < n_in) {
+        float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in + i;
+#pragma unroll
+        for (int f = 0; f < PF; ++f) out[(long long)f * n_in] = p[f];
+    }
+}
+
+__global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_in,
+                                                        float4 *__restrict__ grad) {
+    pdl_wait();
+    const BinGeom &g = tv.geom;
+    const int bin = g.pl_base[0] + blockIdx.x;
+    if (!pair_active(g, tv.offsets, bin)) return;
+    const int l = pair_lb(g, bin);
+    const int nb = g.pl_ni[l], idx = bin - g.pl_base[l];
+    const int a = idx / nb, b = idx - a * nb;
+    const int T = g.pl_T[l], F = g.pl_K[l] * T;
+    const int cols = F >= n_in ? n_in : F;
+    const int col0 = F >= n_in ? 0 : b * T;
+    const float *P = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in;
+    __shared__ float sp[PF][PG_COLS + 1];
+    __shared__ float sphi[PG_COLS][PF + 1];
+    __shared__ float H[PF * PF];
+    const int t = threadIdx.x;
+    const int f = t / PF, gg = t - f * PF;
+    float acc = 0.f;
+    for (int c0 = 0; c0 < cols; c0 += PG_COLS) {
+        const int nc = min(PG_COLS, cols - c0);
+        __syncthreads();
+        for (int e = t; e < PF * nc; e += blockDim.x) {
+            const int ff = e / nc, j = e - ff * nc;
+            int col = col0 + c0 + j;
+            col -= col >= n_in ? n_in : 0;
+            sp[ff][j] = P[(long long)ff * n_in + col];
+        }
+        if (t < nc) {
+            float phi[PF];
+            int col = col0 + c0 + t;
+            col -= col >= n_in ? n_in : 0;
+            pair_basis(col - b * T, F, n_in, phi);
+#pragma unroll
+            for (int e = 0; e < PF; ++e) sphi[t][e] = phi[e];
+        }
+        __syncthreads();
+        if (t < PF * PF)
+            for (int j = 0; j < nc; ++j) acc = fmaf(sp[f][j], sphi[j][gg], acc);
+    }
+    if (t < PF * PF) H[t] = acc;
+    __syncthreads();
+    // Every atom of the pair: one warp, lanes over rows f of H.
+    const int lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
+    const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
+    for (int k = begin + warp; k < end; k += nw) {
+        const long long atom = tv.ids[k];
+        const float *rec = tv.rec + atom * (long long)tv.words;
+        float ao[PF], mo[PF], ro[PF], ai[PF], mi[PF], ri[PF];
+        axis_alpha(rec + 4, ao, mo, ro);
+        axis_alpha(rec + 4 + aw, ai, mi, ri);
+        float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
+        if (lane < PF) {
+            float h1 = 0.f, h2 = 0.f, h3 = 0.f;
+#pragma unroll
+            for (int e = 0; e < PF; ++e) {
+                const float hv = H[lane * PF + e];
+                h1 = fmaf(hv, ai[e], h1);
+                h2 = fmaf(hv, mi[e], h2);
+                h3 = fmaf(hv, ri[e], h3);
+            }
+            // Row `lane` of the output-side vectors (registers are indexed
+            // statically, so select by a loop).
+            float a_f = 0.f, m_f = 0.f, r_f = 0.f;
+#pragma unroll
+            for (int e = 0; e < PF; ++e)
+                if (e == lane) {
+                    a_f = ao[e];
+                    m_f = mo[e];
+                    r_f = ro[e];
+                }
+            s_amp = a_f * h1;
+            s_mo = m_f * h1;
+            s_mi = a_f * h2;
+            s_r = fmaf(r_f, h1, a_f * h3);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            s_amp += __shfl_xor_sync(0xffffffffu, s_amp, off);
+            s_mo += __shfl_xor_sync(0xffffffffu, s_mo, off);
+            s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
+            s_r += __shfl_xor_sync(0xffffffffu, s_r, off);
+        }
+        if (lane == 0) grad[atom] = atom_chain(rec, s_amp, s_mo, s_mi, s_r);
+    }
+}
+
+int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, cudaStream_t st) {
+    const BinGeom &g = tv.geom;
+    if (g.npl == 0 || tv.atoms == 0) return TCST_OK;
+    const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
+    const int aw = axis_words(oa.modes);
+    TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(unsigned(pair_bins)), dim3(320), 0, st, tv, aw));
+    TCST_CUDA(cudaGetLastError());
+    const long long ctas = expand_ctas(g, ia.sites);
+    if (ctas > 0) {
+        TCST_CUDA(launch_pdl(pair_expand_kernel, dim3(unsigned(ctas)), dim3(PX_CHUNK), 0, st, tv,
+                             ia.sites));
+        TCST_CUDA(cudaGetLastError());
+    }
+    return TCST_OK;
+}
+
+int pair_backward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const float *g_dev,
+                  long long ldg, float4 *grad, cudaStream_t st) {
+    const BinGeom &g = tv.geom;
+    if (g.npl == 0 || tv.atoms == 0) return TCST_OK;
+    const long long ctas = expand_ctas(g, ia.sites);
+    if (ctas == 0) return TCST_OK;
+    TCST_CUDA(launch_pdl(pair_project_kernel, dim3(unsigned(ctas)), dim3(PX_CHUNK), 0, st, tv,
+                         oa.sites, ia.sites, g_dev, ldg));
+    TCST_CUDA(cudaGetLastError());
+    const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
+    TCST_CUDA(launch_pdl(pair_grad_kernel, dim3(unsigned(pair_bins)), dim3(320), 0, st, tv,
+                         axis_words(oa.modes), ia.sites, grad));
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+long long expand_ctas(const BinGeom &g, int n_in) {
+    const long long chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
+    long long n = 0;
+    for (int l = 0; l < g.npl; ++l)
+        if (g.pl_exp[l]) n += g.pl_no[l] * chunks;
+    return n;
+}
+
+} // namespace tcst

@@ -1,0 +1,52 @@
+// Owner-pair (Fourier) path of coarse atoms: launches used by the weight
+// assembly (forward) and the pullback (backward). See pairs.cu.
+#pragma once
+
+#include "common.cuh"
+
+namespace tcst {
+
+// Sum over the images of one chart site of the PF footprint functions
+// {1, cos 2 pi k j / F, sin 2 pi k j / F}: d is the site minus the footprint
+// start (any integer), images j = d mod n, d mod n + n, ... < F on an axis of
+// n sites. False when no image lies on the footprint.
+__device__ __forceinline__ bool pair_basis(int d, int F, int n, float *phi) {
+    int j = d % n;
+    j += j < 0 ? n : 0;
+#pragma unroll
+    for (int f = 0; f < PF; ++f) phi[f] = 0.f;
+    bool hit = false;
+    for (; j < F; j += n) {
+        hit = true;
+        float s1, c1;
+        sincospif(2.0f * float(j) / float(F), &s1, &c1);
+        phi[0] += 1.f;
+        float cp = 1.f, cc = c1, sp = 0.f, sc = s1;
+#pragma unroll
+        for (int k = 1; k <= 8; ++k) {
+            phi[2 * k - 1] += cc;
+            phi[2 * k] += sc;
+            const float cn = fmaf(2.f * c1, cc, -cp), sn = fmaf(2.f * c1, sc, -sp);
+            cp = cc;
+            cc = cn;
+            sp = sc;
+            sc = sn;
+        }
+    }
+    return hit;
+}
+
+
+// CTAs of the expand / project launches (0 without expansion level-banks).
+long long expand_ctas(const BinGeom &g, int n_in);
+
+// C of every active pair, then R and the node flags of the expansion
+// level-banks (before the weight gather, which reads them).
+int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, cudaStream_t st);
+
+// P = Phi^T G per flagged node, then the gradients of the atoms of active
+// pairs (G summed over split-K partials, leading dimension ldg).
+int pair_backward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const float *g_dev,
+                  long long ldg, float4 *grad, cudaStream_t st);
+
+} // namespace tcst

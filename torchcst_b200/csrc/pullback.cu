@@ -25,22 +25,13 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "pairs.cuh"
 
 namespace tcst {
 
 constexpr int P0_THREADS = 256;
 constexpr int PC_THREADS = 256;
 constexpr int PC_WARPS = PC_THREADS / 32;
-
-__device__ __forceinline__ float4 chain(const float *rec, float s_amp, float s_mo, float s_mi,
-                                        float s_r) {
-    const int flags = reinterpret_cast<const int *>(rec)[3];
-    const float amp = rec[0], ch0 = rec[1], ch1 = rec[2];
-    if (flags & 2) return make_float4(0.f, 0.f, 0.f, 0.f);
-    if (flags & 1) return make_float4(s_amp * ch0, s_amp * ch1, amp * s_mo, amp * s_mi);
-    const float d_r = amp * s_r;
-    return make_float4(fmaf(d_r, ch0, s_amp), d_r * ch1, amp * s_mo, amp * s_mi);
-}
 
 // G_0 += G_1 + ... + G_{split-1}, in place (rows of ni valid columns).
 __global__ void g_reduce_kernel(float *__restrict__ g, int no, int ni, long long ldg, int split,
@@ -264,7 +255,7 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
             s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
             s_r += __shfl_xor_sync(0xffffffffu, s_r, off);
         }
-        if (live && q == 0) grad[a] = chain(tv.rec + a * (long long)tv.words, s_amp, s_mo, s_mi, s_r);
+        if (live && q == 0) grad[a] = atom_chain(tv.rec + a * (long long)tv.words, s_amp, s_mo, s_mi, s_r);
     }
 }
 
@@ -394,7 +385,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
             s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
             s_r += __shfl_xor_sync(0xffffffffu, s_r, off);
         }
-        if (lane == 0) grad[a] = chain(rec, s_amp, s_mo, s_mi, s_r);
+        if (lane == 0) grad[a] = atom_chain(rec, s_amp, s_mo, s_mi, s_r);
         __syncwarp();
     }
 }
@@ -422,6 +413,7 @@ __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
     const long long begin = *begin_ptr;
     for (long long k = begin + blockIdx.x; k < tv.atoms; k += gridDim.x) {
         const long long a = tv.ids[k];
+        if (pair_active(tv.geom, tv.offsets, tv.bin_of[a])) continue; // owner-pair path
         const float *rec = tv.rec + a * (long long)tv.words;
         const float *ob = rec + 4;
         const float *ib = rec + 4 + aw;
@@ -505,7 +497,7 @@ __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
                 t2 += red[w][2];
                 t3 += red[w][3];
             }
-            grad[a] = chain(rec, t0, t1, t2, t3);
+            grad[a] = atom_chain(rec, t0, t1, t2, t3);
         }
         __syncthreads(); // red and the staged values are reused by the next atom
     }
@@ -535,7 +527,7 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
     }
     if (atoms == 0) return TCST_OK;
     const int words = record_words(oa.modes, ia.modes);
-    const Table tv = table_view(atom_table_dev, atoms, words, oa.sites, ia.sites, oa.modes, ia.modes);
+    const Table tv = table_view(atom_table_dev, atoms, words, axis_geo(oa), axis_geo(ia));
     const BinGeom &geo = tv.geom;
     cudaStream_t st = (cudaStream_t)stream;
     float4 *grad = reinterpret_cast<float4 *>(grad_dev);
@@ -581,8 +573,10 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
             TCST_CUDA(cudaGetLastError());
         }
     }
-    // Coarse classes and invalid atoms (all atoms when unbinned): their range
-    // starts at the first coarse bin and runs to the end of the ids.
+    // Atoms of active owner pairs (their grads), then coarse classes, inactive
+    // pair bins and invalid atoms (all atoms when unbinned): their range starts
+    // at the first coarse bin and runs to the end of the ids.
+    if ((rc = pair_backward(tv, oa, ia, g_dev, ldg, grad, st))) return rc;
     const int first_bin = geo.nclass > 0 ? geo.base[std::min(NFINE, geo.nclass)] : 0;
     const long long ctas = std::min<long long>(atoms, 148LL * 8);
     TCST_CUDA(launch_pdl(pullback_wide_kernel, dim3(unsigned(ctas)), dim3(PW_THREADS), 0, st, 

@@ -20,12 +20,13 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "pairs.cuh"
 
 namespace tcst {
 
 constexpr int WT_THREADS = 128; // 16 x 8 threads, 2 x 4 outputs each
 constexpr int WT_STAGE = 64;          // hits staged per sub-pass
-constexpr int MAX_SCAN = 320;  // bins a weight tile can scan
+constexpr int MAX_SCAN = 512;  // bins a weight tile can scan
 
 __device__ __forceinline__ float tf32_rna(float x) {
     unsigned r;
@@ -47,10 +48,41 @@ __device__ __forceinline__ bool window_hits(int f, int F, int t0, int tl, int n)
 
 // Source tiles (k = 0 .. count-1 steps back from the tile holding `t0`) whose
 // atoms of class c can reach sites [t0, t0 + TS).
-__device__ __forceinline__ int reach_tiles(int c, int tiles, int n) {
+__host__ __device__ __forceinline__ int reach_tiles(int c, int tiles, int n) {
     const int e = class_edge(c);
     const int k = 1 + (class_reach(c) - 1 + e - 1) / e + (n % e != 0);
     return min(k, tiles);
+}
+
+// Nodes (first tiles of T sites, nn of them on an axis of n sites) whose F-site
+// footprint covers some site of [t0, t0 + tl): `count` consecutive nodes from
+// `first` (mod nn). Node a covers the tile iff t0 - F < a T <= t0 + tl - 1
+// modulo n.
+__host__ __device__ __forceinline__ int cover_nodes(int t0, int tl, int T, int F, int nn, int n,
+                                                    int &first) {
+    first = 0;
+    if (F + tl - 1 >= n) return nn;
+    const int x = t0 - F + 1;
+    const int lo = x >= 0 ? (x + T - 1) / T : -((-x) / T);
+    const int hi = (t0 + tl - 1) / T;
+    const int cnt = hi - lo + 1;
+    if (cnt >= nn) return nn;
+    first = lo % nn;
+    first += first < 0 ? nn : 0;
+    return cnt;
+}
+
+// Upper bound of the bins one weight tile scans (class bins within reach and
+// covering pair bins).
+__host__ inline int max_scan_entries(const BinGeom &g, int no, int ni) {
+    if (g.nclass == 0) return 1;
+    int n = 0;
+    for (int c = 0; c < g.nclass; ++c) n += reach_tiles(c, g.tr[c], no) * reach_tiles(c, g.tc[c], ni);
+    for (int l = 0; l < g.npl; ++l) {
+        const int k = g.pl_K[l] + 2;
+        n += (g.pl_no[l] < k ? g.pl_no[l] : k) * (g.pl_ni[l] < k ? g.pl_ni[l] : k);
+    }
+    return n;
 }
 
 // Class 1..NFINE-1 mass cache: cache[a][axis][j] = m_axis(j), j < F_axis.
@@ -144,11 +176,36 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
             spre[1] = tv.offsets[1] - tv.offsets[0];
         }
     } else {
-        nscan = 0;
+        // Class bins within reach, then the pair bins of covering node pairs
+        // (active pairs count no atoms: they come in as rank-one terms below).
+        int ncls = 0;
         for (int c = 0; c < g.nclass; ++c)
-            nscan += reach_tiles(c, g.tr[c], no) * reach_tiles(c, g.tc[c], ni);
-        nscan = min(nscan, MAX_SCAN);
-        for (int i = t; i < nscan; i += WT_THREADS) {
+            ncls += reach_tiles(c, g.tr[c], no) * reach_tiles(c, g.tc[c], ni);
+        nscan = ncls;
+        for (int l = 0; l < g.npl; ++l) {
+            int f0, f1;
+            const int F = g.pl_K[l] * g.pl_T[l];
+            nscan += cover_nodes(R0, TR, g.pl_T[l], F, g.pl_no[l], no, f0) *
+                     cover_nodes(C0, TC, g.pl_T[l], F, g.pl_ni[l], ni, f1);
+        }
+        for (int i = ncls + t; i < nscan; i += WT_THREADS) {
+            int rem = i - ncls, l = 0, co = 0, ci = 0, fo = 0, fi = 0, F = 0;
+            for (; l < g.npl; ++l) {
+                F = g.pl_K[l] * g.pl_T[l];
+                co = cover_nodes(R0, TR, g.pl_T[l], F, g.pl_no[l], no, fo);
+                ci = cover_nodes(C0, TC, g.pl_T[l], F, g.pl_ni[l], ni, fi);
+                if (rem < co * ci) break;
+                rem -= co * ci;
+            }
+            const int u = rem / ci, v = rem - u * ci;
+            const int a = fo + u >= g.pl_no[l] ? fo + u - g.pl_no[l] : fo + u;
+            const int b = fi + v >= g.pl_ni[l] ? fi + v - g.pl_ni[l] : fi + v;
+            const int bin = g.pl_base[l] + a * g.pl_ni[l] + b;
+            sbeg[i] = tv.offsets[bin];
+            spre[i + 1] = pair_active(g, tv.offsets, bin) ? 0 : tv.offsets[bin + 1] - sbeg[i];
+            scls[i] = atom_class(make_int4(0, F, 0, F));
+        }
+        for (int i = t; i < ncls; i += WT_THREADS) {
             int c = 0, rem = i, kr = 0, kc = 0;
             for (; c < g.nclass; ++c) {
                 kr = reach_tiles(c, g.tr[c], no);
@@ -233,41 +290,64 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
         for (int h0 = 0; h0 < n; h0 += WT_STAGE) {
             const int nb = min(WT_STAGE, n - h0);
             // 3. Stage: odd warps the tile columns (m_in), even warps the rows
-            // (amp * m_out); warps 0-1 take even hits, warps 2-3 odd ones.
-            // Main pass: classes with stored masses and no second image, one
-            // independent load per candidate; a second pass evaluates the rest.
+            // (amp * m_out). A warp stages four hits per pass, eight lanes per
+            // hit and four tile sites per lane; warps 0-1 take hit groups
+            // 0-3, 8-11, ..., warps 2-3 groups 4-7, 12-15, ... Main pass:
+            // classes with stored masses and no second image (independent
+            // loads); a second pass evaluates the rest of the same hits.
             {
-                const int side = warp & 1, p = lane, half = warp >> 1;
+                const int side = warp & 1, half = warp >> 1;
+                const int sub = lane >> 3, q = lane & 7;
                 const int lim = side ? TC : TR, nn = side ? ni : no;
-                const int site = (side ? C0 : R0) + p;
+                const int site0 = (side ? C0 : R0) + 4 * q;
                 float(*dst)[TS] = side ? vs : us;
                 bool rest = false;
-#pragma unroll 8
-                for (int s2 = half; s2 < nb; s2 += 2) {
-                    const int4 q = cspan[h0 + s2];
-                    const int f = side ? q.z : q.x, F = side ? q.w : q.y;
-                    const int c = ccls[h0 + s2];
-                    const long long atom = cand[h0 + s2];
-                    int j = site - f;
-                    j += j < 0 ? nn : 0;
-                    const bool stored = c >= 0 && c < NFINE && F <= nn;
-                    const float *src = c == 0 ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
-                                              : cache + (atom * 2 + side) * CACHE_SITES;
-                    float v = 0.f;
-                    const bool inside = p < lim && j < F;
-                    if (stored && inside) v = src[j];
-                    dst[s2][p] = side ? v : v * camp[h0 + s2];
-                    rest |= !stored;
+#pragma unroll 2
+                for (int s0 = 4 * half; s0 < nb; s0 += 8) {
+                    const int s2 = s0 + sub;
+                    unsigned nib = 0;
+                    if (s2 < nb) {
+                        const int4 qs = cspan[h0 + s2];
+                        const int f = side ? qs.z : qs.x, F = side ? qs.w : qs.y;
+                        const int c = ccls[h0 + s2];
+                        const long long atom = cand[h0 + s2];
+                        const bool stored = c >= 0 && c < NFINE && F <= nn;
+                        const float *src = c == 0 ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
+                                                  : cache + (atom * 2 + side) * CACHE_SITES;
+                        int j = site0 - f;
+                        j += j < 0 ? nn : 0;
+                        float v[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int ju = j + u >= nn ? j + u - nn : j + u;
+                            const bool row = 4 * q + u < lim;
+                            const bool inside = row && ju < F;
+                            v[u] = stored && inside ? src[ju] : 0.f;
+                            // With F > N every tile site is covered by some image.
+                            nib |= (inside || (row && F > nn)) ? 1u << u : 0u;
+                        }
+                        if (side == 0) {
+                            const float amp = camp[h0 + s2];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) v[u] *= amp;
+                        }
+                        *reinterpret_cast<float4 *>(&dst[s2][4 * q]) = make_float4(v[0], v[1], v[2], v[3]);
+                        rest |= !stored;
+                    }
                     if (side == 0) {
-                        // With F > N every tile row is covered by some image.
-                        const unsigned m = __ballot_sync(0xffffffffu, inside || (p < lim && F > nn));
-                        if (p == 0) rmask[s2] = m;
+                        unsigned m = nib << (4 * q);
+                        m |= __shfl_xor_sync(0xffffffffu, m, 1);
+                        m |= __shfl_xor_sync(0xffffffffu, m, 2);
+                        m |= __shfl_xor_sync(0xffffffffu, m, 4);
+                        if (s2 < nb && q == 0) rmask[s2] = m;
                     }
                 }
+                __syncwarp();
                 if (__any_sync(0xffffffffu, rest)) {
-                    for (int s2 = half; s2 < nb; s2 += 2) {
-                        const int4 q = cspan[h0 + s2];
-                        const int f = side ? q.z : q.x, F = side ? q.w : q.y;
+                    const int p = lane, site = (side ? C0 : R0) + p;
+                    for (int s2 = 4 * half; s2 < nb; s2 += (s2 & 3) == 3 ? 5 : 1) {
+                        const int4 qs = cspan[h0 + s2];
+                        const int f = side ? qs.z : qs.x, F = side ? qs.w : qs.y;
                         const int c = ccls[h0 + s2];
                         if (c >= 0 && c < NFINE && F <= nn) continue;
                         const long long atom = cand[h0 + s2];
@@ -309,6 +389,48 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
                 for (int ii = 0; ii < 2; ++ii)
 #pragma unroll
                     for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(uu[ii], vv[jj], acc[ii][jj]);
+            }
+            __syncthreads();
+        }
+    }
+
+    // 4. Active owner pairs: PF rank-one terms per covering output node a of an
+    // expansion level-bank that has an active pair, rows phi_f(site - a T)
+    // (images summed), columns R_a[f][site].
+    for (int l = 0; l < g.npl; ++l) {
+        if (!g.pl_exp[l]) continue;
+        const int T = g.pl_T[l], F = g.pl_K[l] * T, nno = g.pl_no[l];
+        int fo;
+        const int co = cover_nodes(R0, TR, T, F, nno, no, fo);
+        for (int u = 0; u < co; ++u) {
+            const int a = fo + u >= nno ? fo + u - nno : fo + u;
+            if (!tv.node_on[g.pl_node[l] + a]) continue; // CTA-uniform
+            if (t < 32) {
+                float phi[PF];
+                const bool on = t < TR && pair_basis(R0 + t - a * T, F, no, phi);
+#pragma unroll
+                for (int f = 0; f < PF; ++f) us[f][t] = on ? phi[f] : 0.f;
+                const unsigned m = __ballot_sync(0xffffffffu, on);
+                if (t < PF) rmask[t] = m;
+            } else {
+                const float *rb = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * ni + C0;
+                for (int e = t - 32; e < PF * TS; e += WT_THREADS - 32) {
+                    const int f = e / TS, c = e - f * TS;
+                    vs[f][c] = c < TC ? rb[(long long)f * ni + c] : 0.f;
+                }
+            }
+            __syncthreads();
+            const unsigned wrows = 0xFFu << (8 * warp);
+#pragma unroll 1
+            for (int s2 = 0; s2 < PF; ++s2) {
+                if (!(rmask[s2] & wrows)) continue;
+                const float2 uu = *reinterpret_cast<const float2 *>(&us[s2][r0]);
+                const float4 vv = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
+                const float ua[2] = {uu.x, uu.y}, va[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+                for (int ii = 0; ii < 2; ++ii)
+#pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(ua[ii], va[jj], acc[ii][jj]);
             }
             __syncthreads();
         }
@@ -577,7 +699,7 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
                     float *weight_hi_dev, float *weight_lo_dev, int64_t ld_split,
                     cudaStream_t st, float *amax_dev = nullptr) {
     const int words = record_words(oa.modes, ia.modes);
-    const Table tv = table_view(atom_table_dev, atoms, words, oa.sites, ia.sites, oa.modes, ia.modes);
+    const Table tv = table_view(atom_table_dev, atoms, words, axis_geo(oa), axis_geo(ia));
     float *cache = static_cast<float *>(scratch);
     if (atoms > 0 && tv.geom.nclass > 0) {
         // The class range is only known on the device; the kernel reads it.
@@ -585,6 +707,12 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
         TCST_CUDA(launch_pdl(mass_cache_kernel, dim3(unsigned((warps + 7) / 8)), dim3(256), 0, st, tv, cache));
         TCST_CUDA(cudaGetLastError());
     }
+    if (max_scan_entries(tv.geom, oa.sites, ia.sites) > MAX_SCAN) {
+        tcst_set_error("weight assembly: a weight tile would scan more than %d bins", MAX_SCAN);
+        return TCST_ERR_UNSUPPORTED;
+    }
+    int rc;
+    if ((rc = pair_forward(tv, oa, ia, st))) return rc;
     const int tiles_r = (oa.sites + TS - 1) / TS, tiles_c = (ia.sites + TS - 1) / TS;
     GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split, amax_dev};
     TCST_CUDA(launch_pdl(weight_gather_kernel, dim3(unsigned(tiles_r * tiles_c)), dim3(WT_THREADS), 0, st, 

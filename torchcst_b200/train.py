@@ -2,15 +2,15 @@
 
 Computes exactly what ``y = layer(x); ((y - t)**2).mean().backward();
 optimizer.step()`` computes, without autograd bookkeeping: the MSE upstream
-gradient is produced directly as TF32 split planes by the loss kernel, every
-buffer is allocated once, and the step is a fixed sequence of native launches
-on the current stream:
+gradient is produced by the epilogue of the forward GEMM (Y itself is never
+stored), every buffer is allocated once, and the step is a fixed sequence of
+native launches on the current stream:
 
     decode/route -> bin sort (count, column prefix, scatter) -> weight (mass
-    cache, tile gather with max |W|, f16 split) | f16 split of X -> GEMM Y ->
-    MSE dY (float32, with absmax) -> f16 split of dY -> GEMM dX -> GEMM dW
-    (split-K) -> pullback (split-K sum, three footprint classes, wide atoms) ->
-    optimizer
+    cache, tile gather with max |W|, f16 split) | f16 split of X -> GEMM Y
+    with the MSE epilogue (dY, loss partials, max |dY|) -> f16 split of dY ->
+    GEMM dX -> GEMM dW (split-K) -> pullback (split-K sum, three footprint
+    classes, wide atoms) -> optimizer
 
 The optimizer reads its per-step scalars (bias corrections) from device memory,
 refreshed from a pinned host ring before each step, so :meth:`capture` can
@@ -52,7 +52,7 @@ def dp_reduce_gradient(grad: torch.Tensor, process_group=None) -> torch.Tensor:
 
 
 class MSETrainStep:
-    LAUNCHES_PER_STEP = 20  # native kernels; torch adds the loss sum, one clear and one copy
+    LAUNCHES_PER_STEP = 19  # native kernels; torch adds the loss sum, one clear and one copy
     RING = 64
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
@@ -80,14 +80,16 @@ class MSETrainStep:
                               scale=self.scales[1:2])
         self.dy16 = R.F16Split(self.rows, plan.n_out, dev, amax=self.amax[2:3],
                                scale=self.scales[2:3])
-        self.y = torch.empty(self.rows, plan.n_out, dtype=f32, device=dev)  # Y, then dY
+        self.y = torch.empty(self.rows, plan.n_out, dtype=f32, device=dev)  # dY
         self.dx = torch.empty(self.rows, plan.n_in, dtype=f32, device=dev) if need_dx else None
         self.split = R.weight_split_k(plan, self.rows)
         self.ldg = R.pad4(plan.n_in)
         self.gstride = plan.n_out * self.ldg
         self.g = torch.empty(self.split * self.gstride, dtype=f32, device=dev)
         self.grad = torch.empty(A, 4, dtype=f32, device=dev)
-        self.partial = torch.empty(1024, dtype=torch.float64, device=dev)
+        # One loss partial per 32 rows of every 128 x 256 tile of the Y GEMM.
+        tiles = -(-plan.n_out // 256) * -(-self.rows // 128)
+        self.partial = torch.empty(max(4 * tiles, 1), dtype=torch.float64, device=dev)
         self.scale = dp_loss_scale(self.rows, plan.n_out, world_rows)
         self.nblocks = ctypes.c_int32(0)
         nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
@@ -168,11 +170,12 @@ class MSETrainStep:
                                              vp(w16.amax), vp(w16.hi), vp(w16.lo), w16.ld,
                                              vp(w16.scale), st), "weight")
         main.wait_stream(side)
-        gemm(rows, plan.n_out, plan.n_in, x16, 0, w16, 0, self.y, plan.n_out, what="gemm y")
-        N.check(lib.tcst_mse_grad_f32(vp(self.y), vp(target), rows, plan.n_out, plan.n_out,
-                                      ctypes.c_float(self.scale), vp(self.y), plan.n_out,
-                                      vp(self.partial), ctypes.byref(self.nblocks),
-                                      vp(dy16.amax), st), "mse")
+        N.check(lib.tcst_gemm_f16x3_mse(rows, plan.n_out, plan.n_in, vp(x16.hi), vp(x16.lo),
+                                        x16.ld, vp(x16.scale), vp(w16.hi), vp(w16.lo), w16.ld,
+                                        vp(w16.scale), vp(target), plan.n_out,
+                                        ctypes.c_float(self.scale), vp(self.y), plan.n_out,
+                                        vp(self.partial), ctypes.byref(self.nblocks),
+                                        vp(dy16.amax), vp(ws.status), st), "gemm y + mse")
         N.check(lib.tcst_split_f16(vp(self.y), rows, plan.n_out, plan.n_out, vp(dy16.amax),
                                    vp(dy16.hi), vp(dy16.lo), dy16.ld, vp(dy16.scale), st),
                 "split dy")
