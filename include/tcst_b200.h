@@ -148,6 +148,20 @@ int tcst_assemble_weight_f16(const void *atom_table_dev, int64_t atoms,
                              int64_t ld_weight, float *amax_dev, void *hi_dev, void *lo_dev,
                              int64_t ld_split, float *scale_dev, void *stream);
 
+/* A window W[row0 : row0 + rows, col0 : col0 + cols] of the same weight
+ * (row0 and col0 multiples of 32; W[r][c] stored at (r - row0, c - col0)),
+ * with its own max |W| and f16 split: the output-row band (and input-column
+ * band) of one rank when a layer is sharded by output rows. No counterpart in
+ * the reference (its layer is not sharded). Values equal the full assembly's
+ * bit for bit. */
+int tcst_assemble_weight_window_f16(const void *atom_table_dev, int64_t atoms,
+                                    const tcst_axis *out_axis, const tcst_axis *in_axis,
+                                    void *scratch_dev, int64_t scratch_bytes, int64_t row0,
+                                    int64_t rows, int64_t col0, int64_t cols, float *weight_dev,
+                                    int64_t ld_weight, float *amax_dev, void *hi_dev,
+                                    void *lo_dev, int64_t ld_split, float *scale_dev,
+                                    void *stream);
+
 /* No counterpart in the reference. The same weight assembly as
  * tcst_assemble_weight for callers that cannot allocate device memory (a plugin
  * inside a host framework whose allocator owns the device, or a fixed-footprint
@@ -236,6 +250,17 @@ int tcst_mse_grad_f32(const float *y_dev, const float *target_dev, int64_t rows,
 int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
                   const tcst_axis *in_axis, float *g_dev, int64_t ldg,
                   int32_t split, int64_t split_stride, float *grad_dev, void *stream);
+
+/* tcst_pullback over the chart rows [row0, row0 + rows) of G only (g_dev holds
+ * those rows, row0 first; split partials as tcst_pullback): every atom gets
+ * the part of its gradient that its footprint rows inside the band
+ * contribute, atoms outside the band get zero. Summed over a partition of the
+ * rows this is tcst_pullback's gradient (up to float32 summation order): the
+ * halo-atom reduction of a layer sharded by output rows. */
+int tcst_pullback_band(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
+                       const tcst_axis *in_axis, float *g_dev, int64_t ldg, int32_t split,
+                       int64_t split_stride, int64_t row0, int64_t rows, float *grad_dev,
+                       void *stream);
 
 /* Fused CSTAdamW step on [atoms][4] rows, in place: AdamW moments and proposal,
  * field_lrs rescale, then the rational projection

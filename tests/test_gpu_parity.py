@@ -409,3 +409,40 @@ def test_empty_batch_and_atoms(R):
     assert y.shape == (0, 8)
     y.sum().backward()
     assert torch.count_nonzero(layer.atoms.p.grad) == 0
+
+
+# -- output-row bands (sharded layer) --------------------------------------------------
+
+
+@pytest.mark.parametrize("name,bands", [("config2", 4), ("config5s", 4), ("config4s", 2)])
+def test_band_windows_and_pullback_match_full(R, name, bands):
+    """Weight windows equal the full assembly bit for bit; band pullbacks sum
+    to the full pullback (float32 summation order aside)."""
+    d = load(name)
+    layer = make_layer(name, d["p0"])
+    plan, p = layer._plan, layer.atoms.p
+    ws = layer._workspace(p.device)
+    A = p.shape[0]
+    table = R.decode_route(plan, p, ws.status)
+    w_full, _, _, _ = R.assemble_weight(plan, table, A, ws, dense=True, split=False)
+    no, ni = plan.n_out, plan.n_in
+    rb, cb = no // bands, ni // bands
+    for k in range(bands):
+        w, sp = R.assemble_weight_window_f16(plan, table, A, ws, k * rb, rb, 0, ni)
+        assert torch.equal(w, w_full[k * rb:(k + 1) * rb])
+        assert float(sp.amax[0]) == float(w.abs().max())
+        w, _ = R.assemble_weight_window_f16(plan, table, A, ws, 0, no, k * cb, cb)
+        assert torch.equal(w, w_full[:, k * cb:(k + 1) * cb])
+    # Pullback: restore the full assembly's owner-pair state, then compare.
+    R.assemble_weight(plan, table, A, ws, dense=True, split=False)
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    ldg = R.pad4(ni)
+    G = torch.randn(no, ldg, device="cuda", generator=gen) * 1e-3
+    full = R.pullback(plan, table, A, G.clone(), ldg, 1, 0, p.device)
+    acc = torch.zeros_like(full, dtype=torch.float64)
+    for k in range(bands):
+        gb = G[k * rb:(k + 1) * rb].clone()
+        acc += R.pullback_band(plan, table, A, gb, ldg, 1, 0, k * rb, rb, p.device).double()
+    torch.cuda.synchronize()
+    for col in range(4):
+        assert rel(acc[:, col].cpu(), full[:, col].double().cpu()) < 1e-5, col

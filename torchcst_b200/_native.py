@@ -103,12 +103,17 @@ SIGNATURES = {
                                            P, P]),
     "tcst_assemble_weight_f16": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis),
                                                 P, I64, P, I64, P, P, P, I64, P, P]),
+    "tcst_assemble_weight_window_f16": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis),
+                                                       ctypes.POINTER(Axis), P, I64, I64, I64,
+                                                       I64, I64, P, I64, P, P, P, I64, P, P]),
     "tcst_absmax": (ctypes.c_int, [P, I64, I64, I64, P, P]),
     "tcst_split_f16": (ctypes.c_int, [P, I64, I64, I64, P, P, P, I64, P, P]),
     "tcst_mse_grad_f32": (ctypes.c_int, [P, P, I64, I64, I64, ctypes.c_float, P, I64, P,
                                          ctypes.POINTER(I32), P, P]),
     "tcst_pullback": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis),
                                      P, I64, I32, I64, P, P]),
+    "tcst_pullback_band": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis),
+                                          P, I64, I32, I64, I64, I64, P, P]),
     "tcst_optimizer_step": (ctypes.c_int, [P, P, P, P, I64, I32, ctypes.POINTER(AdamW), P]),
     "tcst_optimizer_step_device": (ctypes.c_int, [P, P, P, P, I64, I32, P, P]),
     "tcst_mse_grad": (ctypes.c_int, [P, P, I64, I64, I64, ctypes.c_float, P, P, I64, P,

@@ -187,9 +187,9 @@ constexpr int SORT_CHUNK = 512;  // atoms per sort block (128 blocks, more for >
 constexpr int CACHE_SITES = 128; // masses cached per axis for classes 1..NFINE-1
 constexpr int PF = 17;                // owner-pair basis functions per axis (M = 8)
 constexpr int MAX_PAIR_LB = 32;       // pair level-banks
-constexpr int PAIR_MIN = 4;           // atoms that make an owner pair active
+constexpr int PAIR_MIN = 2;           // atoms that make an owner pair active
 constexpr int PAIR_BIN_CAP = 16384;   // owner pairs of a level-bank binned as pairs
-constexpr int PAIR_EXPAND_CAP = 4096; // owner pairs of a level-bank with an expansion buffer
+constexpr int PAIR_EXPAND_CAP = 16384; // owner pairs of a level-bank with an expansion buffer
 
 // What the bin geometry needs of an axis.
 struct AxisGeo {

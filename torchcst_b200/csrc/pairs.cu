@@ -30,6 +30,8 @@
 //   pair_grad_kernel     per active pair H_ab = P_a Phi_b, then the gradient
 //                        of each of its atoms.
 
+#include <algorithm>
+
 #include "pairs.cuh"
 
 namespace tcst {
@@ -80,34 +82,37 @@ __device__ __forceinline__ void axis_alpha(const float *blk, float *alpha, float
 __global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw) {
     pdl_wait();
     const BinGeom &g = tv.geom;
-    const int bin = g.pl_base[0] + blockIdx.x;
-    if (!pair_active(g, tv.offsets, bin)) return;
-    const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
     __shared__ float sa[PC_CHUNK][2 * PF + 1];
     const int t = threadIdx.x;
     const int f = t / PF, gg = t - f * PF;
-    float acc = 0.f;
-    for (int k0 = begin; k0 < end; k0 += PC_CHUNK) {
-        const int n = min(PC_CHUNK, end - k0);
-        if (t < n) {
-            const long long a = tv.ids[k0 + t];
-            const float *rec = tv.rec + a * (long long)tv.words;
-            float ao[PF], ai[PF];
-            axis_alpha(rec + 4, ao, nullptr, nullptr);
-            axis_alpha(rec + 4 + aw, ai, nullptr, nullptr);
-            const float amp = rec[0];
+    const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
+    for (int pb = blockIdx.x; pb < pair_bins; pb += gridDim.x) {
+        const int bin = g.pl_base[0] + pb;
+        if (!pair_active(g, tv.offsets, bin)) continue; // CTA-uniform
+        const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
+        float acc = 0.f;
+        for (int k0 = begin; k0 < end; k0 += PC_CHUNK) {
+            const int n = min(PC_CHUNK, end - k0);
+            if (t < n) {
+                const long long a = tv.ids[k0 + t];
+                const float *rec = tv.rec + a * (long long)tv.words;
+                float ao[PF], ai[PF];
+                axis_alpha(rec + 4, ao, nullptr, nullptr);
+                axis_alpha(rec + 4 + aw, ai, nullptr, nullptr);
+                const float amp = rec[0];
 #pragma unroll
-            for (int e = 0; e < PF; ++e) {
-                sa[t][e] = amp * ao[e];
-                sa[t][PF + e] = ai[e];
+                for (int e = 0; e < PF; ++e) {
+                    sa[t][e] = amp * ao[e];
+                    sa[t][PF + e] = ai[e];
+                }
             }
+            __syncthreads();
+            if (t < PF * PF)
+                for (int j = 0; j < n; ++j) acc = fmaf(sa[j][f], sa[j][PF + gg], acc);
+            __syncthreads();
         }
-        __syncthreads();
-        if (t < PF * PF)
-            for (int j = 0; j < n; ++j) acc = fmaf(sa[j][f], sa[j][PF + gg], acc);
-        __syncthreads();
+        if (t < PF * PF) tv.pair_c[(long long)pb * PF * PF + t] = acc;
     }
-    if (t < PF * PF) tv.pair_c[(long long)blockIdx.x * PF * PF + t] = acc;
 }
 
 // CTA -> (expansion level-bank l, output node a, input chunk ch).
@@ -126,12 +131,28 @@ __device__ __forceinline__ bool expand_cta(const BinGeom &g, int chunks, int &l,
     return true;
 }
 
-__global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_in) {
+// Whether output node a of level-bank l covers a row of [r0, r0 + wr).
+__device__ __forceinline__ bool node_covers(const BinGeom &g, int l, int a, int r0, int wr,
+                                            int n_out) {
+    int first;
+    const int T = g.pl_T[l];
+    const int cnt = cover_nodes(r0, wr, T, g.pl_K[l] * T, g.pl_no[l], n_out, first);
+    int d = a - first;
+    d += d < 0 ? g.pl_no[l] : 0;
+    return d < cnt;
+}
+
+__global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_out, int n_in,
+                                                               Window win) {
     pdl_wait();
     const BinGeom &g = tv.geom;
     const int chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
     int l, a, ch;
     if (!expand_cta(g, chunks, l, a, ch)) return;
+    // Only nodes over the window's rows and chunks over its columns are read
+    // by the gather that follows (CTA-uniform exits).
+    if (!node_covers(g, l, a, win.r0, win.wr, n_out)) return;
+    if ((ch + 1) * PX_CHUNK <= win.c0 || ch * PX_CHUNK >= win.c0 + win.wc) return;
     const int T = g.pl_T[l], F = g.pl_K[l] * T, nb = g.pl_ni[l];
     const int i = ch * PX_CHUNK + threadIdx.x;
     __shared__ float C[PF * PF];
@@ -158,7 +179,7 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_i
             }
         }
     }
-    if (ch == 0 && threadIdx.x == 0) tv.node_on[g.pl_node[l] + a] = any ? 1 : 0;
+    if (ch == win.c0 / PX_CHUNK && threadIdx.x == 0) tv.node_on[g.pl_node[l] + a] = any ? 1 : 0;
     if (any && i < n_in) {
         float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in + i;
 #pragma unroll
@@ -166,15 +187,24 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_i
     }
 }
 
+// G holds chart rows [band.r0, band.r0 + band.wr) at gm + (row - band.r0) ldg.
 __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_out, int n_in,
                                                                 const float *__restrict__ gm,
-                                                                long long ldg) {
+                                                                long long ldg, Window band) {
     pdl_wait();
     const BinGeom &g = tv.geom;
     const int chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
     int l, a, ch;
     if (!expand_cta(g, chunks, l, a, ch)) return;
-    if (!tv.node_on[g.pl_node[l] + a]) return;
+    if (!node_covers(g, l, a, band.r0, band.wr, n_out)) return;
+    {
+        bool any = false; // an active partner (CTA-uniform)
+        for (int b = 0; b < g.pl_ni[l] && !any; ++b) {
+            const int bin = g.pl_base[l] + a * g.pl_ni[l] + b;
+            any = tv.offsets[bin + 1] - tv.offsets[bin] >= PAIR_MIN;
+        }
+        if (!any) return;
+    }
     const int T = g.pl_T[l], F = g.pl_K[l] * T;
     const int i = ch * PX_CHUNK + threadIdx.x;
     // Distinct chart rows of the footprint: all rows when it wraps onto itself.
@@ -191,16 +221,18 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
             float phi[PF];
             int row = row0 + r0 + threadIdx.x;
             row -= row >= n_out ? n_out : 0;
+            const bool in = row >= band.r0 && row < band.r0 + band.wr;
             pair_basis(row - a * T, F, n_out, phi);
 #pragma unroll
-            for (int f = 0; f < PF; ++f) sphi[threadIdx.x][f] = phi[f];
+            for (int f = 0; f < PF; ++f) sphi[threadIdx.x][f] = in ? phi[f] : 0.f;
         }
         __syncthreads();
         if (i < n_in) {
             for (int j = 0; j < nr; ++j) {
                 int row = row0 + r0 + j;
                 row -= row >= n_out ? n_out : 0;
-                const float gv = gm[(long long)row * ldg + i];
+                if (row < band.r0 || row >= band.r0 + band.wr) continue;
+                const float gv = gm[(long long)(row - band.r0) * ldg + i];
 #pragma unroll
                 for (int f = 0; f < PF; ++f) p[f] = fmaf(sphi[j][f], gv, p[f]);
             }
@@ -213,121 +245,131 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
     }
 }
 
-__global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_in,
-                                                        float4 *__restrict__ grad) {
+__global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_out, int n_in,
+                                                        Window band, float4 *__restrict__ grad) {
     pdl_wait();
     const BinGeom &g = tv.geom;
-    const int bin = g.pl_base[0] + blockIdx.x;
-    if (!pair_active(g, tv.offsets, bin)) return;
-    const int l = pair_lb(g, bin);
-    const int nb = g.pl_ni[l], idx = bin - g.pl_base[l];
-    const int a = idx / nb, b = idx - a * nb;
-    const int T = g.pl_T[l], F = g.pl_K[l] * T;
-    const int cols = F >= n_in ? n_in : F;
-    const int col0 = F >= n_in ? 0 : b * T;
-    const float *P = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in;
     __shared__ float sp[PF][PG_COLS + 1];
     __shared__ float sphi[PG_COLS][PF + 1];
     __shared__ float H[PF * PF];
     const int t = threadIdx.x;
     const int f = t / PF, gg = t - f * PF;
-    float acc = 0.f;
-    for (int c0 = 0; c0 < cols; c0 += PG_COLS) {
-        const int nc = min(PG_COLS, cols - c0);
-        __syncthreads();
-        for (int e = t; e < PF * nc; e += blockDim.x) {
-            const int ff = e / nc, j = e - ff * nc;
-            int col = col0 + c0 + j;
-            col -= col >= n_in ? n_in : 0;
-            sp[ff][j] = P[(long long)ff * n_in + col];
-        }
-        if (t < nc) {
-            float phi[PF];
-            int col = col0 + c0 + t;
-            col -= col >= n_in ? n_in : 0;
-            pair_basis(col - b * T, F, n_in, phi);
-#pragma unroll
-            for (int e = 0; e < PF; ++e) sphi[t][e] = phi[e];
-        }
-        __syncthreads();
-        if (t < PF * PF)
-            for (int j = 0; j < nc; ++j) acc = fmaf(sp[f][j], sphi[j][gg], acc);
-    }
-    if (t < PF * PF) H[t] = acc;
-    __syncthreads();
-    // Every atom of the pair: one warp, lanes over rows f of H.
     const int lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
-    const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
-    for (int k = begin + warp; k < end; k += nw) {
-        const long long atom = tv.ids[k];
-        const float *rec = tv.rec + atom * (long long)tv.words;
-        float ao[PF], mo[PF], ro[PF], ai[PF], mi[PF], ri[PF];
-        axis_alpha(rec + 4, ao, mo, ro);
-        axis_alpha(rec + 4 + aw, ai, mi, ri);
-        float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
-        if (lane < PF) {
-            float h1 = 0.f, h2 = 0.f, h3 = 0.f;
-#pragma unroll
-            for (int e = 0; e < PF; ++e) {
-                const float hv = H[lane * PF + e];
-                h1 = fmaf(hv, ai[e], h1);
-                h2 = fmaf(hv, mi[e], h2);
-                h3 = fmaf(hv, ri[e], h3);
+    const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
+    for (int pb = blockIdx.x; pb < pair_bins; pb += gridDim.x) {
+        const int bin = g.pl_base[0] + pb;
+        if (!pair_active(g, tv.offsets, bin)) continue; // CTA-uniform
+        const int l = pair_lb(g, bin);
+        const int nb = g.pl_ni[l], idx = bin - g.pl_base[l];
+        const int a = idx / nb, b = idx - a * nb;
+        // Outside the band the pair's rows contribute nothing (zero gradient).
+        if (!node_covers(g, l, a, band.r0, band.wr, n_out)) continue;
+        const int T = g.pl_T[l], F = g.pl_K[l] * T;
+        const int cols = F >= n_in ? n_in : F;
+        const int col0 = F >= n_in ? 0 : b * T;
+        const float *P = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in;
+        // H = P_a Phi_b over the distinct chart columns of b's footprint.
+        float acc = 0.f;
+        for (int c0 = 0; c0 < cols; c0 += PG_COLS) {
+            const int nc = min(PG_COLS, cols - c0);
+            __syncthreads();
+            for (int e = t; e < PF * nc; e += blockDim.x) {
+                const int ff = e / nc, j = e - ff * nc;
+                int col = col0 + c0 + j;
+                col -= col >= n_in ? n_in : 0;
+                sp[ff][j] = P[(long long)ff * n_in + col];
             }
-            // Row `lane` of the output-side vectors (registers are indexed
-            // statically, so select by a loop).
-            float a_f = 0.f, m_f = 0.f, r_f = 0.f;
+            if (t < nc) {
+                float phi[PF];
+                int col = col0 + c0 + t;
+                col -= col >= n_in ? n_in : 0;
+                pair_basis(col - b * T, F, n_in, phi);
 #pragma unroll
-            for (int e = 0; e < PF; ++e)
-                if (e == lane) {
-                    a_f = ao[e];
-                    m_f = mo[e];
-                    r_f = ro[e];
+                for (int e = 0; e < PF; ++e) sphi[t][e] = phi[e];
+            }
+            __syncthreads();
+            if (t < PF * PF)
+                for (int j = 0; j < nc; ++j) acc = fmaf(sp[f][j], sphi[j][gg], acc);
+        }
+        if (t < PF * PF) H[t] = acc;
+        __syncthreads();
+        // Every atom of the pair: one warp, lanes over rows f of H.
+        const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
+        for (int k = begin + warp; k < end; k += nw) {
+            const long long atom = tv.ids[k];
+            const float *rec = tv.rec + atom * (long long)tv.words;
+            float ao[PF], mo[PF], ro[PF], ai[PF], mi[PF], ri[PF];
+            axis_alpha(rec + 4, ao, mo, ro);
+            axis_alpha(rec + 4 + aw, ai, mi, ri);
+            float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
+            if (lane < PF) {
+                float h1 = 0.f, h2 = 0.f, h3 = 0.f;
+#pragma unroll
+                for (int e = 0; e < PF; ++e) {
+                    const float hv = H[lane * PF + e];
+                    h1 = fmaf(hv, ai[e], h1);
+                    h2 = fmaf(hv, mi[e], h2);
+                    h3 = fmaf(hv, ri[e], h3);
                 }
-            s_amp = a_f * h1;
-            s_mo = m_f * h1;
-            s_mi = a_f * h2;
-            s_r = fmaf(r_f, h1, a_f * h3);
-        }
+                // Row `lane` of the output-side vectors (registers are indexed
+                // statically, so select by a loop).
+                float a_f = 0.f, m_f = 0.f, r_f = 0.f;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            s_amp += __shfl_xor_sync(0xffffffffu, s_amp, off);
-            s_mo += __shfl_xor_sync(0xffffffffu, s_mo, off);
-            s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
-            s_r += __shfl_xor_sync(0xffffffffu, s_r, off);
+                for (int e = 0; e < PF; ++e)
+                    if (e == lane) {
+                        a_f = ao[e];
+                        m_f = mo[e];
+                        r_f = ro[e];
+                    }
+                s_amp = a_f * h1;
+                s_mo = m_f * h1;
+                s_mi = a_f * h2;
+                s_r = fmaf(r_f, h1, a_f * h3);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                s_amp += __shfl_xor_sync(0xffffffffu, s_amp, off);
+                s_mo += __shfl_xor_sync(0xffffffffu, s_mo, off);
+                s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
+                s_r += __shfl_xor_sync(0xffffffffu, s_r, off);
+            }
+            if (lane == 0) grad[atom] = atom_chain(rec, s_amp, s_mo, s_mi, s_r);
         }
-        if (lane == 0) grad[atom] = atom_chain(rec, s_amp, s_mo, s_mi, s_r);
+        __syncthreads(); // H and the staging buffers are reused by the next pair
     }
 }
 
-int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, cudaStream_t st) {
+int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const Window &win,
+                 cudaStream_t st) {
     const BinGeom &g = tv.geom;
     if (g.npl == 0 || tv.atoms == 0) return TCST_OK;
     const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
     const int aw = axis_words(oa.modes);
-    TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(unsigned(pair_bins)), dim3(320), 0, st, tv, aw));
+    const unsigned grid = unsigned(std::min<long long>(pair_bins, 148LL * 4));
+    TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(grid), dim3(320), 0, st, tv, aw));
     TCST_CUDA(cudaGetLastError());
     const long long ctas = expand_ctas(g, ia.sites);
     if (ctas > 0) {
         TCST_CUDA(launch_pdl(pair_expand_kernel, dim3(unsigned(ctas)), dim3(PX_CHUNK), 0, st, tv,
-                             ia.sites));
+                             oa.sites, ia.sites, win));
         TCST_CUDA(cudaGetLastError());
     }
     return TCST_OK;
 }
 
 int pair_backward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const float *g_dev,
-                  long long ldg, float4 *grad, cudaStream_t st) {
+                  long long ldg, const Window &band, float4 *grad, cudaStream_t st) {
     const BinGeom &g = tv.geom;
     if (g.npl == 0 || tv.atoms == 0) return TCST_OK;
     const long long ctas = expand_ctas(g, ia.sites);
     if (ctas == 0) return TCST_OK;
     TCST_CUDA(launch_pdl(pair_project_kernel, dim3(unsigned(ctas)), dim3(PX_CHUNK), 0, st, tv,
-                         oa.sites, ia.sites, g_dev, ldg));
+                         oa.sites, ia.sites, g_dev, ldg, band));
     TCST_CUDA(cudaGetLastError());
     const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
-    TCST_CUDA(launch_pdl(pair_grad_kernel, dim3(unsigned(pair_bins)), dim3(320), 0, st, tv,
-                         axis_words(oa.modes), ia.sites, grad));
+    const unsigned grid = unsigned(std::min<long long>(pair_bins, 148LL * 4));
+    TCST_CUDA(launch_pdl(pair_grad_kernel, dim3(grid), dim3(320), 0, st, tv,
+                         axis_words(oa.modes), oa.sites, ia.sites, band, grad));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

@@ -6,6 +6,31 @@
 
 namespace tcst {
 
+// A window W[r0 : r0 + wr, c0 : c0 + wc] of the weight (r0, c0 multiples of the
+// weight tile), or of G's rows in the pullback.
+struct Window {
+    int r0, c0, wr, wc;
+};
+
+// Nodes (first tiles of T sites, nn of them on an axis of n sites) whose F-site
+// footprint covers some site of [t0, t0 + tl): `count` consecutive nodes from
+// `first` (mod nn). Node a covers the tile iff t0 - F < a T <= t0 + tl - 1
+// modulo n.
+__host__ __device__ __forceinline__ int cover_nodes(int t0, int tl, int T, int F, int nn, int n,
+                                                    int &first) {
+    first = 0;
+    if (F + tl - 1 >= n) return nn;
+    const int x = t0 - F + 1;
+    const int lo = x >= 0 ? (x + T - 1) / T : -((-x) / T);
+    const int hi = (t0 + tl - 1) / T;
+    const int cnt = hi - lo + 1;
+    if (cnt >= nn) return nn;
+    first = lo % nn;
+    first += first < 0 ? nn : 0;
+    return cnt;
+}
+
+
 // Sum over the images of one chart site of the PF footprint functions
 // {1, cos 2 pi k j / F, sin 2 pi k j / F}: d is the site minus the footprint
 // start (any integer), images j = d mod n, d mod n + n, ... < F on an axis of
@@ -41,12 +66,16 @@ __device__ __forceinline__ bool pair_basis(int d, int F, int n, float *phi) {
 long long expand_ctas(const BinGeom &g, int n_in);
 
 // C of every active pair, then R and the node flags of the expansion
-// level-banks (before the weight gather, which reads them).
-int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, cudaStream_t st);
+// level-banks for the nodes and columns the window's gather reads (before that
+// gather).
+int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const Window &win,
+                 cudaStream_t st);
 
-// P = Phi^T G per flagged node, then the gradients of the atoms of active
-// pairs (G summed over split-K partials, leading dimension ldg).
+// P = Phi^T G per output node with an active pair, over the band's rows (G
+// holds chart rows [band.r0, band.r0 + band.wr), summed over split-K
+// partials, leading dimension ldg), then the gradients of the atoms of active
+// pairs.
 int pair_backward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const float *g_dev,
-                  long long ldg, float4 *grad, cudaStream_t st);
+                  long long ldg, const Window &band, float4 *grad, cudaStream_t st);
 
 } // namespace tcst

@@ -33,6 +33,15 @@ constexpr int P0_THREADS = 256;
 constexpr int PC_THREADS = 256;
 constexpr int PC_WARPS = PC_THREADS / 32;
 
+// Whether chart rows {(r + k) mod n : 0 <= k < w} (0 <= r < n) meet the band
+// [b0, b0 + bn) (0 <= b0, b0 + bn <= n).
+__device__ __forceinline__ bool rows_meet(int r, int w, int n, int b0, int bn) {
+    if (bn >= n || w >= n) return true;
+    const int e = r + w;
+    if (e <= n) return r < b0 + bn && b0 < e;
+    return r < b0 + bn || b0 < e - n;
+}
+
 // G_0 += G_1 + ... + G_{split-1}, in place (rows of ni valid columns).
 __global__ void g_reduce_kernel(float *__restrict__ g, int no, int ni, long long ldg, int split,
                                 long long split_stride) {
@@ -71,7 +80,7 @@ __global__ void g_reduce4_kernel(float4 *__restrict__ g, int no, int ni4, long l
 template <int W, int PITCH>
 __device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, int ni,
                                              const float *__restrict__ g, long long ldg, int split,
-                                             long long split_stride) {
+                                             long long split_stride, int b0, int bn) {
     constexpr int W4 = (W + 3) / 4; // float4 columns per row (PITCH >= 4 * W4)
     static_assert(PITCH >= 4 * W4 && PITCH % 4 == 0, "window pitch");
     const bool vec = split == 1 && C0 + 4 * W4 <= ni && ldg % 4 == 0 && C0 % 4 == 0 &&
@@ -89,7 +98,10 @@ __device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, 
                     const int rl = i / W4, c4 = i - rl * W4;
                     int row = R0 + rl;
                     while (row >= no) row -= no;
-                    v[u] = *reinterpret_cast<const float4 *>(g + (long long)row * ldg + C0 + 4 * c4);
+                    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (row >= b0 && row < b0 + bn)
+                        v[u] = *reinterpret_cast<const float4 *>(g + (long long)(row - b0) * ldg +
+                                                                 C0 + 4 * c4);
                     dst[u] = rl * PITCH + 4 * c4;
                 }
             }
@@ -113,9 +125,11 @@ __device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, 
                 int row = R0 + rl, col = C0 + cl;
                 while (row >= no) row -= no;
                 while (col >= ni) col -= ni;
-                const float *gp = g + (long long)row * ldg + col;
-                v[u] = gp[0];
-                for (int s = 1; s < split; ++s) v[u] += gp[s * split_stride];
+                if (row >= b0 && row < b0 + bn) {
+                    const float *gp = g + (long long)(row - b0) * ldg + col;
+                    v[u] = gp[0];
+                    for (int s = 1; s < split; ++s) v[u] += gp[s * split_stride];
+                }
                 dst[u] = rl * PITCH + cl;
             }
         }
@@ -130,7 +144,8 @@ __device__ __forceinline__ void stage_window(float *gw, int R0, int C0, int no, 
 template <int PITCH>
 __device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_lo, int c_hi,
                                            int R0, int C0, int no, int ni,
-                                           const float *__restrict__ g, long long ldg) {
+                                           const float *__restrict__ g, long long ldg, int b0,
+                                           int bn) {
     c_lo &= ~3;
     const int nr = r_hi - r_lo, n4 = (c_hi - c_lo + 3) >> 2;
     if (nr <= 0 || n4 <= 0) return;
@@ -149,8 +164,10 @@ __device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_
                     const int rr = i / n4, c4 = i - rr * n4;
                     int row = R0 + r_lo + rr;
                     while (row >= no) row -= no;
-                    v[u] = *reinterpret_cast<const float4 *>(g + (long long)row * ldg + C0 + c_lo +
-                                                             4 * c4);
+                    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (row >= b0 && row < b0 + bn)
+                        v[u] = *reinterpret_cast<const float4 *>(g + (long long)(row - b0) * ldg +
+                                                                 C0 + c_lo + 4 * c4);
                     dst[u] = (r_lo + rr) * PITCH + c_lo + 4 * c4;
                 }
             }
@@ -173,7 +190,7 @@ __device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_
                 int row = R0 + r_lo + rr, col = C0 + c_lo + cc;
                 while (row >= no) row -= no;
                 while (col >= ni) col -= ni;
-                v[u] = g[(long long)row * ldg + col];
+                v[u] = row >= b0 && row < b0 + bn ? g[(long long)(row - b0) * ldg + col] : 0.f;
                 dst[u] = (r_lo + rr) * PITCH + c_lo + cc;
             }
         }
@@ -189,7 +206,7 @@ __device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_
 // a fixed xor order.
 __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     Table tv, int no, int ni, const float *__restrict__ g, long long ldg, int split,
-    long long split_stride, float4 *__restrict__ grad) {
+    long long split_stride, int b0, int bn, float4 *__restrict__ grad) {
     pdl_wait();
     constexpr int W = TS + REACH - 1;
     constexpr int PITCH = W + 1;
@@ -198,9 +215,9 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     const int tr = blockIdx.x / ct, tc = blockIdx.x - tr * ct;
     const int bin = tv.geom.base[0] + blockIdx.x; // class 0 bins, row-major by tile
     const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
-    if (begin == end) return;
     const int R0 = tr * TS, C0 = tc * TS;
-    stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
+    if (begin == end || !rows_meet(R0, W, no, b0, bn)) return;
+    stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride, b0, bn);
     __syncthreads();
     const int lane = threadIdx.x & 31, q = lane & 3;
     const int quads = blockDim.x >> 2;
@@ -269,7 +286,7 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
 template <int RC>
 __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     Table tv, int cls, int no, int ni, const float *__restrict__ g, long long ldg, int split,
-    long long split_stride, float4 *__restrict__ grad) {
+    long long split_stride, int b0, int bn, float4 *__restrict__ grad) {
     pdl_wait();
     constexpr int W = TS + RC - 1;
     constexpr int PITCH = W + 1;
@@ -281,8 +298,8 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     const int tr = blockIdx.x / nc, tc = blockIdx.x - tr * nc;
     const int bin = geo.base[cls] + blockIdx.x;
     const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
-    if (begin == end) return;
     const int R0 = tr * TS, C0 = tc * TS;
+    if (begin == end || !rows_meet(R0, W, no, b0, bn)) return;
     // Stage only the bounding box of the bin's footprints.
     __shared__ int box[4]; // row lo, row hi, col lo, col hi (window coordinates)
     if (threadIdx.x == 0) box[0] = box[2] = W, box[1] = box[3] = 0;
@@ -305,9 +322,9 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     }
     __syncthreads();
     if (split == 1) {
-        stage_rect<PITCH>(gw, box[0], box[1], box[2], box[3], R0, C0, no, ni, g, ldg);
+        stage_rect<PITCH>(gw, box[0], box[1], box[2], box[3], R0, C0, no, ni, g, ldg, b0, bn);
     } else {
-        stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride);
+        stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride, b0, bn);
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -402,8 +419,8 @@ constexpr int PW_CHUNK = 256;
 
 __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
     Table tv, const int *__restrict__ begin_ptr, AxisCfg out_ax, AxisCfg in_ax,
-    const float *__restrict__ g, long long ldg, int split, long long split_stride,
-    float4 *__restrict__ grad) {
+    const float *__restrict__ g, long long ldg, int split, long long split_stride, int b0,
+    int bn, float4 *__restrict__ grad) {
     pdl_wait();
     __shared__ float so[3][PW_CHUNK], si[3][PW_CHUNK];
     __shared__ float red[PW_THREADS / 32][4];
@@ -419,6 +436,7 @@ __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
         const float *ib = rec + 4 + aw;
         const int4 sp = tv.spans[a];
         const int fo = sp.y, fi = sp.w;
+        if (fo > 0 && !rows_meet(sp.x, fo, no, b0, bn)) continue; // CTA-uniform
         float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
         for (int r0 = 0; r0 < fo; r0 += PW_CHUNK) {
             const int nr = min(PW_CHUNK, fo - r0);
@@ -441,8 +459,9 @@ __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
                 for (int r = warp; r < nr; r += PW_THREADS / 32) {
                     int row = sp.x + r0 + r;
                     while (row >= no) row -= no;
+                    if (row < b0 || row >= b0 + bn) continue; // warp-uniform
                     const float mo = so[0][r], dmo = so[1][r], dro = so[2][r];
-                    const float *grow = g + (long long)row * ldg;
+                    const float *grow = g + (long long)(row - b0) * ldg;
                     float h0 = 0.f, h1 = 0.f, h2 = 0.f;
                     for (int cb = 0; cb < nc; cb += 128) {
                         float gv[4];
@@ -507,9 +526,13 @@ __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
 
 using namespace tcst;
 
-extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
-                             const tcst_axis *in_axis, float *g_dev, int64_t ldg,
-                             int32_t split, int64_t split_stride, float *grad_dev, void *stream) {
+// Pullback of the chart rows [row0, row0 + rows) of G (stored from g_dev, row
+// row0 first); with a partial band every atom's gradient is the part its
+// footprint rows inside the band contribute, and atoms outside it get zero.
+static int pullback(const char *name, const void *atom_table_dev, int64_t atoms,
+                    const tcst_axis *out_axis, const tcst_axis *in_axis, float *g_dev,
+                    int64_t ldg, int32_t split, int64_t split_stride, int64_t row0, int64_t rows,
+                    float *grad_dev, void *stream) {
     char err[256];
     AxisCfg oa, ia;
     int rc;
@@ -518,30 +541,35 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
         tcst_set_error("%s", err);
         return rc;
     }
-    if (atoms < 0 || split < 1 || ldg < ia.sites ||
-        (split > 1 && split_stride < (long long)oa.sites * ldg) ||
-        (atoms && (!atom_table_dev || !g_dev || !grad_dev)) ||
+    if (rows < 0) rows = oa.sites;
+    if (atoms < 0 || split < 1 || ldg < ia.sites || row0 < 0 || row0 + rows > oa.sites ||
+        (split > 1 && split_stride < rows * ldg) ||
+        (atoms && rows && (!atom_table_dev || !g_dev || !grad_dev)) ||
         reinterpret_cast<uintptr_t>(grad_dev) % 16) {
-        tcst_set_error("tcst_pullback: invalid arguments");
+        tcst_set_error("%s: invalid arguments", name);
         return TCST_ERR_ARGUMENT;
     }
     if (atoms == 0) return TCST_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool full = row0 == 0 && rows == oa.sites;
+    if (!full) TCST_CUDA(cudaMemsetAsync(grad_dev, 0, size_t(atoms) * 16, st));
+    if (rows == 0) return TCST_OK;
     const int words = record_words(oa.modes, ia.modes);
     const Table tv = table_view(atom_table_dev, atoms, words, axis_geo(oa), axis_geo(ia));
     const BinGeom &geo = tv.geom;
-    cudaStream_t st = (cudaStream_t)stream;
     float4 *grad = reinterpret_cast<float4 *>(grad_dev);
+    const int b0 = int(row0), bn = int(rows);
     if (split > 1) {
         // Every later read of G then costs one load instead of `split`.
         const bool vec = ia.sites % 4 == 0 && ldg % 4 == 0 && split_stride % 4 == 0 &&
                          reinterpret_cast<uintptr_t>(g_dev) % 16 == 0;
         if (vec) {
-            TCST_CUDA(launch_pdl(g_reduce4_kernel, dim3(148 * 8), dim3(256), 0, st, reinterpret_cast<float4 *>(g_dev), oa.sites,
-                                                      ia.sites / 4, ldg / 4, split,
-                                                      split_stride / 4));
+            TCST_CUDA(launch_pdl(g_reduce4_kernel, dim3(148 * 8), dim3(256), 0, st,
+                                 reinterpret_cast<float4 *>(g_dev), bn, ia.sites / 4, ldg / 4,
+                                 split, split_stride / 4));
         } else {
-            TCST_CUDA(launch_pdl(g_reduce_kernel, dim3(148 * 8), dim3(256), 0, st, g_dev, oa.sites, ia.sites, ldg, split,
-                                                     split_stride));
+            TCST_CUDA(launch_pdl(g_reduce_kernel, dim3(148 * 8), dim3(256), 0, st, g_dev, bn,
+                                 ia.sites, ldg, split, split_stride));
         }
         TCST_CUDA(cudaGetLastError());
         split = 1;
@@ -557,30 +585,54 @@ extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tc
                                            int(class_smem<128>())));
             configured = true;
         }
-        TCST_CUDA(launch_pdl(pullback_class0_kernel, dim3(unsigned(geo.tr[0] * geo.tc[0])), dim3(P0_THREADS), 0, st, 
-            tv, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
+        TCST_CUDA(launch_pdl(pullback_class0_kernel, dim3(unsigned(geo.tr[0] * geo.tc[0])),
+                             dim3(P0_THREADS), 0, st, tv, oa.sites, ia.sites, g_dev, ldg, split,
+                             split_stride, b0, bn, grad));
         TCST_CUDA(cudaGetLastError());
         if (geo.nclass > 1) {
             const unsigned bins = unsigned(geo.tr[1] * geo.tc[1]);
-            TCST_CUDA(launch_pdl(pullback_class_kernel<64>, dim3(bins), dim3(PC_THREADS), class_smem<64>(), st, 
-                tv, 1, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
+            TCST_CUDA(launch_pdl(pullback_class_kernel<64>, dim3(bins), dim3(PC_THREADS),
+                                 class_smem<64>(), st, tv, 1, oa.sites, ia.sites, g_dev, ldg,
+                                 split, split_stride, b0, bn, grad));
             TCST_CUDA(cudaGetLastError());
         }
         if (geo.nclass > 2) {
             const unsigned bins = unsigned(geo.tr[2] * geo.tc[2]);
-            TCST_CUDA(launch_pdl(pullback_class_kernel<128>, dim3(bins), dim3(PC_THREADS), class_smem<128>(), st, 
-                tv, 2, oa.sites, ia.sites, g_dev, ldg, split, split_stride, grad));
+            TCST_CUDA(launch_pdl(pullback_class_kernel<128>, dim3(bins), dim3(PC_THREADS),
+                                 class_smem<128>(), st, tv, 2, oa.sites, ia.sites, g_dev, ldg,
+                                 split, split_stride, b0, bn, grad));
             TCST_CUDA(cudaGetLastError());
         }
     }
     // Atoms of active owner pairs (their grads), then coarse classes, inactive
     // pair bins and invalid atoms (all atoms when unbinned): their range starts
     // at the first coarse bin and runs to the end of the ids.
-    if ((rc = pair_backward(tv, oa, ia, g_dev, ldg, grad, st))) return rc;
+    if ((rc = pair_backward(tv, oa, ia, g_dev, ldg, Window{b0, 0, bn, ia.sites}, grad, st)))
+        return rc;
     const int first_bin = geo.nclass > 0 ? geo.base[std::min(NFINE, geo.nclass)] : 0;
     const long long ctas = std::min<long long>(atoms, 148LL * 8);
-    TCST_CUDA(launch_pdl(pullback_wide_kernel, dim3(unsigned(ctas)), dim3(PW_THREADS), 0, st, 
-        tv, tv.offsets + first_bin, oa, ia, g_dev, ldg, split, split_stride, grad));
+    TCST_CUDA(launch_pdl(pullback_wide_kernel, dim3(unsigned(ctas)), dim3(PW_THREADS), 0, st, tv,
+                         tv.offsets + first_bin, oa, ia, g_dev, ldg, split, split_stride, b0, bn,
+                         grad));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
+}
+
+extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,
+                             const tcst_axis *in_axis, float *g_dev, int64_t ldg,
+                             int32_t split, int64_t split_stride, float *grad_dev, void *stream) {
+    return pullback("tcst_pullback", atom_table_dev, atoms, out_axis, in_axis, g_dev, ldg,
+                          split, split_stride, 0, -1, grad_dev, stream);
+}
+
+extern "C" int tcst_pullback_band(const void *atom_table_dev, int64_t atoms,
+                                  const tcst_axis *out_axis, const tcst_axis *in_axis,
+                                  float *g_dev, int64_t ldg, int32_t split, int64_t split_stride,
+                                  int64_t row0, int64_t rows, float *grad_dev, void *stream) {
+    if (rows < 0) {
+        tcst_set_error("tcst_pullback_band: negative row count");
+        return TCST_ERR_ARGUMENT;
+    }
+    return pullback("tcst_pullback_band", atom_table_dev, atoms, out_axis, in_axis, g_dev,
+                          ldg, split, split_stride, row0, rows, grad_dev, stream);
 }

@@ -54,24 +54,6 @@ __host__ __device__ __forceinline__ int reach_tiles(int c, int tiles, int n) {
     return min(k, tiles);
 }
 
-// Nodes (first tiles of T sites, nn of them on an axis of n sites) whose F-site
-// footprint covers some site of [t0, t0 + tl): `count` consecutive nodes from
-// `first` (mod nn). Node a covers the tile iff t0 - F < a T <= t0 + tl - 1
-// modulo n.
-__host__ __device__ __forceinline__ int cover_nodes(int t0, int tl, int T, int F, int nn, int n,
-                                                    int &first) {
-    first = 0;
-    if (F + tl - 1 >= n) return nn;
-    const int x = t0 - F + 1;
-    const int lo = x >= 0 ? (x + T - 1) / T : -((-x) / T);
-    const int hi = (t0 + tl - 1) / T;
-    const int cnt = hi - lo + 1;
-    if (cnt >= nn) return nn;
-    first = lo % nn;
-    first += first < 0 ? nn : 0;
-    return cnt;
-}
-
 // Upper bound of the bins one weight tile scans (class bins within reach and
 // covering pair bins).
 __host__ inline int max_scan_entries(const BinGeom &g, int no, int ni) {
@@ -143,6 +125,9 @@ struct GatherOut {
     float *w, *hi, *lo;
     long long ldw, lds;
     float *amax; // nullable: max |W| folded in, one atomic per tile
+    // Window W[r0 : r0 + wr, c0 : c0 + wc] (r0, c0 multiples of TS); W[r][c]
+    // is stored at (r - r0, c - c0).
+    int r0, c0, wr, wc;
 };
 
 __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int no, int ni,
@@ -161,8 +146,8 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
     __shared__ unsigned rmask[WT_STAGE]; // tile rows each staged atom covers
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int trow = blockIdx.x / tiles_c, tcol = blockIdx.x - trow * tiles_c;
-    const int R0 = trow * TS, C0 = tcol * TS;
-    const int TR = min(TS, no - R0), TC = min(TS, ni - C0);
+    const int R0 = out.r0 + trow * TS, C0 = out.c0 + tcol * TS;
+    const int TR = min(TS, out.r0 + out.wr - R0), TC = min(TS, out.c0 + out.wc - C0);
     const BinGeom &g = tv.geom;
 
     // 1. The bins to scan, in a fixed order, with their atom counts.
@@ -441,12 +426,12 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
     for (int ii = 0; ii < 2; ++ii) {
         const int r = r0 + ii;
         if (r >= TR) continue;
-        const long long row = R0 + r;
+        const long long row = R0 - out.r0 + r;
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
             const int c = c0 + jj;
             if (c >= TC) continue;
-            const long long col = C0 + c;
+            const long long col = C0 - out.c0 + c;
             const float v = acc[ii][jj];
             vmax = fmaxf(vmax, fabsf(v));
             if (out.w) out.w[row * out.ldw + col] = v;
@@ -697,7 +682,9 @@ extern "C" int64_t tcst_weight_scratch_bytes(int64_t atoms, const tcst_axis *out
 static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa,
                     const AxisCfg &ia, void *scratch, float *weight_dev, int64_t ld_weight,
                     float *weight_hi_dev, float *weight_lo_dev, int64_t ld_split,
-                    cudaStream_t st, float *amax_dev = nullptr) {
+                    cudaStream_t st, float *amax_dev = nullptr,
+                    Window win = Window{0, 0, -1, -1}) {
+    if (win.wr < 0) win = Window{0, 0, oa.sites, ia.sites};
     const int words = record_words(oa.modes, ia.modes);
     const Table tv = table_view(atom_table_dev, atoms, words, axis_geo(oa), axis_geo(ia));
     float *cache = static_cast<float *>(scratch);
@@ -712,9 +699,11 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
         return TCST_ERR_UNSUPPORTED;
     }
     int rc;
-    if ((rc = pair_forward(tv, oa, ia, st))) return rc;
-    const int tiles_r = (oa.sites + TS - 1) / TS, tiles_c = (ia.sites + TS - 1) / TS;
-    GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split, amax_dev};
+    if ((rc = pair_forward(tv, oa, ia, win, st))) return rc;
+    if (win.wr == 0 || win.wc == 0) return TCST_OK;
+    const int tiles_r = (win.wr + TS - 1) / TS, tiles_c = (win.wc + TS - 1) / TS;
+    GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split, amax_dev,
+                     win.r0, win.c0, win.wr, win.wc};
     TCST_CUDA(launch_pdl(weight_gather_kernel, dim3(unsigned(tiles_r * tiles_c)), dim3(WT_THREADS), 0, st, 
         tv, oa.sites, ia.sites, oa.modes, ia.modes, tiles_c, cache, out));
     TCST_CUDA(cudaGetLastError());
@@ -746,12 +735,11 @@ extern "C" int tcst_assemble_weight(const void *atom_table_dev, int64_t atoms,
                     weight_hi_dev, weight_lo_dev, ld_split, (cudaStream_t)stream);
 }
 
-extern "C" int tcst_assemble_weight_f16(const void *atom_table_dev, int64_t atoms,
-                                        const tcst_axis *out_axis, const tcst_axis *in_axis,
-                                        void *scratch_dev, int64_t scratch_bytes,
-                                        float *weight_dev, int64_t ld_weight, float *amax_dev,
-                                        void *hi_dev, void *lo_dev, int64_t ld_split,
-                                        float *scale_dev, void *stream) {
+static int assemble_f16(const char *name, const void *atom_table_dev, int64_t atoms,
+                        const tcst_axis *out_axis, const tcst_axis *in_axis, void *scratch_dev,
+                        int64_t scratch_bytes, int64_t r0, int64_t wr, int64_t c0, int64_t wc,
+                        float *weight_dev, int64_t ld_weight, float *amax_dev, void *hi_dev,
+                        void *lo_dev, int64_t ld_split, float *scale_dev, void *stream) {
     char err[256];
     AxisCfg oa, ia;
     int rc;
@@ -760,19 +748,49 @@ extern "C" int tcst_assemble_weight_f16(const void *atom_table_dev, int64_t atom
         tcst_set_error("%s", err);
         return rc;
     }
+    if (wr < 0) r0 = 0, wr = oa.sites;
+    if (wc < 0) c0 = 0, wc = ia.sites;
     if (atoms < 0 || !scratch_dev || !atom_table_dev || !weight_dev || !amax_dev || !hi_dev ||
         !lo_dev || !scale_dev || scratch_bytes < cache_floats(atoms) * 4 ||
-        reinterpret_cast<uintptr_t>(scratch_dev) % 16 || ld_weight < ia.sites ||
-        ld_split < ia.sites) {
-        tcst_set_error("tcst_assemble_weight_f16: invalid arguments");
+        reinterpret_cast<uintptr_t>(scratch_dev) % 16 || ld_weight < wc || ld_split < wc ||
+        r0 < 0 || c0 < 0 || r0 + wr > oa.sites || c0 + wc > ia.sites || r0 % TS || c0 % TS) {
+        tcst_set_error("%s: invalid arguments", name);
         return TCST_ERR_ARGUMENT;
     }
     cudaStream_t st = (cudaStream_t)stream;
     if ((rc = assemble(atom_table_dev, atoms, oa, ia, scratch_dev, weight_dev, ld_weight, nullptr,
-                       nullptr, 0, st, amax_dev)))
+                       nullptr, 0, st, amax_dev, Window{int(r0), int(c0), int(wr), int(wc)})))
         return rc;
-    return tcst_split_f16(weight_dev, oa.sites, ia.sites, ld_weight, amax_dev, hi_dev, lo_dev,
-                          ld_split, scale_dev, stream);
+    return tcst_split_f16(weight_dev, wr, wc, ld_weight, amax_dev, hi_dev, lo_dev, ld_split,
+                          scale_dev, stream);
+}
+
+extern "C" int tcst_assemble_weight_f16(const void *atom_table_dev, int64_t atoms,
+                                        const tcst_axis *out_axis, const tcst_axis *in_axis,
+                                        void *scratch_dev, int64_t scratch_bytes,
+                                        float *weight_dev, int64_t ld_weight, float *amax_dev,
+                                        void *hi_dev, void *lo_dev, int64_t ld_split,
+                                        float *scale_dev, void *stream) {
+    return assemble_f16("tcst_assemble_weight_f16", atom_table_dev, atoms, out_axis, in_axis,
+                        scratch_dev, scratch_bytes, 0, -1, 0, -1, weight_dev, ld_weight, amax_dev,
+                        hi_dev, lo_dev, ld_split, scale_dev, stream);
+}
+
+extern "C" int tcst_assemble_weight_window_f16(const void *atom_table_dev, int64_t atoms,
+                                               const tcst_axis *out_axis,
+                                               const tcst_axis *in_axis, void *scratch_dev,
+                                               int64_t scratch_bytes, int64_t row0, int64_t rows,
+                                               int64_t col0, int64_t cols, float *weight_dev,
+                                               int64_t ld_weight, float *amax_dev, void *hi_dev,
+                                               void *lo_dev, int64_t ld_split, float *scale_dev,
+                                               void *stream) {
+    if (rows < 0 || cols < 0) {
+        tcst_set_error("tcst_assemble_weight_window_f16: negative window");
+        return TCST_ERR_ARGUMENT;
+    }
+    return assemble_f16("tcst_assemble_weight_window_f16", atom_table_dev, atoms, out_axis,
+                        in_axis, scratch_dev, scratch_bytes, row0, rows, col0, cols, weight_dev,
+                        ld_weight, amax_dev, hi_dev, lo_dev, ld_split, scale_dev, stream);
 }
 
 extern "C" int tcst_split_tf32(const float *x_dev, int64_t rows, int64_t cols, int64_t ld_x,

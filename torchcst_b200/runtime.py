@@ -144,6 +144,20 @@ def assemble_weight_f16(plan: Plan, table, atoms, ws: Workspace):
     return sp
 
 
+def assemble_weight_window_f16(plan: Plan, table, atoms, ws: Workspace, row0, rows, col0, cols):
+    """W[row0 : row0 + rows, col0 : col0 + cols] (fp32) and its f16 split planes."""
+    dev = ws.device
+    scratch = ws.scratch(atoms)
+    w = torch.empty(rows, cols, dtype=torch.float32, device=dev)
+    sp = F16Split(rows, cols, dev)
+    sp.amax.zero_()
+    N.call("tcst_assemble_weight_window_f16", _vp(table), atoms, ctypes.byref(plan.out_axis),
+           ctypes.byref(plan.in_axis), _vp(scratch), scratch.numel() * 4, row0, rows, col0,
+           cols, _vp(w), cols, _vp(sp.amax), _vp(sp.hi), _vp(sp.lo), sp.ld, _vp(sp.scale),
+           _stream(dev))
+    return w, sp
+
+
 def split_tf32(x):
     """Two-term TF32 split of a 2-D float32 CUDA tensor into padded planes."""
     require_cuda(x)
@@ -212,6 +226,15 @@ def pullback(plan: Plan, table, atoms, g, ldg, split, split_stride, device):
     grad = torch.empty(atoms, 4, dtype=torch.float32, device=device)
     N.call("tcst_pullback", _vp(table), atoms, ctypes.byref(plan.out_axis),
            ctypes.byref(plan.in_axis), _vp(g), ldg, split, split_stride, _vp(grad),
+           _stream(device))
+    return grad
+
+
+def pullback_band(plan: Plan, table, atoms, g, ldg, split, split_stride, row0, rows, device):
+    """Atom gradients from the G rows [row0, row0 + rows) alone (g holds them)."""
+    grad = torch.empty(atoms, 4, dtype=torch.float32, device=device)
+    N.call("tcst_pullback_band", _vp(table), atoms, ctypes.byref(plan.out_axis),
+           ctypes.byref(plan.in_axis), _vp(g), ldg, split, split_stride, row0, rows, _vp(grad),
            _stream(device))
     return grad
 
