@@ -235,23 +235,26 @@ def _reach(c):
     return 16 if c == 0 else 64 << (c - 1)
 
 
-def _edge(c):
-    return 32 if c < 3 else _reach(c) // 2
+def _edge(c, fe=32):
+    return fe if c < 3 else _reach(c) // 2
 
 
 def _bin_geom(out_axis, in_axis):
     """Classes, tiles per axis and first bin of each class, restating the device
     bin geometry (fine classes on 32-site tiles, coarse ones on reach/2)."""
     no, ni = out_axis.site_count, in_axis.site_count
-    tr, tc, base, nb, c = [], [], [], 0, 0
-    while True:
-        e = _edge(c)
-        tr.append(-(-no // e))
-        tc.append(-(-ni // e))
-        base.append(nb)
-        nb += tr[-1] * tc[-1]
-        c += 1
-        if _reach(c - 1) >= 2 * max(no, ni):
+    for fe in (32, 64):  # fine bins of 32 sites, 64 when those do not fit
+        tr, tc, base, nb, c = [], [], [], 0, 0
+        while True:
+            e = _edge(c, fe)
+            tr.append(-(-no // e))
+            tc.append(-(-ni // e))
+            base.append(nb)
+            nb += tr[-1] * tc[-1]
+            c += 1
+            if _reach(c - 1) >= 2 * max(no, ni):
+                break
+        if nb + 1 <= 98304:
             break
     if out_axis.modes != 8 or in_axis.modes != 8 or nb + 1 > 98304:
         return dict(nclass=0, nbins=2)
@@ -270,7 +273,7 @@ def _bin_geom(out_axis, in_axis):
                 nb += npair
             t *= out_axis.merge_factor
             level += 1
-    return dict(nclass=c, tr=tr, tc=tc, base=base, nbins=nb + 1, pairs=pairs)
+    return dict(nclass=c, tr=tr, tc=tc, base=base, nbins=nb + 1, pairs=pairs, fe=fe)
 
 
 def _table_sections(out_axis, in_axis, atoms):
@@ -316,7 +319,7 @@ def test_bins_are_stable_and_complete(R, name):
         cls = np.zeros(A, np.int64)
         while (f > np.vectorize(_reach)(cls)).any():
             cls += f > np.vectorize(_reach)(cls)
-        e = np.vectorize(_edge)(cls)
+        e = np.vectorize(lambda c: _edge(c, geo["fe"]))(cls)
         base = np.asarray(geo["base"])[cls]
         tcs = np.asarray(geo["tc"])[cls]
         want = base + (spans[:, 0] // e) * tcs + spans[:, 2] // e
@@ -446,3 +449,36 @@ def test_band_windows_and_pullback_match_full(R, name, bands):
     torch.cuda.synchronize()
     for col in range(4):
         assert rel(acc[:, col].cpu(), full[:, col].double().cpu()) < 1e-5, col
+
+
+def test_large_chart_fine_bins_of_64_sites(R):
+    """A 6144-site chart needs fine bins of 64 sites (3 (6144/32)^2 > 98,304
+    bins of 32): weight and pullback still match the float64 oracle."""
+    from torchcst_b200 import CSTLinear, kernels
+    from torchcst_b200.spec import CellMass, ChebyshevSpec, RegularGrid
+    axis = O.Axis(6144, base_tile_sites=3, merge_factor=2)
+    spec = O.Rational(radius_max=48.0)
+    rng = np.random.default_rng(11)
+    A = 2048
+    p0 = np.stack([rng.normal(0, 0.1, A), rng.uniform(0, 1, A), rng.uniform(0, 6144, A),
+                   rng.uniform(0, 6144, A)], 1).astype(np.float32)
+    prof = CellMass(ChebyshevSpec(8), 3, 2)
+    kernel = kernels.product(prof, prof, coordinates=kernels.rational_radius(
+        radius_min=spec.radius_min, radius_birth=spec.radius_birth,
+        radius_max=spec.radius_max, amplitude_max=spec.amplitude_max))
+    grid = RegularGrid(6144, 1.0, 0.0)
+    layer = CSTLinear(charts=(grid, grid), atoms=torch.as_tensor(p0), kernel=kernel, device="cuda")
+    lay = O.decode(axis, axis, spec, p0)
+    w = layer.weight().cpu().numpy()
+    assert rel(w, O.weight64(lay)) < 1e-5
+    del w
+    plan, p = layer._plan, layer.atoms.p
+    ws = layer._workspace(p.device)
+    table = R.decode_route(plan, p, ws.status)
+    R.assemble_weight(plan, table, A, ws, dense=True, split=False)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    G = torch.randn(6144, 6144, device="cuda", generator=gen) * 1e-3
+    grad = R.pullback(plan, table, A, G, 6144, 1, 0, p.device).cpu().numpy()
+    g64 = O.atom_gradients64(lay, G.double().cpu().numpy())
+    for c in range(4):
+        assert rel(grad[:, c], g64[:, c]) < TOL, c

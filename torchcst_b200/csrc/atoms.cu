@@ -381,7 +381,11 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
     Table tv, long long *__restrict__ keys, int *__restrict__ routing,
     unsigned *__restrict__ status) {
     pdl_wait();
-    if (blockIdx.x == 0 && threadIdx.x == 0) *tv.sync = 0u; // the sort's ticket
+    if (blockIdx.x == 0) {
+        // The sort's ticket, the active owner-pair count and the node flags.
+        if (threadIdx.x == 0) tv.sync[0] = tv.sync[1] = 0u;
+        for (int i = threadIdx.x; i < tv.geom.nodes; i += blockDim.x) tv.node_on[i] = 0;
+    }
     const long long atoms = tv.atoms;
     const int words = tv.words;
     const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -539,7 +543,17 @@ __global__ void __launch_bounds__(COL_SEGS * 32) bin_column_kernel(Table tv) {
                 run += c;
             }
         }
-        if (seg == COL_SEGS - 1) col[g.sort_blocks * stride] = run;
+        if (seg == COL_SEGS - 1) {
+            col[g.sort_blocks * stride] = run;
+            // Owner pairs: an output node of an expansion level-bank is "on"
+            // when one of its pairs holds PAIR_MIN atoms; sync[1] counts the
+            // active pairs (both were zeroed by the decode).
+            const int l = run >= PAIR_MIN ? pair_lb(g, bin) : -1;
+            if (l >= 0 && g.pl_exp[l]) {
+                atomicOr(tv.node_on + g.pl_node[l] + (bin - g.pl_base[l]) / g.pl_ni[l], 1);
+                atomicAdd(tv.sync + 1, 1u);
+            }
+        }
     }
     // Last CTA: bin starts = exclusive scan of the totals.
     __threadfence();
@@ -717,6 +731,7 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
     }
     if (atoms == 0) {
         TCST_CUDA(cudaMemsetAsync(tv.offsets, 0, size_t(g.nbins + 1) * 4, st));
+        TCST_CUDA(cudaMemsetAsync(tv.sync, 0, 16, st));
         return TCST_OK;
     }
     {

@@ -157,7 +157,8 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
 //
 // Bins. An atom's class is the smallest c whose reach class_reach(c) covers
 // its larger footprint max(F_out, F_in). Classes 0..NFINE-1 (reach 16, 64, 128)
-// are binned by the TS x TS tile of (output first site, input first site);
+// are binned by the fe x fe tile of (output first site, input first site),
+// fe = TS (2 TS for charts so large that TS bins do not fit);
 // coarser classes (reach 256, 512, ... up to twice the larger axis, the widest
 // footprint routing produces) by tiles of edge reach / 2. Bins are numbered
 // class by class, tiles row-major, and invalid atoms take the last bin. When
@@ -198,12 +199,17 @@ struct AxisGeo {
 };
 
 __host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : 64 << (c - 1); }
-__host__ __device__ constexpr int class_edge(int c) { return c < NFINE ? TS : class_reach(c) / 2; }
+// Bin edge of class c: fe (the geometry's fine edge, TS or 2 TS) for the fine
+// classes, half the reach for coarser ones.
+__host__ __device__ constexpr int class_edge(int c, int fe) {
+    return c < NFINE ? fe : class_reach(c) / 2;
+}
 
 __host__ __device__ inline long long align16(long long x) { return (x + 15) & ~15LL; }
 
 struct BinGeom {
     int nclass;                   // 0 when not binned
+    int fe;                       // fine bin edge (TS, or 2 TS when TS bins do not fit)
     int tr[MAX_CLASSES], tc[MAX_CLASSES]; // tiles per axis of each class
     int base[MAX_CLASSES + 1];    // first bin of each class; base[nclass] = first bin past them
     int nbins;                    // last pair bin + 2 (invalid bin)
@@ -229,15 +235,22 @@ __host__ __device__ inline BinGeom bin_geom(long long atoms, const AxisGeo &ao,
     const int nmax = n_out > n_in ? n_out : n_in;
     int nc = 0;
     long long nb = 0;
-    while (nc < MAX_CLASSES) {
-        const int e = class_edge(nc);
-        g.tr[nc] = (n_out + e - 1) / e;
-        g.tc[nc] = (n_in + e - 1) / e;
-        g.base[nc] = int(nb < 0x7fffffff ? nb : 0x7fffffff);
-        nb += (long long)g.tr[nc] * g.tc[nc];
-        ++nc;
-        if (class_reach(nc - 1) >= 2 * nmax) break;
+    // Fine bins of TS sites per side, or of 2 TS when those do not fit.
+    for (g.fe = TS; g.fe <= 2 * TS; g.fe *= 2) {
+        nc = 0;
+        nb = 0;
+        while (nc < MAX_CLASSES) {
+            const int e = class_edge(nc, g.fe);
+            g.tr[nc] = (n_out + e - 1) / e;
+            g.tc[nc] = (n_in + e - 1) / e;
+            g.base[nc] = int(nb < 0x7fffffff ? nb : 0x7fffffff);
+            nb += (long long)g.tr[nc] * g.tc[nc];
+            ++nc;
+            if (class_reach(nc - 1) >= 2 * nmax) break;
+        }
+        if (nb + 1 <= MAX_BINS) break;
     }
+    if (g.fe > 2 * TS) g.fe = 2 * TS;
     const long long class_end = nb;
     g.npl = 0;
     g.nodes = 0;
@@ -330,9 +343,11 @@ struct Table {
     const int4 *spans;
     const float *sites;
     int *bin_of, *offsets, *ids, *counts;
-    unsigned *sync; // blocks of the column prefix that finished (reset by the decode)
+    unsigned *sync; // [0] finished blocks of the column prefix (reset by the decode),
+                    // [1] active owner pairs (written by the column prefix)
     float *pair_c;  // [pair bins][PF][PF]: C of active pairs
-    int *node_on;   // [nodes]: output node has an active pair (expansion level-banks)
+    int *node_on;   // [nodes]: output node has an active pair (expansion level-banks),
+                    // written by the sort's column prefix
     float *pair_buf; // expansion buffers: R = C Phi_in^T summed per output node, then
                      // the pullback's projections P = Phi_out^T G
     BinGeom geom;
@@ -368,6 +383,9 @@ __host__ __device__ inline int pair_lb(const BinGeom &g, int bin) {
     return l;
 }
 
+// Active owner pairs of the table (0: every pair kernel has nothing to do).
+__device__ __forceinline__ unsigned active_pairs(const Table &tv) { return tv.sync[1]; }
+
 // Whether a pair bin takes the owner-pair path.
 __device__ __forceinline__ bool pair_active(const BinGeom &g, const int *offsets, int bin) {
     const int l = pair_lb(g, bin);
@@ -396,7 +414,7 @@ __device__ __forceinline__ int atom_bin(int4 span, const BinGeom &g, int lvl_o, 
             return g.pl_base[l] + (span.x / t) * g.pl_ni[l] + span.z / t;
         }
     }
-    const int e = class_edge(c);
+    const int e = class_edge(c, g.fe);
     return g.base[c] + (span.x / e) * g.tc[c] + span.z / e;
 }
 

@@ -325,6 +325,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int quarter = warp & 3;
         const int row = tile_m * BM + quarter * 32 + lane;
         float *out = C + (long long)split * split_stride;
+        if (mse.target && row < M) {
+            // The target tile is read only after the accumulator is ready:
+            // bring its lines into L2 while the MMAs run.
+            const float *tr = mse.target + (long long)row * mse.ldt + tile_n * BN;
+            const int ncol = min(BN, N - tile_n * BN);
+            for (int c = 0; c < ncol; c += 32) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(tr + c));
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(tr + min(c + 31, ncol - 1)));
+            }
+        }
         bool ready = true;
         if (num_kb > 0) {
             ready = mbar_wait(acc_bar, 0);

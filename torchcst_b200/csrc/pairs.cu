@@ -20,11 +20,12 @@
 //
 // Kernels (one launch each, all deterministic):
 //   pair_coef_kernel     C of every active pair bin, atoms in bin (id) order;
-//   pair_expand_kernel   per output node a of an expansion level-bank and
-//                        chunk of input sites: R_a = sum_b C_ab Phi_b^T
-//                        (PF x N_in) over the active partners b in order, and
-//                        the node flag; the weight gather then adds
-//                        Phi_a(rows) R_a(cols) as PF rank-one terms per node;
+//   pair_expand_kernel   per flagged output node a of an expansion level-bank
+//                        and chunk of input sites: R_a = sum_b C_ab Phi_b^T
+//                        (PF x N_in) over the active partners b in order; the
+//                        weight gather then adds Phi_a(rows) R_a(cols) as PF
+//                        rank-one terms per node (node flags and the count of
+//                        active pairs come from the sort, atoms.cu);
 //   pair_project_kernel  the pullback's P_a = Phi_a^T G (PF x N_in) per node
 //                        with an active pair, over its footprint rows in order;
 //   pair_grad_kernel     per active pair H_ab = P_a Phi_b, then the gradient
@@ -81,6 +82,7 @@ __device__ __forceinline__ void axis_alpha(const float *blk, float *alpha, float
 
 __global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw) {
     pdl_wait();
+    if (active_pairs(tv) == 0) return;
     const BinGeom &g = tv.geom;
     __shared__ float sa[PC_CHUNK][2 * PF + 1];
     const int t = threadIdx.x;
@@ -148,7 +150,8 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_o
     const BinGeom &g = tv.geom;
     const int chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
     int l, a, ch;
-    if (!expand_cta(g, chunks, l, a, ch)) return;
+    if (active_pairs(tv) == 0 || !expand_cta(g, chunks, l, a, ch)) return;
+    if (!tv.node_on[g.pl_node[l] + a]) return;
     // Only nodes over the window's rows and chunks over its columns are read
     // by the gather that follows (CTA-uniform exits).
     if (!node_covers(g, l, a, win.r0, win.wr, n_out)) return;
@@ -159,11 +162,9 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_o
     float r[PF];
 #pragma unroll
     for (int f = 0; f < PF; ++f) r[f] = 0.f;
-    bool any = false;
     for (int b = 0; b < nb; ++b) {
         const int bin = g.pl_base[l] + a * nb + b;
         if (tv.offsets[bin + 1] - tv.offsets[bin] < PAIR_MIN) continue; // CTA-uniform
-        any = true;
         __syncthreads();
         for (int e = threadIdx.x; e < PF * PF; e += blockDim.x)
             C[e] = tv.pair_c[(long long)(bin - g.pl_base[0]) * PF * PF + e];
@@ -179,8 +180,7 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_o
             }
         }
     }
-    if (ch == win.c0 / PX_CHUNK && threadIdx.x == 0) tv.node_on[g.pl_node[l] + a] = any ? 1 : 0;
-    if (any && i < n_in) {
+    if (i < n_in) {
         float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in + i;
 #pragma unroll
         for (int f = 0; f < PF; ++f) out[(long long)f * n_in] = r[f];
@@ -195,16 +195,8 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
     const BinGeom &g = tv.geom;
     const int chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
     int l, a, ch;
-    if (!expand_cta(g, chunks, l, a, ch)) return;
-    if (!node_covers(g, l, a, band.r0, band.wr, n_out)) return;
-    {
-        bool any = false; // an active partner (CTA-uniform)
-        for (int b = 0; b < g.pl_ni[l] && !any; ++b) {
-            const int bin = g.pl_base[l] + a * g.pl_ni[l] + b;
-            any = tv.offsets[bin + 1] - tv.offsets[bin] >= PAIR_MIN;
-        }
-        if (!any) return;
-    }
+    if (active_pairs(tv) == 0 || !expand_cta(g, chunks, l, a, ch)) return;
+    if (!tv.node_on[g.pl_node[l] + a] || !node_covers(g, l, a, band.r0, band.wr, n_out)) return;
     const int T = g.pl_T[l], F = g.pl_K[l] * T;
     const int i = ch * PX_CHUNK + threadIdx.x;
     // Distinct chart rows of the footprint: all rows when it wraps onto itself.
@@ -248,6 +240,7 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
 __global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_out, int n_in,
                                                         Window band, float4 *__restrict__ grad) {
     pdl_wait();
+    if (active_pairs(tv) == 0) return;
     const BinGeom &g = tv.geom;
     __shared__ float sp[PF][PG_COLS + 1];
     __shared__ float sphi[PG_COLS][PF + 1];

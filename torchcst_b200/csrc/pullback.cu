@@ -204,18 +204,19 @@ __device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_
 // four of the (at most 16) input sites; the output-site values of the atom are
 // spread over the quad and shuffled per row; the quad sums its four partials in
 // a fixed xor order.
+template <int E>
 __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
     Table tv, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, int b0, int bn, float4 *__restrict__ grad) {
     pdl_wait();
-    constexpr int W = TS + REACH - 1;
+    constexpr int W = E + REACH - 1;
     constexpr int PITCH = W + 1;
     __shared__ __align__(16) float gw[W * PITCH];
     const int ct = tv.geom.tc[0];
     const int tr = blockIdx.x / ct, tc = blockIdx.x - tr * ct;
     const int bin = tv.geom.base[0] + blockIdx.x; // class 0 bins, row-major by tile
     const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
-    const int R0 = tr * TS, C0 = tc * TS;
+    const int R0 = tr * E, C0 = tc * E;
     if (begin == end || !rows_meet(R0, W, no, b0, bn)) return;
     stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride, b0, bn);
     __syncthreads();
@@ -277,18 +278,18 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
 }
 
 // Classes 1 and 2: one CTA per bin (first-site tile). The CTA stages the
-// bounding box of its atoms' footprints inside the (TS + RC - 1)-square G
+// bounding box of its atoms' footprints inside the (E + RC - 1)-square G
 // window, then each warp takes one atom at a time: output-site values
 // (m, dm/dmu, dm/dR) go to the warp's shared rows, lanes own input sites, and
 // each lane accumulates the three row contractions of its columns before the
 // fixed xor tree. Site phases use a per-atom step 2/F (within an ulp of the
 // forward's phase; the gradient tolerance is far wider).
-template <int RC>
+template <int RC, int E>
 __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     Table tv, int cls, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, int b0, int bn, float4 *__restrict__ grad) {
     pdl_wait();
-    constexpr int W = TS + RC - 1;
+    constexpr int W = E + RC - 1;
     constexpr int PITCH = W + 1;
     constexpr int Q = RC / 32;
     extern __shared__ __align__(16) float sm[];
@@ -298,7 +299,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     const int tr = blockIdx.x / nc, tc = blockIdx.x - tr * nc;
     const int bin = geo.base[cls] + blockIdx.x;
     const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
-    const int R0 = tr * TS, C0 = tc * TS;
+    const int R0 = tr * E, C0 = tc * E;
     if (begin == end || !rows_meet(R0, W, no, b0, bn)) return;
     // Stage only the bounding box of the bin's footprints.
     __shared__ int box[4]; // row lo, row hi, col lo, col hi (window coordinates)
@@ -406,8 +407,8 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
         __syncwarp();
     }
 }
-template <int RC> constexpr size_t class_smem() {
-    return size_t(TS + RC - 1) * (TS + RC) * 4 + size_t(PC_WARPS) * RC * 16;
+template <int RC, int E> constexpr size_t class_smem() {
+    return size_t(E + RC - 1) * (E + RC) * 4 + size_t(PC_WARPS) * RC * 16;
 }
 
 // Coarse classes: one CTA per atom. The footprint is walked in chunks of
@@ -526,6 +527,42 @@ __global__ void __launch_bounds__(PW_THREADS) pullback_wide_kernel(
 
 using namespace tcst;
 
+// The fine-class kernels for bins of E sites per side.
+template <int E>
+static int launch_classes(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, float *g_dev,
+                          int64_t ldg, int split, int64_t split_stride, int b0, int bn,
+                          float4 *grad, cudaStream_t st) {
+    const BinGeom &geo = tv.geom;
+    static bool configured = false;
+    if (!configured) {
+        TCST_CUDA(cudaFuncSetAttribute(pullback_class_kernel<64, E>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(class_smem<64, E>())));
+        TCST_CUDA(cudaFuncSetAttribute(pullback_class_kernel<128, E>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(class_smem<128, E>())));
+        configured = true;
+    }
+    TCST_CUDA(launch_pdl(pullback_class0_kernel<E>, dim3(unsigned(geo.tr[0] * geo.tc[0])),
+                         dim3(P0_THREADS), 0, st, tv, oa.sites, ia.sites, g_dev, ldg, split,
+                         split_stride, b0, bn, grad));
+    TCST_CUDA(cudaGetLastError());
+    if (geo.nclass > 1) {
+        TCST_CUDA(launch_pdl(pullback_class_kernel<64, E>, dim3(unsigned(geo.tr[1] * geo.tc[1])),
+                             dim3(PC_THREADS), class_smem<64, E>(), st, tv, 1, oa.sites, ia.sites,
+                             g_dev, ldg, split, split_stride, b0, bn, grad));
+        TCST_CUDA(cudaGetLastError());
+    }
+    if (geo.nclass > 2) {
+        TCST_CUDA(launch_pdl(pullback_class_kernel<128, E>,
+                             dim3(unsigned(geo.tr[2] * geo.tc[2])), dim3(PC_THREADS),
+                             class_smem<128, E>(), st, tv, 2, oa.sites, ia.sites, g_dev, ldg,
+                             split, split_stride, b0, bn, grad));
+        TCST_CUDA(cudaGetLastError());
+    }
+    return TCST_OK;
+}
+
 // Pullback of the chart rows [row0, row0 + rows) of G (stored from g_dev, row
 // row0 first); with a partial band every atom's gradient is the part its
 // footprint rows inside the band contribute, and atoms outside it get zero.
@@ -575,34 +612,11 @@ static int pullback(const char *name, const void *atom_table_dev, int64_t atoms,
         split = 1;
     }
     if (geo.nclass > 0) {
-        static bool configured = false;
-        if (!configured) {
-            TCST_CUDA(cudaFuncSetAttribute(pullback_class_kernel<64>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           int(class_smem<64>())));
-            TCST_CUDA(cudaFuncSetAttribute(pullback_class_kernel<128>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           int(class_smem<128>())));
-            configured = true;
-        }
-        TCST_CUDA(launch_pdl(pullback_class0_kernel, dim3(unsigned(geo.tr[0] * geo.tc[0])),
-                             dim3(P0_THREADS), 0, st, tv, oa.sites, ia.sites, g_dev, ldg, split,
-                             split_stride, b0, bn, grad));
-        TCST_CUDA(cudaGetLastError());
-        if (geo.nclass > 1) {
-            const unsigned bins = unsigned(geo.tr[1] * geo.tc[1]);
-            TCST_CUDA(launch_pdl(pullback_class_kernel<64>, dim3(bins), dim3(PC_THREADS),
-                                 class_smem<64>(), st, tv, 1, oa.sites, ia.sites, g_dev, ldg,
-                                 split, split_stride, b0, bn, grad));
-            TCST_CUDA(cudaGetLastError());
-        }
-        if (geo.nclass > 2) {
-            const unsigned bins = unsigned(geo.tr[2] * geo.tc[2]);
-            TCST_CUDA(launch_pdl(pullback_class_kernel<128>, dim3(bins), dim3(PC_THREADS),
-                                 class_smem<128>(), st, tv, 2, oa.sites, ia.sites, g_dev, ldg,
-                                 split, split_stride, b0, bn, grad));
-            TCST_CUDA(cudaGetLastError());
-        }
+        const int rc2 = geo.fe == TS ? launch_classes<TS>(tv, oa, ia, g_dev, ldg, split,
+                                                           split_stride, b0, bn, grad, st)
+                                     : launch_classes<2 * TS>(tv, oa, ia, g_dev, ldg, split,
+                                                               split_stride, b0, bn, grad, st);
+        if (rc2) return rc2;
     }
     // Atoms of active owner pairs (their grads), then coarse classes, inactive
     // pair bins and invalid atoms (all atoms when unbinned): their range starts

@@ -48,8 +48,8 @@ __device__ __forceinline__ bool window_hits(int f, int F, int t0, int tl, int n)
 
 // Source tiles (k = 0 .. count-1 steps back from the tile holding `t0`) whose
 // atoms of class c can reach sites [t0, t0 + TS).
-__host__ __device__ __forceinline__ int reach_tiles(int c, int tiles, int n) {
-    const int e = class_edge(c);
+__host__ __device__ __forceinline__ int reach_tiles(int c, int fe, int tiles, int n) {
+    const int e = class_edge(c, fe);
     const int k = 1 + (class_reach(c) - 1 + e - 1) / e + (n % e != 0);
     return min(k, tiles);
 }
@@ -59,7 +59,7 @@ __host__ __device__ __forceinline__ int reach_tiles(int c, int tiles, int n) {
 __host__ inline int max_scan_entries(const BinGeom &g, int no, int ni) {
     if (g.nclass == 0) return 1;
     int n = 0;
-    for (int c = 0; c < g.nclass; ++c) n += reach_tiles(c, g.tr[c], no) * reach_tiles(c, g.tc[c], ni);
+    for (int c = 0; c < g.nclass; ++c) n += reach_tiles(c, g.fe, g.tr[c], no) * reach_tiles(c, g.fe, g.tc[c], ni);
     for (int l = 0; l < g.npl; ++l) {
         const int k = g.pl_K[l] + 2;
         n += (g.pl_no[l] < k ? g.pl_no[l] : k) * (g.pl_ni[l] < k ? g.pl_ni[l] : k);
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
         // (active pairs count no atoms: they come in as rank-one terms below).
         int ncls = 0;
         for (int c = 0; c < g.nclass; ++c)
-            ncls += reach_tiles(c, g.tr[c], no) * reach_tiles(c, g.tc[c], ni);
+            ncls += reach_tiles(c, g.fe, g.tr[c], no) * reach_tiles(c, g.fe, g.tc[c], ni);
         nscan = ncls;
         for (int l = 0; l < g.npl; ++l) {
             int f0, f1;
@@ -193,12 +193,12 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
         for (int i = t; i < ncls; i += WT_THREADS) {
             int c = 0, rem = i, kr = 0, kc = 0;
             for (; c < g.nclass; ++c) {
-                kr = reach_tiles(c, g.tr[c], no);
-                kc = reach_tiles(c, g.tc[c], ni);
+                kr = reach_tiles(c, g.fe, g.tr[c], no);
+                kc = reach_tiles(c, g.fe, g.tc[c], ni);
                 if (rem < kr * kc) break;
                 rem -= kr * kc;
             }
-            const int e = class_edge(c);
+            const int e = class_edge(c, g.fe);
             const int k = rem / kc, l = rem - k * kc;
             int sr = R0 / e - k, sc = C0 / e - l;
             sr += sr < 0 ? g.tr[c] : 0;
@@ -381,15 +381,33 @@ __global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int
 
     // 4. Active owner pairs: PF rank-one terms per covering output node a of an
     // expansion level-bank that has an active pair, rows phi_f(site - a T)
-    // (images summed), columns R_a[f][site].
-    for (int l = 0; l < g.npl; ++l) {
-        if (!g.pl_exp[l]) continue;
-        const int T = g.pl_T[l], F = g.pl_K[l] * T, nno = g.pl_no[l];
-        int fo;
-        const int co = cover_nodes(R0, TR, T, F, nno, no, fo);
-        for (int u = 0; u < co; ++u) {
-            const int a = fo + u >= nno ? fo + u - nno : fo + u;
-            if (!tv.node_on[g.pl_node[l] + a]) continue; // CTA-uniform
+    // (images summed), columns R_a[f][site]. The covering nodes and their
+    // flags are read in parallel first.
+    if (active_pairs(tv) > 0) {
+        __shared__ int pnode[MAX_PAIR_LB * 5]; // (l << 16 | a) of flagged nodes, else -1
+        int np = 0;
+        for (int l = 0; l < g.npl; ++l) {
+            int f0;
+            if (g.pl_exp[l])
+                np += cover_nodes(R0, TR, g.pl_T[l], g.pl_K[l] * g.pl_T[l], g.pl_no[l], no, f0);
+        }
+        for (int i = t; i < np; i += WT_THREADS) {
+            int rem = i, l = 0, co = 0, fo = 0;
+            for (; l < g.npl; ++l) {
+                if (!g.pl_exp[l]) continue;
+                co = cover_nodes(R0, TR, g.pl_T[l], g.pl_K[l] * g.pl_T[l], g.pl_no[l], no, fo);
+                if (rem < co) break;
+                rem -= co;
+            }
+            const int a = fo + rem >= g.pl_no[l] ? fo + rem - g.pl_no[l] : fo + rem;
+            pnode[i] = tv.node_on[g.pl_node[l] + a] ? (l << 16 | a) : -1;
+        }
+        __syncthreads();
+        for (int i = 0; i < np; ++i) {
+            const int key = pnode[i];
+            if (key < 0) continue; // CTA-uniform
+            const int l = key >> 16, a = key & 0xFFFF;
+            const int T = g.pl_T[l], F = g.pl_K[l] * T;
             if (t < 32) {
                 float phi[PF];
                 const bool on = t < TR && pair_basis(R0 + t - a * T, F, no, phi);
