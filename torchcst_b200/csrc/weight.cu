@@ -130,7 +130,7 @@ struct GatherOut {
     int r0, c0, wr, wc;
 };
 
-__global__ void __launch_bounds__(WT_THREADS) weight_gather_kernel(Table tv, int no, int ni,
+__global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, int no, int ni,
                                                                    int modes_o, int modes_i,
                                                                    int tiles_c,
                                                                    const float *__restrict__ cache,
