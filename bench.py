@@ -359,6 +359,106 @@ def run_extra_config(args):
     return 0
 
 
+def run_config5(args):
+    """Config 5 (8192 -> 8192, 262,144 atoms) sharded by output-row bands over
+    --gpus ranks (one process per GPU, NCCL; one band on a single GPU): eager
+    RowBandMSETrainStep steps timed with CUDA events, max over ranks. Strong
+    scaling: every step trains the whole layer on the same 16,384 rows. e2e
+    adds each step's pinned host-to-device copies of X and of the rank's target
+    band and the loss read-back."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
+    from torchcst_b200.init import kaiming_normal_
+    from torchcst_b200.shard import RowBandMSETrainStep, band
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+        pg = dist.group.WORLD
+    torch.manual_seed(0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    n, rows = 8192, 16384
+    grid = chart_presets.regular_grid(n, geometry="flat_torus")
+    kernel = kernels.product(kernels.cell_mass(ChebyshevSpec(modes=8)),
+                             coordinates=kernels.rational_radius(radius_max=4096.0,
+                                                                 radius_fraction=0.0))
+    layer = CSTLinear(charts=(grid, grid), atoms=262144, kernel=kernel, device=dev,
+                      validate="off")
+    kaiming_normal_(layer, nonlinearity="relu", q=0.0)
+    with torch.no_grad():
+        layer.atoms.p[:, 1].uniform_(0.0, 1.0, generator=gen)
+    opt = CSTAdamW(layer.parameters(), model=layer, lr=1e-3)
+    x = torch.randn(rows, n, device=dev, generator=gen)
+    t = torch.randn(rows, n, device=dev, generator=gen)
+    step = RowBandMSETrainStep(layer, opt, rows, process_group=pg)
+    for _ in range(args.warmup):
+        step(x, t)
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss = step(x, t)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    # e2e: X and this rank's target band copied from pinned host memory each step.
+    r0, nb = band(n, rank, world)
+    hx = x.cpu().pin_memory()
+    ht = t[:, r0:r0 + nb].cpu().pin_memory()
+    tb = torch.empty(rows, n, device=dev)
+    loss_host = torch.empty(1, dtype=torch.float64).pin_memory()
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    e0.record()
+    for _ in range(max(2, args.steps // 4)):
+        x.copy_(hx, non_blocking=True)
+        tb[:, r0:r0 + nb].copy_(ht, non_blocking=True)
+        lo = step(x, tb)
+        loss_host.copy_(lo.reshape(1), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / max(2, args.steps // 4)], device=dev)
+    if pg is not None:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    ms, e2e = float(ms.item()), float(e2e_ms.item())
+    flops = 3 * 2.0 * rows * n * n
+    spec = EXTRA[5]
+    line = {"metric": spec["metric"], "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": dict(spec["config"], parallelism=f"rowband{world}",
+                           rows_per_rank=rows, band_rows=nb,
+                           l2="inputs 512 MiB each, larger than L2"),
+            "effective_tflops": flops / (ms * 1e-3) / 1e12,
+            "e2e": {"value": 1000.0 / e2e, "unit": "steps/s",
+                    "h2d_bytes_per_step": (hx.numel() + ht.numel()) * 4,
+                    "d2h_bytes_per_step": 8,
+                    "api": "RowBandMSETrainStep(x, target) per rank"},
+            "gpu_launches": RowBandMSETrainStep.LAUNCHES_PER_STEP * args.steps,
+            "clocks": clocks, "loss": float(loss)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -371,9 +471,12 @@ def main():
     ap.add_argument("--breakdown", action="store_true",
                     help="print per-launch CUDA-event times of one step to stderr")
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
-                    help="2: the headline config (default); 3, 4, 5: the other named shapes on one "
-                         "GPU through the drop-in API")
+                    help="2: the headline config (default); 3, 4: the other named shapes on "
+                         "one GPU through the drop-in API; 5: the wide layer sharded by "
+                         "output-row bands over --gpus ranks")
     args = ap.parse_args()
+    if args.config == 5 and args.impl != "reference":
+        return run_config5(args)
     if args.config != 2 and args.impl != "reference":
         return run_extra_config(args)
     if args.impl == "reference":

@@ -321,14 +321,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             mma_commit(acc_bar);
         }
     } else {
-        // Epilogue warps 2..5 own TMEM lane quarters (warp % 4).
+        // Epilogue warps 2..5 own TMEM lane quarters (warp % 4): 32 rows each.
+        // With the MSE epilogue a warp moves each 32 x 32 block through shared
+        // memory (the stage buffers are free once the accumulator is ready),
+        // so target loads and dY stores are whole 128-byte row segments.
         const int quarter = warp & 3;
-        const int row = tile_m * BM + quarter * 32 + lane;
+        const int row_base = tile_m * BM + quarter * 32;
         float *out = C + (long long)split * split_stride;
-        if (mse.target && row < M) {
+        if (mse.target && row_base + lane < M) {
             // The target tile is read only after the accumulator is ready:
             // bring its lines into L2 while the MMAs run.
-            const float *tr = mse.target + (long long)row * mse.ldt + tile_n * BN;
+            const float *tr = mse.target + (long long)(row_base + lane) * mse.ldt + tile_n * BN;
             const int ncol = min(BN, N - tile_n * BN);
             for (int c = 0; c < ncol; c += 32) {
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(tr + c));
@@ -344,11 +347,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         double loss = 0.0;
         float vmax = 0.f;
         if (ready && !*abort_flag) {
-            const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-            const bool vec_t = mse.target && mse.ldt % 4 == 0 &&
-                               (reinterpret_cast<uintptr_t>(mse.target) & 15) == 0;
             // 1 / (s_A s_B): a power of two, so the product is exact.
             const float inv = (scale_a && scale_b) ? 1.0f / (*scale_a * *scale_b) : 1.0f;
+            const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+            float *blk = reinterpret_cast<float *>(smem) + quarter * (32 * 33);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 unsigned r[32];
@@ -370,53 +372,55 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) r[j] = 0u;
                 }
-                if (row < M && mse.target) {
-                    // dY = (Y - T) * scale in place of Y; sum (Y - T)^2 in double.
+                if (!mse.target) {
+                    // Plain output: each lane stores its row's 32 columns.
+                    const int row = row_base + lane;
                     const int col0 = tile_n * BN + c0;
-                    float *dst = out + (long long)row * ldc + col0;
-                    const float *tr = mse.target + (long long)row * mse.ldt + col0;
-                    if (vec && vec_t && col0 + 32 <= N) {
+                    if (row < M) {
+                        float *dst = out + (long long)row * ldc + col0;
+                        if (vec && col0 + 32 <= N) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            const float4 t4 = *reinterpret_cast<const float4 *>(tr + j);
-                            const float d0 = __uint_as_float(r[j]) * inv - t4.x;
-                            const float d1 = __uint_as_float(r[j + 1]) * inv - t4.y;
-                            const float d2 = __uint_as_float(r[j + 2]) * inv - t4.z;
-                            const float d3 = __uint_as_float(r[j + 3]) * inv - t4.w;
-                            loss += double(d0) * d0 + double(d1) * d1 + double(d2) * d2 +
-                                    double(d3) * d3;
-                            const float4 g = make_float4(d0 * mse.scale, d1 * mse.scale,
-                                                         d2 * mse.scale, d3 * mse.scale);
-                            vmax = fmaxf(vmax, fmaxf(fmaxf(fabsf(g.x), fabsf(g.y)),
-                                                     fmaxf(fabsf(g.z), fabsf(g.w))));
-                            *reinterpret_cast<float4 *>(dst + j) = g;
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4 *>(dst + j) = make_float4(
+                                    __uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
+                                    __uint_as_float(r[j + 2]) * inv,
+                                    __uint_as_float(r[j + 3]) * inv);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (col0 + j < N) dst[j] = __uint_as_float(r[j]) * inv;
                         }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < N) {
-                                const float d = __uint_as_float(r[j]) * inv - tr[j];
-                                loss += double(d) * double(d);
-                                const float g = d * mse.scale;
-                                vmax = fmaxf(vmax, fabsf(g));
-                                dst[j] = g;
-                            }
                     }
-                } else if (row < M) {
-                    const int col0 = tile_n * BN + c0;
-                    float *dst = out + (long long)row * ldc + col0;
-                    if (vec && col0 + 32 <= N) {
+                    continue;
+                }
+                // MSE: lane = row on the way in (pitch 33: conflict-free both
+                // ways), lane = column on the way out.
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4 *>(dst + j) = make_float4(
-                                __uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
-                                __uint_as_float(r[j + 2]) * inv, __uint_as_float(r[j + 3]) * inv);
-                    } else {
+                for (int j = 0; j < 32; ++j) blk[lane * 33 + j] = __uint_as_float(r[j]) * inv;
+                __syncwarp();
+                const int col = tile_n * BN + c0 + lane;
+                const bool col_ok = col < N;
+                {
+                    // dY = (Y - T) * scale in place of Y; sum (Y - T)^2 in double.
+                    float t[32];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < N) dst[j] = __uint_as_float(r[j]) * inv;
+                    for (int rr = 0; rr < 32; ++rr) {
+                        const int row = row_base + rr;
+                        t[rr] = row < M && col_ok ? mse.target[(long long)row * mse.ldt + col] : 0.f;
+                    }
+#pragma unroll
+                    for (int rr = 0; rr < 32; ++rr) {
+                        const int row = row_base + rr;
+                        if (row < M && col_ok) {
+                            const float d = blk[rr * 33 + lane] - t[rr];
+                            loss += double(d) * double(d);
+                            const float g = d * mse.scale;
+                            vmax = fmaxf(vmax, fabsf(g));
+                            out[(long long)row * ldc + col] = g;
+                        }
                     }
                 }
+                __syncwarp();
             }
         }
         if (mse.target) {

@@ -1,0 +1,202 @@
+"""One CSTLinear MSE training step sharded by output-row bands (one process per GPU).
+
+Rank g of G owns output rows [r0, r0 + nb) with nb = N_out / G and, for dX,
+input columns [c0, c0 + nc) with nc = N_in / G (both multiples of 32). Atoms,
+their AdamW moments, X and the target are replicated; every rank decodes and
+sorts all atoms (O(A) work). One step:
+
+    W[r0:r0+nb, :] (window assembly, f16 split) | f16 split of X
+    Y band = X W_band^T, then dY band = (Y band - T[:, band]) 2/(B N_out) with
+      its loss partials and max |dY|
+    max |dY|: all-reduce (MAX), so every band splits with one scale
+    dY bands: all-gather (float32 column blocks), split band by band into the
+      f16 planes of the whole dY
+    dX[:, c0:c0+nc] = dY W[:, c0:c0+nc] (second window assembly); all-gather of
+      the dX column blocks
+    dW band = dY_band^T X; banded pullback: each atom's gradient from the band's
+      rows (atoms whose footprints cross band edges -- the halo -- get partial
+      sums on several ranks)
+    atom gradients: all-reduce (SUM); CSTAdamW on every rank (identical)
+
+NCCL carries the dY / dX column-block all-gathers, the halo-atom gradient
+reduction (the whole [A, 4] gradient: 16 B per atom) and two scalars.
+Work per rank is 1/G of the weight assembly (twice: row and column windows),
+of the three GEMMs and of the pullback (plus the halo).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _native as N
+from . import runtime as R
+from .linear import CSTLinear
+from .optim import CSTAdamW
+from .train import OptimizerScalars, dp_loss_scale
+
+
+def band(n: int, rank: int, world: int):
+    """(start, length) of rank's band of n sites: equal bands, 32-site aligned."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    if n % world or (n // world) % 32:
+        raise ValueError(f"{n} sites do not split into {world} bands of a multiple of 32 sites")
+    nb = n // world
+    return rank * nb, nb
+
+
+class RowBandMSETrainStep(OptimizerScalars):
+    """Eager MSE training step of one layer sharded by output-row bands over a
+    process group (NCCL); ``process_group=None`` runs the whole layer as one band."""
+
+    LAUNCHES_PER_STEP = 26  # native kernels at G > 1 (one dY split per band)
+
+    def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
+                 process_group=None):
+        p = layer.atoms.p
+        super().__init__(layer, optimizer, p.device)
+        self.rows, self.need_dx, self.pg = int(rows), need_dx, process_group
+        self.world = dist.get_world_size(process_group) if process_group is not None else 1
+        self.rank = dist.get_rank(process_group) if process_group is not None else 0
+        dev = p.device
+        plan = layer._plan
+        self.plan = plan
+        self.ws = layer._workspace(dev)
+        A = self.atoms = p.shape[0]
+        B, no, ni = self.rows, plan.n_out, plan.n_in
+        self.r0, self.nb = band(no, self.rank, self.world)
+        self.c0, self.nc = band(ni, self.rank, self.world)
+        f32 = torch.float32
+        self.table = torch.empty(max(plan.table_bytes(A) // 4, 1), dtype=f32, device=dev)
+        self.scratch = self.ws.scratch(A)
+        # absmax words and scales: W band, X, dY (global), W column band
+        self.amax = torch.zeros(4, dtype=f32, device=dev)
+        self.scales = torch.ones(4, dtype=f32, device=dev)
+        self.w_band = torch.empty(self.nb, ni, dtype=f32, device=dev)
+        self.w16b = R.F16Split(self.nb, ni, dev, amax=self.amax[0:1], scale=self.scales[0:1])
+        self.x16 = R.F16Split(B, ni, dev, amax=self.amax[1:2], scale=self.scales[1:2])
+        self.dy16 = R.F16Split(B, no, dev, amax=self.amax[2:3], scale=self.scales[2:3])
+        if need_dx and self.world > 1:
+            self.w_col = torch.empty(no, self.nc, dtype=f32, device=dev)
+            self.w16c = R.F16Split(no, self.nc, dev, amax=self.amax[3:4],
+                                   scale=self.scales[3:4])
+        elif need_dx:
+            self.w16c = self.w16b  # one band: the column window is the whole W
+        if need_dx:
+            self.dx_band = torch.empty(B, self.nc, dtype=f32, device=dev)
+            self.dx_all = torch.empty(self.world, B, self.nc, dtype=f32, device=dev)
+        self.y = torch.empty(B, no, dtype=f32, device=dev)  # Y band at columns [r0, r0 + nb)
+        self.dy_band = torch.empty(B, self.nb, dtype=f32, device=dev)
+        self.dy_all = torch.empty(self.world, B, self.nb, dtype=f32, device=dev)
+        tiles = -(-self.nb // 128) * -(-ni // 256)
+        self.split = int(max(1, min(8, -(-B // 32), 148 // max(tiles, 1))))
+        self.ldg = R.pad4(ni)
+        self.gstride = self.nb * self.ldg
+        self.g = torch.empty(self.split * self.gstride, dtype=f32, device=dev)
+        self.grad = torch.empty(A, 4, dtype=f32, device=dev)
+        self.partial = torch.empty(1024, dtype=torch.float64, device=dev)
+        self.loss_sum = torch.zeros(1, dtype=torch.float64, device=dev)
+        self.scale = dp_loss_scale(B, no)
+        self.nblocks = ctypes.c_int32(0)
+        self._side = torch.cuda.Stream(dev)
+
+    def _gemm(self, M, N_, K, a_hi, a_lo, lda, a_mn, a_scale, b_hi, b_lo, ldb, b_mn, b_scale, c,
+              ldc, split=1, sstride=0, stream=None, what="gemm"):
+        st = stream if stream is not None else R._stream(self.layer.atoms.p.device)
+        P = ctypes.c_void_p
+        N.check(N.load().tcst_gemm_f16x3(M, N_, K, P(a_hi), P(a_lo), lda, a_mn, P(a_scale),
+                                         P(b_hi), P(b_lo), ldb, b_mn, P(b_scale), P(c), ldc,
+                                         split, sstride, R._vp(self.ws.status), st), what)
+
+    def _launch_grad(self, x, target):
+        plan, vp, lib = self.plan, R._vp, N.load()
+        p = self.layer.atoms.p
+        main = torch.cuda.current_stream(p.device)
+        side = self._side
+        st, st2 = main.cuda_stream, side.cuda_stream
+        oa, ia = ctypes.byref(plan.out_axis), ctypes.byref(plan.in_axis)
+        A, B, no, ni = self.atoms, self.rows, plan.n_out, plan.n_in
+        r0, nb, c0, nc = self.r0, self.nb, self.c0, self.nc
+        x16, dy16, w16b = self.x16, self.dy16, self.w16b
+        pg = self.pg
+        self.amax.zero_()
+        side.wait_stream(main)  # X split beside decode and weight assembly
+        N.check(lib.tcst_absmax(vp(x), B, ni, x.stride(0), vp(x16.amax), st2), "absmax x")
+        N.check(lib.tcst_split_f16(vp(x), B, ni, x.stride(0), vp(x16.amax), vp(x16.hi),
+                                   vp(x16.lo), x16.ld, vp(x16.scale), st2), "split x")
+        N.check(lib.tcst_decode_route(vp(p), A, oa, ia, ctypes.byref(plan.coords),
+                                      vp(self.table), None, None, vp(self.ws.status), st),
+                "decode")
+        sb = self.scratch.numel() * 4
+        N.check(lib.tcst_assemble_weight_window_f16(
+            vp(self.table), A, oa, ia, vp(self.scratch), sb, r0, nb, 0, ni, vp(self.w_band), ni,
+            vp(w16b.amax), vp(w16b.hi), vp(w16b.lo), w16b.ld, vp(w16b.scale), st), "weight band")
+        if self.need_dx and self.world > 1:
+            w16c = self.w16c
+            N.check(lib.tcst_assemble_weight_window_f16(
+                vp(self.table), A, oa, ia, vp(self.scratch), sb, 0, no, c0, nc, vp(self.w_col),
+                nc, vp(w16c.amax), vp(w16c.hi), vp(w16c.lo), w16c.ld, vp(w16c.scale), st),
+                "weight columns")
+        main.wait_stream(side)
+        y_band = self.y[:, r0:]
+        self._gemm(B, nb, ni, x16.hi.data_ptr(), x16.lo.data_ptr(), x16.ld, 0,
+                   x16.scale.data_ptr(), w16b.hi.data_ptr(), w16b.lo.data_ptr(), w16b.ld, 0,
+                   w16b.scale.data_ptr(), y_band.data_ptr(), no, what="gemm y")
+        N.check(lib.tcst_mse_grad_f32(vp(y_band), vp(target[:, r0:]), B, nb, no,
+                                      ctypes.c_float(self.scale), vp(self.dy_band), nb,
+                                      vp(self.partial), ctypes.byref(self.nblocks),
+                                      vp(dy16.amax), st), "mse")
+        torch.sum(self.partial[: self.nblocks.value], dim=0, keepdim=True, out=self.loss_sum)
+        if pg is not None:
+            dist.all_reduce(dy16.amax, op=dist.ReduceOp.MAX, group=pg)
+            dist.all_gather_into_tensor(self.dy_all, self.dy_band, group=pg)
+            bands = [self.dy_all[k] for k in range(self.world)]
+        else:
+            bands = [self.dy_band]
+        # One scale for the whole dY: every band splits with the global max.
+        for k, src in enumerate(bands):
+            off = 2 * k * nb  # f16 elements -> bytes
+            N.check(lib.tcst_split_f16(vp(src), B, nb, nb, vp(dy16.amax),
+                                       ctypes.c_void_p(dy16.hi.data_ptr() + off),
+                                       ctypes.c_void_p(dy16.lo.data_ptr() + off), dy16.ld,
+                                       vp(dy16.scale), st), "split dy")
+        if self.need_dx:
+            w16c = self.w16c
+            self._gemm(B, nc, no, dy16.hi.data_ptr(), dy16.lo.data_ptr(), dy16.ld, 0,
+                       dy16.scale.data_ptr(), w16c.hi.data_ptr(), w16c.lo.data_ptr(), w16c.ld, 1,
+                       w16c.scale.data_ptr(), self.dx_band.data_ptr(), nc, what="gemm dx")
+            if pg is not None:
+                dist.all_gather_into_tensor(self.dx_all, self.dx_band, group=pg)
+            else:
+                self.dx_all[0].copy_(self.dx_band)
+        off = 2 * r0
+        self._gemm(nb, ni, B, dy16.hi.data_ptr() + off, dy16.lo.data_ptr() + off, dy16.ld, 1,
+                   dy16.scale.data_ptr(), x16.hi.data_ptr(), x16.lo.data_ptr(), x16.ld, 1,
+                   x16.scale.data_ptr(), self.g.data_ptr(), self.ldg, self.split, self.gstride,
+                   what="gemm dw")
+        N.check(lib.tcst_pullback_band(vp(self.table), A, oa, ia, vp(self.g), self.ldg,
+                                       self.split, self.gstride, r0, nb, vp(self.grad), st),
+                "pullback")
+        if pg is not None:
+            dist.all_reduce(self.grad, group=pg)
+            dist.all_reduce(self.loss_sum, group=pg)
+        return self.loss_sum[0] / (B * no)
+
+    def __call__(self, x, target):
+        """One step on this rank's device tensors x [rows, N_in] and target
+        [rows, N_out] (replicated across ranks); returns the loss (0-d float64
+        device tensor, identical on every rank)."""
+        optimize = self._advance()
+        loss = self._launch_grad(x, target)
+        if optimize:
+            self._launch_opt()
+        return loss
+
+    def dx(self):
+        """dX [rows, N_in] of the last step, from the gathered column blocks."""
+        if not self.need_dx:
+            raise RuntimeError("built with need_dx=False")
+        return self.dx_all.permute(1, 0, 2).reshape(self.rows, self.plan.n_in)

@@ -2,15 +2,15 @@
 
 Computes exactly what ``y = layer(x); ((y - t)**2).mean().backward();
 optimizer.step()`` computes, without autograd bookkeeping: the MSE upstream
-gradient is produced by the epilogue of the forward GEMM (Y itself is never
-stored), every buffer is allocated once, and the step is a fixed sequence of
-native launches on the current stream:
+gradient is written over Y in one pass (with its loss partials and max |dY|),
+every buffer is allocated once, and the step is a fixed sequence of native
+launches on the current stream:
 
     decode/route -> bin sort (count, column prefix, scatter) -> weight (mass
-    cache, tile gather with max |W|, f16 split) | f16 split of X -> GEMM Y
-    with the MSE epilogue (dY, loss partials, max |dY|) -> f16 split of dY ->
+    cache, owner-pair coefficients and expansion, tile gather with max |W|,
+    f16 split) | f16 split of X -> GEMM Y -> MSE dY -> f16 split of dY ->
     GEMM dX -> GEMM dW (split-K) -> pullback (split-K sum, three footprint
-    classes, wide atoms) -> optimizer
+    classes, owner-pair projection and gradients, wide atoms) -> optimizer
 
 The optimizer reads its per-step scalars (bias corrections) from device memory,
 refreshed from a pinned host ring before each step, so :meth:`capture` can
@@ -51,13 +51,64 @@ def dp_reduce_gradient(grad: torch.Tensor, process_group=None) -> torch.Tensor:
     return grad
 
 
-class MSETrainStep:
-    LAUNCHES_PER_STEP = 19  # native kernels; torch adds the loss sum, one clear and one copy
+class OptimizerScalars:
+    """Device-side CSTAdamW step of one layer for captured or eager steps: the
+    host computes the step's scalars (bias corrections) and copies them through
+    a pinned ring into device memory, which the fused optimizer kernel reads."""
+
     RING = 64
+
+    def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, device):
+        self.layer, self.opt = layer, optimizer
+        nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
+        self.params_dev = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self._ring = torch.zeros(self.RING, nbytes, dtype=torch.uint8).pin_memory()
+        self._ring_events = [None] * self.RING
+        self._slot = 0
+        self._state = None
+        self._kind = None
+
+    def _upload(self, h):
+        """Copy the step's optimizer scalars to the device through the pinned ring."""
+        slot = self._slot
+        ev = self._ring_events[slot]
+        if ev is not None:
+            ev.synchronize()  # the copy that last read this slot has run
+        ctypes.memmove(self._ring[slot].data_ptr(), ctypes.addressof(h), ctypes.sizeof(h))
+        self.params_dev.copy_(self._ring[slot], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._ring_events[slot] = ev
+        self._slot = (slot + 1) % self.RING
+
+    def _advance(self):
+        """Host side of one optimizer step: step count and scalars to the device.
+        Returns False when the learning rate is 0 (the step leaves p unchanged)."""
+        p = self.layer.atoms.p
+        out = self.opt.site_step(p)
+        p.grad = self.grad
+        if out is None:
+            return False
+        h, self._state, self._kind = out
+        self._upload(h)
+        return True
+
+    def _launch_opt(self):
+        p = self.layer.atoms.p
+        state = self._state
+        vp = R._vp
+        N.check(N.load().tcst_optimizer_step_device(
+            vp(p), vp(self.grad), vp(state["exp_avg"]), vp(state["exp_avg_sq"]), self.atoms,
+            self._kind, vp(self.params_dev), R._stream(p.device)), "optimizer")
+
+
+class MSETrainStep(OptimizerScalars):
+    LAUNCHES_PER_STEP = 24  # native kernels; torch adds the loss sum, one clear and one copy
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
                  process_group=None, world_rows=None):
-        self.layer, self.opt, self.rows = layer, optimizer, int(rows)
+        super().__init__(layer, optimizer, layer.atoms.p.device)
+        self.rows = int(rows)
         self.need_dx = need_dx
         self.pg = process_group
         p = layer.atoms.p
@@ -87,18 +138,9 @@ class MSETrainStep:
         self.gstride = plan.n_out * self.ldg
         self.g = torch.empty(self.split * self.gstride, dtype=f32, device=dev)
         self.grad = torch.empty(A, 4, dtype=f32, device=dev)
-        # One loss partial per 32 rows of every 128 x 256 tile of the Y GEMM.
-        tiles = -(-plan.n_out // 256) * -(-self.rows // 128)
-        self.partial = torch.empty(max(4 * tiles, 1), dtype=torch.float64, device=dev)
+        self.partial = torch.empty(1024, dtype=torch.float64, device=dev)  # loss partials
         self.scale = dp_loss_scale(self.rows, plan.n_out, world_rows)
         self.nblocks = ctypes.c_int32(0)
-        nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
-        self.params_dev = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
-        self._ring = torch.zeros(self.RING, nbytes, dtype=torch.uint8).pin_memory()
-        self._ring_events = [None] * self.RING
-        self._slot = 0
-        self._state = None
-        self._kind = None
         self._graphs = {}
         self._opt_graph = None
         # Side stream for the branches that do not depend on the main chain
@@ -106,19 +148,6 @@ class MSETrainStep:
         self._side = torch.cuda.Stream(dev)
 
     # -- pieces --------------------------------------------------------------------
-
-    def _upload(self, h):
-        """Copy the step's optimizer scalars to the device through the pinned ring."""
-        slot = self._slot
-        ev = self._ring_events[slot]
-        if ev is not None:
-            ev.synchronize()  # the copy that last read this slot has run
-        ctypes.memmove(self._ring[slot].data_ptr(), ctypes.addressof(h), ctypes.sizeof(h))
-        self.params_dev.copy_(self._ring[slot], non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record()
-        self._ring_events[slot] = ev
-        self._slot = (slot + 1) % self.RING
 
     def _launch(self, x, target, optimize=True):
         """Enqueue the step's kernels (and the gradient all-reduce) on the current
@@ -128,14 +157,6 @@ class MSETrainStep:
         if optimize:
             self._launch_opt()
         return loss
-
-    def _launch_opt(self):
-        p = self.layer.atoms.p
-        state = self._state
-        vp = R._vp
-        N.check(N.load().tcst_optimizer_step_device(
-            vp(p), vp(self.grad), vp(state["exp_avg"]), vp(state["exp_avg_sq"]), self.atoms,
-            self._kind, vp(self.params_dev), R._stream(p.device)), "optimizer")
 
     def _launch_grad(self, x, target):
         """Forward and backward kernels up to this rank's atom gradient."""
@@ -170,12 +191,13 @@ class MSETrainStep:
                                              vp(w16.amax), vp(w16.hi), vp(w16.lo), w16.ld,
                                              vp(w16.scale), st), "weight")
         main.wait_stream(side)
-        N.check(lib.tcst_gemm_f16x3_mse(rows, plan.n_out, plan.n_in, vp(x16.hi), vp(x16.lo),
-                                        x16.ld, vp(x16.scale), vp(w16.hi), vp(w16.lo), w16.ld,
-                                        vp(w16.scale), vp(target), plan.n_out,
-                                        ctypes.c_float(self.scale), vp(self.y), plan.n_out,
-                                        vp(self.partial), ctypes.byref(self.nblocks),
-                                        vp(dy16.amax), vp(ws.status), st), "gemm y + mse")
+        # Y, then dY in place with the loss partials and max |dY| (a separate
+        # pass measured faster than folding the loss into the GEMM epilogue).
+        gemm(rows, plan.n_out, plan.n_in, x16, 0, w16, 0, self.y, plan.n_out, what="gemm y")
+        N.check(lib.tcst_mse_grad_f32(vp(self.y), vp(target), rows, plan.n_out, plan.n_out,
+                                      ctypes.c_float(self.scale), vp(self.y), plan.n_out,
+                                      vp(self.partial), ctypes.byref(self.nblocks),
+                                      vp(dy16.amax), st), "mse")
         N.check(lib.tcst_split_f16(vp(self.y), rows, plan.n_out, plan.n_out, vp(dy16.amax),
                                    vp(dy16.hi), vp(dy16.lo), dy16.ld, vp(dy16.scale), st),
                 "split dy")
@@ -193,18 +215,6 @@ class MSETrainStep:
                                   self.gstride, vp(self.grad), st), "pullback")
         main.wait_stream(side)
         return loss
-
-    def _advance(self):
-        """Host side of one optimizer step: step count and scalars to the device.
-        Returns False when the learning rate is 0 (the step leaves p unchanged)."""
-        p = self.layer.atoms.p
-        out = self.opt.site_step(p)
-        p.grad = self.grad
-        if out is None:
-            return False
-        h, self._state, self._kind = out
-        self._upload(h)
-        return True
 
     # -- public --------------------------------------------------------------------
 
