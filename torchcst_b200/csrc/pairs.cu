@@ -188,24 +188,33 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_o
 }
 
 // G holds chart rows [band.r0, band.r0 + band.wr) at gm + (row - band.r0) ldg.
+// A CTA covers PP_COLS input columns, PP_COLS / PX_CHUNK per thread, so each
+// staged basis value feeds several columns.
+constexpr int PP_PER_THREAD = 1;
+constexpr int PP_COLS = PX_CHUNK * PP_PER_THREAD;
+
 __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_out, int n_in,
                                                                 const float *__restrict__ gm,
                                                                 long long ldg, Window band) {
     pdl_wait();
     const BinGeom &g = tv.geom;
-    const int chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
+    const int chunks = (n_in + PP_COLS - 1) / PP_COLS;
     int l, a, ch;
     if (active_pairs(tv) == 0 || !expand_cta(g, chunks, l, a, ch)) return;
     if (!tv.node_on[g.pl_node[l] + a] || !node_covers(g, l, a, band.r0, band.wr, n_out)) return;
     const int T = g.pl_T[l], F = g.pl_K[l] * T;
-    const int i = ch * PX_CHUNK + threadIdx.x;
+    const int i0 = ch * PP_COLS + threadIdx.x;
     // Distinct chart rows of the footprint: all rows when it wraps onto itself.
     const int rows = F >= n_out ? n_out : F;
     const int row0 = F >= n_out ? 0 : a * T;
-    __shared__ float sphi[32][PF + 1];
-    float p[PF];
+    constexpr int PF4 = (PF + 3) / 4; // basis values as float4s (padded with zeros)
+    __shared__ float4 sphi[32][PF4];
+    __shared__ int srow[32]; // band-relative row, or -1 outside the band
+    float p[PP_PER_THREAD][PF];
 #pragma unroll
-    for (int f = 0; f < PF; ++f) p[f] = 0.f;
+    for (int u = 0; u < PP_PER_THREAD; ++u)
+#pragma unroll
+        for (int f = 0; f < PF; ++f) p[u][f] = 0.f;
     for (int r0 = 0; r0 < rows; r0 += 32) {
         const int nr = min(32, rows - r0);
         __syncthreads();
@@ -215,25 +224,43 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
             row -= row >= n_out ? n_out : 0;
             const bool in = row >= band.r0 && row < band.r0 + band.wr;
             pair_basis(row - a * T, F, n_out, phi);
+            float *dst = reinterpret_cast<float *>(sphi[threadIdx.x]);
 #pragma unroll
-            for (int f = 0; f < PF; ++f) sphi[threadIdx.x][f] = in ? phi[f] : 0.f;
+            for (int f = 0; f < 4 * PF4; ++f) dst[f] = f < PF ? phi[f] : 0.f;
+            srow[threadIdx.x] = in ? row - band.r0 : -1;
         }
         __syncthreads();
-        if (i < n_in) {
-            for (int j = 0; j < nr; ++j) {
-                int row = row0 + r0 + j;
-                row -= row >= n_out ? n_out : 0;
-                if (row < band.r0 || row >= band.r0 + band.wr) continue;
-                const float gv = gm[(long long)(row - band.r0) * ldg + i];
+#pragma unroll 4
+        for (int j = 0; j < nr; ++j) {
+            const int br = srow[j]; // rows outside the band contribute zero
+            const float *grow = gm + (long long)max(br, 0) * ldg;
+            float gv[PP_PER_THREAD];
 #pragma unroll
-                for (int f = 0; f < PF; ++f) p[f] = fmaf(sphi[j][f], gv, p[f]);
+            for (int u = 0; u < PP_PER_THREAD; ++u) {
+                const int i = i0 + u * PX_CHUNK;
+                gv[u] = br >= 0 && i < n_in ? grow[i] : 0.f;
+            }
+#pragma unroll
+            for (int q = 0; q < PF4; ++q) {
+                const float4 ph4 = sphi[j][q];
+                const float ph[4] = {ph4.x, ph4.y, ph4.z, ph4.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (4 * q + e < PF)
+#pragma unroll
+                        for (int u = 0; u < PP_PER_THREAD; ++u)
+                            p[u][4 * q + e] = fmaf(ph[e], gv[u], p[u][4 * q + e]);
             }
         }
     }
-    if (i < n_in) {
-        float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in + i;
 #pragma unroll
-        for (int f = 0; f < PF; ++f) out[(long long)f * n_in] = p[f];
+    for (int u = 0; u < PP_PER_THREAD; ++u) {
+        const int i = i0 + u * PX_CHUNK;
+        if (i < n_in) {
+            float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in + i;
+#pragma unroll
+            for (int f = 0; f < PF; ++f) out[(long long)f * n_in] = p[u][f];
+        }
     }
 }
 
@@ -341,7 +368,7 @@ int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const Wi
     const unsigned grid = unsigned(std::min<long long>(pair_bins, 148LL * 4));
     TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(grid), dim3(320), 0, st, tv, aw));
     TCST_CUDA(cudaGetLastError());
-    const long long ctas = expand_ctas(g, ia.sites);
+    const long long ctas = expand_ctas(g, ia.sites, PX_CHUNK);
     if (ctas > 0) {
         TCST_CUDA(launch_pdl(pair_expand_kernel, dim3(unsigned(ctas)), dim3(PX_CHUNK), 0, st, tv,
                              oa.sites, ia.sites, win));
@@ -354,7 +381,7 @@ int pair_backward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const f
                   long long ldg, const Window &band, float4 *grad, cudaStream_t st) {
     const BinGeom &g = tv.geom;
     if (g.npl == 0 || tv.atoms == 0) return TCST_OK;
-    const long long ctas = expand_ctas(g, ia.sites);
+    const long long ctas = expand_ctas(g, ia.sites, PP_COLS);
     if (ctas == 0) return TCST_OK;
     TCST_CUDA(launch_pdl(pair_project_kernel, dim3(unsigned(ctas)), dim3(PX_CHUNK), 0, st, tv,
                          oa.sites, ia.sites, g_dev, ldg, band));
@@ -367,8 +394,8 @@ int pair_backward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const f
     return TCST_OK;
 }
 
-long long expand_ctas(const BinGeom &g, int n_in) {
-    const long long chunks = (n_in + PX_CHUNK - 1) / PX_CHUNK;
+long long expand_ctas(const BinGeom &g, int n_in, int cols_per_cta) {
+    const long long chunks = (n_in + cols_per_cta - 1) / cols_per_cta;
     long long n = 0;
     for (int l = 0; l < g.npl; ++l)
         if (g.pl_exp[l]) n += g.pl_no[l] * chunks;

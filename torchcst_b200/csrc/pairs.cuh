@@ -62,8 +62,9 @@ __device__ __forceinline__ bool pair_basis(int d, int F, int n, float *phi) {
 }
 
 
-// CTAs of the expand / project launches (0 without expansion level-banks).
-long long expand_ctas(const BinGeom &g, int n_in);
+// CTAs of a launch over (expansion level-bank, output node, chunk of
+// cols_per_cta input sites): 0 without expansion level-banks.
+long long expand_ctas(const BinGeom &g, int n_in, int cols_per_cta);
 
 // C of every active pair, then R and the node flags of the expansion
 // level-banks for the nodes and columns the window's gather reads (before that

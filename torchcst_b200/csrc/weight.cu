@@ -403,29 +403,36 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
             pnode[i] = tv.node_on[g.pl_node[l] + a] ? (l << 16 | a) : -1;
         }
         __syncthreads();
-        for (int i = 0; i < np; ++i) {
-            const int key = pnode[i];
-            if (key < 0) continue; // CTA-uniform
-            const int l = key >> 16, a = key & 0xFFFF;
-            const int T = g.pl_T[l], F = g.pl_K[l] * T;
-            if (t < 32) {
+        // Up to three flagged nodes per pass (3 PF <= WT_STAGE staged terms):
+        // warp k stages the rows of node k, every thread the columns.
+        constexpr int PER_PASS = WT_STAGE / PF;
+        int i = 0;
+        while (true) {
+            int key[PER_PASS], nn = 0;
+            for (; i < np && nn < PER_PASS; ++i)
+                if (pnode[i] >= 0) key[nn++] = pnode[i]; // CTA-uniform
+            if (nn == 0) break;
+            if (warp < nn) {
+                const int l = key[warp] >> 16, a = key[warp] & 0xFFFF;
+                const int T = g.pl_T[l], F = g.pl_K[l] * T;
                 float phi[PF];
-                const bool on = t < TR && pair_basis(R0 + t - a * T, F, no, phi);
+                const bool on = lane < TR && pair_basis(R0 + lane - a * T, F, no, phi);
 #pragma unroll
-                for (int f = 0; f < PF; ++f) us[f][t] = on ? phi[f] : 0.f;
+                for (int f = 0; f < PF; ++f) us[warp * PF + f][lane] = on ? phi[f] : 0.f;
                 const unsigned m = __ballot_sync(0xffffffffu, on);
-                if (t < PF) rmask[t] = m;
-            } else {
-                const float *rb = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * ni + C0;
-                for (int e = t - 32; e < PF * TS; e += WT_THREADS - 32) {
-                    const int f = e / TS, c = e - f * TS;
-                    vs[f][c] = c < TC ? rb[(long long)f * ni + c] : 0.f;
-                }
+                if (lane < PF) rmask[warp * PF + lane] = m;
+            }
+            for (int e = t; e < nn * PF * TS; e += WT_THREADS) {
+                const int k = e / (PF * TS), rem = e - k * (PF * TS);
+                const int f = rem / TS, c = rem - f * TS;
+                const int l = key[k] >> 16, a = key[k] & 0xFFFF;
+                const float *rb = tv.pair_buf + g.pl_buf[l] + ((long long)a * PF + f) * ni + C0;
+                vs[k * PF + f][c] = c < TC ? rb[c] : 0.f;
             }
             __syncthreads();
             const unsigned wrows = 0xFFu << (8 * warp);
 #pragma unroll 1
-            for (int s2 = 0; s2 < PF; ++s2) {
+            for (int s2 = 0; s2 < nn * PF; ++s2) {
                 if (!(rmask[s2] & wrows)) continue;
                 const float2 uu = *reinterpret_cast<const float2 *>(&us[s2][r0]);
                 const float4 vv = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
