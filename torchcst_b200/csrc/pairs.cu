@@ -80,7 +80,32 @@ __device__ __forceinline__ void axis_alpha(const float *blk, float *alpha, float
 
 } // namespace
 
-__global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw) {
+// Whether output node a of level-bank l covers a row of [r0, r0 + wr).
+__device__ __forceinline__ bool node_covers(const BinGeom &g, int l, int a, int r0, int wr,
+                                            int n_out) {
+    int first;
+    const int T = g.pl_T[l];
+    const int cnt = cover_nodes(r0, wr, T, g.pl_K[l] * T, g.pl_no[l], n_out, first);
+    int d = a - first;
+    d += d < 0 ? g.pl_no[l] : 0;
+    return d < cnt;
+}
+
+// Whether input node b of level-bank l covers a column of [c0, c0 + wc).
+__device__ __forceinline__ bool in_node_covers(const BinGeom &g, int l, int b, int c0, int wc,
+                                               int n_in) {
+    int first;
+    const int T = g.pl_T[l];
+    const int cnt = cover_nodes(c0, wc, T, g.pl_K[l] * T, g.pl_ni[l], n_in, first);
+    int d = b - first;
+    d += d < 0 ? g.pl_ni[l] : 0;
+    return d < cnt;
+}
+
+// C of the active pairs whose output node covers the window's rows and whose
+// input node covers its columns (the only ones the window's expansion uses).
+__global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw, int n_out, int n_in,
+                                                        Window win) {
     pdl_wait();
     if (active_pairs(tv) == 0) return;
     const BinGeom &g = tv.geom;
@@ -91,6 +116,13 @@ __global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw) {
     for (int pb = blockIdx.x; pb < pair_bins; pb += gridDim.x) {
         const int bin = g.pl_base[0] + pb;
         if (!pair_active(g, tv.offsets, bin)) continue; // CTA-uniform
+        {
+            const int l = pair_lb(g, bin), idx = bin - g.pl_base[l];
+            const int a = idx / g.pl_ni[l], b = idx - a * g.pl_ni[l];
+            if (!node_covers(g, l, a, win.r0, win.wr, n_out) ||
+                !in_node_covers(g, l, b, win.c0, win.wc, n_in))
+                continue;
+        }
         const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
         float acc = 0.f;
         for (int k0 = begin; k0 < end; k0 += PC_CHUNK) {
@@ -133,16 +165,6 @@ __device__ __forceinline__ bool expand_cta(const BinGeom &g, int chunks, int &l,
     return true;
 }
 
-// Whether output node a of level-bank l covers a row of [r0, r0 + wr).
-__device__ __forceinline__ bool node_covers(const BinGeom &g, int l, int a, int r0, int wr,
-                                            int n_out) {
-    int first;
-    const int T = g.pl_T[l];
-    const int cnt = cover_nodes(r0, wr, T, g.pl_K[l] * T, g.pl_no[l], n_out, first);
-    int d = a - first;
-    d += d < 0 ? g.pl_no[l] : 0;
-    return d < cnt;
-}
 
 __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_out, int n_in,
                                                                Window win) {
@@ -204,9 +226,13 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
     if (!tv.node_on[g.pl_node[l] + a] || !node_covers(g, l, a, band.r0, band.wr, n_out)) return;
     const int T = g.pl_T[l], F = g.pl_K[l] * T;
     const int i0 = ch * PP_COLS + threadIdx.x;
-    // Distinct chart rows of the footprint: all rows when it wraps onto itself.
-    const int rows = F >= n_out ? n_out : F;
-    const int row0 = F >= n_out ? 0 : a * T;
+    // Rows to walk: the distinct chart rows of the footprint (all rows when it
+    // wraps onto itself) or the band's rows, whichever is fewer; rows outside
+    // the other set contribute zero.
+    const int foot_rows = F >= n_out ? n_out : F;
+    const bool by_band = band.wr < foot_rows;
+    const int rows = by_band ? band.wr : foot_rows;
+    const int row0 = by_band ? band.r0 : (F >= n_out ? 0 : a * T);
     constexpr int PF4 = (PF + 3) / 4; // basis values as float4s (padded with zeros)
     __shared__ float4 sphi[32][PF4];
     __shared__ int srow[32]; // band-relative row, or -1 outside the band
@@ -222,11 +248,12 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
             float phi[PF];
             int row = row0 + r0 + threadIdx.x;
             row -= row >= n_out ? n_out : 0;
-            const bool in = row >= band.r0 && row < band.r0 + band.wr;
-            pair_basis(row - a * T, F, n_out, phi);
+            // In the band, and on the footprint (pair_basis finds an image).
+            const bool in = row >= band.r0 && row < band.r0 + band.wr &&
+                            pair_basis(row - a * T, F, n_out, phi);
             float *dst = reinterpret_cast<float *>(sphi[threadIdx.x]);
 #pragma unroll
-            for (int f = 0; f < 4 * PF4; ++f) dst[f] = f < PF ? phi[f] : 0.f;
+            for (int f = 0; f < 4 * PF4; ++f) dst[f] = in && f < PF ? phi[f] : 0.f;
             srow[threadIdx.x] = in ? row - band.r0 : -1;
         }
         __syncthreads();
@@ -366,7 +393,8 @@ int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const Wi
     const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
     const int aw = axis_words(oa.modes);
     const unsigned grid = unsigned(std::min<long long>(pair_bins, 148LL * 4));
-    TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(grid), dim3(320), 0, st, tv, aw));
+    TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(grid), dim3(320), 0, st, tv, aw, oa.sites,
+                         ia.sites, win));
     TCST_CUDA(cudaGetLastError());
     const long long ctas = expand_ctas(g, ia.sites, PX_CHUNK);
     if (ctas > 0) {
