@@ -9,14 +9,15 @@ sorts all atoms (O(A) work). One step:
     Y band = X W_band^T, then dY band = (Y band - T[:, band]) 2/(B N_out) with
       its loss partials and max |dY|
     max |dY|: all-reduce (MAX), so every band splits with one scale
-    dY bands: all-gather (float32 column blocks), split band by band into the
-      f16 planes of the whole dY
-    dX[:, c0:c0+nc] = dY W[:, c0:c0+nc] (second window assembly); all-gather of
-      the dX column blocks
-    dW band = dY_band^T X; banded pullback: each atom's gradient from the band's
-      rows (atoms whose footprints cross band edges -- the halo -- get partial
-      sums on several ranks)
-    atom gradients: all-reduce (SUM); CSTAdamW on every rank (identical)
+    dY bands: all-gather (float32 column blocks), overlapped with
+      dW band = dY_band^T X and the banded pullback: each atom's gradient from
+      the band's rows (atoms whose footprints cross band edges -- the halo --
+      get partial sums on several ranks)
+    atom gradients: all-reduce (SUM), overlapped with the split of the gathered
+      dY bands into the f16 planes of the whole dY and
+      dX[:, c0:c0+nc] = dY W[:, c0:c0+nc] (second window assembly); all-gather
+      of the dX column blocks
+    CSTAdamW on every rank (identical)
 
 NCCL carries the dY / dX column-block all-gathers, the halo-atom gradient
 reduction (the whole [A, 4] gradient: 16 B per atom) and two scalars.
@@ -150,28 +151,22 @@ class RowBandMSETrainStep(OptimizerScalars):
                                       vp(self.partial), ctypes.byref(self.nblocks),
                                       vp(dy16.amax), st), "mse")
         torch.sum(self.partial[: self.nblocks.value], dim=0, keepdim=True, out=self.loss_sum)
+        # One scale for the whole dY: every band splits with the global max.
         if pg is not None:
             dist.all_reduce(dy16.amax, op=dist.ReduceOp.MAX, group=pg)
-            dist.all_gather_into_tensor(self.dy_all, self.dy_band, group=pg)
-            bands = [self.dy_all[k] for k in range(self.world)]
-        else:
-            bands = [self.dy_band]
-        # One scale for the whole dY: every band splits with the global max.
-        for k, src in enumerate(bands):
+
+        def split_band(src, k):
             off = 2 * k * nb  # f16 elements -> bytes
             N.check(lib.tcst_split_f16(vp(src), B, nb, nb, vp(dy16.amax),
                                        ctypes.c_void_p(dy16.hi.data_ptr() + off),
                                        ctypes.c_void_p(dy16.lo.data_ptr() + off), dy16.ld,
                                        vp(dy16.scale), st), "split dy")
-        if self.need_dx:
-            w16c = self.w16c
-            self._gemm(B, nc, no, dy16.hi.data_ptr(), dy16.lo.data_ptr(), dy16.ld, 0,
-                       dy16.scale.data_ptr(), w16c.hi.data_ptr(), w16c.lo.data_ptr(), w16c.ld, 1,
-                       w16c.scale.data_ptr(), self.dx_band.data_ptr(), nc, what="gemm dx")
-            if pg is not None:
-                dist.all_gather_into_tensor(self.dx_all, self.dx_band, group=pg)
-            else:
-                self.dx_all[0].copy_(self.dx_band)
+
+        split_band(self.dy_band, self.rank)
+        # The dY all-gather runs beside the dW GEMM and the banded pullback,
+        # which need only this rank's band.
+        gather_dy = (dist.all_gather_into_tensor(self.dy_all, self.dy_band, group=pg,
+                                                 async_op=True) if pg is not None else None)
         off = 2 * r0
         self._gemm(nb, ni, B, dy16.hi.data_ptr() + off, dy16.lo.data_ptr() + off, dy16.ld, 1,
                    dy16.scale.data_ptr(), x16.hi.data_ptr(), x16.lo.data_ptr(), x16.ld, 1,
@@ -180,8 +175,27 @@ class RowBandMSETrainStep(OptimizerScalars):
         N.check(lib.tcst_pullback_band(vp(self.table), A, oa, ia, vp(self.g), self.ldg,
                                        self.split, self.gstride, r0, nb, vp(self.grad), st),
                 "pullback")
+        # The halo-atom reduction runs beside the dX GEMM.
+        reduce_grad = (dist.all_reduce(self.grad, group=pg, async_op=True)
+                       if pg is not None else None)
+        if self.need_dx:
+            if gather_dy is not None:
+                gather_dy.wait()
+                for k in range(self.world):
+                    if k != self.rank:
+                        split_band(self.dy_all[k], k)
+            w16c = self.w16c
+            self._gemm(B, nc, no, dy16.hi.data_ptr(), dy16.lo.data_ptr(), dy16.ld, 0,
+                       dy16.scale.data_ptr(), w16c.hi.data_ptr(), w16c.lo.data_ptr(), w16c.ld, 1,
+                       w16c.scale.data_ptr(), self.dx_band.data_ptr(), nc, what="gemm dx")
+            if pg is not None:
+                dist.all_gather_into_tensor(self.dx_all, self.dx_band, group=pg)
+            else:
+                self.dx_all[0].copy_(self.dx_band)
+        elif gather_dy is not None:
+            gather_dy.wait()
         if pg is not None:
-            dist.all_reduce(self.grad, group=pg)
+            reduce_grad.wait()
             dist.all_reduce(self.loss_sum, group=pg)
         return self.loss_sum[0] / (B * no)
 
