@@ -622,6 +622,39 @@ def main():
     log(f"timed {args.steps} steps: {ms:.3f} ms device, {wall * 1e3:.3f} ms wall, "
         f"loss {float(loss):.5f}, gemm {gemm_ms:.3f} ms over 3 eager steps")
 
+    # No-dX variant (X as data, no dX GEMM): the same start state, its own graphs,
+    # exactly --steps timed steps.
+    def restore():
+        with torch.no_grad():
+            p.copy_(saved_p)
+        for k, v in saved_state.items():
+            if torch.is_tensor(v):
+                opt.state[p][k].copy_(v)
+            else:
+                opt.state[p][k] = v
+
+    restore()
+    step_nodx = MSETrainStep(layer, opt, ROWS, need_dx=False, process_group=pg,
+                             world_rows=ROWS * world)
+    for i in range(2):
+        step_nodx(xs[i % nbuf], ts[i % nbuf])
+    step_nodx.capture(list(zip(xs, ts)))
+    restore()
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    start.record()
+    for i in range(args.steps):
+        step_nodx(xs[i % nbuf], ts[i % nbuf])
+    end.record()
+    torch.cuda.synchronize()
+    ms_nodx = torch.tensor([start.elapsed_time(end) / args.steps], device=device)
+    if pg is not None:
+        dist.all_reduce(ms_nodx, op=dist.ReduceOp.MAX)
+    ms_nodx = float(ms_nodx.item())
+    step_nodx.release()
+    del step_nodx
+
     # End-to-end through the drop-in API with pinned host inputs: every step
     # copies its X and target from pinned host memory (on a copy stream, one step
     # ahead, into alternating device buffers) and reads its loss back.
@@ -716,6 +749,8 @@ def main():
                     "h2d_bytes_per_step": 2 * ROWS * N_IO * 4, "d2h_bytes_per_step": 4,
                     "api": "layer(x); loss.backward(); CSTAdamW.step()",
                     "copies": "pinned host -> device on a copy stream one step ahead"},
+            "no_dx": {"value": world * 1000.0 / ms_nodx, "ms_per_step": ms_nodx,
+                      "note": "the same step without dX (X as data): no dX GEMM"},
             "gpu_launches": MSETrainStep.LAUNCHES_PER_STEP * args.steps,
             "roofline": roofline, "clocks": clocks,
             "init": {"amplitude_scale": report.amplitude_scale,
