@@ -101,9 +101,12 @@ const char *tcst_version(void);
 const char *tcst_last_error(void);
 
 /* Bytes of the atom table written by tcst_decode_route: per-atom records,
- * footprint spans, the site values of narrow footprints, and the atoms sorted
- * into footprint-class x first-site-tile bins (in id order inside each bin)
- * that the weight assembly and the pullback walk. */
+ * footprint spans, the site values of narrow footprints, the atoms sorted into
+ * bins (footprint class x first-site tile, or owner pair for wide atoms of a
+ * shared tile hierarchy; id order inside each bin) that the weight assembly and
+ * the pullback walk, and the owner-pair region (per-pair 17 x 17 coefficient
+ * matrices, node flags and the expansion buffers of the Fourier owner-pair
+ * path, which the assembly and the pullback of the same table fill). */
 int64_t tcst_atom_table_bytes(int64_t atoms, const tcst_axis *out_axis,
                               const tcst_axis *in_axis);
 
@@ -124,7 +127,9 @@ int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_axis *out_ax
 /* Assemble the dense weight W = sum_a amp_a m_out,a (x) m_in,a (images folded
  * modulo N) from the atom table. Replaces the W side of factors/weight
  * (radius_cell_mass.py:225-263). Each 32 x 32 tile of W gathers, in a fixed
- * order, the bins whose atoms can reach it, so W is bitwise reproducible.
+ * order, the bins whose atoms can reach it; atoms of owner pairs with two or
+ * more atoms come in through the pair's 17 x 17 Fourier coefficients instead
+ * (the reference's wide-atom factorisation). W is bitwise reproducible.
  * scratch_dev is 16-byte aligned and tcst_weight_scratch_bytes() long
  * (2 x 128 floats per atom: the masses of mid-size footprints, written and read
  * within the call); its contents need no initialization. Any of

@@ -10,17 +10,19 @@
 //
 // The atoms come from the bins of the atom table. Each binned class has its
 // own kernel: a CTA stages in shared memory the window of G that every atom of
-// its tile(s) can reach (first-site tile + the class reach - 1 sites on both
-// axes, split-K partials summed while loading), then
-//   class 0 (footprints <= 16):  one thread per atom, site values from the
+// its bin can reach (first-site bin + the class reach - 1 sites on both axes),
+// then
+//   class 0 (footprints <= 16):   four threads per atom, site values from the
 //                                 table's site buffer;
 //   classes 1, 2 (<= 64, <= 128): one CTA per bin, one warp per atom, lanes
 //                                 over input sites, output-site values in
 //                                 per-warp shared memory.
-// Coarser classes (and every atom of an unbinned geometry): one CTA per atom
+// Atoms of active owner pairs take the owner-pair projection (pairs.cu). The
+// other coarse atoms (and every atom of an unbinned geometry): one CTA per atom
 // walks the footprint in chunks, G from global memory. Every atom is reduced by
-// one thread, one warp (fixed xor tree) or one CTA (fixed tree), so the
-// gradient is bitwise reproducible.
+// one thread group, one warp (fixed xor tree) or one CTA (fixed tree), so the
+// gradient is bitwise reproducible. A band of G's rows can stand in for G (the
+// output-row sharding): rows outside it read as zero.
 
 #include <algorithm>
 

@@ -1,18 +1,22 @@
-// Dense weight assembly W = sum_a amp_a m_out,a (x) m_in,a, the TF32 split and
-// the fused MSE gradient.
+// Dense weight assembly W = sum_a amp_a m_out,a (x) m_in,a (or a window of it),
+// the f16 / TF32 splits and the MSE gradient.
 //
 // Weight assembly uses the bins that tcst_decode_route stored in the atom
-// table (footprint class x first-site tile, atoms in id order inside a bin):
+// table (footprint class x first-site tile, or owner pair; atoms in id order
+// inside a bin):
 //   cache:  one warp per atom of classes 1..NFINE-1 writes the atom's masses on
 //           both footprints into the caller's scratch (class 0 masses are in the
 //           atom table's site buffer; coarser classes are evaluated where used);
+//   pairs:  the owner-pair coefficients and expansions (pairs.cu);
 //   gather: one CTA per TS x TS weight tile lists, in a fixed order, every bin
-//           whose atoms can reach the tile, keeps the atoms that do, stages their
-//           masses on the tile's rows and columns in shared memory (images folded
-//           modulo N) and accumulates the outer products in registers (2 x 4 per
-//           thread), then writes W and/or its TF32 split planes.
-// A fixed bin order and id-ordered bins make W bitwise reproducible; there are
-// no atomics.
+//           whose atoms can reach the tile (active owner pairs excepted), keeps
+//           the atoms that do, stages their masses on the tile's rows and
+//           columns in shared memory (images folded modulo N) and accumulates
+//           the outer products in registers (2 x 4 per thread), adds the
+//           rank-one terms of the active owner nodes that cover the tile, then
+//           writes W (or its TF32 split planes) and folds max |W| in.
+// A fixed bin order and id-ordered bins make W bitwise reproducible; the only
+// atomic is the max.
 
 #include <algorithm>
 #include <mutex>
