@@ -436,6 +436,32 @@ def run_config5(args):
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     ms, e2e = float(ms.item()), float(e2e_ms.item())
     flops = 3 * 2.0 * rows * n * n
+    # Roofline of the dominant kernel class, the tensor-core GEMM: this rank's Y
+    # band GEMM (2 B nb N fp32-equivalent flops) timed alone with CUDA events on
+    # the planes the last step left.
+    x16, w16b = step.x16, step.w16b
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(3):
+        step._gemm(rows, nb, n, x16.hi.data_ptr(), x16.lo.data_ptr(), x16.ld, 0,
+                   x16.scale.data_ptr(), w16b.hi.data_ptr(), w16b.lo.data_ptr(), w16b.ld, 0,
+                   w16b.scale.data_ptr(), step.y.data_ptr() + 4 * r0, n)
+    e1.record()
+    torch.cuda.synchronize()
+    gemm_ms = e0.elapsed_time(e1) / 3
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    bf16 = peaks.get("bf16_tflops", 1590.0)
+    achieved = 2.0 * rows * nb * n / (gemm_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": "tcst gemm_x3_kernel<F16> Y band = X W_band^T",
+                "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
+                "frac_of_3x_ceiling": achieved * 3.0 / bf16,
+                "peak_source": "bf16 dense burst, "
+                               + ("measured" if "bf16_tflops" in peaks else "fallback")
+                               + " (MEASURED_PEAKS.json)",
+                "traffic": None,
+                "note": "fp32-equivalent flops of one band GEMM / its CUDA-event time; three "
+                        "f16 tensor products per flop cap frac at 1/3"}
     spec = EXTRA[5]
     line = {"metric": spec["metric"], "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -450,7 +476,7 @@ def run_config5(args):
                     "d2h_bytes_per_step": 8,
                     "api": "RowBandMSETrainStep(x, target) per rank"},
             "gpu_launches": RowBandMSETrainStep.LAUNCHES_PER_STEP * args.steps,
-            "clocks": clocks, "loss": float(loss)}
+            "roofline": roofline, "clocks": clocks, "loss": float(loss)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
