@@ -99,3 +99,26 @@ def test_reference_layer_routed_to_the_plugin_needs_sm100(tc):
     layer.selector = plugin.selector()
     with pytest.raises(Exception, match="sm_100"):
         layer(torch.randn(4, 16))
+
+
+def test_state_dict_round_trips_with_the_reference(tc):
+    """A reference layer's state dict loads into the B200 layer and back
+    unchanged (atoms under atom_state.atoms.p, reference row order)."""
+    from torchcst import kernels as rk
+    from torchcst_b200 import CSTLinear, ChebyshevSpec, chart_presets, kernels
+    ref = _reference_layer(tc, 8, 16, rk.rational_radius(radius_max=4.0, radius_fraction=0.0),
+                           atoms=12)
+    ref_sd = ref.state_dict()
+    own = CSTLinear(charts=(chart_presets.regular_grid(8, geometry="flat_torus"),
+                            chart_presets.regular_grid(16, geometry="flat_torus")),
+                    atoms=12,
+                    kernel=kernels.product(kernels.cell_mass(ChebyshevSpec(modes=8)),
+                                           coordinates=kernels.rational_radius(radius_max=4.0)))
+    atoms_key = "atom_state.atoms.p"
+    assert atoms_key in ref_sd and atoms_key in own.state_dict()
+    own.load_state_dict({atoms_key: ref_sd[atoms_key]}, strict=False)
+    assert torch.equal(own.atoms.p.detach(), ref_sd[atoms_key])
+    with torch.no_grad():
+        own.atoms.p.add_(0.125)
+    ref.load_state_dict({atoms_key: own.state_dict()[atoms_key]}, strict=False)
+    assert torch.equal(ref.state_dict()[atoms_key], own.atoms.p.detach())
