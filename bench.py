@@ -692,7 +692,7 @@ def main():
     ht = [ts[i].cpu().pin_memory() for i in range(2)]
     dxb = [torch.empty(ROWS, N_IO, device=device) for _ in range(2)]
     dtb = [torch.empty(ROWS, N_IO, device=device) for _ in range(2)]
-    loss_host = torch.empty(2, dtype=torch.float32).pin_memory()
+    loss_host = torch.empty(2, dtype=torch.float64).pin_memory()
     copy_stream = torch.cuda.Stream(device)
     compute = torch.cuda.current_stream(device)
     ready = [torch.cuda.Event() for _ in range(2)]
@@ -706,9 +706,7 @@ def main():
             dtb[b].copy_(ht[b], non_blocking=True)
             ready[b].record(copy_stream)
 
-    def e2e_step(i):
-        b = i % 2
-        compute.wait_event(ready[b])
+    def autograd_step(b):
         opt.zero_grad(set_to_none=True)
         y = layer(dxb[b])
         lo = (y - dtb[b]).square().mean()
@@ -717,34 +715,57 @@ def main():
             dist.all_reduce(layer.atoms.p.grad, group=pg)
             layer.atoms.p.grad.div_(world)
         opt.step()
-        free[b].record(compute)
-        loss_host[b:b + 1].copy_(lo.detach().reshape(1), non_blocking=True)
+        return lo.detach().double()
 
-    for b in range(2):
-        free[b].record(compute)
-    e2e_copy(0)
-    for i in range(3):
-        e2e_copy(i + 1)
-        e2e_step(i)
-    torch.cuda.synchronize()
-    if pg is not None:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(3, args.steps)
-    e0.record()
-    copy_stream.wait_event(e0)
-    e2e_copy(0)
-    for i in range(e2e_steps):
-        if i + 1 < e2e_steps:
+    def e2e_ms_of(run_step):
+        """Per-step time of the pipelined host->device copies + run_step + loss
+        read-back, CUDA events around exactly max(3, steps) steps."""
+
+        def e2e_step(i):
+            b = i % 2
+            compute.wait_event(ready[b])
+            lo = run_step(b)
+            free[b].record(compute)
+            loss_host[b:b + 1].copy_(lo.reshape(1), non_blocking=True)
+
+        for b in range(2):
+            free[b].record(compute)
+        e2e_copy(0)
+        for i in range(3):
             e2e_copy(i + 1)
-        e2e_step(i)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=device)
-    if pg is not None:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = world * 1000.0 / float(e2e_ms.item())
+            e2e_step(i)
+        torch.cuda.synchronize()
+        if pg is not None:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n = max(3, args.steps)
+        e0.record()
+        copy_stream.wait_event(e0)
+        e2e_copy(0)
+        for i in range(n):
+            if i + 1 < n:
+                e2e_copy(i + 1)
+            e2e_step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / n], device=device)
+        if pg is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # The drop-in autograd API (layer(x), loss.backward(), CSTAdamW.step()) ...
+    e2e_autograd = world * 1000.0 / e2e_ms_of(autograd_step)
+    # ... and the fused step, graph-captured over the two device buffers.
+    with torch.no_grad():
+        p.copy_(saved_p)
+    step_e2e = MSETrainStep(layer, opt, ROWS, need_dx=True, process_group=pg,
+                            world_rows=ROWS * world)
+    step_e2e(dxb[0], dtb[0])
+    step_e2e.capture([(dxb[0], dtb[0]), (dxb[1], dtb[1])])
+    e2e_value = world * 1000.0 / e2e_ms_of(lambda b: step_e2e(dxb[b], dtb[b]))
+    step_e2e.release()
+    del step_e2e
 
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peaks = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
@@ -772,9 +793,11 @@ def main():
                                                 rows_per_rank=ROWS, parallelism=f"dp{world}",
                                                 l2="rotating inputs, 10 x 32 MiB buffers > L2"),
             "e2e": {"value": e2e_value, "unit": "steps/s",
-                    "h2d_bytes_per_step": 2 * ROWS * N_IO * 4, "d2h_bytes_per_step": 4,
-                    "api": "layer(x); loss.backward(); CSTAdamW.step()",
-                    "copies": "pinned host -> device on a copy stream one step ahead"},
+                    "h2d_bytes_per_step": 2 * ROWS * N_IO * 4, "d2h_bytes_per_step": 8,
+                    "api": "MSETrainStep(layer, CSTAdamW)(x, target), graph-captured",
+                    "copies": "pinned host -> device on a copy stream one step ahead",
+                    "autograd_api_value": e2e_autograd,
+                    "autograd_api": "layer(x); loss.backward(); CSTAdamW.step()"},
             "no_dx": {"value": world * 1000.0 / ms_nodx, "ms_per_step": ms_nodx,
                       "note": "the same step without dX (X as data): no dX GEMM"},
             "gpu_launches": MSETrainStep.LAUNCHES_PER_STEP * args.steps,
