@@ -189,7 +189,7 @@ struct MseEpilogue {
     float *amax;
 };
 
-template <class P, int BN, int STAGES, bool A_MN, bool B_MN>
+template <class P, int BN, int STAGES, bool A_MN, bool B_MN, bool MSE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_x3_kernel(const __grid_constant__ CUtensorMap map_a_hi,
                    const __grid_constant__ CUtensorMap map_a_lo,
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int quarter = warp & 3;
         const int row_base = tile_m * BM + quarter * 32;
         float *out = C + (long long)split * split_stride;
-        if (mse.target && row_base + lane < M) {
+        if (MSE && row_base + lane < M) {
             // The target tile is read only after the accumulator is ready:
             // bring its lines into L2 while the MMAs run.
             const float *tr = mse.target + (long long)(row_base + lane) * mse.ldt + tile_n * BN;
@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) r[j] = 0u;
                 }
-                if (!mse.target) {
+                if (!MSE) {
                     // Plain output: each lane stores its row's 32 columns.
                     const int row = row_base + lane;
                     const int col0 = tile_n * BN + c0;
@@ -423,7 +423,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 __syncwarp();
             }
         }
-        if (mse.target) {
+        if (MSE) {
             // One loss partial per epilogue warp (fixed xor tree), one max
             // atomic per warp.
 #pragma unroll
@@ -512,12 +512,12 @@ __global__ void zero_fill_kernel(float *__restrict__ C, long long M, long long N
     C[s * split_stride + r * ldc + c] = 0.0f;
 }
 
-template <class P, int BN, int STAGES, bool A_MN, bool B_MN>
+template <class P, int BN, int STAGES, bool A_MN, bool B_MN, bool MSE = false>
 static int launch(int M, int N, int K, const CUtensorMap *maps, int kps, int splits, float *C,
                   long long ldc, long long sstride, const float *sa, const float *sb,
                   unsigned *status, cudaStream_t stream, const MseEpilogue &mse) {
     using L = Layout<P, BN, STAGES>;
-    auto kern = gemm_x3_kernel<P, BN, STAGES, A_MN, B_MN>;
+    auto kern = gemm_x3_kernel<P, BN, STAGES, A_MN, B_MN, MSE>;
     static bool configured = false;
     if (!configured) {
         TCST_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -587,10 +587,15 @@ static int gemm_x3(const char *name, int64_t M, int64_t N, int64_t K, const void
     int kps = int(kb_per * BK);
     cudaStream_t st = (cudaStream_t)stream;
     unsigned *status = status_dev;
-    if (!a_mn_major && !b_mn_major)
+    if (!a_mn_major && !b_mn_major) {
+        if (mse.target)
+            return launch<P, BN, STAGES, false, false, true>(int(M), int(N), int(K), maps, kps,
+                                                             split_k, c_dev, ldc, split_stride,
+                                                             sa, sb, status, st, mse);
         return launch<P, BN, STAGES, false, false>(int(M), int(N), int(K), maps, kps, split_k,
                                                    c_dev, ldc, split_stride, sa, sb, status, st,
                                                    mse);
+    }
     if (!a_mn_major && b_mn_major)
         return launch<P, BN, STAGES, false, true>(int(M), int(N), int(K), maps, kps, split_k,
                                                   c_dev, ldc, split_stride, sa, sb, status, st,
