@@ -40,6 +40,8 @@ namespace tcst {
 namespace {
 
 constexpr int PC_CHUNK = 32;  // atoms staged per pass of pair_coef_kernel
+constexpr int PC_THREADS = 96; // >= PF * PF4 accumulating threads and PC_CHUNK stagers
+constexpr int PF4 = (PF + 3) / 4; // basis-length vectors as float4s (padded with zeros)
 constexpr int PX_CHUNK = 256; // input sites per CTA of expand / project
 constexpr int PG_COLS = 64;   // columns staged per pass of pair_grad_kernel
 
@@ -104,14 +106,15 @@ __device__ __forceinline__ bool in_node_covers(const BinGeom &g, int l, int b, i
 
 // C of the active pairs whose output node covers the window's rows and whose
 // input node covers its columns (the only ones the window's expansion uses).
-__global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw, int n_out, int n_in,
-                                                        Window win) {
+__global__ void __launch_bounds__(PC_THREADS) pair_coef_kernel(Table tv, int aw, int n_out,
+                                                               int n_in, Window win) {
     pdl_wait();
     if (active_pairs(tv) == 0) return;
     const BinGeom &g = tv.geom;
-    __shared__ float sa[PC_CHUNK][2 * PF + 1];
+    // amp alpha_out and alpha_in of PC_CHUNK atoms, rows padded to PF4 float4s.
+    __shared__ float4 so[PC_CHUNK][PF4], si[PC_CHUNK][PF4];
     const int t = threadIdx.x;
-    const int f = t / PF, gg = t - f * PF;
+    const int f = t / PF4, q = t - f * PF4; // C[f][4q .. 4q + 3] for t < PF * PF4
     const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
     for (int pb = blockIdx.x; pb < pair_bins; pb += gridDim.x) {
         const int bin = g.pl_base[0] + pb;
@@ -124,7 +127,7 @@ __global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw, int n_
                 continue;
         }
         const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
-        float acc = 0.f;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int k0 = begin; k0 < end; k0 += PC_CHUNK) {
             const int n = min(PC_CHUNK, end - k0);
             if (t < n) {
@@ -134,20 +137,34 @@ __global__ void __launch_bounds__(320) pair_coef_kernel(Table tv, int aw, int n_
                 axis_alpha(rec + 4, ao, nullptr, nullptr);
                 axis_alpha(rec + 4 + aw, ai, nullptr, nullptr);
                 const float amp = rec[0];
+                float *po = reinterpret_cast<float *>(so[t]), *pi = reinterpret_cast<float *>(si[t]);
 #pragma unroll
-                for (int e = 0; e < PF; ++e) {
-                    sa[t][e] = amp * ao[e];
-                    sa[t][PF + e] = ai[e];
+                for (int e = 0; e < 4 * PF4; ++e) {
+                    po[e] = e < PF ? amp * ao[e] : 0.f;
+                    pi[e] = e < PF ? ai[e] : 0.f;
                 }
             }
             __syncthreads();
-            if (t < PF * PF)
-                for (int j = 0; j < n; ++j) acc = fmaf(sa[j][f], sa[j][PF + gg], acc);
+            if (t < PF * PF4)
+                for (int j = 0; j < n; ++j) {
+                    const float a = reinterpret_cast<const float *>(so[j])[f];
+                    const float4 v = si[j][q];
+                    acc[0] = fmaf(a, v.x, acc[0]);
+                    acc[1] = fmaf(a, v.y, acc[1]);
+                    acc[2] = fmaf(a, v.z, acc[2]);
+                    acc[3] = fmaf(a, v.w, acc[3]);
+                }
             __syncthreads();
         }
-        if (t < PF * PF) tv.pair_c[(long long)pb * PF * PF + t] = acc;
+        if (t < PF * PF4) {
+            float *out = tv.pair_c + (long long)pb * PF * PF + f * PF;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (4 * q + e < PF) out[4 * q + e] = acc[e];
+        }
     }
 }
+
 
 // CTA -> (expansion level-bank l, output node a, input chunk ch).
 __device__ __forceinline__ bool expand_cta(const BinGeom &g, int chunks, int &l, int &a,
@@ -180,7 +197,7 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_o
     if ((ch + 1) * PX_CHUNK <= win.c0 || ch * PX_CHUNK >= win.c0 + win.wc) return;
     const int T = g.pl_T[l], F = g.pl_K[l] * T, nb = g.pl_ni[l];
     const int i = ch * PX_CHUNK + threadIdx.x;
-    __shared__ float C[PF * PF];
+    __shared__ float4 C4[PF][PF4]; // C rows padded to float4s
     float r[PF];
 #pragma unroll
     for (int f = 0; f < PF; ++f) r[f] = 0.f;
@@ -188,16 +205,27 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_o
         const int bin = g.pl_base[l] + a * nb + b;
         if (tv.offsets[bin + 1] - tv.offsets[bin] < PAIR_MIN) continue; // CTA-uniform
         __syncthreads();
-        for (int e = threadIdx.x; e < PF * PF; e += blockDim.x)
-            C[e] = tv.pair_c[(long long)(bin - g.pl_base[0]) * PF * PF + e];
+        for (int e = threadIdx.x; e < PF * 4 * PF4; e += blockDim.x) {
+            const int f = e / (4 * PF4), k = e - f * (4 * PF4);
+            reinterpret_cast<float *>(C4[f])[k] =
+                k < PF ? tv.pair_c[(long long)(bin - g.pl_base[0]) * PF * PF + f * PF + k] : 0.f;
+        }
         __syncthreads();
-        float phi[PF];
+        float phi[4 * PF4];
         if (i < n_in && pair_basis(i - b * T, F, n_in, phi)) {
+#pragma unroll
+            for (int k = PF; k < 4 * PF4; ++k) phi[k] = 0.f;
 #pragma unroll
             for (int f = 0; f < PF; ++f) {
                 float v = r[f];
 #pragma unroll
-                for (int e = 0; e < PF; ++e) v = fmaf(C[f * PF + e], phi[e], v);
+                for (int q = 0; q < PF4; ++q) {
+                    const float4 c = C4[f][q];
+                    v = fmaf(c.x, phi[4 * q], v);
+                    v = fmaf(c.y, phi[4 * q + 1], v);
+                    v = fmaf(c.z, phi[4 * q + 2], v);
+                    v = fmaf(c.w, phi[4 * q + 3], v);
+                }
                 r[f] = v;
             }
         }
@@ -233,7 +261,6 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
     const bool by_band = band.wr < foot_rows;
     const int rows = by_band ? band.wr : foot_rows;
     const int row0 = by_band ? band.r0 : (F >= n_out ? 0 : a * T);
-    constexpr int PF4 = (PF + 3) / 4; // basis values as float4s (padded with zeros)
     __shared__ float4 sphi[32][PF4];
     __shared__ int srow[32]; // band-relative row, or -1 outside the band
     float p[PP_PER_THREAD][PF];
@@ -297,10 +324,10 @@ __global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_
     if (active_pairs(tv) == 0) return;
     const BinGeom &g = tv.geom;
     __shared__ float sp[PF][PG_COLS + 1];
-    __shared__ float sphi[PG_COLS][PF + 1];
+    __shared__ float4 sphi[PG_COLS][PF4]; // basis rows padded to float4s
     __shared__ float H[PF * PF];
     const int t = threadIdx.x;
-    const int f = t / PF, gg = t - f * PF;
+    const int f = t / PF4, q = t - f * PF4; // H[f][4q .. 4q + 3] for t < PF * PF4
     const int lane = t & 31, warp = t >> 5, nw = blockDim.x >> 5;
     const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
     for (int pb = blockIdx.x; pb < pair_bins; pb += gridDim.x) {
@@ -316,7 +343,7 @@ __global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_
         const int col0 = F >= n_in ? 0 : b * T;
         const float *P = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in;
         // H = P_a Phi_b over the distinct chart columns of b's footprint.
-        float acc = 0.f;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int c0 = 0; c0 < cols; c0 += PG_COLS) {
             const int nc = min(PG_COLS, cols - c0);
             __syncthreads();
@@ -331,14 +358,26 @@ __global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_
                 int col = col0 + c0 + t;
                 col -= col >= n_in ? n_in : 0;
                 pair_basis(col - b * T, F, n_in, phi);
+                float *dst = reinterpret_cast<float *>(sphi[t]);
 #pragma unroll
-                for (int e = 0; e < PF; ++e) sphi[t][e] = phi[e];
+                for (int e = 0; e < 4 * PF4; ++e) dst[e] = e < PF ? phi[e] : 0.f;
             }
             __syncthreads();
-            if (t < PF * PF)
-                for (int j = 0; j < nc; ++j) acc = fmaf(sp[f][j], sphi[j][gg], acc);
+            if (t < PF * PF4)
+                for (int j = 0; j < nc; ++j) {
+                    const float pv = sp[f][j];
+                    const float4 v = sphi[j][q];
+                    acc[0] = fmaf(pv, v.x, acc[0]);
+                    acc[1] = fmaf(pv, v.y, acc[1]);
+                    acc[2] = fmaf(pv, v.z, acc[2]);
+                    acc[3] = fmaf(pv, v.w, acc[3]);
+                }
         }
-        if (t < PF * PF) H[t] = acc;
+        if (t < PF * PF4) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (4 * q + e < PF) H[f * PF + 4 * q + e] = acc[e];
+        }
         __syncthreads();
         // Every atom of the pair: one warp, lanes over rows f of H.
         const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
@@ -392,9 +431,9 @@ int pair_forward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const Wi
     if (g.npl == 0 || tv.atoms == 0) return TCST_OK;
     const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
     const int aw = axis_words(oa.modes);
-    const unsigned grid = unsigned(std::min<long long>(pair_bins, 148LL * 4));
-    TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(grid), dim3(320), 0, st, tv, aw, oa.sites,
-                         ia.sites, win));
+    const unsigned grid = unsigned(std::min<long long>(pair_bins, 148LL * 8));
+    TCST_CUDA(launch_pdl(pair_coef_kernel, dim3(grid), dim3(PC_THREADS), 0, st, tv, aw,
+                         oa.sites, ia.sites, win));
     TCST_CUDA(cudaGetLastError());
     const long long ctas = expand_ctas(g, ia.sites, PX_CHUNK);
     if (ctas > 0) {
