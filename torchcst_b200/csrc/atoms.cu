@@ -274,12 +274,23 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
             ac.phase0 = phase0;
             ac.omega = omega;
             float4 *s4 = reinterpret_cast<float4 *>(sites);
+            // cos / sin of pi t_j for consecutive sites by rotation from site 0
+            // (t_j = phase0 + 2 j / F): one sincospif for the start and one for
+            // the step instead of one per site.
+            float sj, cj, sd, cd;
+            sincospif(phase0, &sj, &cj);
+            sincospif(2.0f / float(F), &sd, &cd);
 #pragma unroll
             for (int q = 0; q < REACH / 4; ++q) {
                 if (4 * q < F) {
                     SiteVals v[4];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) v[u] = ac.values(4 * q + u);
+                    for (int u = 0; u < 4; ++u) {
+                        v[u] = ac.values_cs(cj, sj);
+                        const float cn = fmaf(cj, cd, -sj * sd);
+                        sj = fmaf(sj, cd, cj * sd);
+                        cj = cn;
+                    }
                     s4[q] = make_float4(v[0].m, v[1].m, v[2].m, v[3].m);
                     s4[REACH / 4 + q] = make_float4(v[0].dmu, v[1].dmu, v[2].dmu, v[3].dmu);
                     s4[REACH / 2 + q] = make_float4(v[0].dR, v[1].dR, v[2].dR, v[3].dR);
@@ -555,13 +566,17 @@ __global__ void __launch_bounds__(COL_SEGS * 32) bin_column_kernel(Table tv) {
             }
         }
     }
-    // Last CTA: bin starts = exclusive scan of the totals.
-    __threadfence();
+    // Last CTA: bin starts = exclusive scan of the totals. The barrier orders
+    // this CTA's column writes before thread 0's device-scope fence and ticket
+    // (the fence is cumulative), and the last CTA fences after its ticket.
     __syncthreads();
-    if (t == 0) last = atomicAdd(tv.sync, 1u) == gridDim.x - 1;
+    if (t == 0) {
+        __threadfence();
+        last = atomicAdd(tv.sync, 1u) == gridDim.x - 1;
+        if (last) __threadfence();
+    }
     __syncthreads();
     if (!last) return;
-    __threadfence();
     // Totals of other CTAs are read from L2 (__ldcg), past any stale L1 line,
     // COL_RUN at a time so their latencies overlap.
     const int *total = tv.counts + (long long)g.sort_blocks * g.nbins;

@@ -447,6 +447,10 @@ template <int M> struct AxisCoef {
         const float t = phase0 + 2.0f * float(j) / float(F);
         float s1, c1;
         sincospif(t, &s1, &c1);
+        return mass_c(c1);
+    }
+    // Mass from c1 = cos(pi t).
+    __device__ __forceinline__ float mass_c(float c1) const {
         float acc = c[0], cprev = 1.0f, ccur = c1;
 #pragma unroll
         for (int k = 1; k <= M; ++k) {
@@ -464,6 +468,10 @@ template <int M> struct AxisCoef {
     __device__ __forceinline__ SiteVals values_at(float t) const {
         float s1, c1;
         sincospif(t, &s1, &c1);
+        return values_cs(c1, s1);
+    }
+    // Values from c1 = cos(pi t), s1 = sin(pi t).
+    __device__ __forceinline__ SiteVals values_cs(float c1, float s1) const {
         float m = c[0], dR = dc[0], dmu = 0.0f;
         float cprev = 1.0f, ccur = c1, sprev = 0.0f, scur = s1;
 #pragma unroll

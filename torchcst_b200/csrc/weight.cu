@@ -90,7 +90,16 @@ __global__ void __launch_bounds__(256) mass_cache_kernel(Table tv, float *__rest
         ac.load_mass(rec + 4 + side * aw);
         const int F = side ? sp.w : sp.y;
         float *dst = cache + (a * 2 + side) * CACHE_SITES;
-        for (int j = l; j < F; j += 16) dst[j] = ac.mass(j);
+        // cos / sin of pi t_j by rotation along the lane's sites j = l, l + 16, ...
+        float sj, cj, sd, cd;
+        sincospif(ac.phase0 + 2.0f * float(l) / float(F), &sj, &cj);
+        sincospif(32.0f / float(F), &sd, &cd);
+        for (int j = l; j < F; j += 16) {
+            dst[j] = ac.mass_c(cj);
+            const float cn = fmaf(cj, cd, -sj * sd);
+            sj = fmaf(sj, cd, cj * sd);
+            cj = cn;
+        }
     }
 }
 
