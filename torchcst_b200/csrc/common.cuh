@@ -423,25 +423,43 @@ template <int M> struct AxisCoef {
     int first, F;
     float phase0, omega;
     float c[M + 1], dc[M + 1];
+    // The axis block is read as float4s: records and their axis blocks are
+    // multiples of 16 bytes in a 16-byte aligned table.
     __device__ __forceinline__ void load(const float *blk) {
-        first = reinterpret_cast<const int *>(blk)[0];
-        F = reinterpret_cast<const int *>(blk)[1];
-        phase0 = blk[2];
-        omega = blk[3];
+        constexpr int NW = (6 + 2 * M + 3) / 4 * 4; // header + c + dc, padded
+        float w[NW];
+        const float4 *b4 = reinterpret_cast<const float4 *>(blk);
+#pragma unroll
+        for (int i = 0; i < NW / 4; ++i) {
+            const float4 v = b4[i];
+            w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+        }
+        first = __float_as_int(w[0]);
+        F = __float_as_int(w[1]);
+        phase0 = w[2];
+        omega = w[3];
 #pragma unroll
         for (int k = 0; k <= M; ++k) {
-            c[k] = blk[4 + k];
-            dc[k] = blk[5 + M + k];
+            c[k] = w[4 + k];
+            dc[k] = w[5 + M + k];
         }
     }
     // Header and mass coefficients only (dcoef left unset).
     __device__ __forceinline__ void load_mass(const float *blk) {
-        first = reinterpret_cast<const int *>(blk)[0];
-        F = reinterpret_cast<const int *>(blk)[1];
-        phase0 = blk[2];
-        omega = blk[3];
+        constexpr int NW = (5 + M + 3) / 4 * 4; // header + c, padded
+        float w[NW];
+        const float4 *b4 = reinterpret_cast<const float4 *>(blk);
 #pragma unroll
-        for (int k = 0; k <= M; ++k) c[k] = blk[4 + k];
+        for (int i = 0; i < NW / 4; ++i) {
+            const float4 v = b4[i];
+            w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+        }
+        first = __float_as_int(w[0]);
+        F = __float_as_int(w[1]);
+        phase0 = w[2];
+        omega = w[3];
+#pragma unroll
+        for (int k = 0; k <= M; ++k) c[k] = w[4 + k];
     }
     __device__ __forceinline__ float mass(int j) const {
         const float t = phase0 + 2.0f * float(j) / float(F);

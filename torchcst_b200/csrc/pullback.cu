@@ -584,7 +584,8 @@ static int pullback(const char *name, const void *atom_table_dev, int64_t atoms,
     if (atoms < 0 || split < 1 || ldg < ia.sites || row0 < 0 || row0 + rows > oa.sites ||
         (split > 1 && split_stride < rows * ldg) ||
         (atoms && rows && (!atom_table_dev || !g_dev || !grad_dev)) ||
-        reinterpret_cast<uintptr_t>(grad_dev) % 16) {
+        reinterpret_cast<uintptr_t>(grad_dev) % 16 ||
+        reinterpret_cast<uintptr_t>(atom_table_dev) % 16) {
         tcst_set_error("%s: invalid arguments", name);
         return TCST_ERR_ARGUMENT;
     }

@@ -174,52 +174,78 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
             spre[1] = tv.offsets[1] - tv.offsets[0];
         }
     } else {
-        // Class bins within reach, then the pair bins of covering node pairs
-        // (active pairs count no atoms: they come in as rank-one terms below).
-        int ncls = 0;
-        for (int c = 0; c < g.nclass; ++c)
-            ncls += reach_tiles(c, g.fe, g.tr[c], no) * reach_tiles(c, g.fe, g.tc[c], ni);
-        nscan = ncls;
-        for (int l = 0; l < g.npl; ++l) {
-            int f0, f1;
-            const int F = g.pl_K[l] * g.pl_T[l];
-            nscan += cover_nodes(R0, TR, g.pl_T[l], F, g.pl_no[l], no, f0) *
-                     cover_nodes(C0, TC, g.pl_T[l], F, g.pl_ni[l], ni, f1);
-        }
-        for (int i = ncls + t; i < nscan; i += WT_THREADS) {
-            int rem = i - ncls, l = 0, co = 0, ci = 0, fo = 0, fi = 0, F = 0;
-            for (; l < g.npl; ++l) {
-                F = g.pl_K[l] * g.pl_T[l];
-                co = cover_nodes(R0, TR, g.pl_T[l], F, g.pl_no[l], no, fo);
-                ci = cover_nodes(C0, TC, g.pl_T[l], F, g.pl_ni[l], ni, fi);
-                if (rem < co * ci) break;
-                rem -= co * ci;
+        // Groups: the classes (their bins within reach), then the level-banks
+        // (the pair bins of covering node pairs; active pairs count no atoms:
+        // they come in as rank-one terms below). One thread per group finds
+        // its covering rows and columns, warp 0 forms the prefix over groups,
+        // and every entry then finds its group by bisection. Group
+        // descriptors and prefix borrow cspan / ccls, free until step 2.
+        const int ngroups = g.nclass + g.npl; // <= MAX_CLASSES + MAX_PAIR_LB <= 64
+        int4 *gdesc = cspan;                  // (first row, first column, columns, entries)
+        int *gpre = ccls;
+        if (t < ngroups) {
+            int cr, cc, fr, fc;
+            if (t < g.nclass) {
+                // Class edges are powers of two: the tile holding R0 by a shift.
+                const int sh = 31 - __clz(class_edge(t, g.fe));
+                cr = reach_tiles(t, g.fe, g.tr[t], no);
+                cc = reach_tiles(t, g.fe, g.tc[t], ni);
+                fr = R0 >> sh;
+                fc = C0 >> sh;
+            } else {
+                const int l = t - g.nclass, T = g.pl_T[l], F = g.pl_K[l] * T;
+                cr = cover_nodes(R0, TR, T, F, g.pl_no[l], no, fr);
+                cc = cover_nodes(C0, TC, T, F, g.pl_ni[l], ni, fc);
             }
-            const int u = rem / ci, v = rem - u * ci;
-            const int a = fo + u >= g.pl_no[l] ? fo + u - g.pl_no[l] : fo + u;
-            const int b = fi + v >= g.pl_ni[l] ? fi + v - g.pl_ni[l] : fi + v;
-            const int bin = g.pl_base[l] + a * g.pl_ni[l] + b;
-            sbeg[i] = tv.offsets[bin];
-            spre[i + 1] = pair_active(g, tv.offsets, bin) ? 0 : tv.offsets[bin + 1] - sbeg[i];
-            scls[i] = atom_class(make_int4(0, F, 0, F));
+            gdesc[t] = make_int4(fr, fc, cc, cr * cc);
         }
-        for (int i = t; i < ncls; i += WT_THREADS) {
-            int c = 0, rem = i, kr = 0, kc = 0;
-            for (; c < g.nclass; ++c) {
-                kr = reach_tiles(c, g.fe, g.tr[c], no);
-                kc = reach_tiles(c, g.fe, g.tc[c], ni);
-                if (rem < kr * kc) break;
-                rem -= kr * kc;
+        __syncthreads();
+        if (warp == 0) {
+            int lo = lane < ngroups ? gdesc[lane].w : 0;
+            int hi = lane + 32 < ngroups ? gdesc[lane + 32].w : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y0 = __shfl_up_sync(0xffffffffu, lo, o);
+                const int y1 = __shfl_up_sync(0xffffffffu, hi, o);
+                if (lane >= o) {
+                    lo += y0;
+                    hi += y1;
+                }
             }
-            const int e = class_edge(c, g.fe);
-            const int k = rem / kc, l = rem - k * kc;
-            int sr = R0 / e - k, sc = C0 / e - l;
-            sr += sr < 0 ? g.tr[c] : 0;
-            sc += sc < 0 ? g.tc[c] : 0;
-            const int bin = g.base[c] + sr * g.tc[c] + sc;
-            sbeg[i] = tv.offsets[bin];
-            spre[i + 1] = tv.offsets[bin + 1] - sbeg[i];
-            scls[i] = c;
+            const int lo_total = __shfl_sync(0xffffffffu, lo, 31);
+            gpre[lane + 1] = lo;
+            gpre[lane + 33] = lo_total + hi;
+            if (lane == 0) gpre[0] = 0;
+        }
+        __syncthreads();
+        nscan = gpre[ngroups];
+        for (int i = t; i < nscan; i += WT_THREADS) {
+            int lo = 0, hi = ngroups - 1; // last group with gpre[k] <= i
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (gpre[mid] <= i) lo = mid;
+                else hi = mid - 1;
+            }
+            const int4 d = gdesc[lo];
+            const int rem = i - gpre[lo], u = rem / d.z, v = rem - u * d.z;
+            if (lo < g.nclass) {
+                const int c = lo;
+                int sr = d.x - u, sc = d.y - v;
+                sr += sr < 0 ? g.tr[c] : 0;
+                sc += sc < 0 ? g.tc[c] : 0;
+                const int bin = g.base[c] + sr * g.tc[c] + sc;
+                sbeg[i] = tv.offsets[bin];
+                spre[i + 1] = tv.offsets[bin + 1] - sbeg[i];
+                scls[i] = c;
+            } else {
+                const int l = lo - g.nclass, F = g.pl_K[l] * g.pl_T[l];
+                const int a = d.x + u >= g.pl_no[l] ? d.x + u - g.pl_no[l] : d.x + u;
+                const int b = d.y + v >= g.pl_ni[l] ? d.y + v - g.pl_ni[l] : d.y + v;
+                const int bin = g.pl_base[l] + a * g.pl_ni[l] + b;
+                sbeg[i] = tv.offsets[bin];
+                spre[i + 1] = pair_active(g, tv.offsets, bin) ? 0 : tv.offsets[bin + 1] - sbeg[i];
+                scls[i] = atom_class(make_int4(0, F, 0, F));
+            }
         }
         __syncthreads();
         // Inclusive prefix of the counts in spre[1..nscan], contiguous runs per thread.
@@ -398,20 +424,37 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
     // flags are read in parallel first.
     if (active_pairs(tv) > 0) {
         __shared__ int pnode[MAX_PAIR_LB * 5]; // (l << 16 | a) of flagged nodes, else -1
-        int np = 0;
-        for (int l = 0; l < g.npl; ++l) {
-            int f0;
-            if (g.pl_exp[l])
-                np += cover_nodes(R0, TR, g.pl_T[l], g.pl_K[l] * g.pl_T[l], g.pl_no[l], no, f0);
+        // Covering output nodes per expansion level-bank (one thread each),
+        // prefix by warp 0, then one node per entry.
+        int *lfirst = ccls, *lpre = ccls + MAX_PAIR_LB; // ccls is free again
+        if (t < g.npl) {
+            int fo = 0, co = 0;
+            if (g.pl_exp[t])
+                co = cover_nodes(R0, TR, g.pl_T[t], g.pl_K[t] * g.pl_T[t], g.pl_no[t], no, fo);
+            lfirst[t] = fo;
+            lpre[t + 1] = co;
         }
-        for (int i = t; i < np; i += WT_THREADS) {
-            int rem = i, l = 0, co = 0, fo = 0;
-            for (; l < g.npl; ++l) {
-                if (!g.pl_exp[l]) continue;
-                co = cover_nodes(R0, TR, g.pl_T[l], g.pl_K[l] * g.pl_T[l], g.pl_no[l], no, fo);
-                if (rem < co) break;
-                rem -= co;
+        __syncthreads();
+        if (warp == 0) {
+            int inc = lane < g.npl ? lpre[lane + 1] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += y;
             }
+            if (lane < g.npl) lpre[lane + 1] = inc;
+            if (lane == 0) lpre[0] = 0;
+        }
+        __syncthreads();
+        const int np = lpre[g.npl];
+        for (int i = t; i < np; i += WT_THREADS) {
+            int lo = 0, hi = g.npl - 1; // last bank with lpre[l] <= i
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (lpre[mid] <= i) lo = mid;
+                else hi = mid - 1;
+            }
+            const int l = lo, rem = i - lpre[l], fo = lfirst[l];
             const int a = fo + rem >= g.pl_no[l] ? fo + rem - g.pl_no[l] : fo + rem;
             pnode[i] = tv.node_on[g.pl_node[l] + a] ? (l << 16 | a) : -1;
         }
@@ -723,6 +766,10 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
                     cudaStream_t st, float *amax_dev = nullptr,
                     Window win = Window{0, 0, -1, -1}) {
     if (win.wr < 0) win = Window{0, 0, oa.sites, ia.sites};
+    if (reinterpret_cast<uintptr_t>(atom_table_dev) % 16) {
+        tcst_set_error("weight assembly: the atom table must be 16-byte aligned");
+        return TCST_ERR_ARGUMENT;
+    }
     const int words = record_words(oa.modes, ia.modes);
     const Table tv = table_view(atom_table_dev, atoms, words, axis_geo(oa), axis_geo(ia));
     float *cache = static_cast<float *>(scratch);
