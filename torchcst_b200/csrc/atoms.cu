@@ -335,29 +335,48 @@ struct Decoded {
     unsigned bad;
 };
 
-// Physical amplitude, radii and chain-rule factors of one atom row.
+// Physical amplitude, radii and chain-rule factors of one atom row. Every lane
+// of the warp calls it outside divergent code: lanes 2i and 2i + 1 hold the same
+// row and split the rational path's two logarithms and two of its divisions
+// (`odd` is the lane's parity), exchanging the results by shuffles.
 __device__ inline Decoded decode_atom(float4 row, const CoordCfg &cc, const AxisCfg &out_ax,
-                                      const AxisCfg &in_ax) {
+                                      const AxisCfg &in_ax, bool odd) {
     Decoded d = {0, 0, 0, 0, 0, 0, 0u};
     if (!(isfinite(row.x) && isfinite(row.y) && isfinite(row.z) && isfinite(row.w)))
         d.bad |= TCST_STATUS_NONFINITE;
-    if (!d.bad && cc.kind == TCST_RATIONAL) {
+    const int lane = threadIdx.x & 31;
+    if (cc.kind == TCST_RATIONAL) {
         // _backends/torch/parameterizations/rational_radius.py:6-38.
+        const bool fin = !d.bad;
         const double av = row.x, q = row.y;
-        if (q < 0 || q > 1 || fabs(av) > cc.amax) d.bad |= TCST_STATUS_BOUNDS;
-        const double ratio = ddiv(av, 0.3);
-        const double denom = dadd(1.0, dmul(3.0, dmul(ratio, ratio)));
-        const double lower = dadd(cc.rmin, ddiv(dsub(cc.rbirth, cc.rmin), denom));
-        const double log_lower = log(lower), log_high = log(cc.rmax);
-        const double raw = exp(dadd(dmul(dsub(1.0, q), log_lower), dmul(q, log_high)));
-        const double value = q == 0 ? lower : (q == 1 ? cc.rmax : raw);
-        float enc = __double2float_rn(value);
-        enc = fminf(fmaxf(enc, cc.lo32), cc.hi32);
-        d.r_out = d.r_in = double(enc);
-        d.amp = av;
-        const double dlower = -(cc.rbirth - cc.rmin) * (6.0 * av / 0.09) / (denom * denom);
-        d.ch0 = raw * (1.0 - q) / lower * dlower;
-        d.ch1 = raw * (log_high - log_lower);
+        double denom = 1.0, lower = 1.0, raw = 0.0;
+        if (fin) {
+            if (q < 0 || q > 1 || fabs(av) > cc.amax) d.bad |= TCST_STATUS_BOUNDS;
+            const double ratio = ddiv(av, 0.3);
+            denom = dadd(1.0, dmul(3.0, dmul(ratio, ratio)));
+            lower = dadd(cc.rmin, ddiv(dsub(cc.rbirth, cc.rmin), denom));
+        }
+        // log(lower) on the even lane, log(r_max) on the odd one.
+        const double lx = log(odd ? cc.rmax : lower);
+        const double log_lower = __shfl_sync(0xffffffffu, lx, lane & ~1);
+        const double log_high = __shfl_sync(0xffffffffu, lx, lane | 1);
+        if (fin) {
+            raw = exp(dadd(dmul(dsub(1.0, q), log_lower), dmul(q, log_high)));
+            const double value = q == 0 ? lower : (q == 1 ? cc.rmax : raw);
+            float enc = __double2float_rn(value);
+            enc = fminf(fmaxf(enc, cc.lo32), cc.hi32);
+            d.r_out = d.r_in = double(enc);
+            d.amp = av;
+        }
+        // raw (1 - q) / lower on the even lane, 6 a / 0.09 on the odd one.
+        const double quot = odd ? (6.0 * av) / 0.09 : (raw * (1.0 - q)) / lower;
+        const double q_even = __shfl_sync(0xffffffffu, quot, lane & ~1);
+        const double q_odd = __shfl_sync(0xffffffffu, quot, lane | 1);
+        if (fin) {
+            const double dlower = -(cc.rbirth - cc.rmin) * q_odd / (denom * denom);
+            d.ch0 = q_even * dlower;
+            d.ch1 = raw * (log_high - log_lower);
+        }
     } else if (!d.bad) {
         // _backends/torch/parameterizations/polar_amp_width.py:127-139.
         const double s = row.x, t = row.y;
@@ -404,7 +423,7 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
     const int side = int(tid & 1); // 0 = output axis, 1 = input axis
     const bool live = a < atoms;
     const float4 row = live ? reinterpret_cast<const float4 *>(p)[a] : make_float4(0, 0, 0, 0);
-    const Decoded d = decode_atom(row, cc, out_ax, in_ax);
+    const Decoded d = decode_atom(row, cc, out_ax, in_ax, side != 0);
     const AxisCfg &ax = side ? in_ax : out_ax;
     float *rec = const_cast<float *>(tv.rec) + a * (long long)words;
     float *blk = rec + 4 + (side ? axis_words(out_ax.modes) : 0);

@@ -244,7 +244,9 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
         for (int j = 0; j < 4; ++j)
             if (4 * q + j >= fi) cm[j] = cd[j] = cr[j] = 0.f;
         const float *g0 = gw + (live ? (span.x - R0) * PITCH + (span.z - C0) + 4 * q : 0);
-        float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
+        // Row contractions of the thread's four columns with (m, dm/dmu,
+        // dm/dR) of the output sites, then one dot with the column values.
+        float h0[4] = {}, h1[4] = {}, h2[4] = {};
         const int base = lane & ~3;
 #pragma unroll
         for (int r = 0; r < REACH; ++r) {
@@ -259,14 +261,19 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const float gv = grow[j];
-                    const float t = gv * cm[j];
-                    const float u = gv * rm;
-                    s_amp = fmaf(t, rm, s_amp);
-                    s_mo = fmaf(t, rdmu, s_mo);
-                    s_mi = fmaf(u, cd[j], s_mi);
-                    s_r = fmaf(t, rdr, fmaf(u, cr[j], s_r));
+                    h0[j] = fmaf(gv, rm, h0[j]);
+                    h1[j] = fmaf(gv, rdmu, h1[j]);
+                    h2[j] = fmaf(gv, rdr, h2[j]);
                 }
             }
+        }
+        float s_amp = 0.f, s_mo = 0.f, s_mi = 0.f, s_r = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            s_amp = fmaf(h0[j], cm[j], s_amp);
+            s_mo = fmaf(h1[j], cm[j], s_mo);
+            s_mi = fmaf(h0[j], cd[j], s_mi);
+            s_r = fmaf(h2[j], cm[j], fmaf(h0[j], cr[j], s_r));
         }
 #pragma unroll
         for (int off = 1; off < 4; off <<= 1) {
