@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -30,6 +31,89 @@ extern "C" const char *tcst_last_error(void) { return g_error; }
 extern "C" const char *tcst_version(void) { return "tcst_b200 1.0 sm_100a"; }
 
 namespace tcst {
+
+namespace {
+struct SideSet {
+    std::mutex mu;
+    bool ready = false;
+    cudaStream_t s[SideStreams::MAX];
+    cudaEvent_t fork, join[SideStreams::MAX];
+};
+constexpr int MAX_SIDE_DEVICES = 64;
+SideSet g_sides[MAX_SIDE_DEVICES];
+
+cudaError_t create_side_set(SideSet &set, int dev) {
+    int cur = 0;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e == cudaSuccess && cur != dev) e = cudaSetDevice(dev);
+    for (int i = 0; e == cudaSuccess && i < SideStreams::MAX; ++i) {
+        e = cudaStreamCreateWithFlags(&set.s[i], cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&set.join[i], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&set.fork, cudaEventDisableTiming);
+    if (cur != dev) {
+        const cudaError_t e2 = cudaSetDevice(cur);
+        if (e == cudaSuccess) e = e2;
+    }
+    return e;
+}
+} // namespace
+
+SideStreams::SideStreams(cudaStream_t st, int n) : st_(st) {
+    // The calling stream belongs to the current device (as for every launch
+    // here); cudaStreamGetDevice is not permitted while the stream captures.
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        rc_ = tcst_cuda_check(e, "cudaGetDevice");
+        return;
+    }
+    if (dev < 0 || dev >= MAX_SIDE_DEVICES || n < 0 || n > MAX) {
+        tcst_set_error("side streams: device %d or count %d out of range", dev, n);
+        rc_ = TCST_ERR_UNSUPPORTED;
+        return;
+    }
+    SideSet &set = g_sides[dev];
+    set.mu.lock();
+    set_ = &set;
+    if (!set.ready) {
+        if ((e = create_side_set(set, dev)) != cudaSuccess) {
+            rc_ = tcst_cuda_check(e, "side stream creation");
+            return;
+        }
+        set.ready = true;
+    }
+    if ((e = cudaEventRecord(set.fork, st)) != cudaSuccess) {
+        rc_ = tcst_cuda_check(e, "cudaEventRecord (fork)");
+        return;
+    }
+    for (; n_ < n; ++n_) {
+        if ((e = cudaStreamWaitEvent(set.s[n_], set.fork, 0)) != cudaSuccess) {
+            rc_ = tcst_cuda_check(e, "cudaStreamWaitEvent (fork)");
+            return;
+        }
+        side_[n_] = set.s[n_];
+    }
+}
+
+int SideStreams::join() {
+    if (!set_) return rc_;
+    SideSet &set = *static_cast<SideSet *>(set_);
+    int rc = rc_;
+    for (int i = 0; i < n_; ++i) {
+        cudaError_t e = cudaEventRecord(set.join[i], side_[i]);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st_, set.join[i], 0);
+        if (e != cudaSuccess && rc == 0) rc = tcst_cuda_check(e, "side stream join");
+    }
+    joined_ = true;
+    set_ = nullptr;
+    set.mu.unlock();
+    return rc;
+}
+
+SideStreams::~SideStreams() {
+    if (set_) join();
+}
 
 __host__ int make_axis(const tcst_axis *in, AxisCfg *out, char *err, int errlen) {
     if (!in) {

@@ -572,3 +572,34 @@ int tcst_cuda_check(cudaError_t e, const char *what);
         cudaError_t e_ = (call);                                                 \
         if (e_ != cudaSuccess) return tcst_cuda_check(e_, #call);                \
     } while (0)
+
+namespace tcst {
+
+// Side streams for independent launches inside one entry point. The
+// constructor makes n (<= MAX) side streams of the current device wait
+// for the work queued so far on `st`; join() makes `st` wait for everything
+// queued on them since. The streams are created once per device and shared, so
+// the object holds the device's lock from fork to join (concurrent callers
+// serialize their host-side launch sequences, not their device work). Under
+// stream capture the side streams join the capture and are joined back before
+// the entry point returns. The destructor joins if join() was not called.
+class SideStreams {
+  public:
+    static constexpr int MAX = 4;
+    SideStreams(cudaStream_t st, int n);
+    ~SideStreams();
+    SideStreams(const SideStreams &) = delete;
+    SideStreams &operator=(const SideStreams &) = delete;
+    int status() const { return rc_; }
+    cudaStream_t operator[](int i) const { return side_[i]; }
+    int join();
+
+  private:
+    cudaStream_t st_;
+    cudaStream_t side_[MAX] = {};
+    void *set_ = nullptr;
+    int n_ = 0, rc_ = 0;
+    bool joined_ = false;
+};
+
+} // namespace tcst

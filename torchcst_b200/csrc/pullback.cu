@@ -540,7 +540,7 @@ using namespace tcst;
 template <int E>
 static int launch_classes(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, float *g_dev,
                           int64_t ldg, int split, int64_t split_stride, int b0, int bn,
-                          float4 *grad, cudaStream_t st) {
+                          float4 *grad, cudaStream_t st, cudaStream_t st1, cudaStream_t st2) {
     const BinGeom &geo = tv.geom;
     static bool configured = false;
     if (!configured) {
@@ -558,14 +558,14 @@ static int launch_classes(const Table &tv, const AxisCfg &oa, const AxisCfg &ia,
     TCST_CUDA(cudaGetLastError());
     if (geo.nclass > 1) {
         TCST_CUDA(launch_pdl(pullback_class_kernel<64, E>, dim3(unsigned(geo.tr[1] * geo.tc[1])),
-                             dim3(PC_THREADS), class_smem<64, E>(), st, tv, 1, oa.sites, ia.sites,
+                             dim3(PC_THREADS), class_smem<64, E>(), st1, tv, 1, oa.sites, ia.sites,
                              g_dev, ldg, split, split_stride, b0, bn, grad));
         TCST_CUDA(cudaGetLastError());
     }
     if (geo.nclass > 2) {
         TCST_CUDA(launch_pdl(pullback_class_kernel<128, E>,
                              dim3(unsigned(geo.tr[2] * geo.tc[2])), dim3(PC_THREADS),
-                             class_smem<128, E>(), st, tv, 2, oa.sites, ia.sites, g_dev, ldg,
+                             class_smem<128, E>(), st2, tv, 2, oa.sites, ia.sites, g_dev, ldg,
                              split, split_stride, b0, bn, grad));
         TCST_CUDA(cudaGetLastError());
     }
@@ -621,25 +621,31 @@ static int pullback(const char *name, const void *atom_table_dev, int64_t atoms,
         TCST_CUDA(cudaGetLastError());
         split = 1;
     }
+    // The class kernels, the owner-pair kernels and the wide kernel write
+    // disjoint atoms' gradients: they run side by side on four side streams
+    // beside the class-0 kernel, joined before returning.
+    SideStreams side(st, 4);
+    if ((rc = side.status())) return rc;
     if (geo.nclass > 0) {
-        const int rc2 = geo.fe == TS ? launch_classes<TS>(tv, oa, ia, g_dev, ldg, split,
-                                                           split_stride, b0, bn, grad, st)
-                                     : launch_classes<2 * TS>(tv, oa, ia, g_dev, ldg, split,
-                                                               split_stride, b0, bn, grad, st);
-        if (rc2) return rc2;
+        rc = geo.fe == TS ? launch_classes<TS>(tv, oa, ia, g_dev, ldg, split, split_stride, b0,
+                                               bn, grad, st, side[0], side[1])
+                          : launch_classes<2 * TS>(tv, oa, ia, g_dev, ldg, split, split_stride,
+                                                   b0, bn, grad, st, side[0], side[1]);
     }
     // Atoms of active owner pairs (their grads), then coarse classes, inactive
     // pair bins and invalid atoms (all atoms when unbinned): their range starts
     // at the first coarse bin and runs to the end of the ids.
-    if ((rc = pair_backward(tv, oa, ia, g_dev, ldg, Window{b0, 0, bn, ia.sites}, grad, st)))
-        return rc;
-    const int first_bin = geo.nclass > 0 ? geo.base[std::min(NFINE, geo.nclass)] : 0;
-    const long long ctas = std::min<long long>(atoms, 148LL * 8);
-    TCST_CUDA(launch_pdl(pullback_wide_kernel, dim3(unsigned(ctas)), dim3(PW_THREADS), 0, st, tv,
-                         tv.offsets + first_bin, oa, ia, g_dev, ldg, split, split_stride, b0, bn,
-                         grad));
-    TCST_CUDA(cudaGetLastError());
-    return TCST_OK;
+    if (!rc) rc = pair_backward(tv, oa, ia, g_dev, ldg, Window{b0, 0, bn, ia.sites}, grad, side[2]);
+    if (!rc) {
+        const int first_bin = geo.nclass > 0 ? geo.base[std::min(NFINE, geo.nclass)] : 0;
+        const long long ctas = std::min<long long>(atoms, 148LL * 8);
+        const cudaError_t e = launch_pdl(pullback_wide_kernel, dim3(unsigned(ctas)),
+                                         dim3(PW_THREADS), 0, side[3], tv, tv.offsets + first_bin,
+                                         oa, ia, g_dev, ldg, split, split_stride, b0, bn, grad);
+        if (e != cudaSuccess) rc = tcst_cuda_check(e, "pullback_wide_kernel");
+    }
+    const int rj = side.join();
+    return rc ? rc : rj;
 }
 
 extern "C" int tcst_pullback(const void *atom_table_dev, int64_t atoms, const tcst_axis *out_axis,

@@ -773,18 +773,28 @@ static int assemble(const void *atom_table_dev, int64_t atoms, const AxisCfg &oa
     const int words = record_words(oa.modes, ia.modes);
     const Table tv = table_view(atom_table_dev, atoms, words, axis_geo(oa), axis_geo(ia));
     float *cache = static_cast<float *>(scratch);
-    if (atoms > 0 && tv.geom.nclass > 0) {
-        // The class range is only known on the device; the kernel reads it.
-        const long long warps = std::min<long long>(atoms, sm_count() * 64LL);
-        TCST_CUDA(launch_pdl(mass_cache_kernel, dim3(unsigned((warps + 7) / 8)), dim3(256), 0, st, tv, cache));
-        TCST_CUDA(cudaGetLastError());
-    }
     if (max_scan_entries(tv.geom, oa.sites, ia.sites) > MAX_SCAN) {
         tcst_set_error("weight assembly: a weight tile would scan more than %d bins", MAX_SCAN);
         return TCST_ERR_UNSUPPORTED;
     }
-    int rc;
-    if ((rc = pair_forward(tv, oa, ia, win, st))) return rc;
+    int rc = 0;
+    {
+        // The mass cache and the owner-pair coefficients and expansions are
+        // independent: the pair kernels run on a side stream, joined before
+        // the gather.
+        SideStreams side(st, 1);
+        if ((rc = side.status())) return rc;
+        if (atoms > 0 && tv.geom.nclass > 0) {
+            // The class range is only known on the device; the kernel reads it.
+            const long long warps = std::min<long long>(atoms, sm_count() * 64LL);
+            const cudaError_t e = launch_pdl(mass_cache_kernel, dim3(unsigned((warps + 7) / 8)),
+                                             dim3(256), 0, st, tv, cache);
+            if (e != cudaSuccess) rc = tcst_cuda_check(e, "mass_cache_kernel");
+        }
+        if (!rc) rc = pair_forward(tv, oa, ia, win, side[0]);
+        const int rj = side.join();
+        if (rc || (rc = rj)) return rc;
+    }
     if (win.wr == 0 || win.wc == 0) return TCST_OK;
     const int tiles_r = (win.wr + TS - 1) / TS, tiles_c = (win.wc + TS - 1) / TS;
     GatherOut out = {weight_dev, weight_hi_dev, weight_lo_dev, ld_weight, ld_split, amax_dev,
