@@ -751,7 +751,14 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_scatter_kernel(Table tv) {
             __syncthreads();
         }
         start = __shfl_sync(0xffffffffu, start, leader);
-        if (live) tv.ids[start + rank] = int(a);
+        if (live) {
+            // The span and amplitude travel with the id, so that readers in
+            // sorted order load them beside the id instead of through it.
+            const int k = start + rank;
+            tv.ids[k] = int(a);
+            tv.sspan[k] = tv.spans[a];
+            tv.samp[k] = tv.rec[a * tv.words];
+        }
     }
 }
 

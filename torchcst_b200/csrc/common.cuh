@@ -312,7 +312,7 @@ __host__ __device__ inline BinGeom bin_geom(long long atoms, const AxisGeo &ao,
 
 struct TableLayout {
     long long spans_off, sites_off, binof_off, offsets_off, ids_off, counts_off, sync_off,
-        pair_c_off, node_off, buf_off, total; // bytes
+        pair_c_off, node_off, buf_off, sspan_off, samp_off, total; // bytes
     BinGeom geom;
 };
 
@@ -332,7 +332,10 @@ __host__ __device__ inline TableLayout table_layout(long long atoms, int words, 
     t.pair_c_off = t.sync_off + 16;
     t.node_off = align16(t.pair_c_off + 4LL * PF * PF * pair_bins);
     t.buf_off = align16(t.node_off + 4LL * t.geom.nodes);
-    t.total = align16(t.buf_off + 4LL * t.geom.buf_floats);
+    // Spans and amplitudes in sorted (ids) order, written by the scatter.
+    t.sspan_off = align16(t.buf_off + 4LL * t.geom.buf_floats);
+    t.samp_off = align16(t.sspan_off + atoms * 16);
+    t.total = align16(t.samp_off + atoms * 4);
     return t;
 }
 
@@ -351,6 +354,8 @@ struct Table {
                     // written by the sort's column prefix
     float *pair_buf; // expansion buffers: R = C Phi_in^T summed per output node, then
                      // the pullback's projections P = Phi_out^T G
+    int4 *sspan;     // spans[ids[k]] at sorted position k (scatter)
+    float *samp;     // amplitude (record word 0) of ids[k] at sorted position k (scatter)
     BinGeom geom;
 };
 
@@ -372,6 +377,8 @@ __host__ __device__ inline Table table_view(const void *base, long long atoms, i
     t.pair_c = reinterpret_cast<float *>(b + l.pair_c_off);
     t.node_on = reinterpret_cast<int *>(b + l.node_off);
     t.pair_buf = reinterpret_cast<float *>(b + l.buf_off);
+    t.sspan = reinterpret_cast<int4 *>(b + l.sspan_off);
+    t.samp = reinterpret_cast<float *>(b + l.samp_off);
     t.geom = l.geom;
     return t;
 }

@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
         float4 om = make_float4(0, 0, 0, 0), od = om, orr = om, im = om, id = om, ir = om;
         if (live) {
             a = tv.ids[k];
-            span = tv.spans[a];
+            span = tv.sspan[k];
             const float4 *sv = reinterpret_cast<const float4 *>(tv.sites + a * SITE_FLOATS);
             om = sv[q], od = sv[4 + q], orr = sv[8 + q];   // output rows 4q .. 4q+3
             im = sv[12 + q], id = sv[16 + q], ir = sv[20 + q]; // input columns 4q .. 4q+3
@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     {
         int rlo = W, rhi = 0, clo = W, chi = 0;
         for (int k = begin + threadIdx.x; k < end; k += blockDim.x) {
-            const int4 sp = tv.spans[tv.ids[k]];
+            const int4 sp = tv.sspan[k];
             rlo = min(rlo, sp.x - R0);
             rhi = max(rhi, sp.x - R0 + sp.y);
             clo = min(clo, sp.z - C0);
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(PC_THREADS) pullback_class_kernel(
     for (int k = begin + warp; k < end; k += PC_WARPS) {
         const long long a = a_next;
         if (k + PC_WARPS < end) a_next = tv.ids[k + PC_WARPS];
-        const int4 span = tv.spans[a];
+        const int4 span = tv.sspan[k];
         const float *rec = tv.rec + a * (long long)tv.words;
         const int fo = span.y, fi = span.w;
         {

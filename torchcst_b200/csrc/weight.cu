@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(256) mass_cache_kernel(Table tv, float *__rest
     for (long long k = begin + warp; k < end; k += nwarps) {
         const long long a = tv.ids[k];
         const float *rec = tv.rec + a * (long long)tv.words;
-        const int4 sp = tv.spans[a];
+        const int4 sp = tv.sspan[k];
         AxisCoef<8> ac;
         ac.load_mass(rec + 4 + side * aw);
         const int F = side ? sp.w : sp.y;
@@ -281,6 +281,7 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
         const int i = base + t;
         bool hit = false;
         int a = 0, cls = 0;
+        float amp = 0.f;
         int4 sp = make_int4(0, 0, 0, 0);
         if (i < total) {
             int lo = 0, hi = nscan - 1; // last slot with spre[slot] <= i
@@ -289,9 +290,11 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
                 if (spre[mid] <= i) lo = mid;
                 else hi = mid - 1;
             }
-            a = tv.ids[sbeg[lo] + (i - spre[lo])];
+            const int k = sbeg[lo] + (i - spre[lo]);
+            a = tv.ids[k];
             cls = scls[lo];
-            sp = tv.spans[a];
+            sp = tv.sspan[k];
+            amp = tv.samp[k];
             hit = window_hits(sp.x, sp.y, R0, TR, no) && window_hits(sp.z, sp.w, C0, TC, ni);
         }
         const unsigned m = __ballot_sync(0xffffffffu, hit);
@@ -308,7 +311,7 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
             cand[slot] = a;
             ccls[slot] = cls;
             cspan[slot] = sp;
-            camp[slot] = tv.rec[(long long)a * tv.words];
+            camp[slot] = amp;
         }
         __syncthreads();
         for (int h0 = 0; h0 < n; h0 += WT_STAGE) {
