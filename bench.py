@@ -205,8 +205,7 @@ def run_reference_arm(args):
     if rank != 0:
         return 0
     import numpy as np  # noqa: F401
-    steps = args.steps
-    warmup = min(args.warmup, 1)
+    steps, warmup = args.steps, args.warmup
     base = cpu_reference(steps, warmup, sample_rows=args.ref_rows)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "steps/s",
             "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
