@@ -13,6 +13,11 @@
  *   - Every pointer argument named *_dev is CUDA device memory of the current
  *     device; nothing here allocates device memory. Sizes are element counts.
  *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy stream.
+ *     It belongs to the current device. The weight assembly and pullback entry
+ *     points fork independent kernels onto internal side streams of that device
+ *     and join them back to `stream` before returning (event records and waits
+ *     only: the work completes in `stream` order and can be graph-captured).
+ *   - The atom table is 16-byte aligned (checked).
  *   - Every function returns TCST_OK (0) or a nonzero TCST_ERR_* code; the text
  *     of the most recent failure on the calling host thread is returned by
  *     tcst_last_error().
