@@ -14,7 +14,8 @@ import sys
 import pytest
 import torch
 
-REF_SRC = "/root/reference/src"
+# The reference source tree (its src/ directory); override with TORCHCST_REFERENCE_SRC.
+REF_SRC = os.environ.get("TORCHCST_REFERENCE_SRC", "/root/reference/src")
 
 
 @pytest.fixture(scope="module")
