@@ -75,8 +75,9 @@ def variance_scaling_(module: CSTLinear, variance, *, q=0.0, generator=None):
         else:
             cand[:, :2] = torch.stack((ratio, (1 - ratio.square()).sqrt()), -1) * rho
         dev = cand.to(device)
-        table = R.decode_route(plan, dev, ws.status)
-        energies = R.atom_energies(plan, table, cand.shape[0], device)
+        with R.on_device(device):
+            table = R.decode_route(plan, dev, ws.status)
+            energies = R.atom_energies(plan, table, cand.shape[0], device)
         energy = float(energies.sum())
         code = int(ws.status.item())
         if code:

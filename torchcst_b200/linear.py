@@ -219,7 +219,8 @@ class CSTLinear(nn.Module):
         if x.dtype != torch.float32:
             raise TypeError("the B200 backend computes the float32 CSTLinear contract")
         flat = x.reshape(-1, self.in_features).contiguous()
-        y = _CellMassLinear.apply(flat, p, self)
+        with R.on_device(p.device):  # the backward runs on the device's autograd thread
+            y = _CellMassLinear.apply(flat, p, self)
         return y.reshape(*x.shape[:-1], self.out_features)
 
     # -- diagnostics ---------------------------------------------------------------
@@ -229,10 +230,11 @@ class CSTLinear(nn.Module):
         """Dense float32 W [out, in] assembled on the device."""
         p = self.atoms.p
         ws = self._workspace(p.device)
-        table = R.decode_route(self._plan, p, ws.status)
-        self._maybe_check(ws)
-        w, _, _, _ = R.assemble_weight(self._plan, table, p.shape[0], ws, dense=True,
-                                       split=False)
+        with R.on_device(p.device):
+            table = R.decode_route(self._plan, p, ws.status)
+            self._maybe_check(ws)
+            w, _, _, _ = R.assemble_weight(self._plan, table, p.shape[0], ws, dense=True,
+                                           split=False)
         return w
 
     @torch.no_grad()
@@ -242,8 +244,9 @@ class CSTLinear(nn.Module):
         ws = self._workspace(p.device)
         routing = torch.empty(p.shape[0], 6, dtype=torch.int32, device=p.device)
         keys = torch.empty(p.shape[0], dtype=torch.int64, device=p.device)
-        R.decode_route(self._plan, p, ws.status, owner_keys=keys, routing=routing)
-        self._maybe_check(ws)
+        with R.on_device(p.device):
+            R.decode_route(self._plan, p, ws.status, owner_keys=keys, routing=routing)
+            self._maybe_check(ws)
         return routing, keys
 
     def extra_repr(self):

@@ -204,9 +204,10 @@ class CSTAdamW(AdamW):
                 h = self._native_params(site, group, int(state["step"].item()))
                 kind = N.TCST_POLAR if isinstance(site.kernel.coordinates, PolarRadius) else N.TCST_RATIONAL
                 grad = p.grad.contiguous()
-                N.call("tcst_optimizer_step", R._vp(p), R._vp(grad), R._vp(state["exp_avg"]),
-                       R._vp(state["exp_avg_sq"]), p.shape[0], kind, ctypes.byref(h),
-                       R._stream(p.device))
+                with R.on_device(p.device):
+                    N.call("tcst_optimizer_step", R._vp(p), R._vp(grad),
+                           R._vp(state["exp_avg"]), R._vp(state["exp_avg_sq"]), p.shape[0],
+                           kind, ctypes.byref(h), R._stream(p.device))
             if plain[0]:
                 beta1, beta2 = group["betas"]
                 torch.optim._functional.adamw(

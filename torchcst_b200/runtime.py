@@ -29,6 +29,13 @@ def _stream(device=None):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+def on_device(device):
+    """Context that makes ``device`` the current CUDA device for the native calls
+    inside it (the C ABI works on the current device and its streams); free when
+    it already is."""
+    return torch.cuda.device(device)
+
+
 def require_cuda(*tensors):
     for t in tensors:
         if t is not None and (not t.is_cuda):

@@ -203,10 +203,11 @@ class RowBandMSETrainStep(OptimizerScalars):
         """One step on this rank's device tensors x [rows, N_in] and target
         [rows, N_out] (replicated across ranks); returns the loss (0-d float64
         device tensor, identical on every rank)."""
-        optimize = self._advance()
-        loss = self._launch_grad(x, target)
-        if optimize:
-            self._launch_opt()
+        with R.on_device(self.layer.atoms.p.device):
+            optimize = self._advance()
+            loss = self._launch_grad(x, target)
+            if optimize:
+                self._launch_opt()
         return loss
 
     def dx(self):

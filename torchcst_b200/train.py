@@ -221,6 +221,10 @@ class MSETrainStep(OptimizerScalars):
     def __call__(self, x, target):
         """Run one step on device tensors x [rows, in], target [rows, out]; returns the
         loss as a 0-d float64 device tensor (no host synchronization)."""
+        with R.on_device(self.layer.atoms.p.device):
+            return self._step(x, target)
+
+    def _step(self, x, target):
         optimize = self._advance()
         key = (x.data_ptr(), target.data_ptr())
         graph = self._graphs.get(key) if optimize else None
@@ -239,6 +243,10 @@ class MSETrainStep(OptimizerScalars):
         between the two."""
         if self._state is None:
             raise RuntimeError("run one eager step before capturing")
+        with R.on_device(self.layer.atoms.p.device):
+            self._capture(pairs)
+
+    def _capture(self, pairs):
         torch.cuda.synchronize()
         for x, target in pairs:
             key = (x.data_ptr(), target.data_ptr())
