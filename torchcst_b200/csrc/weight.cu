@@ -180,7 +180,10 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
         // its covering rows and columns, warp 0 forms the prefix over groups,
         // and every entry then finds its group by bisection. Group
         // descriptors and prefix borrow cspan / ccls, free until step 2.
-        const int ngroups = g.nclass + g.npl; // <= MAX_CLASSES + MAX_PAIR_LB <= 64
+        static_assert(MAX_CLASSES + MAX_PAIR_LB <= 64, "groups: two per lane of warp 0");
+        static_assert(MAX_CLASSES + MAX_PAIR_LB <= WT_THREADS && 65 <= WT_THREADS,
+                      "group descriptors and prefix fit cspan / ccls");
+        const int ngroups = g.nclass + g.npl;
         int4 *gdesc = cspan;                  // (first row, first column, columns, entries)
         int *gpre = ccls;
         if (t < ngroups) {
@@ -429,6 +432,8 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
         __shared__ int pnode[MAX_PAIR_LB * 5]; // (l << 16 | a) of flagged nodes, else -1
         // Covering output nodes per expansion level-bank (one thread each),
         // prefix by warp 0, then one node per entry.
+        static_assert(2 * MAX_PAIR_LB + 1 <= WT_THREADS && MAX_PAIR_LB <= 32,
+                      "level-bank firsts and prefix fit ccls; one bank per lane");
         int *lfirst = ccls, *lpre = ccls + MAX_PAIR_LB; // ccls is free again
         if (t < g.npl) {
             int fo = 0, co = 0;
