@@ -196,7 +196,8 @@ def algorithm_class():
                 _BINDINGS[site] = native
             R.require_cuda(x, p)
             flat = x.reshape(-1, x.shape[-1]).contiguous()
-            return _CellMassLinear.apply(flat, p, native[1])
+            with R.on_device(p.device):
+                return _CellMassLinear.apply(flat, p, native[1])
 
     return B200RadiusCellMassAlgorithm
 
