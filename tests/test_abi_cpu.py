@@ -32,6 +32,41 @@ def test_header_matches_binding_table():
     assert declared_functions() == sorted(_native.SIGNATURES)
 
 
+def _declarations():
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    return text, dict(re.findall(r"\b(tcst_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text))
+
+
+def test_header_argument_counts_match_binding_table():
+    """Every declared function takes as many parameters as its ctypes binding."""
+    from torchcst_b200 import _native
+    _, decls = _declarations()
+    for name, params in decls.items():
+        params = params.strip()
+        count = 0 if params in ("", "void") else len(params.split(","))
+        assert count == len(_native.SIGNATURES[name][1]), name
+
+
+def test_adamw_struct_matches_header():
+    """tcst_adamw (all 4-byte members) has the ctypes mirror's size and order."""
+    from torchcst_b200 import _native as N
+    text, _ = _declarations()
+    body = re.search(r"typedef struct tcst_adamw \{(.*?)\} tcst_adamw;", text, re.S).group(1)
+    names = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        for item in decl.split(None, 1)[1].split(","):
+            m = re.match(r"\s*(\w+)\s*(?:\[(\d+)\])?", item)
+            names += [m.group(1)] * int(m.group(2) or 1)
+    mirror = []
+    for fname, ftype in N.AdamW._fields_:
+        mirror += [fname] * (ctypes.sizeof(ftype) // 4)
+    assert names == mirror
+    assert ctypes.sizeof(N.AdamW) == 4 * len(names)
+
+
 def test_library_exports_every_declared_symbol(lib):
     for name in declared_functions():
         assert hasattr(lib, name), name
