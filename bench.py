@@ -624,6 +624,7 @@ def main():
         i_post += 1
         torch.cuda.synchronize()
     clocks = sampler.stop()
+    step.check_status()  # raises if a kernel flagged bad atoms or gave up a bounded wait
     ms = start.elapsed_time(end)
     ms_t = torch.tensor([ms], device=device)
     if pg is not None:

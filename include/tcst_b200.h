@@ -100,6 +100,10 @@ typedef struct tcst_adamw {
     float polar_decay;     /* exp(-4 * radial_regularization * lr) in float32 */
     float polar_energy_step; /* lr for activity_mode time_energy, else 0 */
     float period_out, period_in;
+    /* Polar decoupled amplitude decay after the activity law
+     * (_backends/torch/algorithms/polar_update/executor.py:18-41): float32 of
+     * lr * amplitude_weight_decay; 0 leaves the step unchanged. */
+    float amplitude_decay;
 } tcst_adamw;
 
 const char *tcst_version(void);
@@ -276,10 +280,25 @@ int tcst_pullback_band(const void *atom_table_dev, int64_t atoms, const tcst_axi
  * field_lrs rescale, then the rational projection
  * (_backends/torch/updates/rational_radius.py:10-29) or the Polar activity law
  * with torus retraction (_backends/torch/algorithms/polar_update/executor.py:42-112,
- * _backends/torch/geometry/flat_torus.py:30-35). */
+ * _backends/torch/geometry/flat_torus.py:30-35) and, when amplitude_decay is
+ * nonzero, the Polar amplitude decay (executor.py:18-41). A nonzero
+ * amplitude_decay with kind TCST_RATIONAL is an argument error, as the reference
+ * rejects amplitude decay for non-Polar atoms (operators/atom_update.py:42-66). */
 int tcst_optimizer_step(float *p_dev, const float *grad_dev, float *exp_avg_dev,
                         float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
                         const tcst_adamw *params, void *stream);
+
+/* The coordinate law alone, for an optimizer that computed its own AdamW
+ * proposal and field rescale: proposal_dev ([atoms][4], in place) becomes the
+ * rational projection or the Polar activity law with torus retraction and
+ * amplitude decay, applied from previous_dev ([atoms][4], the point before the
+ * step; must not alias the proposal). Only the coordinate-law fields of params
+ * are read (amplitude_cap, polar_*, period_out/in, amplitude_decay). Replaces
+ * the torch atom_update Algorithm's execute
+ * (_backends/torch/algorithms/atom_update/algorithm.py:58-83:
+ * apply_parameter_update, then decay_amplitude). */
+int tcst_coordinate_update(float *proposal_dev, const float *previous_dev, int64_t atoms,
+                           int32_t kind, const tcst_adamw *params, void *stream);
 
 /* The same step with the tcst_adamw scalars in device memory (16-byte aligned),
  * read when the kernel runs, so a captured CUDA graph can replay the step while

@@ -451,6 +451,55 @@ def routing_table(lay: Layer):
     )
 
 
+def routing_only(out_axis: Axis, in_axis: Axis, spec, p, dtype=F32):
+    """Integer routing and owner keys without evaluating any profile, for layers
+    too large for :func:`decode` (every atom of a 262,144-atom layer): the
+    decode of rational_radius.py:6-38 or polar_amp_width.py:127-245 and the
+    routing expressions of radius_cell_mass.py:81-123, nothing else."""
+    out_axis.validate()
+    in_axis.validate()
+    p = np.asarray(p, dtype)
+    dec = (rational_decode(p, spec, dtype) if isinstance(spec, Rational)
+           else polar_decode(p, spec))
+    ro = route(out_axis, dec["radius_out"], p[:, 2])
+    ri = route(in_axis, dec["radius_in"], p[:, 3])
+    return dict(out_level=ro["level"], out_count=ro["count"], out_first_tile=ro["first_tile"],
+                in_level=ri["level"], in_count=ri["count"], in_first_tile=ri["first_tile"],
+                owner_key=owner_keys(ro, ri, in_axis))
+
+
+def factored64(lay: Layer, x, dy):
+    """(Y, dX, p.grad) in float64 through dense factors, the association of the
+    reference's factored path (_backends/torch/operators/linear.py:47-66):
+    Y = (X phi_in) phi_out^T with phi_out = amp m_out. Its cost is O(B A N)
+    rather than O(A F_out F_in), so it serves layers of few atoms with wide
+    (folded) footprints, such as the 128-atom model of a wide-layer check."""
+    x = np.asarray(x, F64)
+    dy = np.asarray(dy, F64)
+    A = lay.atoms
+    amp = lay.dec["amplitude"]
+    m_out, dmu_out, dR_out = (lay.out_prof.dense(A, k) for k in range(3))
+    m_in, dmu_in, dR_in = (lay.in_prof.dense(A, k) for k in range(3))
+    u = x @ m_in          # [B, A] atom values before the amplitude
+    v = dy @ m_out        # [B, A] upstream cotangent per atom
+    y = (u * amp) @ m_out.T
+    dx = (v * amp) @ m_in.T
+    d_amp = (u * v).sum(0)
+    d_mu_out = amp * (u * (dy @ dmu_out)).sum(0)
+    d_mu_in = amp * (v * (x @ dmu_in)).sum(0)
+    d_R = amp * ((u * (dy @ dR_out)).sum(0) + (v * (x @ dR_in)).sum(0))
+    grad = np.zeros((A, 4))
+    if isinstance(lay.spec, Rational):
+        grad[:, 0] = d_amp + d_R * lay.dec["dr_da"]
+        grad[:, 1] = d_R * lay.dec["dr_dq"]
+    else:
+        grad[:, 0] = d_amp * lay.dec["damp_ds"]
+        grad[:, 1] = d_amp * lay.dec["damp_dt"]
+    grad[:, 2] = d_mu_out
+    grad[:, 3] = d_mu_in
+    return y, dx, grad
+
+
 def _pairs(lay: Layer):
     """Yield matched (indices, out sites, out vals, in sites, in vals) chunks."""
     out_map = {}
@@ -746,16 +795,48 @@ def polar_update(previous, point, spec: Polar, *, step_size, periods):
     return out
 
 
+def decay_amplitude(previous, updated, amount):
+    """Decoupled Polar amplitude decay in float32 at the accepted radius
+    (_backends/torch/algorithms/polar_update/executor.py:18-41): the normalized
+    first coordinate loses ``amount`` times its old value, t keeps its sign."""
+    if amount == 0:
+        return updated
+    prev = previous.astype(F32)
+    out = updated.astype(F32).copy()
+    tiny = F32(TINY32)
+    one = F32(1)
+    old_r = np.sqrt(np.maximum((prev[:, 0] * prev[:, 0] + prev[:, 1] * prev[:, 1]).astype(F32),
+                               tiny)).astype(F32)
+    new_r = np.sqrt(np.maximum((out[:, 0] * out[:, 0] + out[:, 1] * out[:, 1]).astype(F32),
+                               tiny)).astype(F32)
+    old_amp = (prev[:, 0] / old_r).astype(F32)
+    target = ((out[:, 0] / new_r).astype(F32) - (F32(amount) * old_amp).astype(F32)).astype(F32)
+    target = np.clip(target, F32(-1), one)
+    absolute = np.abs(target)
+    room = np.maximum(((one - absolute).astype(F32) * (one + absolute).astype(F32)).astype(F32),
+                      F32(0))
+    magnitude = (new_r * np.sqrt(room).astype(F32)).astype(F32)
+    s = (new_r * target).astype(F32)
+    out[:, 1] = np.copysign(magnitude, out[:, 1]).astype(F32)
+    out[:, 0] = s
+    return out
+
+
 def optimizer_step(p, grad, state: AdamState, spec, *, lr, field_ratios=(),
-                   betas=(0.9, 0.999), eps=1e-8, periods=None):
-    """One CSTAdamW step on an atom table (optim/adamw.py:230-247)."""
+                   betas=(0.9, 0.999), eps=1e-8, periods=None, amplitude_weight_decay=0.0):
+    """One CSTAdamW step on an atom table (optim/adamw.py:230-247): AdamW, the
+    field rates, the coordinate law and, for Polar rows, the amplitude decay
+    (_backends/torch/algorithms/atom_update/algorithm.py:58-83)."""
     previous = p.astype(F32).copy()
     point = adamw32(p, grad, state, lr=lr, beta1=betas[0], beta2=betas[1], eps=eps)
     if field_ratios:
         point = apply_field_lrs(point, previous, field_ratios)
     if isinstance(spec, Rational):
+        if amplitude_weight_decay:
+            raise ValueError("amplitude decay requires Polar atoms")
         return rational_update(previous, point, spec)
-    return polar_update(previous, point, spec, step_size=lr, periods=periods)
+    out = polar_update(previous, point, spec, step_size=lr, periods=periods)
+    return decay_amplitude(previous, out, lr * amplitude_weight_decay)
 
 
 def field_ratios(spec, field_lrs, lr):

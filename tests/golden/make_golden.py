@@ -2,7 +2,9 @@
 
 Run in a container where the reference source tree is available:
 
-    PYTHONPATH=<torchcst>/src python tests/golden/make_golden.py
+    PYTHONPATH=<torchcst>/src python tests/golden/make_golden.py            # base cases
+    PYTHONPATH=<torchcst>/src python tests/golden/make_golden.py config3_decay config2_init \
+        trajectory1 trajectory_mid                                          # extra cases
 
 It writes ``tests/golden/*.npz``. The GPU box never runs this script; the tests
 only read the committed fixtures. Each case records the reference inputs
@@ -205,8 +207,121 @@ def synthetic_images(batch, generator):
     return x.reshape(batch, 784)
 
 
+def decay_case():
+    """Polar config-3 layer, three CSTAdamW steps with amplitude_weight_decay on
+    fixed synthetic gradients: the atoms after every step."""
+    CSTAdamW = _imports()[0]
+    layer = polar_layer(1024, 784, 16384)
+    p0 = layer.atoms.p.detach().clone()
+    g = torch.Generator().manual_seed(11)
+    grads = torch.randn(3, 16384, 4, generator=g) * 1e-2
+    opt = CSTAdamW(layer.parameters(), model=layer, lr=2e-3, amplitude_weight_decay=0.25)
+    rows = slice(0, 4096)  # the update is row by row: the first 4096 rows suffice
+    out = dict(p0=p0[rows].numpy(), grads=grads[:, rows].numpy(), lr=np.float64(2e-3),
+               amplitude_weight_decay=np.float64(0.25))
+    for step in range(3):
+        layer.atoms.p.grad = grads[step].clone()
+        opt.step()
+        out[f"p{step + 1}"] = layer.atoms.p.detach()[rows].clone().numpy()
+    # The decay law alone on fixed inputs (executor.py:18-41), bit for bit.
+    from torchcst._backends.torch.algorithms.polar_update.executor import decay_amplitude
+    prev = torch.randn(4096, 4, generator=g)
+    upd = prev + torch.randn(4096, 4, generator=g) * 1e-2
+    out["decay_previous"], out["decay_updated"] = prev.numpy(), upd.numpy()
+    out["decay_amount"] = np.float64(2e-3 * 0.25)
+    out["decay_out"] = decay_amplitude(prev, upd, amount=2e-3 * 0.25).numpy()
+    return out
+
+
+def init_case():
+    """The reference's He initialisation report at config 2 (seed 0): the scale
+    its bounded search accepted and the energy it matched (p0 is config2's)."""
+    _, _, _, _, _, _, cst_init = _imports()
+    layer = rational_layer(1024, 1024, 65536, radius_max=512.0)
+    report = cst_init.kaiming_normal_(layer, nonlinearity="relu", q=0.0)
+    out = {k: np.float64(getattr(report, k)) for k in
+           ("amplitude_scale", "relative_error", "target_energy", "expected_energy",
+            "amplitude_rms")}
+    out["evaluations"] = np.int64(report.evaluations)
+    # The atoms themselves equal config2's p0 (same seed and calls).
+    assert np.array_equal(layer.atoms.p.detach().numpy(),
+                          np.load(os.path.join(HERE, "config2.npz"))["p0"])
+    return out
+
+
+def trajectory_case(n_out, n_in, atoms, *, radius_max, rows, steps, lr, field_lrs, seed,
+                    keep=1):
+    """An MSE training trajectory of the reference (fixed X and target): the
+    loss of every step and the atoms after every step. With a large radius
+    field rate the footprints widen through several bin classes on the way."""
+    CSTAdamW = _imports()[0]
+    layer = rational_layer(n_out, n_in, atoms, radius_max=radius_max, init="kaiming",
+                           seed=seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    x = torch.randn(rows, n_in, generator=g)
+    target = torch.randn(rows, n_out, generator=g)
+    opt = CSTAdamW(layer.parameters(), model=layer, lr=lr,
+                   **({"field_lrs": field_lrs} if field_lrs else {}))
+    out = dict(p0=layer.atoms.p.detach().clone().numpy(), x=x.numpy(), target=target.numpy(),
+               lr=np.float64(lr))
+    if field_lrs:
+        out["field_amplitude"] = np.float64(field_lrs.get("amplitude", np.nan))
+        out["field_radius_fraction"] = np.float64(field_lrs.get("radius_fraction", np.nan))
+    losses, ps = [], []
+    for _ in range(steps):
+        opt.zero_grad(set_to_none=True)
+        loss = (layer(x) - target).square().mean()
+        loss.backward()
+        opt.step()
+        losses.append(loss.item())
+        if len(losses) % keep == 0:
+            ps.append(layer.atoms.p.detach().clone().numpy())
+    out["losses"] = np.asarray(losses)
+    out["p_steps"] = np.stack(ps)  # atoms after steps keep, 2 keep, ...
+    out["keep"] = np.int64(keep)
+    return out
+
+
+def reference_file():
+    """The config-1 reference layer (seed 0) saved as a Safetensors file the way
+    a torchcst user saves one: every tensor of its state dict, after an atom
+    relayout (the row-to-id maps are in the file)."""
+    from safetensors.torch import save_file
+    layer = rational_layer(8, 16, 12, radius_max=4.0)
+    layer.atom_state.relayout(torch.arange(11, -1, -1))
+    path = os.path.join(HERE, "config1_reference.safetensors")
+    save_file({k: v.detach().contiguous() for k, v in layer.state_dict().items()
+               if torch.is_tensor(v)}, path)
+    # The relayout reversed the rows (the sum over atoms, the model, is the same).
+    assert np.array_equal(layer.atoms.p.detach().numpy(),
+                          np.load(os.path.join(HERE, "config1.npz"))["p0"][::-1])
+    return None
+
+
+EXTRA_CASES = {
+    "config1_reference_file": reference_file,
+    "config3_decay": decay_case,
+    "config2_init": init_case,
+    "trajectory1": lambda: trajectory_case(8, 16, 12, radius_max=4.0, rows=4, steps=20,
+                                           lr=1e-2, field_lrs=None, seed=0),
+    "trajectory_mid": lambda: trajectory_case(
+        256, 256, 4096, radius_max=128.0, rows=64, steps=12, lr=1e-2,
+        field_lrs={"amplitude": 1e-2, "radius_fraction": 6e-2}, seed=3, keep=4),
+}
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 1)
+    only = [a for a in sys.argv[1:] if not a.startswith("-")]
+    if only:
+        for name in only:
+            value = EXTRA_CASES[name]()
+            if value is None:
+                continue
+            path = os.path.join(HERE, f"{name}.npz")
+            np.savez_compressed(path, **value)
+            print(name, os.path.getsize(path), "bytes", sorted(value))
+        return 0
     cases = {}
 
     # Config 1: README example (16 -> 8, 12 atoms, radius_max 4, seed 0).

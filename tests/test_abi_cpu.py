@@ -95,3 +95,14 @@ def test_argument_errors_without_device(lib):
     assert rc == 1
     with pytest.raises(ValueError):
         N.check(1, "probe")
+    # Atom counts whose scratch byte count would overflow 64 bits are refused
+    # before any size arithmetic or device call.
+    ax = N.Axis(1024, 1, 2, 8, 1.0, 0.0)
+    for atoms in (1 << 62, (1 << 63) - 1, 32769):
+        rc = lib.tcst_assemble_weight_static(None, atoms, ctypes.byref(ax), ctypes.byref(ax),
+                                             None, 0, None, None, 0, None)
+        assert rc == 3, atoms
+        assert b"more than the built-in" in lib.tcst_last_error()
+    rc = lib.tcst_assemble_weight_static(None, -1, ctypes.byref(ax), ctypes.byref(ax),
+                                         None, 0, None, None, 0, None)
+    assert rc == 1

@@ -4,7 +4,8 @@ reference golden vectors.
 Tolerances: routing and owner keys bit-exact; the optimizer step bit-exact
 against the oracle; Y, dX, W and atom gradients within 1e-4 of the output scale
 (max |err| / max |ref|, float64 truth), the north-star bound for fp32-accurate
-tensor-core arithmetic (three-product TF32 split).
+tensor-core arithmetic (three-product f16 split with power-of-two scales; the
+exported TF32 variant is held to the same bound).
 """
 
 import numpy as np
@@ -482,3 +483,45 @@ def test_large_chart_fine_bins_of_64_sites(R):
     g64 = O.atom_gradients64(lay, G.double().cpu().numpy())
     for c in range(4):
         assert rel(grad[:, c], g64[:, c]) < TOL, c
+
+
+PARITY_CASES = ["config1", "config2", "hierarchy", "config3", "config4s", "config5s"]
+
+
+def test_parity_report(R):
+    """Errors against the reference's float32 results (the goldens) and against
+    float64 truth side by side, with the reference's own float32 error for
+    scale (max |a - b| / max |b|; gradients: the worst of the four columns on
+    the goldens' rows). Prints the table; every figure must be within 1e-4."""
+    lines = ["| case | tensor | new vs reference fp32 | new vs fp64 | reference fp32 vs fp64 |",
+             "|---|---|---|---|---|"]
+    worst = 0.0
+    for name in PARITY_CASES:
+        d = load(name)
+        layer = make_layer(name, d["p0"])
+        x = torch.as_tensor(d["x"]).cuda().requires_grad_("dx" in d)
+        y = layer(x)
+        y.backward(torch.as_tensor(d["dy"]).cuda())
+        torch.cuda.synchronize()
+        out_axis, in_axis, spec = CASES[name]
+        lay = O.decode(out_axis, in_axis, spec, d["p0"])
+        W = O.weight64(lay)
+        x64, dy64 = d["x"].astype(np.float64), d["dy"].astype(np.float64)
+        rows = d.get("rows", slice(None))
+        g64 = O.atom_gradients64(lay, dy64.T @ x64)[rows]
+        grad = layer.atoms.p.grad.cpu().numpy()[rows]
+        out = {"Y": (y.detach().cpu().numpy(), d["y"], x64 @ W.T)}
+        if "dx" in d:
+            out["dX"] = (x.grad.cpu().numpy(), d["dx"], dy64 @ W)
+        out["grad"] = (grad, d["grad"], g64)
+        for what, (new, ref32, truth) in out.items():
+            if what == "grad":
+                e32 = max(rel(new[:, c], ref32[:, c]) for c in range(4))
+                e64 = max(rel(new[:, c], truth[:, c]) for c in range(4))
+                r64 = max(rel(ref32[:, c], truth[:, c]) for c in range(4))
+            else:
+                e32, e64, r64 = rel(new, ref32), rel(new, truth), rel(ref32, truth)
+            worst = max(worst, e32, e64)
+            lines.append(f"| {name} | {what} | {e32:.2e} | {e64:.2e} | {r64:.2e} |")
+    print("\n".join(lines))
+    assert worst < TOL

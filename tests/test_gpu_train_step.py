@@ -51,6 +51,7 @@ def test_graph_replay_matches_eager_steps():
         for i in range(1, 5):
             losses.append(float(step(xs[i % 2], ts[i % 2])))
         torch.cuda.synchronize()
+        assert step.check_status() == 0
         runs.append((losses, _state(layer, opt), int(opt.state[layer.atoms.p]["step"])))
         step.release()
     (l0, s0, n0), (l1, s1, n1) = runs
@@ -67,6 +68,7 @@ def test_fused_step_matches_autograd_api():
     layer, opt, xs, ts = _setup()
     step = MSETrainStep(layer, opt, 256)
     fused_loss = float(step(xs[0], ts[0]))
+    assert step.check_status() == 0
     fused = _state(layer, opt)
 
     layer2, opt2, _, _ = _setup()

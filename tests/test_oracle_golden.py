@@ -115,3 +115,84 @@ def test_invalid_inputs_raise():
         O.decode(out_axis, in_axis, spec, p)
     with pytest.raises(ValueError):
         O.Axis(12, base_tile_sites=5).validate()
+
+
+def test_amplitude_decay_law():
+    """The Polar amplitude decay of the oracle against the reference's own decay
+    law (executor.py:18-41) on fixed inputs. The oracle's square roots are IEEE
+    (correctly rounded) and torch's CPU ones are not (about 0.7% of float32
+    inputs differ by one ulp), and t = new_r sqrt((1 - |u|)(1 + |u|)) amplifies
+    a one-ulp change of u by |u| / (1 - u^2) as |u| -> 1. So: centers exact,
+    s within two ulps, t within two ulps plus that conditioning times 4 ulps
+    of u."""
+    d = load("config3_decay")
+    out = O.decay_amplitude(d["decay_previous"], d["decay_updated"], float(d["decay_amount"]))
+    ref = d["decay_out"]
+    np.testing.assert_array_equal(out[:, 2:], ref[:, 2:])
+    ulp = np.spacing(np.abs(ref).astype(np.float32)).astype(np.float64)
+    err = np.abs(out.astype(np.float64) - ref)
+    assert (err[:, 0] <= 2 * ulp[:, 0]).all()
+    r = np.hypot(ref[:, 0].astype(np.float64), ref[:, 1])
+    u = np.clip(np.abs(ref[:, 0]) / r, 0, 1)
+    cond = r * u / np.sqrt(np.maximum(1 - u * u, 2.0 ** -24)) * 4 * 2.0 ** -24
+    assert (err[:, 1] <= 2 * ulp[:, 1] + cond).all()
+    assert (out != ref).mean() < 0.02
+
+
+def test_optimizer_steps_with_amplitude_decay():
+    """Three reference CSTAdamW steps with amplitude_weight_decay on Polar rows.
+    The decay itself is bit-exact (above); torch's CPU sqrt (one ulp off on a
+    fraction of a percent of elements) reaches s through the Polar law with
+    cancellation, so allow eight float32 ulps of the result (1e-9 floor)."""
+    out_axis, in_axis, spec = CASES["config3"]
+    d = load("config3_decay")
+    p = d["p0"].copy()
+    state = O.AdamState(0, np.zeros_like(p), np.zeros_like(p))
+    lr, decay = float(d["lr"]), float(d["amplitude_weight_decay"])
+    undecayed = O.optimizer_step(d["p0"], d["grads"][0], O.AdamState(0, np.zeros_like(p),
+                                                                      np.zeros_like(p)),
+                                 spec, lr=lr, periods=(out_axis.period, in_axis.period))
+    assert np.abs(undecayed - d["p1"]).max() > 1e-7  # the decay matters at this size
+    for step in range(3):
+        p = O.optimizer_step(p, d["grads"][step], state, spec, lr=lr,
+                             periods=(out_axis.period, in_axis.period),
+                             amplitude_weight_decay=decay)
+        ref = d[f"p{step + 1}"]
+        ulp = np.spacing(np.abs(ref).astype(np.float32)).astype(np.float64)
+        assert (np.abs(p.astype(np.float64) - ref) <= 8 * ulp + 1e-9).all(), step
+        assert (p != ref).mean() < 0.02
+
+
+def test_amplitude_decay_rejects_rational_rows():
+    out_axis, in_axis, spec = CASES["config1"]
+    d = load("config1")
+    state = O.AdamState(0, np.zeros_like(d["p0"]), np.zeros_like(d["p0"]))
+    with pytest.raises(ValueError, match="Polar"):
+        O.optimizer_step(d["p0"], d["grad"], state, spec, lr=1e-3, amplitude_weight_decay=0.1)
+
+
+TRAJECTORIES = {
+    "trajectory1": (O.Axis(8), O.Axis(16), O.Rational(radius_max=4.0)),
+    "trajectory_mid": (O.Axis(256), O.Axis(256), O.Rational(radius_max=128.0)),
+}
+
+
+@pytest.mark.parametrize("name", sorted(TRAJECTORIES))
+def test_reference_trajectory(name):
+    """The oracle's reference-precision step, iterated, follows the reference's
+    own training trajectory: every step's loss to 1e-6, the atoms to 1e-3
+    (Adam normalises each coordinate's step, so a near-zero gradient whose
+    last bits differ can move a coordinate by up to one step size)."""
+    out_axis, in_axis, spec = TRAJECTORIES[name]
+    d = load(name)
+    lr, keep = float(d["lr"]), int(d["keep"])
+    p = d["p0"].copy()
+    state = O.AdamState(0, np.zeros_like(p), np.zeros_like(p))
+    for step, want in enumerate(d["losses"]):
+        loss, _, _, _, p = O.reference_step(out_axis, in_axis, spec, p, d["x"], d["target"],
+                                            state, lr=lr, field_lrs=field_lrs(d) or None)
+        assert abs(loss - want) <= 1e-6 * want, step
+        if (step + 1) % keep == 0:
+            ref = d["p_steps"][(step + 1) // keep - 1]
+            assert np.abs(p - ref).max() <= 1e-3, step
+            assert np.quantile(np.abs(p - ref), 0.999) <= 1e-5, step

@@ -73,6 +73,7 @@ class AdamW(ctypes.Structure):
         ("polar_energy_step", ctypes.c_float),
         ("period_out", ctypes.c_float),
         ("period_in", ctypes.c_float),
+        ("amplitude_decay", ctypes.c_float),
     ]
 
 
@@ -116,6 +117,7 @@ SIGNATURES = {
                                           P, I64, I32, I64, I64, I64, P, P]),
     "tcst_optimizer_step": (ctypes.c_int, [P, P, P, P, I64, I32, ctypes.POINTER(AdamW), P]),
     "tcst_optimizer_step_device": (ctypes.c_int, [P, P, P, P, I64, I32, P, P]),
+    "tcst_coordinate_update": (ctypes.c_int, [P, P, I64, I32, ctypes.POINTER(AdamW), P]),
     "tcst_mse_grad": (ctypes.c_int, [P, P, I64, I64, I64, ctypes.c_float, P, P, I64, P,
                                      ctypes.POINTER(I32), P]),
     "tcst_atom_energies": (ctypes.c_int, [P, I64, ctypes.POINTER(Axis), ctypes.POINTER(Axis),

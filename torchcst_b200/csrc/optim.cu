@@ -40,21 +40,8 @@ __device__ __forceinline__ float torus(float x, float period) {
     return mod;
 }
 
-__device__ __forceinline__ void step_row(long long a, float4 *__restrict__ p,
-                                         const float4 *__restrict__ grad, float4 *__restrict__ m,
-                                         float4 *__restrict__ v, int kind, const tcst_adamw &h) {
-    float4 prev = p[a], g = grad[a], mm = m[a], vv = v[a];
-    float4 pt;
-    pt.x = adam_one(prev.x, g.x, mm.x, vv.x, h);
-    pt.y = adam_one(prev.y, g.y, mm.y, vv.y, h);
-    pt.z = adam_one(prev.z, g.z, mm.z, vv.z, h);
-    pt.w = adam_one(prev.w, g.w, mm.w, vv.w, h);
-    m[a] = mm;
-    v[a] = vv;
-    pt.x = field(pt.x, prev.x, 0, h);
-    pt.y = field(pt.y, prev.y, 1, h);
-    pt.z = field(pt.z, prev.z, 2, h);
-    pt.w = field(pt.w, prev.w, 3, h);
+__device__ __forceinline__ float4 coordinate_law(float4 prev, float4 pt, int kind,
+                                                 const tcst_adamw &h) {
     // displacement = proposal - previous; the coordinate law restarts from previous.
     float4 d = make_float4(fsub(pt.x, prev.x), fsub(pt.y, prev.y), fsub(pt.z, prev.z),
                            fsub(pt.w, prev.w));
@@ -105,8 +92,40 @@ __device__ __forceinline__ void step_row(long long a, float4 *__restrict__ p,
         // Flat-torus retraction of both centers (flat_torus.py:30-35).
         out.z = torus(fadd(prev.z, d.z), h.period_out);
         out.w = torus(fadd(prev.w, d.w), h.period_in);
+        if (h.amplitude_decay != 0.0f) {
+            // decay_amplitude (executor.py:18-41): subtract the decayed old
+            // normalized amplitude at the accepted radius, keep t's sign.
+            float old_r = fsqrt(fmaxf(fadd(fmul(prev.x, prev.x), fmul(prev.y, prev.y)), tiny));
+            float new_r = fsqrt(fmaxf(fadd(fmul(out.x, out.x), fmul(out.y, out.y)), tiny));
+            float old_amp = fdiv(prev.x, old_r);
+            float target = fsub(fdiv(out.x, new_r), fmul(h.amplitude_decay, old_amp));
+            target = fminf(fmaxf(target, -1.0f), 1.0f);
+            float absolute = fabsf(target);
+            float room = fmaxf(fmul(fsub(1.0f, absolute), fadd(1.0f, absolute)), 0.0f);
+            float magnitude = fmul(new_r, fsqrt(room));
+            out.x = fmul(new_r, target);
+            out.y = copysignf(magnitude, out.y);
+        }
     }
-    p[a] = out;
+    return out;
+}
+
+__device__ __forceinline__ void step_row(long long a, float4 *__restrict__ p,
+                                         const float4 *__restrict__ grad, float4 *__restrict__ m,
+                                         float4 *__restrict__ v, int kind, const tcst_adamw &h) {
+    float4 prev = p[a], g = grad[a], mm = m[a], vv = v[a];
+    float4 pt;
+    pt.x = adam_one(prev.x, g.x, mm.x, vv.x, h);
+    pt.y = adam_one(prev.y, g.y, mm.y, vv.y, h);
+    pt.z = adam_one(prev.z, g.z, mm.z, vv.z, h);
+    pt.w = adam_one(prev.w, g.w, mm.w, vv.w, h);
+    m[a] = mm;
+    v[a] = vv;
+    pt.x = field(pt.x, prev.x, 0, h);
+    pt.y = field(pt.y, prev.y, 1, h);
+    pt.z = field(pt.z, prev.z, 2, h);
+    pt.w = field(pt.w, prev.w, 3, h);
+    p[a] = coordinate_law(prev, pt, kind, h);
 }
 
 __global__ void optimizer_kernel(float4 *__restrict__ p, const float4 *__restrict__ grad,
@@ -130,6 +149,16 @@ __global__ void optimizer_dev_kernel(float4 *__restrict__ p, const float4 *__res
     if (a < atoms) step_row(a, p, grad, m, v, kind, h);
 }
 
+// The coordinate law alone: proposal (written by an outside AdamW and field
+// rescale) is replaced in place by the law applied from previous.
+__global__ void coordinate_update_kernel(float4 *__restrict__ proposal,
+                                         const float4 *__restrict__ previous, long long atoms,
+                                         int kind, tcst_adamw h) {
+    pdl_wait();
+    const long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (a < atoms) proposal[a] = coordinate_law(previous[a], proposal[a], kind, h);
+}
+
 } // namespace tcst
 
 using namespace tcst;
@@ -146,6 +175,10 @@ extern "C" int tcst_optimizer_step(float *p_dev, const float *grad_dev, float *e
          reinterpret_cast<uintptr_t>(exp_avg_dev) | reinterpret_cast<uintptr_t>(exp_avg_sq_dev)) %
         16) {
         tcst_set_error("tcst_optimizer_step: tensors must be 16-byte aligned");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (kind == TCST_RATIONAL && params->amplitude_decay != 0.0f) {
+        tcst_set_error("tcst_optimizer_step: amplitude decay requires Polar atoms");
         return TCST_ERR_ARGUMENT;
     }
     if (atoms == 0) return TCST_OK;
@@ -175,6 +208,35 @@ extern "C" int tcst_optimizer_step_device(float *p_dev, const float *grad_dev, f
     TCST_CUDA(launch_pdl(optimizer_dev_kernel, dim3(unsigned((atoms + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, 
         (float4 *)p_dev, (const float4 *)grad_dev, (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev,
         atoms, kind, params_dev));
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+extern "C" int tcst_coordinate_update(float *proposal_dev, const float *previous_dev,
+                                      int64_t atoms, int32_t kind, const tcst_adamw *params,
+                                      void *stream) {
+    if (atoms < 0 || !params || (kind != TCST_RATIONAL && kind != TCST_POLAR) ||
+        (atoms && (!proposal_dev || !previous_dev))) {
+        tcst_set_error("tcst_coordinate_update: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(proposal_dev) | reinterpret_cast<uintptr_t>(previous_dev)) %
+        16) {
+        tcst_set_error("tcst_coordinate_update: tensors must be 16-byte aligned");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (proposal_dev == previous_dev && atoms) {
+        tcst_set_error("tcst_coordinate_update: previous must not alias the proposal");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (kind == TCST_RATIONAL && params->amplitude_decay != 0.0f) {
+        tcst_set_error("tcst_coordinate_update: amplitude decay requires Polar atoms");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (atoms == 0) return TCST_OK;
+    TCST_CUDA(launch_pdl(coordinate_update_kernel, dim3(unsigned((atoms + 255) / 256)), dim3(256),
+                         0, (cudaStream_t)stream, (float4 *)proposal_dev,
+                         (const float4 *)previous_dev, atoms, kind, *params));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

@@ -1078,13 +1078,21 @@ extern "C" int tcst_assemble_weight_static(const void *atom_table_dev, int64_t a
         tcst_set_error("%s", err);
         return rc;
     }
-    if (cache_floats(atoms) * 4 > STATIC_SCRATCH_BYTES) {
-        tcst_set_error("tcst_assemble_weight_static: %lld atoms need %lld scratch bytes, "
-                       "more than the built-in %lld; use tcst_assemble_weight",
-                       (long long)atoms, cache_floats(atoms) * 4, STATIC_SCRATCH_BYTES);
+    if (atoms < 0) {
+        tcst_set_error("tcst_assemble_weight_static: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    // Range first, so the byte count below cannot overflow: the scratch holds
+    // 2 x CACHE_SITES floats per atom.
+    if (atoms > STATIC_SCRATCH_BYTES / (8LL * CACHE_SITES) ||
+        cache_floats(atoms) * 4 > STATIC_SCRATCH_BYTES) {
+        tcst_set_error("tcst_assemble_weight_static: %lld atoms need more than the built-in "
+                       "%lld scratch bytes (%lld atoms at most); use tcst_assemble_weight",
+                       (long long)atoms, STATIC_SCRATCH_BYTES,
+                       STATIC_SCRATCH_BYTES / (8LL * CACHE_SITES));
         return TCST_ERR_UNSUPPORTED;
     }
-    if (atoms < 0 || !atom_table_dev ||
+    if (!atom_table_dev ||
         ((weight_hi_dev == nullptr) != (weight_lo_dev == nullptr)) ||
         (weight_dev && ld_weight < ia.sites) || (weight_hi_dev && ld_split < ia.sites)) {
         tcst_set_error("tcst_assemble_weight_static: invalid arguments");

@@ -3,7 +3,9 @@
 Mirrors torchcst's ``CSTAdamW(params, model=..., lr=..., field_lrs=...)``
 (optim/adamw.py:26-360): atom groups default to raw ``weight_decay=0``,
 ``field_lrs`` are absolute rates relative to the group ``lr`` recorded when the
-group is configured (optim/_field_lrs.py:29-38), per-parameter state is torch's
+group is configured (optim/_field_lrs.py:29-38), ``amplitude_weight_decay`` is
+the decoupled Polar amplitude decay (optim/adamw.py:41,146-183; raw
+``weight_decay`` must stay 0 on atom groups), per-parameter state is torch's
 ``step`` / ``exp_avg`` / ``exp_avg_sq`` (so ``state_dict`` round-trips), and
 ordinary parameters take torch's own functional AdamW. Atom parameters of
 ``torchcst_b200.CSTLinear`` sites are updated by ``tcst_optimizer_step``: the
@@ -33,13 +35,65 @@ def _f32(x) -> float:
     return float(np.float32(x))
 
 
+def law_fields(h: N.AdamW, coords, axes, lr: float, amplitude_weight_decay: float = 0.0):
+    """Fill the coordinate-law fields of a tcst_adamw block: the rational
+    amplitude cap (_backends/torch/updates/rational_radius.py:10-29), the Polar
+    activity-law scalars at step size ``lr`` with torch's float32 scalar
+    arithmetic (_backends/torch/algorithms/polar_update/executor.py:42-112), the
+    chart periods of the torus retraction and the float32 Polar amplitude decay
+    ``lr * amplitude_weight_decay`` (executor.py:18-41)."""
+    if amplitude_weight_decay:
+        if not isinstance(coords, PolarRadius):
+            # operators/atom_update.py:42-66: decay is a Polar-only law.
+            raise ValueError("amplitude decay requires Polar atoms")
+        h.amplitude_decay = _f32(lr * amplitude_weight_decay)
+    oa, ia = axes
+    h.period_out = _f32(oa.period)
+    h.period_in = _f32(ia.period)
+    if isinstance(coords, RationalRadius):
+        cap = torch.tensor(coords.amplitude_max, dtype=torch.float32)
+        if cap.double() > coords.amplitude_max:
+            cap = torch.nextafter(cap, torch.zeros_like(cap))
+        h.amplitude_cap = float(cap)
+    else:
+        p32 = torch.float32
+        h.polar_amplitude_max = _f32(coords.amplitude_max)
+        h.polar_w_c = _f32(coords.w_c)
+        h.polar_activity_gain = _f32(coords.activity_gain)
+        rate = torch.tensor(coords.dormant_expansion_rate, dtype=p32)
+        h.polar_dormant_q_scale = float(3.0 * rate * torch.tensor(lr, dtype=p32))
+        rr = torch.tensor(coords.radial_regularization, dtype=p32)
+        h.polar_decay = float(torch.exp(-4.0 * rr * torch.tensor(lr, dtype=p32)))
+        h.polar_energy_step = _f32(lr) if coords.activity_mode == "time_energy" else 0.0
+    return h
+
+
+def coordinate_update_(proposal, previous, coords, axes, step_size: float,
+                       amplitude_weight_decay: float = 0.0):
+    """Apply the coordinate law in place: ``proposal`` (an outside optimizer's
+    AdamW + field-rate point) becomes the law's result from ``previous``, on the
+    current CUDA stream (``tcst_coordinate_update``)."""
+    R.require_cuda(proposal, previous)
+    if proposal.dtype != torch.float32 or previous.dtype != torch.float32:
+        raise TypeError("the B200 update computes float32 atoms")
+    if not proposal.is_contiguous() or not previous.is_contiguous():
+        raise ValueError("the B200 update needs contiguous [atoms, 4] tensors")
+    if proposal.shape != previous.shape or proposal.ndim != 2 or proposal.shape[1] != 4:
+        raise ValueError("previous point must match the bound atom shape")
+    h = law_fields(N.AdamW(), coords, axes, step_size, amplitude_weight_decay)
+    kind = N.TCST_POLAR if isinstance(coords, PolarRadius) else N.TCST_RATIONAL
+    with R.on_device(proposal.device):
+        N.call("tcst_coordinate_update", R._vp(proposal), R._vp(previous), proposal.shape[0],
+               kind, ctypes.byref(h), R._stream(proposal.device))
+    return proposal
+
+
 class CSTAdamW(AdamW):
     def __init__(self, params, *, model, amplitude_weight_decay: float = 0.0, field_lrs=None,
                  check_finite: bool = False, **adamw_options):
         if not isinstance(model, torch.nn.Module):
             raise TypeError("model must be a torch.nn.Module")
-        if type(amplitude_weight_decay) not in (int, float) or amplitude_weight_decay != 0:
-            raise NotImplementedError("amplitude_weight_decay is not implemented by the B200 update")
+        self._validate_decay(amplitude_weight_decay)
         self.model = model
         self.check_finite = check_finite
         self._sites = {id(m.atoms.p): m for m in model.modules() if isinstance(m, CSTLinear)}
@@ -55,12 +109,39 @@ class CSTAdamW(AdamW):
             g["params"] = list(g["params"]) if not isinstance(g["params"], torch.Tensor) else [g["params"]]
             if any(id(p) in self._sites for p in g["params"]):
                 g.setdefault("weight_decay", adamw_options.get("weight_decay", 0.0))
+                g.setdefault("amplitude_weight_decay", amplitude_weight_decay)
                 if "field_lrs" not in g and self._field_lrs:
                     g["field_lrs"] = dict(self._field_lrs)
                 if g.get("field_lrs"):
                     g["field_lrs"] = self._rates(g["field_lrs"])
                     g.setdefault(REFERENCE, g.get("lr", default_lr))
         super().__init__(groups, **adamw_options)
+
+    @staticmethod
+    def _validate_decay(decay):
+        """optim/adamw.py:126-131."""
+        if type(decay) not in (int, float) or not math.isfinite(decay) or decay < 0:
+            raise ValueError("amplitude_weight_decay must be a finite nonnegative Python scalar")
+
+    def _validate_group(self, group):
+        """The per-step group rules of optim/adamw.py:146-183: atom groups keep raw
+        weight_decay=0 and take the decoupled Polar amplitude decay instead."""
+        has_atoms = any(id(p) in self._sites for p in group["params"])
+        if "amplitude_weight_decay" in group:
+            if not has_atoms:
+                raise ValueError("amplitude_weight_decay requires an atom group")
+            decay = group["amplitude_weight_decay"]
+            self._validate_decay(decay)
+            rate = group.get("lr", self.defaults["lr"])
+            if (type(rate) not in (int, float) or not math.isfinite(rate) or rate < 0
+                    or rate * decay > 1):
+                raise ValueError(
+                    "lr * amplitude_weight_decay must be in [0, 1] with finite Python lr")
+        if has_atoms:
+            raw = group.get("weight_decay", self.defaults["weight_decay"])
+            if type(raw) not in (int, float) or raw != 0:
+                raise ValueError(
+                    "managed atoms require raw weight_decay=0; use amplitude_weight_decay")
 
     @staticmethod
     def _rates(value):
@@ -79,6 +160,7 @@ class CSTAdamW(AdamW):
         lr = group["lr"]
         beta1, beta2 = group["betas"]
         key = (id(site), lr, beta1, beta2, group["eps"], group["weight_decay"],
+               group.get("amplitude_weight_decay", 0.0),
                tuple(sorted((group.get("field_lrs") or {}).items())), group.get(REFERENCE))
         cache = self.__dict__.setdefault("_params_cache", {})
         base = cache.get(key)
@@ -119,24 +201,7 @@ class CSTAdamW(AdamW):
             if unknown:
                 raise ValueError(f"unknown field_lrs {sorted(unknown)}")
         h.field_mask = mask
-        oa, ia = site.axes
-        h.period_out = _f32(oa.period)
-        h.period_in = _f32(ia.period)
-        if isinstance(coords, RationalRadius):
-            cap = torch.tensor(coords.amplitude_max, dtype=torch.float32)
-            if cap.double() > coords.amplitude_max:
-                cap = torch.nextafter(cap, torch.zeros_like(cap))
-            h.amplitude_cap = float(cap)
-        else:
-            p32 = torch.float32
-            h.polar_amplitude_max = _f32(coords.amplitude_max)
-            h.polar_w_c = _f32(coords.w_c)
-            h.polar_activity_gain = _f32(coords.activity_gain)
-            rate = torch.tensor(coords.dormant_expansion_rate, dtype=p32)
-            h.polar_dormant_q_scale = float(3.0 * rate * torch.tensor(lr, dtype=p32))
-            rr = torch.tensor(coords.radial_regularization, dtype=p32)
-            h.polar_decay = float(torch.exp(-4.0 * rr * torch.tensor(lr, dtype=p32)))
-            h.polar_energy_step = _f32(lr) if coords.activity_mode == "time_energy" else 0.0
+        law_fields(h, coords, site.axes, lr, group.get("amplitude_weight_decay", 0.0))
         return h
 
     def site_step(self, p):
@@ -147,6 +212,7 @@ class CSTAdamW(AdamW):
         if site is None:
             raise ValueError("not an atom parameter of a managed CSTLinear")
         group = next(g for g in self.param_groups if any(q is p for q in g["params"]))
+        self._validate_group(group)
         if group.get("amsgrad") or group.get("maximize"):
             raise NotImplementedError("amsgrad/maximize are not implemented for atom groups")
         lr = group["lr"]
@@ -170,6 +236,8 @@ class CSTAdamW(AdamW):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        for group in self.param_groups:
+            self._validate_group(group)
         for group in self.param_groups:
             if group.get("amsgrad") or group.get("maximize"):
                 if any(id(p) in self._sites for p in group["params"]):

@@ -93,6 +93,18 @@ class OptimizerScalars:
         self._upload(h)
         return True
 
+    def check_status(self):
+        """Read and clear the device status word once (a host synchronization;
+        call it off the hot path, e.g. after a run of steps). Raises
+        ``RuntimeError`` if any kernel since the last check flagged invalid
+        atoms or gave up a bounded wait: the steps since then may hold partial
+        results."""
+        code = int(self.ws.status.item())
+        if code:
+            self.ws.status.zero_()
+            raise RuntimeError(f"device status {code:#x}: {R.status_error(code)}")
+        return 0
+
     def _launch_opt(self):
         p = self.layer.atoms.p
         state = self._state
