@@ -13,9 +13,8 @@ opt.step()) with pinned host inputs copied in and the loss read back every step.
 Multi-GPU (torchrun): data parallel, each rank runs the full config-2 step on
 its own 4096 rows with replicated atoms and an NCCL all-reduce of the atom
 gradient; ``value`` is the aggregate (rows/s / 4096).
-``--impl reference``: the reference's factored CPU algorithm (the oracle port)
-on the host cores over a bounded row sample: row-independent phases plus the
-row-proportional phases scaled to 4096 rows.
+``--impl reference``: the reference's factored CPU algorithm (the oracle's port
+of it) on every host core, each step the whole 4096-row config-2 step.
 """
 
 from __future__ import annotations
@@ -112,13 +111,24 @@ def build_layer(device):
     return layer, opt, report
 
 
-def cpu_reference(steps, warmup, sample_rows=512, log=None):
-    """Time the reference factored algorithm (oracle port) on the host cores.
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    Each step runs the whole algorithm on ``sample_rows`` of the 4096 rows and
-    times its phases; the config-2 step time is the row-independent part
-    (decode, factor build, factor chain, optimizer) plus the row-proportional
-    part (six GEMMs, loss) scaled to 4096 rows.
+
+def cpu_reference(steps, warmup, rows=ROWS, log=None):
+    """Time the reference's factored algorithm (the oracle's port of it) on the
+    host cores: every step is the whole config-2 step on ``rows`` rows (all
+    4,096 by default; nothing extrapolated): decode, float64 factors cast to
+    float32, the six float32 GEMMs of the factored forward and backward (numpy
+    BLAS on every host thread), the MSE gradient, the float64 factor chain and
+    the float32 CSTAdamW step with the field rates.
     """
     import numpy as np
     from oracle import cst_oracle as O
@@ -128,37 +138,29 @@ def cpu_reference(steps, warmup, sample_rows=512, log=None):
     p = d["p0"].copy()
     oa, ia, spec = O.Axis(N_IO), O.Axis(N_IO), O.Rational(radius_max=512.0)
     state = O.AdamState(0, np.zeros_like(p), np.zeros_like(p))
-    x = rng.standard_normal((sample_rows, N_IO), dtype=np.float32)
-    t = rng.standard_normal((sample_rows, N_IO), dtype=np.float32)
-    ratios = O.field_ratios(spec, FIELD_LRS, 1e-3)
-    est = []
+    x = rng.standard_normal((rows, N_IO), dtype=np.float32)
+    t = rng.standard_normal((rows, N_IO), dtype=np.float32)
+    times = []
     for i in range(warmup + steps):
         c0 = time.perf_counter()
-        lay = O.decode(oa, ia, spec, p)
-        phi_in, phi_out = O.factors32(lay)
-        c1 = time.perf_counter()
-        atom_values = x @ phi_in
-        y = atom_values @ phi_out.T
-        dy = ((y - t) * np.float32(2.0 / (ROWS * N_IO))).astype(np.float32)
-        dx, d_phi_out, d_phi_in = O.factored_backward_gemms32(x, dy, (phi_in, phi_out,
-                                                                      atom_values))
-        c2 = time.perf_counter()
-        grad = O.factor_chain(lay, d_phi_out, d_phi_in)
-        p = O.optimizer_step(p, grad, state, spec, lr=1e-3, field_ratios=ratios)
-        c3 = time.perf_counter()
-        fixed = (c1 - c0) + (c3 - c2)
-        full = fixed + (c2 - c1) * (ROWS / sample_rows)
+        _, _, _, _, p = O.reference_step(oa, ia, spec, p, x, t, state, lr=1e-3,
+                                         field_lrs=FIELD_LRS)
+        dt = time.perf_counter() - c0
         if i >= warmup:
-            est.append(full)
+            times.append(dt)
         if log:
-            log(f"reference step {i}: sample {c3 - c0:.2f}s, config-2 estimate {full:.2f}s")
-    per_step = statistics.median(est)
-    return {"value": 1.0 / per_step, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{sample_rows} of {ROWS} rows, all {ATOMS} atoms per step; reference "
-                      f"factored algorithm (float64 factors, float32 numpy-BLAS GEMMs, float64 "
-                      f"factor chain, float32 AdamW); config-2 time = row-independent phases + "
-                      f"GEMM/loss phases x {ROWS // sample_rows}; median of {len(est)} steps",
-            "seconds_per_step": per_step}
+            log(f"reference step {i}: {dt:.2f}s")
+    per_step = statistics.median(times)
+    scale = ROWS / rows
+    return {"value": 1.0 / (per_step * scale), "unit": "steps/s", "cores": os.cpu_count(),
+            "kind": "port", "cpu": cpu_model(),
+            "sample": (f"{rows} of {ROWS} rows" if rows != ROWS else f"all {ROWS} rows")
+            + f", all {ATOMS} atoms per step; the oracle's port of the reference factored "
+              f"algorithm (float64 factors, float32 numpy-BLAS GEMMs on {os.cpu_count()} "
+              f"threads, float64 factor chain, float32 CSTAdamW); median of {len(times)} "
+              f"timed steps after {warmup} warm-up"
+            + ("" if rows == ROWS else f"; time x {scale:g} for the full batch"),
+            "seconds_per_step": per_step * scale}
 
 
 def breakdown(lib, step, x, t):
@@ -206,12 +208,13 @@ def run_reference_arm(args):
         return 0
     import numpy as np  # noqa: F401
     steps, warmup = args.steps, args.warmup
-    base = cpu_reference(steps, warmup, sample_rows=args.ref_rows)
+    base = cpu_reference(steps, warmup, rows=args.ref_rows)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "steps/s",
             "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
             "ms_per_step": 1000.0 / base["value"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": CONFIG,
-            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample",
+                                                  "cpu")},
             "e2e": {"value": base["value"], "unit": "steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -219,6 +222,10 @@ def run_reference_arm(args):
 
 
 EXTRA = {
+    1: {"metric": "train steps/s (fwd+bwd+CSTAdamW), README layer 16->8, 12 atoms, B=4",
+        "config": {"workload": "config1: CSTLinear 16->8, 12 atoms, rational radius radius_max=4 "
+                               "q=0, constructor defaults (seed 0), MSE, CSTAdamW lr 1e-3",
+                   "global_batch": 4, "atoms": 12}},
     3: {"metric": "train steps/s (fwd+bwd+CSTAdamW), Polar 784->1024 + ReLU + Linear(1024,10), B=256",
         "config": {"workload": "config3: CSTLinear 784->1024 Polar cell mass (atoms 16384, M=8, "
                                "input base tile 49), ReLU, dense 1024->10, cross-entropy, "
@@ -237,124 +244,157 @@ EXTRA = {
 }
 
 
-def run_extra_config(args):
-    """Configs 3, 4 and 5 through the drop-in autograd API (layer(s), torch loss,
-    CSTAdamW), timed over exactly --steps steps with CUDA events; e2e adds the
-    pinned host-to-device copy of each step's inputs and the loss read-back."""
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    got = json.load(open(path)) if os.path.exists(path) else {}
+    src = "measured" if "bf16_tflops" in got else "fallback"
+    return got.get("bf16_tflops", 1590.0), got.get("hbm_gbs", 6650.0), src
+
+
+def layer_floor_s(rows, n_in, n_out, atoms, need_dx=True):
+    """The survey's roofline time of one layer's training step: for each phase
+    max(flops / tensor peak, bytes / HBM bandwidth), GEMMs costed as the three
+    f16 products of the float32-accurate split at the measured bf16 peak;
+    algorithmic bytes (float32): assembly 16A + 4 N_in N_out, each GEMM
+    4 (B N_in + N_in N_out + B N_out), loss 12 B N_out, pullback
+    4 N_in N_out + 32 A, optimizer 112 A."""
+    bf16, hbm, _ = peaks()
+    P, BW = bf16 * 1e12, hbm * 1e9
+    gemm_bytes = 4.0 * (rows * n_in + n_in * n_out + rows * n_out)
+    gemm = max(3 * 2.0 * rows * n_in * n_out / P, gemm_bytes / BW)
+    other = (16 * atoms + 4 * n_in * n_out + 12 * rows * n_out + 4 * n_in * n_out + 32 * atoms
+             + 112 * atoms) / BW
+    return (3 if need_dx else 2) * gemm + other
+
+
+def _time_steps(call, xs, ts, steps, warmup):
     import torch
-    import torch.nn.functional as F
-    from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
-    from torchcst_b200.init import xavier_normal_
-    from torchcst_b200.spec import RadiusBounds
-
-    world, rank, local = dist_info()
-    if world > 1:
-        raise SystemExit("configs 3, 4 and 5 run on one GPU")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    torch.manual_seed(0)
-    gen = torch.Generator(device=dev).manual_seed(1)
-    grid = lambda n: chart_presets.regular_grid(n, geometry="flat_torus")
-    cheb = ChebyshevSpec(modes=8)
-    if args.config == 3:
-        b = RadiusBounds(minimum=0.5, birth=4.0, maximum=50.0, upper_floor=1.0)
-        kernel = kernels.product(kernels.cell_mass(cheb), kernels.cell_mass(cheb, base_tile_sites=49),
-                                 coordinates=kernels.polar(amplitude_max=1.0, w_c=0.3, bounds=b))
-        layer = CSTLinear(charts=(grid(1024), grid(784)), atoms=16384, kernel=kernel, device=dev,
-                          validate="off")
-        model = torch.nn.Sequential(layer, torch.nn.ReLU(), torch.nn.Linear(1024, 10).to(dev))
-        rows = 256
-
-        def batch():
-            img = torch.zeros(rows, 28, 28, device=dev)
-            crop = torch.rand(rows, 20, 20, device=dev, generator=gen)
-            keep = torch.rand(rows, 20, 20, device=dev, generator=gen) < 0.37  # ~19% of 784
-            img[:, 4:24, 4:24] = crop * keep
-            return img.reshape(rows, 784), torch.randint(0, 10, (rows,), device=dev,
-                                                         generator=gen)
-
-        loss_fn = F.cross_entropy
-    elif args.config == 5:
-        from torchcst_b200.init import kaiming_normal_
-        kernel = kernels.product(kernels.cell_mass(cheb), coordinates=kernels.rational_radius(
-            radius_max=4096.0, radius_fraction=0.0))
-        layer = CSTLinear(charts=(grid(8192), grid(8192)), atoms=262144, kernel=kernel,
-                          device=dev, validate="off")
-        kaiming_normal_(layer, nonlinearity="relu", q=0.0)
-        with torch.no_grad():
-            layer.atoms.p[:, 1].uniform_(0.0, 1.0, generator=gen)
-        model = layer
-        rows = 16384
-
-        def batch():
-            return (torch.randn(rows, 8192, device=dev, generator=gen),
-                    torch.randn(rows, 8192, device=dev, generator=gen))
-
-        loss_fn = F.mse_loss
-    else:
-        kernel = kernels.product(kernels.cell_mass(cheb), coordinates=kernels.rational_radius(
-            radius_max=1024.0, radius_fraction=0.25))
-        l1 = CSTLinear(charts=(grid(8192), grid(2048)), atoms=32768, kernel=kernel, device=dev,
-                       validate="off")
-        l2 = CSTLinear(charts=(grid(2048), grid(8192)), atoms=32768, kernel=kernel, device=dev,
-                       validate="off")
-        xavier_normal_(l1, gain=1.0, q=0.25)
-        xavier_normal_(l2, gain=1.0, q=0.25)
-        model = torch.nn.Sequential(l1, torch.nn.GELU(), l2)
-        rows = 8192
-
-        def batch():
-            return (torch.randn(rows, 2048, device=dev, generator=gen),
-                    torch.randn(rows, 2048, device=dev, generator=gen))
-
-        loss_fn = F.mse_loss
-    opt = CSTAdamW(model.parameters(), model=model, lr=1e-3)
-    data = [batch() for _ in range(2)]
-
-    def step(x, y):
-        opt.zero_grad(set_to_none=True)
-        loss = loss_fn(model(x), y)
-        loss.backward()
-        opt.step()
-        return loss
-
-    for i in range(args.warmup):
-        step(*data[i % 2])
+    for i in range(warmup):
+        call(xs[i % len(xs)], ts[i % len(ts)])
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(args.steps):
-        loss = step(*data[i % 2])
+    for i in range(steps):
+        out = call(xs[i % len(xs)], ts[i % len(ts)])
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    # e2e: inputs from pinned host memory every step, loss read back.
-    host = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in data]
-    dx = [torch.empty_like(x) for x, _ in data]
-    dy = [torch.empty_like(y) for _, y in data]
-    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
-    torch.cuda.synchronize()
-    e0.record()
-    for i in range(args.steps):
-        b = i % 2
-        dx[b].copy_(host[b][0], non_blocking=True)
-        dy[b].copy_(host[b][1], non_blocking=True)
-        lo = step(dx[b], dy[b])
-        loss_host.copy_(lo.detach().reshape(1), non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    h2d = sum(t.numel() * t.element_size() for t in host[0])
-    spec = EXTRA[args.config]
-    line = {"metric": spec["metric"], "value": 1000.0 / ms, "unit": "steps/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": dict(spec["config"], parallelism="dp1"),
-            "e2e": {"value": 1000.0 / e2e_ms, "unit": "steps/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": 4, "api": "model(x); loss.backward(); CSTAdamW.step()"},
-            "loss": float(loss.detach())}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return e0.elapsed_time(e1) / steps, out
+
+
+def measure_config(k, device, steps, warmup):
+    """Configs 1, 3, 4 and 5 on one GPU. Configs 1 and 5 (one layer, MSE) run
+    the fused step (MSETrainStep), 3 and 4 (a dense head or GELU between
+    layers) the drop-in autograd step captured by GraphedStep; both replay CUDA
+    graphs over two input buffers. Returns steps/s, effective float32 GEMM
+    TFLOP/s and the step's time against its roofline floor."""
+    import torch
+    import torch.nn.functional as F
+    from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
+    from torchcst_b200.init import kaiming_normal_, xavier_normal_
+    from torchcst_b200.spec import RadiusBounds
+    from torchcst_b200.train import GraphedStep, MSETrainStep
+
+    torch.manual_seed(0)
+    gen = torch.Generator(device=device).manual_seed(1)
+    grid = lambda n: chart_presets.regular_grid(n, geometry="flat_torus")
+    cheb = ChebyshevSpec(modes=8)
+    rat = lambda rmax, q=0.0: kernels.product(kernels.cell_mass(cheb), coordinates=kernels.rational_radius(
+        radius_max=rmax, radius_fraction=q))
+    if k in (1, 5):
+        if k == 1:
+            layer = CSTLinear(charts=(grid(8), grid(16)), atoms=12, kernel=rat(4.0), device=device,
+                              validate="off")
+            rows, n = 4, (16, 8)
+        else:
+            layer = CSTLinear(charts=(grid(8192), grid(8192)), atoms=262144, kernel=rat(4096.0),
+                              device=device, validate="off")
+            kaiming_normal_(layer, nonlinearity="relu", q=0.0)
+            with torch.no_grad():
+                layer.atoms.p[:, 1].uniform_(0.0, 1.0, generator=gen)
+            rows, n = 16384, (8192, 8192)
+        opt = CSTAdamW(layer.parameters(), model=layer, lr=1e-3)
+        xs = [torch.randn(rows, n[0], device=device, generator=gen) for _ in range(2)]
+        ts = [torch.randn(rows, n[1], device=device, generator=gen) for _ in range(2)]
+        step = MSETrainStep(layer, opt, rows)
+        step(xs[0], ts[0])
+        step.capture(list(zip(xs, ts)))
+        ms, loss = _time_steps(step, xs, ts, steps, warmup)
+        step.check_status()
+        step.release()
+        api = "MSETrainStep (fused step), CUDA-graph replays"
+        layers = [(rows, n[0], n[1], layer.atoms.p.shape[0], True)]
+    else:
+        if k == 3:
+            b = RadiusBounds(minimum=0.5, birth=4.0, maximum=50.0, upper_floor=1.0)
+            kernel = kernels.product(kernels.cell_mass(cheb), kernels.cell_mass(cheb, base_tile_sites=49),
+                                     coordinates=kernels.polar(amplitude_max=1.0, w_c=0.3, bounds=b))
+            layer = CSTLinear(charts=(grid(1024), grid(784)), atoms=16384, kernel=kernel,
+                              device=device, validate="off")
+            model = torch.nn.Sequential(layer, torch.nn.ReLU(), torch.nn.Linear(1024, 10).to(device))
+            rows = 256
+
+            def batch():
+                img = torch.zeros(rows, 28, 28, device=device)
+                crop = torch.rand(rows, 20, 20, device=device, generator=gen)
+                keep = torch.rand(rows, 20, 20, device=device, generator=gen) < 0.37  # ~19% of 784
+                img[:, 4:24, 4:24] = crop * keep
+                return img.reshape(rows, 784), torch.randint(0, 10, (rows,), device=device,
+                                                             generator=gen)
+
+            loss_fn = F.cross_entropy
+            layers = [(rows, 784, 1024, 16384, False)]
+        else:
+            l1 = CSTLinear(charts=(grid(8192), grid(2048)), atoms=32768, kernel=rat(1024.0, 0.25),
+                           device=device, validate="off")
+            l2 = CSTLinear(charts=(grid(2048), grid(8192)), atoms=32768, kernel=rat(1024.0, 0.25),
+                           device=device, validate="off")
+            xavier_normal_(l1, gain=1.0, q=0.25)
+            xavier_normal_(l2, gain=1.0, q=0.25)
+            model = torch.nn.Sequential(l1, torch.nn.GELU(), l2)
+            rows = 8192
+
+            def batch():
+                return (torch.randn(rows, 2048, device=device, generator=gen),
+                        torch.randn(rows, 2048, device=device, generator=gen))
+
+            loss_fn = F.mse_loss
+            layers = [(rows, 2048, 8192, 32768, True), (rows, 8192, 2048, 32768, True)]
+        opt = CSTAdamW(model.parameters(), model=model, lr=1e-3, capturable=True)
+        data = [batch() for _ in range(2)]
+        xs, ts = [d[0] for d in data], [d[1] for d in data]
+
+        def step_fn(x, y):
+            opt.zero_grad(set_to_none=True)
+            loss = loss_fn(model(x), y)
+            loss.backward()
+            opt.step()
+            return loss
+
+        step = GraphedStep(step_fn, opt)
+        ms, loss = _time_steps(step, xs, ts, steps, max(warmup, 3) + 2)
+        step.release()
+        api = "model(x); loss.backward(); CSTAdamW.step() captured by GraphedStep"
+    flops = sum((3 if dx else 2) * 2.0 * r * a * b for r, a, b, _, dx in layers)
+    floor = sum(layer_floor_s(r, a, b, A, dx) for r, a, b, A, dx in layers)
+    return {"metric": EXTRA[k]["metric"], "value": 1000.0 / ms, "unit": "steps/s",
+            "ms_per_step": ms, "steps": steps, "effective_tflops": flops / (ms * 1e-3) / 1e12,
+            "step_floor_us": floor * 1e6, "frac_of_step_floor": floor / (ms * 1e-3),
+            "api": api, "config": EXTRA[k]["config"], "loss": float(loss.detach())}
+
+
+def run_extra_config(args):
+    """One of configs 1, 3, 4, 5 on one GPU as its own JSON line (see
+    measure_config); config 5 over several GPUs goes to run_config5."""
+    import torch
+    world, rank, local = dist_info()
+    if world > 1:
+        raise SystemExit("configs 1, 3 and 4 run on one GPU")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    line = measure_config(args.config, dev, args.steps, args.warmup)
+    line.update({"n_gpus": 1, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                 "vs_baseline": None, "dtype": "f32", "data": "synthetic"})
+    print(json.dumps(line), flush=True)
     return 0
 
 
@@ -490,15 +530,20 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--ref-rows", type=int, default=512)
+    ap.add_argument("--ref-rows", type=int, default=ROWS,
+                    help="rows per reference step (default: the whole 4096-row batch)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--breakdown", action="store_true",
                     help="print per-launch CUDA-event times of one step to stderr")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
-                    help="2: the headline config (default); 3, 4: the other named shapes on "
-                         "one GPU through the drop-in API; 5: the wide layer sharded by "
-                         "output-row bands over --gpus ranks")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
+                    help="2: the headline config (default); 1, 3, 4: the other named shapes on "
+                         "one GPU; 5: the wide layer sharded by output-row bands over --gpus "
+                         "ranks")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="leave out the per-config lines (configs 1, 3, 4, 5 at N=1; the "
+                         "config-5 row-band step at N>1) of the headline run")
+    ap.add_argument("--config-steps", type=int, default=10)
     args = ap.parse_args()
     if args.config == 5 and args.impl != "reference":
         return run_config5(args)
@@ -510,7 +555,7 @@ def main():
     import torch
     import torch.distributed as dist
     from torchcst_b200 import _native
-    from torchcst_b200.train import MSETrainStep
+    from torchcst_b200.train import GraphedStep, MSETrainStep
 
     world, rank, local = dist_info()
     if args.warmup < 3:
@@ -706,20 +751,24 @@ def main():
             dtb[b].copy_(ht[b], non_blocking=True)
             ready[b].record(copy_stream)
 
-    def autograd_step(b):
+    def autograd_body(x, t):
         opt.zero_grad(set_to_none=True)
-        y = layer(dxb[b])
-        lo = (y - dtb[b]).square().mean()
+        y = layer(x)
+        lo = (y - t).square().mean()
         lo.backward()
         if pg is not None:
             dist.all_reduce(layer.atoms.p.grad, group=pg)
             layer.atoms.p.grad.div_(world)
         opt.step()
-        return lo.detach().double()
+        return lo
 
-    def e2e_ms_of(run_step):
+    def autograd_step(b):
+        return autograd_body(dxb[b], dtb[b]).detach().double()
+
+    def e2e_ms_of(run_step, warm=3):
         """Per-step time of the pipelined host->device copies + run_step + loss
-        read-back, CUDA events around exactly max(3, steps) steps."""
+        read-back, CUDA events around exactly max(3, steps) steps after ``warm``
+        untimed steps."""
 
         def e2e_step(i):
             b = i % 2
@@ -731,7 +780,7 @@ def main():
         for b in range(2):
             free[b].record(compute)
         e2e_copy(0)
-        for i in range(3):
+        for i in range(warm):
             e2e_copy(i + 1)
             e2e_step(i)
         torch.cuda.synchronize()
@@ -754,8 +803,20 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # The drop-in autograd API (layer(x), loss.backward(), CSTAdamW.step()) ...
+    # The drop-in autograd API (layer(x), loss.backward(), CSTAdamW.step()),
+    # eagerly ...
     e2e_autograd = world * 1000.0 / e2e_ms_of(autograd_step)
+    # ... and captured by GraphedStep (one CUDA graph per input buffer: three
+    # eager warm-up calls and the two captures stay outside the timed region) ...
+    e2e_graphed = None
+    if pg is None:
+        with torch.no_grad():
+            p.copy_(saved_p)
+        graphed = GraphedStep(autograd_body, opt)
+        e2e_graphed = 1000.0 / e2e_ms_of(
+            lambda b: graphed(dxb[b], dtb[b]).detach().double(), warm=5)
+        graphed.release()
+        del graphed
     # ... and the fused step, graph-captured over the two device buffers.
     with torch.no_grad():
         p.copy_(saved_p)
@@ -777,9 +838,9 @@ def main():
         "achieved": achieved, "peak": bf16, "unit": "TFLOP/s", "frac": achieved / bf16,
         "peak_source": f"bf16 dense burst, {peak_src} (MEASURED_PEAKS.json)",
         "traffic": GEMM_TRAFFIC,
-        "traffic_note": "bytes per launch, mean of the Y, dX and dW launches: ncu "
-                        "dram__bytes_read.sum + dram__bytes_write.sum "
-                        "(profiles/gemm_f16x3_config2.md)",
+        "traffic_source": "static, not measured in this run: ncu dram__bytes_read.sum + "
+                          "dram__bytes_write.sum per launch, mean of this kernel's Y, dX and "
+                          "dW launches at this shape, from a capture of this build",
         "note": "achieved = algorithmic fp32 GEMM flops 2*M*N*K per launch / CUDA-event time; "
                 "each flop costs 3 f16 tensor products (hi*hi+hi*lo+lo*hi) at the bf16 rate, "
                 "so the three-product split caps frac at 1/3",
@@ -797,7 +858,16 @@ def main():
                     "api": "MSETrainStep(layer, CSTAdamW)(x, target), graph-captured",
                     "copies": "pinned host -> device on a copy stream one step ahead",
                     "autograd_api_value": e2e_autograd,
-                    "autograd_api": "layer(x); loss.backward(); CSTAdamW.step()"},
+                    "autograd_api": "layer(x); loss.backward(); CSTAdamW.step(), eager",
+                    "autograd_api_graphed_value": e2e_graphed,
+                    "autograd_api_graphed": "the same step function under "
+                                            "torchcst_b200.train.GraphedStep (N=1)"},
+            "step_roofline": {
+                "floor_us": layer_floor_s(ROWS, N_IO, N_IO, ATOMS) * 1e6,
+                "measured_us": ms_per_step * 1e3,
+                "frac": layer_floor_s(ROWS, N_IO, N_IO, ATOMS) / (ms_per_step * 1e-3),
+                "note": "whole step against the sum over phases of max(flops / bf16 peak, "
+                        "bytes / HBM bandwidth), GEMMs as three f16 products, measured peaks"},
             "no_dx": {"value": world * 1000.0 / ms_nodx, "ms_per_step": ms_nodx,
                       "note": "the same step without dX (X as data): no dX GEMM"},
             "gpu_launches": MSETrainStep.LAUNCHES_PER_STEP * args.steps,
@@ -805,9 +875,15 @@ def main():
             "init": {"amplitude_scale": report.amplitude_scale,
                      "relative_error": report.relative_error},
             "wall_s_timed": wall}
+    if world == 1 and not args.no_configs:
+        # The other named shapes, each timed over --config-steps graph replays.
+        line["configs"] = {}
+        for k in (1, 3, 4, 5):
+            line["configs"][str(k)] = measure_config(k, device, args.config_steps, args.warmup)
+            torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_reference(2, 1, args.ref_rows).items()
-                                if k in ("value", "unit", "cores", "kind", "sample")}
+                                if k in ("value", "unit", "cores", "kind", "sample", "cpu")}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:

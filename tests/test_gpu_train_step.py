@@ -83,3 +83,78 @@ def test_fused_step_matches_autograd_api():
     for a, b in zip(fused, api):
         a, b = a.cpu().numpy().astype(np.float64), b.cpu().numpy().astype(np.float64)
         assert np.abs(a - b).max() <= 1e-4 * max(np.abs(b).max(), 1e-30)
+
+
+def _graphed_vs_eager(build, steps=7):
+    """Run the same drop-in step function eagerly and through GraphedStep
+    (3 eager warm-up calls, then captured replays over two buffer sets)."""
+    from torchcst_b200.train import GraphedStep
+    runs = []
+    for graphed in (False, True):
+        model, opt, step_fn, xs, ts = build()
+        call = GraphedStep(step_fn, opt) if graphed else step_fn
+        losses = [float(call(xs[i % 2], ts[i % 2])) for i in range(steps)]
+        torch.cuda.synchronize()
+        state = [t.detach().clone() for t in model.parameters()]
+        for p in model.parameters():
+            st = opt.state[p]
+            state += [st["exp_avg"].clone(), st["exp_avg_sq"].clone()]
+        runs.append((losses, state))
+        if graphed:
+            call.release()
+    (l0, s0), (l1, s1) = runs
+    assert l0 == l1
+    for a, b in zip(s0, s1):
+        assert torch.equal(a, b)
+
+
+def test_graphed_autograd_step_matches_eager_mse():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+    def build():
+        layer, opt, xs, ts = _setup()
+
+        def step(x, t):
+            opt.zero_grad(set_to_none=True)
+            loss = (layer(x) - t).square().mean()
+            loss.backward()
+            opt.step()
+            return loss
+
+        return layer, opt, step, xs, ts
+
+    _graphed_vs_eager(build)
+
+
+def test_graphed_autograd_step_matches_eager_classifier():
+    """The config-3 shape of model (Polar CSTLinear, ReLU, dense head,
+    cross-entropy) with a capturable group for the dense parameters."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from tests.test_gpu_parity import make_layer
+    import torch.nn.functional as F
+    from torchcst_b200 import CSTAdamW
+
+    def build():
+        d = load("config3")
+        torch.manual_seed(0)
+        layer = make_layer("config3", d["p0"])
+        layer.validate = "off"
+        head = torch.nn.Linear(1024, 10).cuda()
+        model = torch.nn.Sequential(layer, torch.nn.ReLU(), head)
+        opt = CSTAdamW(model.parameters(), model=model, lr=1e-3, capturable=True)
+        g = torch.Generator(device="cuda").manual_seed(3)
+        xs = [torch.rand(64, 784, device="cuda", generator=g) for _ in range(2)]
+        ts = [torch.randint(0, 10, (64,), device="cuda", generator=g) for _ in range(2)]
+
+        def step(x, t):
+            opt.zero_grad(set_to_none=True)
+            loss = F.cross_entropy(model(x), t)
+            loss.backward()
+            opt.step()
+            return loss
+
+        return model, opt, step, xs, ts
+
+    _graphed_vs_eager(build)

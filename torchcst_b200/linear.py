@@ -200,7 +200,9 @@ class CSTLinear(nn.Module):
         return ws
 
     def _maybe_check(self, ws):
-        if self.validate == "sync":
+        # Inside a CUDA graph capture the status stays on the device (read it
+        # later with check_status); a host read there would break the capture.
+        if self.validate == "sync" and not torch.cuda.is_current_stream_capturing():
             self.check_status(ws)
 
     def check_status(self, ws=None):

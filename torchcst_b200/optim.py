@@ -246,15 +246,25 @@ class CSTAdamW(AdamW):
             if type(lr) not in (int, float) or not math.isfinite(lr) or lr < 0:
                 raise ValueError("CST learning rates must be finite nonnegative Python scalars")
             plain = ([], [], [], [], [])
+            capturing = torch.cuda.is_current_stream_capturing()
             for p in group["params"]:
                 if p.grad is None:
                     continue
                 site = self._sites.get(id(p))
                 state = self.state[p]
                 if not state:
-                    state["step"] = torch.tensor(0.0, dtype=torch.float32)
+                    # torch's AdamW keeps a capturable group's step count on the device.
+                    on_device = site is None and group["capturable"]
+                    state["step"] = (torch.zeros((), dtype=torch.float32, device=p.device)
+                                     if on_device else torch.tensor(0.0, dtype=torch.float32))
                     state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
                     state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                if capturing and site is None and not group["capturable"]:
+                    raise RuntimeError("capturing a CSTAdamW step needs capturable=True for "
+                                       "the groups of ordinary parameters")
+                if capturing and site is not None:
+                    self._capture_site_step(p, site, state)
+                    continue
                 if site is None:
                     plain[0].append(p)
                     plain[1].append(p.grad)
@@ -262,6 +272,8 @@ class CSTAdamW(AdamW):
                     plain[3].append(state["exp_avg_sq"])
                     plain[4].append(state["step"])
                     continue
+                if p.is_cuda:
+                    self._graph_entry(p)  # ready for a later capture
                 if self.check_finite and not bool(torch.isfinite(p.grad).all()):
                     raise FloatingPointError("non-finite parameter gradient")
                 if p.grad.is_sparse:
@@ -286,6 +298,65 @@ class CSTAdamW(AdamW):
                     weight_decay=group["weight_decay"], eps=group["eps"],
                     maximize=group["maximize"], has_complex=False)
         return loss
+
+    # -- CUDA graph capture ------------------------------------------------------
+
+    RING = 64
+
+    def _graph_entry(self, p):
+        """The device scalar block (and its pinned upload ring) of atom site
+        ``p`` for captured steps. Made by an eager step: an allocation inside
+        a capture would come with an initialising kernel that every replay
+        would run after the scalar upload."""
+        entries = self.__dict__.setdefault("_graph_entries", {})
+        entry = entries.get(id(p))
+        if entry is None:
+            nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
+            entry = entries[id(p)] = {
+                "p": p, "params": torch.zeros(nbytes, dtype=torch.uint8, device=p.device),
+                "ring": torch.zeros(self.RING, nbytes, dtype=torch.uint8).pin_memory(),
+                "events": [None] * self.RING, "slot": 0}
+        return entry
+
+    def _capture_site_step(self, p, site, state):
+        """Record the atom update of ``p`` into the CUDA graph being captured.
+        The kernel reads its per-step scalars from a device block that
+        :meth:`refresh_captured` fills before every replay; the step count is
+        advanced there too, once per replay, not here."""
+        entry = self.__dict__.get("_graph_entries", {}).get(id(p))
+        if entry is None:
+            raise RuntimeError("run one eager CSTAdamW step before capturing one")
+        self.__dict__.setdefault("_graph_sites", {})[id(p)] = entry
+        kind = N.TCST_POLAR if isinstance(site.kernel.coordinates, PolarRadius) else N.TCST_RATIONAL
+        if not p.grad.is_contiguous():
+            raise ValueError("captured atom updates need a contiguous gradient")
+        with R.on_device(p.device):
+            N.call("tcst_optimizer_step_device", R._vp(p), R._vp(p.grad),
+                   R._vp(state["exp_avg"]), R._vp(state["exp_avg_sq"]), p.shape[0], kind,
+                   R._vp(entry["params"]), R._stream(p.device))
+
+    def refresh_captured(self):
+        """Host half of one replayed step of every captured atom site: advance its
+        step count exactly as :meth:`step` does and copy the step's scalars (bias
+        corrections, rates) to its device block through a pinned ring, on the
+        current stream, ahead of the replay."""
+        for entry in self.__dict__.get("_graph_sites", {}).values():
+            p = entry["p"]
+            out = self.site_step(p)
+            if out is None:
+                raise ValueError("a captured CSTAdamW step needs a positive learning rate")
+            h = out[0]
+            slot = entry["slot"]
+            ev = entry["events"][slot]
+            if ev is not None:
+                ev.synchronize()  # the copy that last read this slot has run
+            ring = entry["ring"][slot]
+            ctypes.memmove(ring.data_ptr(), ctypes.addressof(h), ctypes.sizeof(h))
+            entry["params"].copy_(ring, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            entry["events"][slot] = ev
+            entry["slot"] = (slot + 1) % self.RING
 
     def get_field_lrs(self):
         out = []

@@ -126,7 +126,7 @@ class NativeBinding:
         return ws
 
     def _maybe_check(self, ws):
-        if self.validate == "sync":
+        if self.validate == "sync" and not torch.cuda.is_current_stream_capturing():
             code = int(ws.status.item())
             if code:
                 ws.status.zero_()

@@ -280,3 +280,64 @@ class MSETrainStep(OptimizerScalars):
         """Drop the captured graphs."""
         self._graphs.clear()
         self._opt_graph = None
+
+
+class GraphedStep:
+    """One CUDA graph per input-buffer set for a training step written with the
+    drop-in API::
+
+        def step(x, target):
+            optimizer.zero_grad(set_to_none=True)
+            loss = loss_fn(model(x), target)
+            loss.backward()
+            optimizer.step()
+            return loss
+
+        graphed = GraphedStep(step, optimizer)
+        loss = graphed(x, target)   # every call is exactly one training step
+
+    The first ``warmup`` calls run eagerly on a side stream (the warm-up CUDA
+    graph capture needs); the next call with a given set of input buffers
+    captures the step and every later call with those buffers replays it, the
+    host doing only the optimizer's per-step scalar refresh
+    (:meth:`CSTAdamW.refresh_captured`). Inputs are identified by their device
+    pointers: pass the same buffers (refilled) to reuse a graph. Returns the
+    step function's result; for replays it is the captured output tensor,
+    overwritten by the next replay. Ordinary parameters need a capturable
+    optimizer group (``capturable=True``); CSTLinear status checks run on the
+    device inside replays (read them with ``check_status``)."""
+
+    def __init__(self, step_fn, optimizer: CSTAdamW, *, warmup: int = 3):
+        if int(warmup) < 1:
+            raise ValueError("GraphedStep needs at least one eager warm-up step")
+        self.step_fn, self.opt, self.warmup = step_fn, optimizer, int(warmup)
+        self._eager = 0
+        self._graphs = {}
+        self._side = None
+
+    def __call__(self, *tensors):
+        key = tuple(t.data_ptr() for t in tensors)
+        entry = self._graphs.get(key)
+        if entry is None and self._eager < self.warmup:
+            self._eager += 1
+            main = torch.cuda.current_stream()
+            if self._side is None:
+                self._side = torch.cuda.Stream(main.device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                out = self.step_fn(*tensors)
+            main.wait_stream(self._side)
+            return out
+        if entry is None:
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = self.step_fn(*tensors)
+            entry = self._graphs[key] = (graph, out)
+        self.opt.refresh_captured()
+        entry[0].replay()
+        return entry[1]
+
+    def release(self):
+        """Drop the captured graphs (and their memory pools)."""
+        self._graphs.clear()
