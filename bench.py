@@ -398,29 +398,19 @@ def run_extra_config(args):
     return 0
 
 
-def run_config5(args):
-    """Config 5 (8192 -> 8192, 262,144 atoms) sharded by output-row bands over
-    --gpus ranks (one process per GPU, NCCL; one band on a single GPU): eager
-    RowBandMSETrainStep steps timed with CUDA events, max over ranks. Strong
-    scaling: every step trains the whole layer on the same 16,384 rows. e2e
-    adds each step's pinned host-to-device copies of X and of the rank's target
-    band and the loss read-back."""
-    import datetime
-
+def rowband_config5(pg, world, rank, dev, steps, warmup):
+    """The config-5 row-band step on this process group (strong scaling: the
+    whole 16,384-row step over ``world`` bands), timed with CUDA events over
+    ``steps`` steps, max over ranks; plus a per-phase breakdown of one more
+    step (events at the phase boundaries on the main stream, max over ranks),
+    the bytes each rank receives in the all-gathers, and the time of one
+    all-gather of a dY band block measured alone."""
     import torch
     import torch.distributed as dist
     from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
     from torchcst_b200.init import kaiming_normal_
     from torchcst_b200.shard import RowBandMSETrainStep, band
 
-    world, rank, local = dist_info()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
-        pg = dist.group.WORLD
     torch.manual_seed(0)
     gen = torch.Generator(device=dev).manual_seed(1)
     n, rows = 8192, 16384
@@ -437,21 +427,86 @@ def run_config5(args):
     x = torch.randn(rows, n, device=dev, generator=gen)
     t = torch.randn(rows, n, device=dev, generator=gen)
     step = RowBandMSETrainStep(layer, opt, rows, process_group=pg)
-    for _ in range(args.warmup):
+    step._x_ref, step._t_ref = x, t
+    for _ in range(warmup):
         step(x, t)
     torch.cuda.synchronize()
     if pg is not None:
         dist.barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         loss = step(x, t)
     e1.record()
     torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    step.marks = []
+    step(x, t)
+    torch.cuda.synchronize()
+    marks, step.marks = step.marks, None
+    phases = torch.tensor([a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])],
+                          device=dev)
+    step.check_status()
+    # One dY-band all-gather alone (the step's largest collective).
+    nb = band(n, rank, world)[1]
+    coll_ms = 0.0
+    if pg is not None:
+        src = torch.empty(rows, nb, device=dev)
+        dst = torch.empty(world, rows, nb, device=dev)
+        dist.all_gather_into_tensor(dst, src, group=pg)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(3):
+            dist.all_gather_into_tensor(dst, src, group=pg)
+        e1.record()
+        torch.cuda.synchronize()
+        c = torch.tensor([e0.elapsed_time(e1) / 3], device=dev)
+        dist.all_reduce(c, op=dist.ReduceOp.MAX)
+        coll_ms = float(c.item())
+        del src, dst
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(phases, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    received = 2 * (world - 1) * rows * nb * 4  # dY and dX column blocks from the others
+    return {"metric": EXTRA[5]["metric"], "value": 1000.0 / ms, "unit": "steps/s",
+            "ms_per_step": ms, "n_gpus": world, "steps": steps, "scaling": "strong",
+            "parallelism": f"rowband{world}", "band_rows": nb,
+            "effective_tflops": 3 * 2.0 * rows * n * n / (ms * 1e-3) / 1e12,
+            "phases_ms": {name: float(v) for (name, _), v in zip(marks[1:], phases.tolist())},
+            "allgather_bytes_received_per_step": received,
+            "allgather_dy_block_ms": coll_ms,
+            "gradient_allreduce_bytes": 262144 * 16 if world > 1 else 0,
+            "loss": float(loss), "config": EXTRA[5]["config"]}, step
+
+
+def run_config5(args):
+    """Config 5 (8192 -> 8192, 262,144 atoms) sharded by output-row bands over
+    --gpus ranks (one process per GPU, NCCL; one band on a single GPU): eager
+    RowBandMSETrainStep steps timed with CUDA events, max over ranks. Strong
+    scaling: every step trains the whole layer on the same 16,384 rows. e2e
+    adds each step's pinned host-to-device copies of X and of the rank's target
+    band and the loss read-back."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from torchcst_b200.shard import RowBandMSETrainStep, band
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+        pg = dist.group.WORLD
+    sampler = ClockSampler(local)
+    sampler.start()
+    info, step = rowband_config5(pg, world, rank, dev, args.steps, args.warmup)
     clocks = sampler.stop()
-    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    n, rows = 8192, 16384
+    x, t = step._x_ref, step._t_ref
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # e2e: X and this rank's target band copied from pinned host memory each step.
     r0, nb = band(n, rank, world)
     hx = x.cpu().pin_memory()
@@ -471,9 +526,8 @@ def run_config5(args):
     torch.cuda.synchronize()
     e2e_ms = torch.tensor([e0.elapsed_time(e1) / max(2, args.steps // 4)], device=dev)
     if pg is not None:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    ms, e2e = float(ms.item()), float(e2e_ms.item())
+    ms, e2e = info["ms_per_step"], float(e2e_ms.item())
     flops = 3 * 2.0 * rows * n * n
     # Roofline of the dominant kernel class, the tensor-core GEMM: this rank's Y
     # band GEMM (2 B nb N fp32-equivalent flops) timed alone with CUDA events on
@@ -515,7 +569,10 @@ def run_config5(args):
                     "d2h_bytes_per_step": 8,
                     "api": "RowBandMSETrainStep(x, target) per rank"},
             "gpu_launches": RowBandMSETrainStep.LAUNCHES_PER_STEP * args.steps,
-            "roofline": roofline, "clocks": clocks, "loss": float(loss)}
+            "phases_ms": info["phases_ms"],
+            "allgather_bytes_received_per_step": info["allgather_bytes_received_per_step"],
+            "allgather_dy_block_ms": info["allgather_dy_block_ms"],
+            "roofline": roofline, "clocks": clocks, "loss": info["loss"]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
@@ -875,6 +932,13 @@ def main():
             "init": {"amplitude_scale": report.amplitude_scale,
                      "relative_error": report.relative_error},
             "wall_s_timed": wall}
+    if world > 1 and not args.no_configs:
+        # The north star's split: config 5 sharded by output-row bands over the
+        # same ranks (strong scaling), under its own key.
+        step.release()
+        torch.cuda.empty_cache()
+        line["config5_rowband"], _ = rowband_config5(pg, world, rank, device,
+                                                     args.config_steps // 2 or 1, 2)
     if world == 1 and not args.no_configs:
         # The other named shapes, each timed over --config-steps graph replays.
         line["configs"] = {}

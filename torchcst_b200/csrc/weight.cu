@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
         int4 *gdesc = cspan;                  // (first row, first column, columns, entries)
         int *gpre = ccls;
         if (t < ngroups) {
-            int cr, cc, fr, fc;
+            int cr, cc, fr, fc, first_bin, end_bin;
             if (t < g.nclass) {
                 // Class edges are powers of two: the tile holding R0 by a shift.
                 const int sh = 31 - __clz(class_edge(t, g.fe));
@@ -195,12 +195,17 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
                 cc = reach_tiles(t, g.fe, g.tc[t], ni);
                 fr = R0 >> sh;
                 fc = C0 >> sh;
+                first_bin = g.base[t], end_bin = g.base[t + 1];
             } else {
                 const int l = t - g.nclass, T = g.pl_T[l], F = g.pl_K[l] * T;
                 cr = cover_nodes(R0, TR, T, F, g.pl_no[l], no, fr);
                 cc = cover_nodes(C0, TC, T, F, g.pl_ni[l], ni, fc);
+                first_bin = g.pl_base[l], end_bin = g.pl_base[l + 1];
             }
-            gdesc[t] = make_int4(fr, fc, cc, cr * cc);
+            // A group without atoms (early in training most classes are empty)
+            // contributes no scan entries.
+            const bool empty = tv.offsets[first_bin] == tv.offsets[end_bin];
+            gdesc[t] = make_int4(fr, fc, cc, empty ? 0 : cr * cc);
         }
         __syncthreads();
         if (warp == 0) {

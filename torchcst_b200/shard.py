@@ -103,6 +103,13 @@ class RowBandMSETrainStep(OptimizerScalars):
         self.scale = dp_loss_scale(B, no)
         self.nblocks = ctypes.c_int32(0)
         self._side = torch.cuda.Stream(dev)
+        self.marks = None  # a list: CUDA events at the phase boundaries of the next steps
+
+    def _mark(self, name):
+        if self.marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.marks.append((name, ev))
 
     def _gemm(self, M, N_, K, a_hi, a_lo, lda, a_mn, a_scale, b_hi, b_lo, ldb, b_mn, b_scale, c,
               ldc, split=1, sstride=0, stream=None, what="gemm"):
@@ -123,6 +130,7 @@ class RowBandMSETrainStep(OptimizerScalars):
         r0, nb, c0, nc = self.r0, self.nb, self.c0, self.nc
         x16, dy16, w16b = self.x16, self.dy16, self.w16b
         pg = self.pg
+        self._mark("start")
         self.amax.zero_()
         side.wait_stream(main)  # X split beside decode and weight assembly
         N.check(lib.tcst_absmax(vp(x), B, ni, x.stride(0), vp(x16.amax), st2), "absmax x")
@@ -142,6 +150,7 @@ class RowBandMSETrainStep(OptimizerScalars):
                 nc, vp(w16c.amax), vp(w16c.hi), vp(w16c.lo), w16c.ld, vp(w16c.scale), st),
                 "weight columns")
         main.wait_stream(side)
+        self._mark("decode+sort+weights")
         y_band = self.y[:, r0:]
         self._gemm(B, nb, ni, x16.hi.data_ptr(), x16.lo.data_ptr(), x16.ld, 0,
                    x16.scale.data_ptr(), w16b.hi.data_ptr(), w16b.lo.data_ptr(), w16b.ld, 0,
@@ -162,6 +171,7 @@ class RowBandMSETrainStep(OptimizerScalars):
                                        ctypes.c_void_p(dy16.lo.data_ptr() + off), dy16.ld,
                                        vp(dy16.scale), st), "split dy")
 
+        self._mark("gemm Y+loss+max")
         split_band(self.dy_band, self.rank)
         # The dY all-gather runs beside the dW GEMM and the banded pullback,
         # which need only this rank's band.
@@ -175,6 +185,7 @@ class RowBandMSETrainStep(OptimizerScalars):
         N.check(lib.tcst_pullback_band(vp(self.table), A, oa, ia, vp(self.g), self.ldg,
                                        self.split, self.gstride, r0, nb, vp(self.grad), st),
                 "pullback")
+        self._mark("gemm dW+pullback")
         # The halo-atom reduction runs beside the dX GEMM.
         reduce_grad = (dist.all_reduce(self.grad, group=pg, async_op=True)
                        if pg is not None else None)
@@ -184,19 +195,23 @@ class RowBandMSETrainStep(OptimizerScalars):
                 for k in range(self.world):
                     if k != self.rank:
                         split_band(self.dy_all[k], k)
+            self._mark("dY gather wait+split")
             w16c = self.w16c
             self._gemm(B, nc, no, dy16.hi.data_ptr(), dy16.lo.data_ptr(), dy16.ld, 0,
                        dy16.scale.data_ptr(), w16c.hi.data_ptr(), w16c.lo.data_ptr(), w16c.ld, 1,
                        w16c.scale.data_ptr(), self.dx_band.data_ptr(), nc, what="gemm dx")
+            self._mark("gemm dX")
             if pg is not None:
                 dist.all_gather_into_tensor(self.dx_all, self.dx_band, group=pg)
             else:
                 self.dx_all[0].copy_(self.dx_band)
+            self._mark("dX gather")
         elif gather_dy is not None:
             gather_dy.wait()
         if pg is not None:
             reduce_grad.wait()
             dist.all_reduce(self.loss_sum, group=pg)
+        self._mark("gradient all-reduce wait")
         return self.loss_sum[0] / (B * no)
 
     def __call__(self, x, target):
@@ -208,6 +223,7 @@ class RowBandMSETrainStep(OptimizerScalars):
             loss = self._launch_grad(x, target)
             if optimize:
                 self._launch_opt()
+            self._mark("optimizer")
         return loss
 
     def dx(self):
