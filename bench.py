@@ -783,6 +783,7 @@ def main():
     step_nodx.release()
     del step_nodx
 
+
     # End-to-end through the drop-in API with pinned host inputs: every step
     # copies its X and target from pinned host memory (on a copy stream, one step
     # ahead, into alternating device buffers) and reads its loss back.

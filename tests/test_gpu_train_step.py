@@ -158,3 +158,4 @@ def test_graphed_autograd_step_matches_eager_classifier():
         return model, opt, step, xs, ts
 
     _graphed_vs_eager(build)
+

@@ -341,3 +341,4 @@ class GraphedStep:
     def release(self):
         """Drop the captured graphs (and their memory pools)."""
         self._graphs.clear()
+
