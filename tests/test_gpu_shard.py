@@ -33,6 +33,7 @@ def test_single_band_matches_unsharded_step():
         a, b = step.grad[:, c], ref.grad[:, c]
         assert float((a - b).abs().max() / b.abs().max()) < 1e-4, c
     assert float((step.dx() - ref.dx).abs().max() / ref.dx.abs().max()) < 1e-4
+    assert step.check_status() == 0
 
 
 @pytest.mark.parametrize("world", [2])

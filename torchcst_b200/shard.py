@@ -1,28 +1,27 @@
 """One CSTLinear MSE training step sharded by output-row bands (one process per GPU).
 
-Rank g of G owns output rows [r0, r0 + nb) with nb = N_out / G and, for dX,
-input columns [c0, c0 + nc) with nc = N_in / G (both multiples of 32). Atoms,
-their AdamW moments, X and the target are replicated; every rank decodes and
-sorts all atoms (O(A) work). One step:
+Rank g of G owns output rows [r0, r0 + nb) with nb = N_out / G (a multiple of
+32). Atoms, their AdamW moments, X and the target are replicated; every rank
+decodes and sorts all atoms (O(A) work, small beside the band's work at the
+sizes that shard). One step:
 
     W[r0:r0+nb, :] (window assembly, f16 split) | f16 split of X
     Y band = X W_band^T, then dY band = (Y band - T[:, band]) 2/(B N_out) with
-      its loss partials and max |dY|
-    max |dY|: all-reduce (MAX), so every band splits with one scale
-    dY bands: all-gather (float32 column blocks), overlapped with
-      dW band = dY_band^T X and the banded pullback: each atom's gradient from
-      the band's rows (atoms whose footprints cross band edges -- the halo --
-      get partial sums on several ranks)
-    atom gradients: all-reduce (SUM), overlapped with the split of the gathered
-      dY bands into the f16 planes of the whole dY and
-      dX[:, c0:c0+nc] = dY W[:, c0:c0+nc] (second window assembly); all-gather
-      of the dX column blocks
+      its loss partials and max |dY| (the band's own split scale)
+    dW band = dY_band^T X and the banded pullback: each atom's gradient from
+      the band's rows; atoms whose footprints cross band edges (the halo) get
+      partial sums on several ranks
+    | beside them: the band's share of dX, dY_band W_band (B x N_in, K = nb),
+      all-reduced (sum) over the ranks on a second communicator, so every rank
+      ends with the whole dX = sum over bands of dY_band W_band
+    atom gradients: all-reduce (sum) -- the halo exchange (atoms inside one
+      band add zeros elsewhere)
     CSTAdamW on every rank (identical)
 
-NCCL carries the dY / dX column-block all-gathers, the halo-atom gradient
-reduction (the whole [A, 4] gradient: 16 B per atom) and two scalars.
-Work per rank is 1/G of the weight assembly (twice: row and column windows),
-of the three GEMMs and of the pullback (plus the halo).
+NCCL carries the dX partial all-reduce (a reduce-scatter of the dX column
+blocks and their all-gather), the halo-atom gradient reduction (the whole
+[A, 4] gradient: 16 B per atom) and the loss sum. Work per rank is 1/G of the
+weight assembly, of the three GEMMs and of the pullback (plus the halo).
 """
 
 from __future__ import annotations
@@ -49,11 +48,27 @@ def band(n: int, rank: int, world: int):
     return rank * nb, nb
 
 
+def meets_band(first, length, n: int, r0: int, nb: int):
+    """Which cyclic footprints [first, first + length) (mod n) meet the band
+    [r0, r0 + nb): elementwise over array-likes of first sites and lengths (the
+    rule the banded pullback applies on the device). Atoms that meet several
+    bands are the halo: their gradients are partial sums on each of them."""
+    import numpy as np
+    first = np.mod(np.asarray(first, np.int64), n)
+    length = np.asarray(length, np.int64)
+    if nb >= n:
+        return length > 0
+    end = first + length
+    inside = (first < r0 + nb) & (r0 < end)          # no wrap past n
+    wrapped = (end > n) & (r0 < end - n)              # the part past n, from site 0
+    return (length > 0) & ((length >= n) | inside | wrapped)
+
+
 class RowBandMSETrainStep(OptimizerScalars):
     """Eager MSE training step of one layer sharded by output-row bands over a
     process group (NCCL); ``process_group=None`` runs the whole layer as one band."""
 
-    LAUNCHES_PER_STEP = 26  # native kernels at G > 1 (one dY split per band)
+    LAUNCHES_PER_STEP = 22  # native kernels (decode, sort, assembly, splits, GEMMs, pullback, optimizer)
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
                  process_group=None):
@@ -62,6 +77,10 @@ class RowBandMSETrainStep(OptimizerScalars):
         self.rows, self.need_dx, self.pg = int(rows), need_dx, process_group
         self.world = dist.get_world_size(process_group) if process_group is not None else 1
         self.rank = dist.get_rank(process_group) if process_group is not None else 0
+        # A second communicator for the dX all-reduce, so that it runs beside
+        # the dW GEMM, the pullback and the gradient all-reduce.
+        self.pg_dx = (dist.new_group(dist.get_process_group_ranks(process_group))
+                      if process_group is not None and need_dx else None)
         dev = p.device
         plan = layer._plan
         self.plan = plan
@@ -69,29 +88,19 @@ class RowBandMSETrainStep(OptimizerScalars):
         A = self.atoms = p.shape[0]
         B, no, ni = self.rows, plan.n_out, plan.n_in
         self.r0, self.nb = band(no, self.rank, self.world)
-        self.c0, self.nc = band(ni, self.rank, self.world)
         f32 = torch.float32
         self.table = torch.empty(max(plan.table_bytes(A) // 4, 1), dtype=f32, device=dev)
         self.scratch = self.ws.scratch(A)
-        # absmax words and scales: W band, X, dY (global), W column band
-        self.amax = torch.zeros(4, dtype=f32, device=dev)
-        self.scales = torch.ones(4, dtype=f32, device=dev)
+        # absmax words and scales: W band, X, dY band
+        self.amax = torch.zeros(3, dtype=f32, device=dev)
+        self.scales = torch.ones(3, dtype=f32, device=dev)
         self.w_band = torch.empty(self.nb, ni, dtype=f32, device=dev)
         self.w16b = R.F16Split(self.nb, ni, dev, amax=self.amax[0:1], scale=self.scales[0:1])
         self.x16 = R.F16Split(B, ni, dev, amax=self.amax[1:2], scale=self.scales[1:2])
-        self.dy16 = R.F16Split(B, no, dev, amax=self.amax[2:3], scale=self.scales[2:3])
-        if need_dx and self.world > 1:
-            self.w_col = torch.empty(no, self.nc, dtype=f32, device=dev)
-            self.w16c = R.F16Split(no, self.nc, dev, amax=self.amax[3:4],
-                                   scale=self.scales[3:4])
-        elif need_dx:
-            self.w16c = self.w16b  # one band: the column window is the whole W
-        if need_dx:
-            self.dx_band = torch.empty(B, self.nc, dtype=f32, device=dev)
-            self.dx_all = torch.empty(self.world, B, self.nc, dtype=f32, device=dev)
+        self.dy16 = R.F16Split(B, self.nb, dev, amax=self.amax[2:3], scale=self.scales[2:3])
+        self.dx_full = torch.empty(B, ni, dtype=f32, device=dev) if need_dx else None
         self.y = torch.empty(B, no, dtype=f32, device=dev)  # Y band at columns [r0, r0 + nb)
         self.dy_band = torch.empty(B, self.nb, dtype=f32, device=dev)
-        self.dy_all = torch.empty(self.world, B, self.nb, dtype=f32, device=dev)
         tiles = -(-self.nb // 128) * -(-ni // 256)
         self.split = int(max(1, min(8, -(-B // 32), 148 // max(tiles, 1))))
         self.ldg = R.pad4(ni)
@@ -103,6 +112,7 @@ class RowBandMSETrainStep(OptimizerScalars):
         self.scale = dp_loss_scale(B, no)
         self.nblocks = ctypes.c_int32(0)
         self._side = torch.cuda.Stream(dev)
+        self._dx_side = torch.cuda.Stream(dev)
         self.marks = None  # a list: CUDA events at the phase boundaries of the next steps
 
     def _mark(self, name):
@@ -127,7 +137,7 @@ class RowBandMSETrainStep(OptimizerScalars):
         st, st2 = main.cuda_stream, side.cuda_stream
         oa, ia = ctypes.byref(plan.out_axis), ctypes.byref(plan.in_axis)
         A, B, no, ni = self.atoms, self.rows, plan.n_out, plan.n_in
-        r0, nb, c0, nc = self.r0, self.nb, self.c0, self.nc
+        r0, nb = self.r0, self.nb
         x16, dy16, w16b = self.x16, self.dy16, self.w16b
         pg = self.pg
         self._mark("start")
@@ -143,12 +153,6 @@ class RowBandMSETrainStep(OptimizerScalars):
         N.check(lib.tcst_assemble_weight_window_f16(
             vp(self.table), A, oa, ia, vp(self.scratch), sb, r0, nb, 0, ni, vp(self.w_band), ni,
             vp(w16b.amax), vp(w16b.hi), vp(w16b.lo), w16b.ld, vp(w16b.scale), st), "weight band")
-        if self.need_dx and self.world > 1:
-            w16c = self.w16c
-            N.check(lib.tcst_assemble_weight_window_f16(
-                vp(self.table), A, oa, ia, vp(self.scratch), sb, 0, no, c0, nc, vp(self.w_col),
-                nc, vp(w16c.amax), vp(w16c.hi), vp(w16c.lo), w16c.ld, vp(w16c.scale), st),
-                "weight columns")
         main.wait_stream(side)
         self._mark("decode+sort+weights")
         y_band = self.y[:, r0:]
@@ -160,25 +164,23 @@ class RowBandMSETrainStep(OptimizerScalars):
                                       vp(self.partial), ctypes.byref(self.nblocks),
                                       vp(dy16.amax), st), "mse")
         torch.sum(self.partial[: self.nblocks.value], dim=0, keepdim=True, out=self.loss_sum)
-        # One scale for the whole dY: every band splits with the global max.
-        if pg is not None:
-            dist.all_reduce(dy16.amax, op=dist.ReduceOp.MAX, group=pg)
-
-        def split_band(src, k):
-            off = 2 * k * nb  # f16 elements -> bytes
-            N.check(lib.tcst_split_f16(vp(src), B, nb, nb, vp(dy16.amax),
-                                       ctypes.c_void_p(dy16.hi.data_ptr() + off),
-                                       ctypes.c_void_p(dy16.lo.data_ptr() + off), dy16.ld,
-                                       vp(dy16.scale), st), "split dy")
-
-        self._mark("gemm Y+loss+max")
-        split_band(self.dy_band, self.rank)
-        # The dY all-gather runs beside the dW GEMM and the banded pullback,
-        # which need only this rank's band.
-        gather_dy = (dist.all_gather_into_tensor(self.dy_all, self.dy_band, group=pg,
-                                                 async_op=True) if pg is not None else None)
-        off = 2 * r0
-        self._gemm(nb, ni, B, dy16.hi.data_ptr() + off, dy16.lo.data_ptr() + off, dy16.ld, 1,
+        N.check(lib.tcst_split_f16(vp(self.dy_band), B, nb, nb, vp(dy16.amax), vp(dy16.hi),
+                                   vp(dy16.lo), dy16.ld, vp(dy16.scale), st), "split dy")
+        self._mark("gemm Y+loss+split")
+        reduce_dx = None
+        if self.need_dx:
+            # The band's share of dX = dY_band W_band beside the dW GEMM and the
+            # pullback, then its all-reduce on the second communicator.
+            dxs = self._dx_side
+            dxs.wait_stream(main)
+            self._gemm(B, ni, nb, dy16.hi.data_ptr(), dy16.lo.data_ptr(), dy16.ld, 0,
+                       dy16.scale.data_ptr(), w16b.hi.data_ptr(), w16b.lo.data_ptr(), w16b.ld, 1,
+                       w16b.scale.data_ptr(), self.dx_full.data_ptr(), ni,
+                       stream=dxs.cuda_stream, what="gemm dx")
+            if self.pg_dx is not None:
+                with torch.cuda.stream(dxs):
+                    reduce_dx = dist.all_reduce(self.dx_full, group=self.pg_dx, async_op=True)
+        self._gemm(nb, ni, B, dy16.hi.data_ptr(), dy16.lo.data_ptr(), dy16.ld, 1,
                    dy16.scale.data_ptr(), x16.hi.data_ptr(), x16.lo.data_ptr(), x16.ld, 1,
                    x16.scale.data_ptr(), self.g.data_ptr(), self.ldg, self.split, self.gstride,
                    what="gemm dw")
@@ -186,32 +188,15 @@ class RowBandMSETrainStep(OptimizerScalars):
                                        self.split, self.gstride, r0, nb, vp(self.grad), st),
                 "pullback")
         self._mark("gemm dW+pullback")
-        # The halo-atom reduction runs beside the dX GEMM.
-        reduce_grad = (dist.all_reduce(self.grad, group=pg, async_op=True)
-                       if pg is not None else None)
-        if self.need_dx:
-            if gather_dy is not None:
-                gather_dy.wait()
-                for k in range(self.world):
-                    if k != self.rank:
-                        split_band(self.dy_all[k], k)
-            self._mark("dY gather wait+split")
-            w16c = self.w16c
-            self._gemm(B, nc, no, dy16.hi.data_ptr(), dy16.lo.data_ptr(), dy16.ld, 0,
-                       dy16.scale.data_ptr(), w16c.hi.data_ptr(), w16c.lo.data_ptr(), w16c.ld, 1,
-                       w16c.scale.data_ptr(), self.dx_band.data_ptr(), nc, what="gemm dx")
-            self._mark("gemm dX")
-            if pg is not None:
-                dist.all_gather_into_tensor(self.dx_all, self.dx_band, group=pg)
-            else:
-                self.dx_all[0].copy_(self.dx_band)
-            self._mark("dX gather")
-        elif gather_dy is not None:
-            gather_dy.wait()
         if pg is not None:
-            reduce_grad.wait()
+            dist.all_reduce(self.grad, group=pg)  # the halo exchange
             dist.all_reduce(self.loss_sum, group=pg)
-        self._mark("gradient all-reduce wait")
+        self._mark("gradient all-reduce")
+        if self.need_dx:
+            if reduce_dx is not None:
+                reduce_dx.wait()
+            main.wait_stream(self._dx_side)
+            self._mark("dX all-reduce wait")
         return self.loss_sum[0] / (B * no)
 
     def __call__(self, x, target):
@@ -227,7 +212,7 @@ class RowBandMSETrainStep(OptimizerScalars):
         return loss
 
     def dx(self):
-        """dX [rows, N_in] of the last step, from the gathered column blocks."""
+        """dX [rows, N_in] of the last step (the sum of every band's share)."""
         if not self.need_dx:
             raise RuntimeError("built with need_dx=False")
-        return self.dx_all.permute(1, 0, 2).reshape(self.rows, self.plan.n_in)
+        return self.dx_full
