@@ -27,7 +27,8 @@
 //                        rank-one terms per node (node flags and the count of
 //                        active pairs come from the sort, atoms.cu);
 //   pair_project_kernel  the pullback's P_a = Phi_a^T G (PF x N_in) per node
-//                        with an active pair, over its footprint rows in order;
+//                        with an active pair, over its footprint rows in order
+//                        (a GEMM: tensor cores, three-product TF32);
 //   pair_grad_kernel     per active pair H_ab = P_a Phi_b, then the gradient
 //                        of each of its atoms.
 
@@ -238,12 +239,51 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_expand_kernel(Table tv, int n_o
 }
 
 // G holds chart rows [band.r0, band.r0 + band.wr) at gm + (row - band.r0) ldg.
-// A CTA covers PP_COLS input columns, PP_COLS / PX_CHUNK per thread, so each
-// staged basis value feeds several columns.
-constexpr int PP_PER_THREAD = 1;
-constexpr int PP_COLS = PX_CHUNK * PP_PER_THREAD;
+// P_a = Phi_a^T G is a GEMM (PF x rows times rows x N_in) per node: it runs on
+// the tensor cores as mma.sync m16n8k8 TF32 with the three-product split of
+// both operands (hi*hi + hi*lo + lo*hi, float32 accumulation), which keeps the
+// float32 accuracy of the scalar form. A CTA owns PP_COLS input columns of one
+// node; per chunk of PP_ROWS footprint rows it stages the basis values
+// (transposed, PF padded to 32 with zeros) and the G block in shared memory,
+// then each of the 8 warps multiplies the 32 x PP_ROWS basis block by its 32
+// columns (2 x 4 tiles of 16 x 8). The row order of the sum is fixed, so P is
+// deterministic.
+constexpr int PP_COLS = 256;
+constexpr int PP_ROWS = 32;
+constexpr int PP_THREADS = 256;
+constexpr int PP_GPITCH = PP_COLS + 8; // shared G row pitch (conflict-free fragment loads)
+constexpr int PP_APITCH = 32 + 8;      // shared basis row pitch (conflict-free fragment loads)
 
-__global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_out, int n_in,
+__device__ __forceinline__ unsigned tf32_bits(float x) {
+    unsigned r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+// D += A B for one m16n8k8 TF32 tile.
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const unsigned (&a)[4], const unsigned (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    const int n = valid ? 16 : 0; // a zero source size fills the 16 bytes with zeros
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+struct ProjectSmem {
+    float sa[2][PP_ROWS][PP_APITCH]; // basis: [row][f], f >= PF zero
+    float sg[2][PP_ROWS][PP_GPITCH]; // G block: [row][column]
+};
+
+__global__ void __launch_bounds__(PP_THREADS) pair_project_kernel(Table tv, int n_out, int n_in,
                                                                 const float *__restrict__ gm,
                                                                 long long ldg, Window band) {
     pdl_wait();
@@ -253,7 +293,7 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
     if (active_pairs(tv) == 0 || !expand_cta(g, chunks, l, a, ch)) return;
     if (!tv.node_on[g.pl_node[l] + a] || !node_covers(g, l, a, band.r0, band.wr, n_out)) return;
     const int T = g.pl_T[l], F = g.pl_K[l] * T;
-    const int i0 = ch * PP_COLS + threadIdx.x;
+    const int c0 = ch * PP_COLS;
     // Rows to walk: the distinct chart rows of the footprint (all rows when it
     // wraps onto itself) or the band's rows, whichever is fewer; rows outside
     // the other set contribute zero.
@@ -261,61 +301,116 @@ __global__ void __launch_bounds__(PX_CHUNK) pair_project_kernel(Table tv, int n_
     const bool by_band = band.wr < foot_rows;
     const int rows = by_band ? band.wr : foot_rows;
     const int row0 = by_band ? band.r0 : (F >= n_out ? 0 : a * T);
-    __shared__ float4 sphi[32][PF4];
-    __shared__ int srow[32]; // band-relative row, or -1 outside the band
-    float p[PP_PER_THREAD][PF];
+    extern __shared__ __align__(16) unsigned char pp_smem[];
+    ProjectSmem &sm = *reinterpret_cast<ProjectSmem *>(pp_smem);
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int gq = lane >> 2, tq = lane & 3; // fragment coordinates
+    const int wc = warp * 32;                // the warp's first column in the CTA
+    const bool vec = (ldg & 3) == 0 && (reinterpret_cast<uintptr_t>(gm) & 15) == 0;
+    float acc[2][4][4];
 #pragma unroll
-    for (int u = 0; u < PP_PER_THREAD; ++u)
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int f = 0; f < PF; ++f) p[u][f] = 0.f;
-    for (int r0 = 0; r0 < rows; r0 += 32) {
-        const int nr = min(32, rows - r0);
-        __syncthreads();
-        if (threadIdx.x < nr) {
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
+    // Stage chunk r0 into buffer b: basis values by warp 0 (one row per lane),
+    // the G block by every thread (asynchronous 16-byte copies; rows outside
+    // the band or footprint and columns past N_in fill with zeros).
+    auto stage = [&](int r0, int b) {
+        const int nr = min(PP_ROWS, rows - r0);
+        if (warp == 0) {
             float phi[PF];
-            int row = row0 + r0 + threadIdx.x;
+            int row = row0 + r0 + lane;
             row -= row >= n_out ? n_out : 0;
-            // In the band, and on the footprint (pair_basis finds an image).
-            const bool in = row >= band.r0 && row < band.r0 + band.wr &&
+            const bool in = lane < nr && row >= band.r0 && row < band.r0 + band.wr &&
                             pair_basis(row - a * T, F, n_out, phi);
-            float *dst = reinterpret_cast<float *>(sphi[threadIdx.x]);
 #pragma unroll
-            for (int f = 0; f < 4 * PF4; ++f) dst[f] = in && f < PF ? phi[f] : 0.f;
-            srow[threadIdx.x] = in ? row - band.r0 : -1;
+            for (int f = 0; f < 32; ++f) sm.sa[b][lane][f] = in && f < PF ? phi[f] : 0.f;
         }
-        __syncthreads();
-#pragma unroll 4
-        for (int j = 0; j < nr; ++j) {
-            const int br = srow[j]; // rows outside the band contribute zero
-            const float *grow = gm + (long long)max(br, 0) * ldg;
-            float gv[PP_PER_THREAD];
-#pragma unroll
-            for (int u = 0; u < PP_PER_THREAD; ++u) {
-                const int i = i0 + u * PX_CHUNK;
-                gv[u] = br >= 0 && i < n_in ? grow[i] : 0.f;
+        // Whether each staged row is in the band and on the footprint, per
+        // thread (the rule pair_basis applies for warp 0's basis values).
+        for (int i = t; i < PP_ROWS * (PP_COLS / 4); i += PP_THREADS) {
+            const int r = i / (PP_COLS / 4), c4 = i - r * (PP_COLS / 4);
+            int row = row0 + r0 + r;
+            row -= row >= n_out ? n_out : 0;
+            bool in = r < nr && row >= band.r0 && row < band.r0 + band.wr;
+            if (in && F < n_out) { // on the footprint: (row - a T) mod n_out < F
+                int d = (row - a * T) % n_out;
+                d += d < 0 ? n_out : 0;
+                in = d < F;
             }
-#pragma unroll
-            for (int q = 0; q < PF4; ++q) {
-                const float4 ph4 = sphi[j][q];
-                const float ph[4] = {ph4.x, ph4.y, ph4.z, ph4.w};
+            const int col = c0 + 4 * c4;
+            float *dst = &sm.sg[b][r][4 * c4];
+            const float *src = gm + (long long)(in ? row - band.r0 : 0) * ldg + (col < n_in ? col : 0);
+            if (vec && col + 4 <= n_in) {
+                cp_async16(dst, src, in);
+            } else {
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                    if (4 * q + e < PF)
-#pragma unroll
-                        for (int u = 0; u < PP_PER_THREAD; ++u)
-                            p[u][4 * q + e] = fmaf(ph[e], gv[u], p[u][4 * q + e]);
+                    dst[e] = in && col + e < n_in ? gm[(long long)(row - band.r0) * ldg + col + e] : 0.f;
             }
         }
-    }
-#pragma unroll
-    for (int u = 0; u < PP_PER_THREAD; ++u) {
-        const int i = i0 + u * PX_CHUNK;
-        if (i < n_in) {
-            float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in + i;
-#pragma unroll
-            for (int f = 0; f < PF; ++f) out[(long long)f * n_in] = p[u][f];
+        cp_async_commit();
+    };
+    const int nchunks = (rows + PP_ROWS - 1) / PP_ROWS;
+    stage(0, 0);
+    for (int k = 0; k < nchunks; ++k) {
+        const int b = k & 1;
+        if (k + 1 < nchunks) {
+            stage((k + 1) * PP_ROWS, b ^ 1);
+            cp_async_wait1();
+        } else {
+            cp_async_wait0();
         }
+        __syncthreads(); // chunk k staged (basis writes and copies) for every warp
+#pragma unroll
+        for (int k0 = 0; k0 < PP_ROWS; k0 += 8) {
+            // A fragments (rows f = m, columns = footprint rows k), both m tiles.
+            unsigned ah[2][4], al[2][4];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const float av[4] = {sm.sa[b][k0 + tq][mt * 16 + gq], sm.sa[b][k0 + tq][mt * 16 + gq + 8],
+                                     sm.sa[b][k0 + tq + 4][mt * 16 + gq],
+                                     sm.sa[b][k0 + tq + 4][mt * 16 + gq + 8]};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    ah[mt][e] = tf32_bits(av[e]);
+                    al[mt][e] = tf32_bits(av[e] - __uint_as_float(ah[mt][e]));
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const int col = wc + nt * 8 + gq;
+                const float bv[2] = {sm.sg[b][k0 + tq][col], sm.sg[b][k0 + tq + 4][col]};
+                unsigned bh[2], bl[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    bh[e] = tf32_bits(bv[e]);
+                    bl[e] = tf32_bits(bv[e] - __uint_as_float(bh[e]));
+                }
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                    mma_tf32(acc[mt][nt], al[mt], bh);
+                    mma_tf32(acc[mt][nt], ah[mt], bl);
+                    mma_tf32(acc[mt][nt], ah[mt], bh);
+                }
+            }
+        }
+        __syncthreads(); // buffer b is free for chunk k + 2
     }
+    // Accumulator (m = f, n = column): c0 (gq, 2tq), c1 (gq, 2tq+1), c2 (gq+8, 2tq), c3 (gq+8, 2tq+1).
+    float *out = tv.pair_buf + g.pl_buf[l] + (long long)a * PF * n_in;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int f = mt * 16 + gq + (e >= 2 ? 8 : 0);
+                const int i = c0 + wc + nt * 8 + 2 * tq + (e & 1);
+                if (f < PF && i < n_in) out[(long long)f * n_in + i] = acc[mt][nt][e];
+            }
 }
 
 __global__ void __launch_bounds__(320) pair_grad_kernel(Table tv, int aw, int n_out, int n_in,
@@ -450,7 +545,15 @@ int pair_backward(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, const f
     if (g.npl == 0 || tv.atoms == 0) return TCST_OK;
     const long long ctas = expand_ctas(g, ia.sites, PP_COLS);
     if (ctas == 0) return TCST_OK;
-    TCST_CUDA(launch_pdl(pair_project_kernel, dim3(unsigned(ctas)), dim3(PX_CHUNK), 0, st, tv,
+    static bool configured = false;
+    if (!configured) {
+        TCST_CUDA(cudaFuncSetAttribute(pair_project_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(sizeof(ProjectSmem))));
+        configured = true;
+    }
+    TCST_CUDA(launch_pdl(pair_project_kernel, dim3(unsigned(ctas)), dim3(PP_THREADS),
+                         sizeof(ProjectSmem), st, tv,
                          oa.sites, ia.sites, g_dev, ldg, band));
     TCST_CUDA(cudaGetLastError());
     const int pair_bins = g.pl_base[g.npl] - g.pl_base[0];
