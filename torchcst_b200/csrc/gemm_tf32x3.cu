@@ -16,7 +16,9 @@
 //   warp 1       TMEM allocator and MMA issuer: 3 x (BK / KSTEP) tcgen05.mma
 //                per stage into one fp32 accumulator of BN TMEM columns; a
 //                tcgen05.commit frees the stage, a final one signals the epilogue;
-//   warps 2..5   epilogue: tcgen05.ld 32 columns at a time, fp32 stores.
+//   warps 2..5   epilogue: tcgen05.ld 32 columns at a time, each 32 x 32
+//                block transposed through shared memory (the stage buffers
+//                are free by then) into whole-row-segment fp32 stores.
 // K-major operands are staged as swizzled rows of BK elements; MN-major
 // operands as strips of 128 bytes of MN by BK k-rows (TF32: 128-byte swizzle
 // with 32-byte units, the MN-major tf32 layout; F16: 128-byte swizzle, with
@@ -238,6 +240,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                      "r"(BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    if (warp == 0 && lane == 0) {
+        // Descriptor fetches overlap the previous kernel's tail.
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a_hi) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_a_lo) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_b_hi) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&map_b_lo) : "memory");
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -350,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // 1 / (s_A s_B): a power of two, so the product is exact.
             const float inv = (scale_a && scale_b) ? 1.0f / (*scale_a * *scale_b) : 1.0f;
             const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-            float *blk = reinterpret_cast<float *>(smem) + quarter * (32 * 33);
+            float *blk = reinterpret_cast<float *>(smem) + quarter * (32 * 36);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 unsigned r[32];
@@ -372,32 +381,46 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) r[j] = 0u;
                 }
-                if (!MSE) {
-                    // Plain output: each lane stores its row's 32 columns.
+                const int col0 = tile_n * BN + c0;
+                if (!MSE && !(vec && col0 + 32 <= N)) {
+                    // Ragged or unaligned output: each lane stores its row.
                     const int row = row_base + lane;
-                    const int col0 = tile_n * BN + c0;
                     if (row < M) {
                         float *dst = out + (long long)row * ldc + col0;
-                        if (vec && col0 + 32 <= N) {
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4 *>(dst + j) = make_float4(
-                                    __uint_as_float(r[j]) * inv, __uint_as_float(r[j + 1]) * inv,
-                                    __uint_as_float(r[j + 2]) * inv,
-                                    __uint_as_float(r[j + 3]) * inv);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (col0 + j < N) dst[j] = __uint_as_float(r[j]) * inv;
-                        }
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < N) dst[j] = __uint_as_float(r[j]) * inv;
                     }
                     continue;
                 }
-                // MSE: lane = row on the way in (pitch 33: conflict-free both
-                // ways), lane = column on the way out.
+                // The 32 x 32 block goes through shared memory, lane = row on
+                // the way in (float4 writes, pitch 36: each 8-lane phase hits
+                // 32 distinct banks), so that the global accesses are whole
+                // 128-byte row segments.
+                {
+                    float4 *b4 = reinterpret_cast<float4 *>(blk + lane * 36);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) blk[lane * 33 + j] = __uint_as_float(r[j]) * inv;
+                    for (int j = 0; j < 8; ++j)
+                        b4[j] = make_float4(__uint_as_float(r[4 * j]) * inv,
+                                            __uint_as_float(r[4 * j + 1]) * inv,
+                                            __uint_as_float(r[4 * j + 2]) * inv,
+                                            __uint_as_float(r[4 * j + 3]) * inv);
+                }
                 __syncwarp();
+                if (!MSE) {
+                    // Eight lanes per row, four rows per store instruction.
+                    const int sub = lane >> 3, c4 = 4 * (lane & 7);
+#pragma unroll
+                    for (int rr = 0; rr < 32; rr += 4) {
+                        const int row = row_base + rr + sub;
+                        if (row < M)
+                            *reinterpret_cast<float4 *>(out + (long long)row * ldc + col0 + c4) =
+                                *reinterpret_cast<const float4 *>(blk + (rr + sub) * 36 + c4);
+                    }
+                    __syncwarp();
+                    continue;
+                }
+                // MSE: lane = column on the way out.
                 const int col = tile_n * BN + c0 + lane;
                 const bool col_ok = col < N;
                 {
@@ -412,7 +435,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int rr = 0; rr < 32; ++rr) {
                         const int row = row_base + rr;
                         if (row < M && col_ok) {
-                            const float d = blk[rr * 33 + lane] - t[rr];
+                            const float d = blk[rr * 36 + lane] - t[rr];
                             loss += double(d) * double(d);
                             const float g = d * mse.scale;
                             vmax = fmaxf(vmax, fabsf(g));
