@@ -45,6 +45,7 @@ extern "C" {
 #define TCST_STATUS_RADIUS 4u        /* radius outside (0, chart period / 2] */
 #define TCST_STATUS_TIMEOUT 8u       /* a bounded device wait gave up */
 #define TCST_STATUS_FOOTPRINT 16u    /* footprint longer than this build supports */
+#define TCST_STATUS_SEQUENCE 32u     /* a scalar ring slot did not hold the expected step */
 
 #define TCST_RATIONAL 0
 #define TCST_POLAR 1
@@ -307,6 +308,28 @@ int tcst_coordinate_update(float *proposal_dev, const float *previous_dev, int64
 int tcst_optimizer_step_device(float *p_dev, const float *grad_dev, float *exp_avg_dev,
                                float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
                                const tcst_adamw *params_dev, void *stream);
+
+/* Per-step optimizer scalars without a host-to-device copy in front of a
+ * captured step: a ring of `slots` slots in pinned (device-mapped) host memory,
+ * `slot_bytes` apart (a multiple of 16, at least TCST_RING_SLOT_MIN), each a
+ * tcst_adamw at offset 0 and a uint32 sequence number at TCST_RING_SEQ_OFFSET.
+ * tcst_scalar_ring_fetch (one CTA) copies slot c % slots into the device state
+ * block (TCST_RING_STATE_BYTES, 16-byte aligned, zero before the first fetch;
+ * word 0 is the use count c, advanced by one per fetch), marking it valid when
+ * the slot's sequence number is c and raising TCST_STATUS_SEQUENCE in
+ * status_dev when it is not. tcst_optimizer_step_ring is
+ * tcst_optimizer_step with the scalars of the state block, and leaves p,
+ * exp_avg and exp_avg_sq unchanged when the block is not valid. The host
+ * writes slot c before enqueuing fetch c and may rewrite it once that fetch
+ * has run. No reference counterpart (see tcst_optimizer_step_device). */
+#define TCST_RING_SEQ_OFFSET ((sizeof(tcst_adamw) + 15) / 16 * 16)
+#define TCST_RING_SLOT_MIN (TCST_RING_SEQ_OFFSET + 16)
+#define TCST_RING_STATE_BYTES (16 + TCST_RING_SEQ_OFFSET)
+int tcst_scalar_ring_fetch(const void *ring_host, int32_t slots, int64_t slot_bytes,
+                           void *ring_state_dev, uint32_t *status_dev, void *stream);
+int tcst_optimizer_step_ring(float *p_dev, const float *grad_dev, float *exp_avg_dev,
+                             float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
+                             const void *ring_state_dev, void *stream);
 
 /* MSE upstream gradient dY = (Y - T) * scale split into TF32 hi/lo planes, plus
  * per-block partial sums of (Y - T)^2 in loss_partial_dev[blocks] (double).

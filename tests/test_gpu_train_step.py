@@ -159,3 +159,51 @@ def test_graphed_autograd_step_matches_eager_classifier():
 
     _graphed_vs_eager(build)
 
+
+
+def test_scalar_ring_matches_host_scalars_and_flags_stale_slots():
+    """tcst_scalar_ring_fetch + tcst_optimizer_step_ring take each launch's
+    scalars from its ring slot: three launches equal three host-scalar steps bit
+    for bit, and a slot whose sequence number is not the fetch's raises
+    TCST_STATUS_SEQUENCE and leaves the atoms and moments unchanged (the use
+    count still advances)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import ctypes
+    from torchcst_b200 import _native as N
+    from torchcst_b200 import runtime as R
+    layer, opt, _, _ = _setup()
+    p = layer.atoms.p
+    g = torch.Generator(device="cuda").manual_seed(3)
+    grads = [torch.randn(p.shape, device="cuda", generator=g) * 1e-3 for _ in range(3)]
+    kind = N.TCST_RATIONAL
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = R._stream(p.device)
+    host = [p.detach().clone(), torch.zeros_like(p), torch.zeros_like(p)]
+    dev = [t.clone() for t in host]
+    ring = R.ScalarRing(p.device)
+    for step, grad in enumerate(grads, start=1):
+        h = opt._native_params(layer, opt.param_groups[0], step)
+        N.call("tcst_optimizer_step", R._vp(host[0]), R._vp(grad), R._vp(host[1]),
+               R._vp(host[2]), p.shape[0], kind, ctypes.byref(h), stream)
+        ring.write(h)
+        ring.fetch(status, stream)
+        ring.launch(dev[0], grad, dev[1], dev[2], kind, stream)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert int(ring.state[0].item()) == 3
+    for a, b in zip(host, dev):
+        assert torch.equal(a, b)
+    # A slot written for another launch: flagged, nothing updated.
+    h = opt._native_params(layer, opt.param_groups[0], 4)
+    ring.write(h)
+    slot = ring.host[(ring.uses - 1) % ring.SLOTS]
+    ctypes.c_uint32.from_address(slot.data_ptr() + ring.seq_offset).value = 12345
+    before = [t.clone() for t in dev]
+    ring.fetch(status, stream)
+    ring.launch(dev[0], grads[0], dev[1], dev[2], kind, stream)
+    torch.cuda.synchronize()
+    assert int(status.item()) == N.STATUS_SEQUENCE
+    assert int(ring.state[0].item()) == 4
+    for a, b in zip(before, dev):
+        assert torch.equal(a, b)

@@ -22,6 +22,7 @@ STATUS_BOUNDS = 2
 STATUS_RADIUS = 4
 STATUS_TIMEOUT = 8
 STATUS_FOOTPRINT = 16
+STATUS_SEQUENCE = 32
 
 
 class Axis(ctypes.Structure):
@@ -117,6 +118,8 @@ SIGNATURES = {
                                           P, I64, I32, I64, I64, I64, P, P]),
     "tcst_optimizer_step": (ctypes.c_int, [P, P, P, P, I64, I32, ctypes.POINTER(AdamW), P]),
     "tcst_optimizer_step_device": (ctypes.c_int, [P, P, P, P, I64, I32, P, P]),
+    "tcst_scalar_ring_fetch": (ctypes.c_int, [P, I32, I64, P, P, P]),
+    "tcst_optimizer_step_ring": (ctypes.c_int, [P, P, P, P, I64, I32, P, P]),
     "tcst_coordinate_update": (ctypes.c_int, [P, P, I64, I32, ctypes.POINTER(AdamW), P]),
     "tcst_mse_grad": (ctypes.c_int, [P, P, I64, I64, I64, ctypes.c_float, P, P, I64, P,
                                      ctypes.POINTER(I32), P]),

@@ -149,6 +149,52 @@ __global__ void optimizer_dev_kernel(float4 *__restrict__ p, const float4 *__res
     if (a < atoms) step_row(a, p, grad, m, v, kind, h);
 }
 
+// Scalar ring: one CTA copies the slot of use count c from the host ring
+// (device mapping, ld.global.cv so that no cached copy of an earlier use of
+// the slot is seen; one 16-byte load per thread, all in flight together) into
+// the device state block [count, valid, -, -, tcst_adamw]. Nothing here
+// depends on the preceding kernels (the state is written only by earlier
+// fetches, which have completed), so it runs before the dependency wait.
+__global__ void scalar_ring_fetch_kernel(const uint4 *ring, int slots, long long slot_vecs,
+                                         unsigned *state, unsigned *status) {
+    constexpr int VECS = int(TCST_RING_SEQ_OFFSET / 16);
+    __shared__ uint4 buf[VECS + 1];
+    const unsigned c = state[0];
+    const uint4 *slot = ring + (long long)(c % unsigned(slots)) * slot_vecs;
+    if (threadIdx.x <= VECS) {
+        uint4 v;
+        asm volatile("ld.global.cv.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(slot + threadIdx.x));
+        buf[threadIdx.x] = v;
+    }
+    __syncthreads();
+    pdl_wait();
+    const bool ok = buf[VECS].x == c;
+    if (threadIdx.x < VECS) reinterpret_cast<uint4 *>(state + 4)[threadIdx.x] = buf[threadIdx.x];
+    if (threadIdx.x == 0) {
+        state[1] = ok ? 1u : 0u;
+        state[0] = c + 1u;
+        if (!ok) atomicOr(status, TCST_STATUS_SEQUENCE);
+    }
+}
+
+// The optimizer step with the scalars of a fetched ring state block.
+__global__ void optimizer_ring_kernel(float4 *__restrict__ p, const float4 *__restrict__ grad,
+                                      float4 *__restrict__ m, float4 *__restrict__ v,
+                                      long long atoms, int kind, const unsigned *__restrict__ state) {
+    pdl_wait();
+    __shared__ tcst_adamw h;
+    __shared__ bool ok;
+    if (threadIdx.x == 0) {
+        ok = state[1] != 0u;
+        h = *reinterpret_cast<const tcst_adamw *>(state + 4);
+    }
+    __syncthreads();
+    const long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (ok && a < atoms) step_row(a, p, grad, m, v, kind, h);
+}
+
 // The coordinate law alone: proposal (written by an outside AdamW and field
 // rescale) is replaced in place by the law applied from previous.
 __global__ void coordinate_update_kernel(float4 *__restrict__ proposal,
@@ -208,6 +254,58 @@ extern "C" int tcst_optimizer_step_device(float *p_dev, const float *grad_dev, f
     TCST_CUDA(launch_pdl(optimizer_dev_kernel, dim3(unsigned((atoms + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, 
         (float4 *)p_dev, (const float4 *)grad_dev, (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev,
         atoms, kind, params_dev));
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+extern "C" int tcst_scalar_ring_fetch(const void *ring_host, int32_t slots, int64_t slot_bytes,
+                                      void *ring_state_dev, uint32_t *status_dev, void *stream) {
+    if (!ring_host || slots < 1 || slot_bytes < (int64_t)TCST_RING_SLOT_MIN || slot_bytes % 16 ||
+        !ring_state_dev || !status_dev) {
+        tcst_set_error("tcst_scalar_ring_fetch: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(ring_host) | reinterpret_cast<uintptr_t>(ring_state_dev)) %
+        16) {
+        tcst_set_error("tcst_scalar_ring_fetch: the ring and the state block must be 16-byte aligned");
+        return TCST_ERR_ARGUMENT;
+    }
+    // The kernel reads the ring through its device mapping.
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, ring_host) != cudaSuccess ||
+        attr.type != cudaMemoryTypeHost || !attr.devicePointer) {
+        cudaGetLastError();
+        tcst_set_error("tcst_scalar_ring_fetch: the ring must be pinned, device-mapped host memory");
+        return TCST_ERR_ARGUMENT;
+    }
+    TCST_CUDA(launch_pdl(scalar_ring_fetch_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream,
+                         static_cast<const uint4 *>(attr.devicePointer), int(slots),
+                         (long long)(slot_bytes / 16), static_cast<unsigned *>(ring_state_dev),
+                         status_dev));
+    TCST_CUDA(cudaGetLastError());
+    return TCST_OK;
+}
+
+extern "C" int tcst_optimizer_step_ring(float *p_dev, const float *grad_dev, float *exp_avg_dev,
+                                        float *exp_avg_sq_dev, int64_t atoms, int32_t kind,
+                                        const void *ring_state_dev, void *stream) {
+    if (atoms < 0 || !ring_state_dev || (kind != TCST_RATIONAL && kind != TCST_POLAR) ||
+        (atoms && (!p_dev || !grad_dev || !exp_avg_dev || !exp_avg_sq_dev))) {
+        tcst_set_error("tcst_optimizer_step_ring: invalid arguments");
+        return TCST_ERR_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(p_dev) | reinterpret_cast<uintptr_t>(grad_dev) |
+         reinterpret_cast<uintptr_t>(exp_avg_dev) | reinterpret_cast<uintptr_t>(exp_avg_sq_dev) |
+         reinterpret_cast<uintptr_t>(ring_state_dev)) %
+        16) {
+        tcst_set_error("tcst_optimizer_step_ring: pointers must be 16-byte aligned");
+        return TCST_ERR_ARGUMENT;
+    }
+    if (atoms == 0) return TCST_OK;
+    TCST_CUDA(launch_pdl(optimizer_ring_kernel, dim3(unsigned((atoms + 255) / 256)), dim3(256), 0,
+                         (cudaStream_t)stream, (float4 *)p_dev, (const float4 *)grad_dev,
+                         (float4 *)exp_avg_dev, (float4 *)exp_avg_sq_dev, atoms, kind,
+                         static_cast<const unsigned *>(ring_state_dev)));
     TCST_CUDA(cudaGetLastError());
     return TCST_OK;
 }

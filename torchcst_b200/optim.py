@@ -301,27 +301,22 @@ class CSTAdamW(AdamW):
 
     # -- CUDA graph capture ------------------------------------------------------
 
-    RING = 64
-
     def _graph_entry(self, p):
-        """The device scalar block (and its pinned upload ring) of atom site
-        ``p`` for captured steps. Made by an eager step: an allocation inside
+        """The scalar ring of atom site ``p`` for captured steps (pinned host
+        slots the captured optimizer kernel reads through their device mapping,
+        and its device use counter). Made by an eager step: an allocation inside
         a capture would come with an initialising kernel that every replay
-        would run after the scalar upload."""
+        would run."""
         entries = self.__dict__.setdefault("_graph_entries", {})
         entry = entries.get(id(p))
         if entry is None:
-            nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
-            entry = entries[id(p)] = {
-                "p": p, "params": torch.zeros(nbytes, dtype=torch.uint8, device=p.device),
-                "ring": torch.zeros(self.RING, nbytes, dtype=torch.uint8).pin_memory(),
-                "events": [None] * self.RING, "slot": 0}
+            entry = entries[id(p)] = {"p": p, "ring": R.ScalarRing(p.device)}
         return entry
 
     def _capture_site_step(self, p, site, state):
         """Record the atom update of ``p`` into the CUDA graph being captured.
-        The kernel reads its per-step scalars from a device block that
-        :meth:`refresh_captured` fills before every replay; the step count is
+        The kernel reads its per-step scalars from the ring slot that
+        :meth:`refresh_captured` writes before every replay; the step count is
         advanced there too, once per replay, not here."""
         entry = self.__dict__.get("_graph_entries", {}).get(id(p))
         if entry is None:
@@ -331,32 +326,20 @@ class CSTAdamW(AdamW):
         if not p.grad.is_contiguous():
             raise ValueError("captured atom updates need a contiguous gradient")
         with R.on_device(p.device):
-            N.call("tcst_optimizer_step_device", R._vp(p), R._vp(p.grad),
-                   R._vp(state["exp_avg"]), R._vp(state["exp_avg_sq"]), p.shape[0], kind,
-                   R._vp(entry["params"]), R._stream(p.device))
+            stream = R._stream(p.device)
+            entry["ring"].fetch(site._workspace(p.device).status, stream)
+            entry["ring"].launch(p, p.grad, state["exp_avg"], state["exp_avg_sq"], kind, stream)
 
     def refresh_captured(self):
         """Host half of one replayed step of every captured atom site: advance its
-        step count exactly as :meth:`step` does and copy the step's scalars (bias
-        corrections, rates) to its device block through a pinned ring, on the
-        current stream, ahead of the replay."""
+        step count exactly as :meth:`step` does and write the step's scalars
+        (bias corrections, rates) into the ring slot the replay's optimizer
+        kernel reads. Call it once before every replay."""
         for entry in self.__dict__.get("_graph_sites", {}).values():
-            p = entry["p"]
-            out = self.site_step(p)
+            out = self.site_step(entry["p"])
             if out is None:
                 raise ValueError("a captured CSTAdamW step needs a positive learning rate")
-            h = out[0]
-            slot = entry["slot"]
-            ev = entry["events"][slot]
-            if ev is not None:
-                ev.synchronize()  # the copy that last read this slot has run
-            ring = entry["ring"][slot]
-            ctypes.memmove(ring.data_ptr(), ctypes.addressof(h), ctypes.sizeof(h))
-            entry["params"].copy_(ring, non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record()
-            entry["events"][slot] = ev
-            entry["slot"] = (slot + 1) % self.RING
+            entry["ring"].write(out[0])
 
     def get_field_lrs(self):
         out = []

@@ -260,6 +260,58 @@ def atom_energies(plan: Plan, table, atoms, device):
     return e
 
 
+class ScalarRing:
+    """Per-launch optimizer scalars for steps replayed from a CUDA graph, with no
+    host-to-device copy in front of the replay: a ring of slots in pinned host
+    memory, a device state block that ``fetch`` (``tcst_scalar_ring_fetch``, one
+    CTA reading the ring through its device mapping) fills from the next slot
+    and that ``launch`` (``tcst_optimizer_step_ring``) reads, and one event per
+    slot marking when its fetch has run. Every ``write`` must be followed by
+    exactly one ``fetch`` execution (eager or replayed), before its ``launch``."""
+
+    SLOTS = 64
+
+    def __init__(self, device):
+        size = ctypes.sizeof(N.AdamW)
+        self.seq_offset = (size + 15) // 16 * 16
+        self.slot_bytes = self.seq_offset + 16
+        self.host = torch.zeros(self.SLOTS, self.slot_bytes, dtype=torch.uint8).pin_memory()
+        # [use count, valid, -, -, tcst_adamw]
+        self.state = torch.zeros((16 + self.seq_offset) // 4, dtype=torch.int32, device=device)
+        self.events = [None] * self.SLOTS
+        self.uses = 0
+        self._pending = None
+
+    def write(self, h):
+        """Fill the next fetch's slot from the ``N.AdamW`` struct ``h`` (host
+        side, before that fetch is enqueued on the current stream)."""
+        if self._pending is not None:
+            # Recorded after the previous fetch was enqueued: it fires once
+            # that fetch has read its slot.
+            ev = torch.cuda.Event()
+            ev.record()
+            self.events[self._pending] = ev
+        slot = self.uses % self.SLOTS
+        ev = self.events[slot]
+        if ev is not None:
+            ev.synchronize()
+        base = self.host[slot].data_ptr()
+        ctypes.memmove(base, ctypes.addressof(h), ctypes.sizeof(h))
+        ctypes.c_uint32.from_address(base + self.seq_offset).value = self.uses & 0xFFFFFFFF
+        self._pending = slot
+        self.uses += 1
+
+    def fetch(self, status, stream):
+        """Enqueue the copy of the next slot into the device state (capturable)."""
+        N.call("tcst_scalar_ring_fetch", _vp(self.host), self.SLOTS, self.slot_bytes,
+               _vp(self.state), _vp(status), stream)
+
+    def launch(self, p, grad, exp_avg, exp_avg_sq, kind, stream):
+        """Enqueue the optimizer step on the fetched scalars (capturable)."""
+        N.call("tcst_optimizer_step_ring", _vp(p), _vp(grad), _vp(exp_avg), _vp(exp_avg_sq),
+               p.shape[0], kind, _vp(self.state), stream)
+
+
 def status_error(code: int) -> str | None:
     if code == 0:
         return None
@@ -274,6 +326,8 @@ def status_error(code: int) -> str | None:
         parts.append("a bounded device wait expired")
     if code & N.STATUS_FOOTPRINT:
         parts.append("footprint exceeds this build's limits")
+    if code & N.STATUS_SEQUENCE:
+        parts.append("an optimizer scalar ring slot was out of step (no update applied)")
     return "; ".join(parts)
 
 

@@ -12,10 +12,11 @@ launches on the current stream:
     GEMM dX -> GEMM dW (split-K) -> pullback (split-K sum, three footprint
     classes, owner-pair projection and gradients, wide atoms) -> optimizer
 
-The optimizer reads its per-step scalars (bias corrections) from device memory,
-refreshed from a pinned host ring before each step, so :meth:`capture` can
-record the whole sequence as one CUDA graph per input buffer pair and replay it
-with the host doing only the scalar refresh.
+The optimizer reads its per-step scalars (bias corrections) from a pinned host
+ring through its device mapping (the host writes the step's slot before
+enqueuing it), so :meth:`capture` can record the whole sequence as one CUDA
+graph per input buffer pair and replay it with the host doing only the scalar
+write, and no copy in front of the replay.
 
 With ``process_group`` set (data parallel, rows sharded across ranks, atoms
 replicated), the loss is scaled by the global row count and the atom gradient
@@ -53,33 +54,19 @@ def dp_reduce_gradient(grad: torch.Tensor, process_group=None) -> torch.Tensor:
 
 class OptimizerScalars:
     """Device-side CSTAdamW step of one layer for captured or eager steps: the
-    host computes the step's scalars (bias corrections) and copies them through
-    a pinned ring into device memory, which the fused optimizer kernel reads."""
-
-    RING = 64
+    host computes the step's scalars (bias corrections) and writes them into a
+    pinned ring that the fused optimizer kernel reads through its device
+    mapping, so no host-to-device copy stands in front of a replay."""
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, device):
         self.layer, self.opt = layer, optimizer
-        nbytes = (ctypes.sizeof(N.AdamW) + 15) // 16 * 16
-        self.params_dev = torch.zeros(nbytes, dtype=torch.uint8, device=device)
-        self._ring = torch.zeros(self.RING, nbytes, dtype=torch.uint8).pin_memory()
-        self._ring_events = [None] * self.RING
-        self._slot = 0
+        self._ring = R.ScalarRing(device)
         self._state = None
         self._kind = None
 
     def _upload(self, h):
-        """Copy the step's optimizer scalars to the device through the pinned ring."""
-        slot = self._slot
-        ev = self._ring_events[slot]
-        if ev is not None:
-            ev.synchronize()  # the copy that last read this slot has run
-        ctypes.memmove(self._ring[slot].data_ptr(), ctypes.addressof(h), ctypes.sizeof(h))
-        self.params_dev.copy_(self._ring[slot], non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record()
-        self._ring_events[slot] = ev
-        self._slot = (slot + 1) % self.RING
+        """Write the next optimizer launch's scalars into the ring."""
+        self._ring.write(h)
 
     def _advance(self):
         """Host side of one optimizer step: step count and scalars to the device.
@@ -105,13 +92,19 @@ class OptimizerScalars:
             raise RuntimeError(f"device status {code:#x}: {R.status_error(code)}")
         return 0
 
-    def _launch_opt(self):
+    def _fetch(self, stream):
+        """Enqueue the device copy of this step's ring slot on ``stream``."""
+        self._ring.fetch(self.ws.status, stream)
+
+    def _launch_opt(self, fetched=False):
+        """Enqueue the optimizer step; ``fetched``: the step's slot was already
+        fetched earlier in the step (on a stream joined before this one)."""
         p = self.layer.atoms.p
         state = self._state
-        vp = R._vp
-        N.check(N.load().tcst_optimizer_step_device(
-            vp(p), vp(self.grad), vp(state["exp_avg"]), vp(state["exp_avg_sq"]), self.atoms,
-            self._kind, vp(self.params_dev), R._stream(p.device)), "optimizer")
+        stream = R._stream(p.device)
+        if not fetched:
+            self._fetch(stream)
+        self._ring.launch(p, self.grad, state["exp_avg"], state["exp_avg_sq"], self._kind, stream)
 
 
 class MSETrainStep(OptimizerScalars):
@@ -164,14 +157,16 @@ class MSETrainStep(OptimizerScalars):
     def _launch(self, x, target, optimize=True):
         """Enqueue the step's kernels (and the gradient all-reduce) on the current
         stream; returns the loss."""
-        loss = self._launch_grad(x, target)
+        loss = self._launch_grad(x, target, fetch=optimize)
         dp_reduce_gradient(self.grad, self.pg)
         if optimize:
-            self._launch_opt()
+            self._launch_opt(fetched=True)
         return loss
 
-    def _launch_grad(self, x, target):
-        """Forward and backward kernels up to this rank's atom gradient."""
+    def _launch_grad(self, x, target, fetch=False):
+        """Forward and backward kernels up to this rank's atom gradient; with
+        ``fetch``, also this step's optimizer scalars (side stream, beside the
+        decode)."""
         plan, ws, vp = self.plan, self.ws, R._vp
         p = self.layer.atoms.p
         main = torch.cuda.current_stream(p.device)
@@ -195,6 +190,8 @@ class MSETrainStep(OptimizerScalars):
 
         self.amax.zero_()
         side.wait_stream(main)  # X split runs beside decode and weight assembly
+        if fetch:
+            self._fetch(st2)
         split(x16, x, x.stride(0), st2)
         N.check(lib.tcst_decode_route(vp(p), A, oa, ia, ctypes.byref(plan.coords), vp(self.table),
                                       None, None, vp(ws.status), st), "decode")
@@ -266,14 +263,14 @@ class MSETrainStep(OptimizerScalars):
                 continue
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                loss = self._launch_grad(x, target)
+                loss = self._launch_grad(x, target, fetch=True)
                 if self.pg is None:
-                    self._launch_opt()
+                    self._launch_opt(fetched=True)
             self._graphs[key] = (graph, loss)
         if self.pg is not None and self._opt_graph is None:
             self._opt_graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self._opt_graph):
-                self._launch_opt()
+                self._launch_opt(fetched=True)
         torch.cuda.synchronize()
 
     def release(self):
