@@ -233,11 +233,11 @@ def _align16(x):
 
 
 def _reach(c):
-    return 16 if c == 0 else 64 << (c - 1)
+    return 16 << c
 
 
 def _edge(c, fe=32):
-    return fe if c < 3 else _reach(c) // 2
+    return fe if c < 4 else _reach(c) // 2
 
 
 def _bin_geom(out_axis, in_axis):
@@ -285,7 +285,7 @@ def _table_sections(out_axis, in_axis, atoms):
     geo = _bin_geom(out_axis, in_axis)
     spans = _align16(atoms * words * 4)
     sites = _align16(spans + atoms * 16)
-    binof = _align16(sites + atoms * 96 * 4)
+    binof = _align16(sites + atoms * 192 * 4)  # 2 axes x 3 values x 32 sites
     offsets = _align16(binof + atoms * 4)
     ids = _align16(offsets + 4 * (geo["nbins"] + 1))
     return dict(spans=spans, binof=binof, offsets=offsets, ids=ids, geo=geo)
@@ -327,7 +327,7 @@ def test_bins_are_stable_and_complete(R, name):
         # Coarse atoms with the same level and bank on both axes: owner-pair bins.
         lo, li = d["route_out_level"], d["route_in_level"]
         ko, ki = d["route_out_count"], d["route_in_count"]
-        for j in np.nonzero((cls >= 3) & (lo == li) & (ko == ki))[0]:
+        for j in np.nonzero((cls >= 4) & (lo == li) & (ko == ki))[0]:
             pl = geo["pairs"].get((int(lo[j]), int(ko[j])))
             if pl is not None:
                 want[j] = pl["base"] + (spans[j, 0] // pl["T"]) * pl["ni"] + spans[j, 2] // pl["T"]

@@ -1,8 +1,10 @@
-// Per-atom decode, hierarchy routing and Chebyshev-square Fourier profile.
+// Per-atom decode, hierarchy routing and Chebyshev-square Fourier profile,
+// then the bin sort and (beside it) the site values of narrow footprints.
 //
-// One thread per atom, float64 throughout. Routing (level, K, first tile, owner
-// key) reproduces the reference's float64 operation order with non-contracted
-// arithmetic, so it is bit-exact whenever exp/log agree in the last ulp.
+// Two threads per atom (one per axis), float64 throughout. Routing (level, K,
+// first tile, owner key) reproduces the reference's float64 operation order
+// with non-contracted arithmetic, so it is bit-exact whenever exp/log agree in
+// the last ulp.
 
 #include <cmath>
 #include <cstdarg>
@@ -286,7 +288,7 @@ __host__ inline void make_profile_tab(int M, ProfileTab *t) {
 
 template <int MT>
 __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, const AxisCfg &ax,
-                                          const ProfileTab &tab, float *sites) {
+                                          const ProfileTab &tab) {
     constexpr int CAP = MT > 0 ? MT : MAX_MODES;
     const int M = MT > 0 ? MT : ax.modes;
     const double P = dmul(double(r.count * r.tile), ax.spacing);
@@ -346,41 +348,6 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
         float4 *b4 = reinterpret_cast<float4 *>(blk);
 #pragma unroll
         for (int q = 0; q < 6; ++q) b4[q] = make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-        if (sites && F <= REACH) {
-            AxisCoef<MT> ac;
-#pragma unroll
-            for (int k = 0; k <= MT; ++k) {
-                ac.c[k] = w[4 + k];
-                ac.dc[k] = w[5 + MT + k];
-            }
-            ac.first = int(first);
-            ac.F = F;
-            ac.phase0 = phase0;
-            ac.omega = omega;
-            float4 *s4 = reinterpret_cast<float4 *>(sites);
-            // cos / sin of pi t_j for consecutive sites by rotation from site 0
-            // (t_j = phase0 + 2 j / F): one sincospif for the start and one for
-            // the step instead of one per site.
-            float sj, cj, sd, cd;
-            sincospif(phase0, &sj, &cj);
-            sincospif(2.0f / float(F), &sd, &cd);
-#pragma unroll
-            for (int q = 0; q < REACH / 4; ++q) {
-                if (4 * q < F) {
-                    SiteVals v[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        v[u] = ac.values_cs(cj, sj);
-                        const float cn = fmaf(cj, cd, -sj * sd);
-                        sj = fmaf(sj, cd, cj * sd);
-                        cj = cn;
-                    }
-                    s4[q] = make_float4(v[0].m, v[1].m, v[2].m, v[3].m);
-                    s4[REACH / 4 + q] = make_float4(v[0].dmu, v[1].dmu, v[2].dmu, v[3].dmu);
-                    s4[REACH / 2 + q] = make_float4(v[0].dR, v[1].dR, v[2].dR, v[3].dR);
-                }
-            }
-        }
     } else {
         int *iblk = reinterpret_cast<int *>(blk);
         iblk[0] = int(first);
@@ -406,11 +373,51 @@ __device__ inline void write_axis_block_t(float *blk, const Route &r, double R, 
 }
 
 __device__ inline void write_axis_block(float *blk, const Route &r, double R, const AxisCfg &ax,
-                                        const ProfileTab &tab, float *sites) {
+                                        const ProfileTab &tab) {
     if (ax.modes == 8)
-        write_axis_block_t<8>(blk, r, R, ax, tab, sites);
+        write_axis_block_t<8>(blk, r, R, ax, tab);
     else
-        write_axis_block_t<0>(blk, r, R, ax, tab, nullptr);
+        write_axis_block_t<0>(blk, r, R, ax, tab);
+}
+
+// Site values (m, dm/dmu, dm/dR on the first REACH footprint sites of each
+// axis) of the atoms of the site classes, from their records: two threads per
+// atom (one per axis), like the decode. cos / sin of pi t_j for consecutive
+// sites by rotation from site 0 (t_j = phase0 + 2 j / F): one sincospif for the
+// start and one for the step instead of one per site. Runs beside the sort,
+// which does not read the site values.
+__global__ void __launch_bounds__(256) site_values_kernel(Table tv) {
+    pdl_wait();
+    const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long a = tid >> 1;
+    const int side = int(tid & 1);
+    if (a >= tv.atoms) return;
+    const int4 span = tv.spans[a];
+    if (span.y <= 0 || span.w <= 0 || max(span.y, span.w) > REACH) return;
+    AxisCoef<8> ac;
+    ac.load(tv.rec + a * (long long)tv.words + 4 + side * axis_words(8));
+    const int F = ac.F;
+    float4 *s4 = reinterpret_cast<float4 *>(const_cast<float *>(tv.sites) + a * SITE_FLOATS +
+                                            side * 3 * REACH);
+    float sj, cj, sd, cd;
+    sincospif(ac.phase0, &sj, &cj);
+    sincospif(2.0f / float(F), &sd, &cd);
+#pragma unroll 2
+    for (int q = 0; q < REACH / 4; ++q) {
+        if (4 * q < F) {
+            SiteVals v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                v[u] = ac.values_cs(cj, sj);
+                const float cn = fmaf(cj, cd, -sj * sd);
+                sj = fmaf(sj, cd, cj * sd);
+                cj = cn;
+            }
+            s4[q] = make_float4(v[0].m, v[1].m, v[2].m, v[3].m);
+            s4[REACH / 4 + q] = make_float4(v[0].dmu, v[1].dmu, v[2].dmu, v[3].dmu);
+            s4[REACH / 2 + q] = make_float4(v[0].dR, v[1].dR, v[2].dR, v[3].dR);
+        }
+    }
 }
 
 struct Decoded {
@@ -512,7 +519,6 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
     float *rec = const_cast<float *>(tv.rec) + a * (long long)words;
     float *blk = rec + 4 + (side ? axis_words(out_ax.modes) : 0);
     int4 *spans = const_cast<int4 *>(tv.spans);
-    float *sites = const_cast<float *>(tv.sites) + a * SITE_FLOATS + side * 3 * REACH;
     int node = 0, wrapped = 0, foot = 0, lvl = -1, kk = 0;
     if (live && d.bad) {
         if (side == 0) {
@@ -530,7 +536,7 @@ __global__ void __launch_bounds__(256, 4) decode_route_kernel(
     } else if (live) {
         const double R = side ? d.r_in : d.r_out;
         const Route r = route_axis(R, double(side ? row.w : row.z), ax);
-        write_axis_block(blk, r, R, ax, side ? tab_in : tab_out, sites);
+        write_axis_block(blk, r, R, ax, side ? tab_in : tab_out);
         {
             const long long first = (long long)r.first_tile * r.tile;
             const long long wr = first % ax.sites;
@@ -868,14 +874,25 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
         TCST_CUDA(launch_pdl(decode_route_kernel, dim3(unsigned(blocks)), dim3(threads), 0, st, 
             p_dev, oa, ia, cc, to, ti, tv, (long long *)owner_keys_dev, routing_dev, status_dev));
         TCST_CUDA(cudaGetLastError());
-        TCST_CUDA(launch_pdl(bin_count_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv));
-        TCST_CUDA(cudaGetLastError());
     }
-    TCST_CUDA(launch_pdl(bin_column_kernel, dim3(unsigned((g.nbins + 31) / 32)), dim3(COL_SEGS * 32), 0, st, tv));
-    TCST_CUDA(cudaGetLastError());
-    TCST_CUDA(launch_pdl(bin_scatter_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv));
-    TCST_CUDA(cudaGetLastError());
-    return TCST_OK;
+    // The site values of the site classes on a side stream, beside the sort
+    // (binned geometries only: they have eight modes on both axes).
+    SideStreams side(st, g.nclass > 0 ? 1 : 0);
+    rc = side.status();
+    if (!rc && g.nclass > 0) {
+        const cudaError_t e = launch_pdl(site_values_kernel, dim3(unsigned((2 * atoms + 255) / 256)),
+                                         dim3(256), 0, side[0], tv);
+        if (e != cudaSuccess) rc = tcst_cuda_check(e, "site_values_kernel");
+    }
+    cudaError_t e = cudaSuccess;
+    if (!rc) e = launch_pdl(bin_count_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv);
+    if (!rc && e == cudaSuccess)
+        e = launch_pdl(bin_column_kernel, dim3(unsigned((g.nbins + 31) / 32)), dim3(COL_SEGS * 32), 0, st, tv);
+    if (!rc && e == cudaSuccess)
+        e = launch_pdl(bin_scatter_kernel, dim3(unsigned(g.sort_blocks)), dim3(SORT_THREADS), hist_bytes, st, tv);
+    if (!rc && e != cudaSuccess) rc = tcst_cuda_check(e, "bin sort");
+    const int rj = side.join();
+    return rc ? rc : rj;
 }
 
 extern "C" int tcst_atom_energies(const void *atom_table_dev, int64_t atoms,

@@ -149,7 +149,8 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
 //   spans   [atoms] int4: output first site wrapped, output footprint,
 //                         input first site wrapped, input footprint
 //   sites   [atoms][2 axes][3 values][REACH]: m, dm/dmu, dm/dR of the first
-//           REACH footprint sites of each axis (filled when F <= REACH)
+//           REACH footprint sites of each axis (filled when F <= REACH, i.e.
+//           for the site classes 0 .. SITE_CLASSES-1)
 //   bin_of  [atoms] int: the atom's bin
 //   offsets [nbins + 1] int, ids [atoms] int: atom ids grouped by bin, in
 //           increasing id order inside every bin (stable counting sort)
@@ -157,8 +158,9 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
 //   sync    one word (+ padding): finished blocks of the sort's column prefix
 //
 // Bins. An atom's class is the smallest c whose reach class_reach(c) covers
-// its larger footprint max(F_out, F_in). Classes 0..NFINE-1 (reach 16, 64, 128)
-// are binned by the fe x fe tile of (output first site, input first site),
+// its larger footprint max(F_out, F_in), reach 16 << c. Classes 0..NFINE-1
+// (reach 16, 32, 64, 128) are binned by the fe x fe tile of (output first
+// site, input first site),
 // fe = TS (2 TS for charts so large that TS bins do not fit);
 // coarser classes (reach 256, 512, ... up to twice the larger axis, the widest
 // footprint routing produces) by tiles of edge reach / 2. Bins are numbered
@@ -179,14 +181,15 @@ __device__ __forceinline__ SiteVals site_values(const float *blk, int modes, int
 // that path in the weight assembly and the pullback; the atoms of other pairs
 // are treated one by one like any coarse atom.
 // ---------------------------------------------------------------------------
-constexpr int REACH = 16;
+constexpr int REACH = 32;        // footprint sites whose values the decode stores
+constexpr int SITE_CLASSES = 2;  // classes with footprints of at most REACH sites
 constexpr int SITE_FLOATS = 2 * 3 * REACH;
 constexpr int TS = 32;          // fine bin tile edge and weight tile edge, in sites
-constexpr int NFINE = 3;        // classes binned by TS tiles
+constexpr int NFINE = 4;        // classes binned by TS tiles
 constexpr int MAX_CLASSES = 16;
 constexpr int MAX_BINS = 98304;  // 16-bit per-CTA bin counters fit in shared memory
 constexpr int SORT_CHUNK = 512;  // atoms per sort block (128 blocks, more for > 8M atoms)
-constexpr int CACHE_SITES = 128; // masses cached per axis for classes 1..NFINE-1
+constexpr int CACHE_SITES = 128; // masses cached per axis for classes SITE_CLASSES..NFINE-1
 constexpr int PF = 17;                // owner-pair basis functions per axis (M = 8)
 constexpr int MAX_PAIR_LB = 32;       // pair level-banks
 constexpr int PAIR_MIN = 2;           // atoms that make an owner pair active
@@ -199,7 +202,9 @@ struct AxisGeo {
     double spacing;
 };
 
-__host__ __device__ constexpr int class_reach(int c) { return c == 0 ? 16 : 64 << (c - 1); }
+__host__ __device__ constexpr int class_reach(int c) { return 16 << c; }
+static_assert(class_reach(SITE_CLASSES - 1) == REACH, "site classes end at REACH");
+static_assert(class_reach(NFINE - 1) <= CACHE_SITES, "cached classes fit the mass cache");
 // Bin edge of class c: fe (the geometry's fine edge, TS or 2 TS) for the fine
 // classes, half the reach for coarser ones.
 __host__ __device__ constexpr int class_edge(int c, int fe) {

@@ -254,21 +254,6 @@ constexpr int PP_THREADS = 256;
 constexpr int PP_GPITCH = PP_COLS + 8; // shared G row pitch (conflict-free fragment loads)
 constexpr int PP_APITCH = 32 + 8;      // shared basis row pitch (conflict-free fragment loads)
 
-__device__ __forceinline__ unsigned tf32_bits(float x) {
-    unsigned r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
-
-// D += A B for one m16n8k8 TF32 tile.
-__device__ __forceinline__ void mma_tf32(float (&d)[4], const unsigned (&a)[4], const unsigned (&b)[2]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, "
-        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
-
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
     const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
     const int n = valid ? 16 : 0; // a zero source size fills the 16 bytes with zeros

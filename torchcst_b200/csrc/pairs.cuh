@@ -12,6 +12,25 @@ struct Window {
     int r0, c0, wr, wc;
 };
 
+// TF32 bit pattern of x (round to nearest, ties away): the hi term of the
+// three-product split x ~ hi + lo, lo = rn_tf32(x - hi).
+__device__ __forceinline__ unsigned tf32_bits(float x) {
+    unsigned r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+// D += A B for one m16n8k8 TF32 tile. Fragments (g = lane / 4, q = lane % 4):
+// a = A[g][q], A[g+8][q], A[g][q+4], A[g+8][q+4]; b = B[q][g], B[q+4][g];
+// d = D[g][2q], D[g][2q+1], D[g+8][2q], D[g+8][2q+1].
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const unsigned (&a)[4], const unsigned (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
 // Nodes (first tiles of T sites, nn of them on an axis of n sites) whose F-site
 // footprint covers some site of [t0, t0 + tl): `count` consecutive nodes from
 // `first` (mod nn). Node a covers the tile iff t0 - F < a T <= t0 + tl - 1

@@ -12,9 +12,9 @@
 // own kernel: a CTA stages in shared memory the window of G that every atom of
 // its bin can reach (first-site bin + the class reach - 1 sites on both axes),
 // then
-//   class 0 (footprints <= 16):   four threads per atom, site values from the
-//                                 table's site buffer;
-//   classes 1, 2 (<= 64, <= 128): one CTA per bin, one warp per atom, lanes
+//   classes 0, 1 (footprints <= 16, <= 32): four / eight threads per atom,
+//                                 site values from the table's site buffer;
+//   classes 2, 3 (<= 64, <= 128): one CTA per bin, one warp per atom, lanes
 //                                 over input sites, output-site values in
 //                                 per-warp shared memory.
 // Atoms of active owner pairs take the owner-pair projection (pairs.cu). The
@@ -202,30 +202,35 @@ __device__ __forceinline__ void stage_rect(float *gw, int r_lo, int r_hi, int c_
     }
 }
 
-// Class 0: one CTA per first-site tile; four threads per atom, each owning
-// four of the (at most 16) input sites; the output-site values of the atom are
-// spread over the quad and shuffled per row; the quad sums its four partials in
-// a fixed xor order.
-template <int E>
-__global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
-    Table tv, int no, int ni, const float *__restrict__ g, long long ldg, int split,
+// Site classes (footprints of at most 4 LANES sites: class 0 with LANES = 4,
+// class 1 with LANES = 8): one CTA per first-site tile; LANES threads per atom,
+// each owning four of the input sites; the output-site values of the atom are
+// spread over the group and shuffled per row; the group sums its partials in a
+// fixed xor order.
+template <int E, int LANES>
+__global__ void __launch_bounds__(P0_THREADS) pullback_site_kernel(
+    Table tv, int cls, int no, int ni, const float *__restrict__ g, long long ldg, int split,
     long long split_stride, int b0, int bn, float4 *__restrict__ grad) {
     pdl_wait();
-    constexpr int W = E + REACH - 1;
-    constexpr int PITCH = W + 1;
+    constexpr int RS = 4 * LANES; // the class reach
+    static_assert(RS <= REACH, "site values stored for the whole reach");
+    constexpr int W = E + RS - 1;
+    // Row pitch: W + 1 for the quads; for octets a multiple of 4 that is 4 mod 32
+    // banks apart, so the eight rows one instruction reads spread over banks.
+    constexpr int PITCH = LANES == 4 ? W + 1 : (W + 3) / 4 * 4 + ((W + 3) / 4 % 8 == 0 ? 4 : 0);
     __shared__ __align__(16) float gw[W * PITCH];
-    const int ct = tv.geom.tc[0];
+    const int ct = tv.geom.tc[cls];
     const int tr = blockIdx.x / ct, tc = blockIdx.x - tr * ct;
-    const int bin = tv.geom.base[0] + blockIdx.x; // class 0 bins, row-major by tile
+    const int bin = tv.geom.base[cls] + blockIdx.x; // the class's bins, row-major by tile
     const int begin = tv.offsets[bin], end = tv.offsets[bin + 1];
     const int R0 = tr * E, C0 = tc * E;
     if (begin == end || !rows_meet(R0, W, no, b0, bn)) return;
     stage_window<W, PITCH>(gw, R0, C0, no, ni, g, ldg, split, split_stride, b0, bn);
     __syncthreads();
-    const int lane = threadIdx.x & 31, q = lane & 3;
-    const int quads = blockDim.x >> 2;
-    for (int k0 = begin; k0 < end; k0 += quads) {
-        const int k = k0 + (threadIdx.x >> 2);
+    const int lane = threadIdx.x & 31, q = lane & (LANES - 1);
+    const int groups = blockDim.x / LANES;
+    for (int k0 = begin; k0 < end; k0 += groups) {
+        const int k = k0 + threadIdx.x / LANES;
         const bool live = k < end;
         long long a = 0;
         int4 span = make_int4(0, 0, 0, 0);
@@ -234,8 +239,9 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
             a = tv.ids[k];
             span = tv.sspan[k];
             const float4 *sv = reinterpret_cast<const float4 *>(tv.sites + a * SITE_FLOATS);
-            om = sv[q], od = sv[4 + q], orr = sv[8 + q];   // output rows 4q .. 4q+3
-            im = sv[12 + q], id = sv[16 + q], ir = sv[20 + q]; // input columns 4q .. 4q+3
+            constexpr int V = REACH / 4; // float4s per stored value row
+            om = sv[q], od = sv[V + q], orr = sv[2 * V + q];           // output rows 4q .. 4q+3
+            im = sv[3 * V + q], id = sv[4 * V + q], ir = sv[5 * V + q]; // input columns 4q .. 4q+3
         }
         const int fo = span.y, fi = span.w;
         float cm[4] = {im.x, im.y, im.z, im.w}, cd[4] = {id.x, id.y, id.z, id.w},
@@ -247,9 +253,9 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
         // Row contractions of the thread's four columns with (m, dm/dmu,
         // dm/dR) of the output sites, then one dot with the column values.
         float h0[4] = {}, h1[4] = {}, h2[4] = {};
-        const int base = lane & ~3;
+        const int base = lane & ~(LANES - 1);
 #pragma unroll
-        for (int r = 0; r < REACH; ++r) {
+        for (int r = 0; r < RS; ++r) {
             const float vm = (r & 3) == 0 ? om.x : (r & 3) == 1 ? om.y : (r & 3) == 2 ? om.z : om.w;
             const float vd = (r & 3) == 0 ? od.x : (r & 3) == 1 ? od.y : (r & 3) == 2 ? od.z : od.w;
             const float vr = (r & 3) == 0 ? orr.x : (r & 3) == 1 ? orr.y : (r & 3) == 2 ? orr.z : orr.w;
@@ -276,7 +282,7 @@ __global__ void __launch_bounds__(P0_THREADS) pullback_class0_kernel(
             s_r = fmaf(h2[j], cm[j], fmaf(h0[j], cr[j], s_r));
         }
 #pragma unroll
-        for (int off = 1; off < 4; off <<= 1) {
+        for (int off = 1; off < LANES; off <<= 1) {
             s_amp += __shfl_xor_sync(0xffffffffu, s_amp, off);
             s_mo += __shfl_xor_sync(0xffffffffu, s_mo, off);
             s_mi += __shfl_xor_sync(0xffffffffu, s_mi, off);
@@ -552,20 +558,28 @@ static int launch_classes(const Table &tv, const AxisCfg &oa, const AxisCfg &ia,
                                        int(class_smem<128, E>())));
         configured = true;
     }
-    TCST_CUDA(launch_pdl(pullback_class0_kernel<E>, dim3(unsigned(geo.tr[0] * geo.tc[0])),
-                         dim3(P0_THREADS), 0, st, tv, oa.sites, ia.sites, g_dev, ldg, split,
+    TCST_CUDA(launch_pdl(pullback_site_kernel<E, 4>, dim3(unsigned(geo.tr[0] * geo.tc[0])),
+                         dim3(P0_THREADS), 0, st, tv, 0, oa.sites, ia.sites, g_dev, ldg, split,
                          split_stride, b0, bn, grad));
     TCST_CUDA(cudaGetLastError());
     if (geo.nclass > 1) {
-        TCST_CUDA(launch_pdl(pullback_class_kernel<64, E>, dim3(unsigned(geo.tr[1] * geo.tc[1])),
-                             dim3(PC_THREADS), class_smem<64, E>(), st1, tv, 1, oa.sites, ia.sites,
+        TCST_CUDA(launch_pdl(pullback_site_kernel<E, 8>, dim3(unsigned(geo.tr[1] * geo.tc[1])),
+                             dim3(P0_THREADS), 0, st1, tv, 1, oa.sites, ia.sites, g_dev, ldg,
+                             split, split_stride, b0, bn, grad));
+        TCST_CUDA(cudaGetLastError());
+    }
+    // The two cached classes share a stream: few atoms reach them early in
+    // training.
+    if (geo.nclass > 2) {
+        TCST_CUDA(launch_pdl(pullback_class_kernel<64, E>, dim3(unsigned(geo.tr[2] * geo.tc[2])),
+                             dim3(PC_THREADS), class_smem<64, E>(), st2, tv, 2, oa.sites, ia.sites,
                              g_dev, ldg, split, split_stride, b0, bn, grad));
         TCST_CUDA(cudaGetLastError());
     }
-    if (geo.nclass > 2) {
+    if (geo.nclass > 3) {
         TCST_CUDA(launch_pdl(pullback_class_kernel<128, E>,
-                             dim3(unsigned(geo.tr[2] * geo.tc[2])), dim3(PC_THREADS),
-                             class_smem<128, E>(), st2, tv, 2, oa.sites, ia.sites, g_dev, ldg,
+                             dim3(unsigned(geo.tr[3] * geo.tc[3])), dim3(PC_THREADS),
+                             class_smem<128, E>(), st2, tv, 3, oa.sites, ia.sites, g_dev, ldg,
                              split, split_stride, b0, bn, grad));
         TCST_CUDA(cudaGetLastError());
     }

@@ -4,17 +4,20 @@
 // Weight assembly uses the bins that tcst_decode_route stored in the atom
 // table (footprint class x first-site tile, or owner pair; atoms in id order
 // inside a bin):
-//   cache:  one warp per atom of classes 1..NFINE-1 writes the atom's masses on
-//           both footprints into the caller's scratch (class 0 masses are in the
-//           atom table's site buffer; coarser classes are evaluated where used);
+//   cache:  one warp per atom of classes SITE_CLASSES..NFINE-1 writes the atom's
+//           masses on both footprints into the caller's scratch (the masses of
+//           footprints of at most REACH sites are in the atom table's site
+//           buffer; coarser classes are evaluated where used);
 //   pairs:  the owner-pair coefficients and expansions (pairs.cu);
 //   gather: one CTA per TS x TS weight tile lists, in a fixed order, every bin
 //           whose atoms can reach the tile (active owner pairs excepted), keeps
 //           the atoms that do, stages their masses on the tile's rows and
-//           columns in shared memory (images folded modulo N) and accumulates
-//           the outer products in registers (2 x 4 per thread), adds the
-//           rank-one terms of the active owner nodes that cover the tile, then
-//           writes W (or its TF32 split planes) and folds max |W| in.
+//           columns in shared memory as [site][hit] planes (images folded
+//           modulo N; one thread per hit and axis) and accumulates the outer
+//           products as a [32 x hits] x [hits x 32] product on the tensor cores
+//           (mma.sync TF32, three-product split), adds the rank-one terms of the
+//           active owner nodes that cover the tile the same way, then writes W
+//           (or its TF32 split planes) and folds max |W| in.
 // A fixed bin order and id-ordered bins make W bitwise reproducible; the only
 // atomic is the max.
 
@@ -28,8 +31,11 @@
 
 namespace tcst {
 
-constexpr int WT_THREADS = 128; // 16 x 8 threads, 2 x 4 outputs each
-constexpr int WT_STAGE = 64;          // hits staged per sub-pass
+constexpr int WT_THREADS = 128; // four warps, a 16 x 16 quarter of the tile each
+constexpr int WT_STAGE = 56;    // hits staged per sub-pass (eight CTAs fit an SM)
+constexpr int WT_KP = WT_STAGE + 4; // pitch of the staged [site][hit] planes: 60 = -4
+                                    // (mod 32 banks), so the MMA fragment loads
+                                    // (8 rows x 4 hits) hit 32 distinct banks
 constexpr int MAX_SCAN = 512;  // bins a weight tile can scan
 
 __device__ __forceinline__ float tf32_rna(float x) {
@@ -71,14 +77,14 @@ __host__ inline int max_scan_entries(const BinGeom &g, int no, int ni) {
     return n;
 }
 
-// Class 1..NFINE-1 mass cache: cache[a][axis][j] = m_axis(j), j < F_axis.
+// Class SITE_CLASSES..NFINE-1 mass cache: cache[a][axis][j] = m_axis(j), j < F_axis.
 __global__ void __launch_bounds__(256) mass_cache_kernel(Table tv, float *__restrict__ cache) {
     pdl_wait();
     const int lane = threadIdx.x & 31;
     const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const long long nwarps = (gridDim.x * (long long)blockDim.x) >> 5;
     const BinGeom &g = tv.geom;
-    const int begin = tv.offsets[g.base[min(1, g.nclass)]];
+    const int begin = tv.offsets[g.base[min(SITE_CLASSES, g.nclass)]];
     const int end = tv.offsets[g.base[min(NFINE, g.nclass)]];
     const int aw = axis_words(8);
     const int side = lane >> 4, l = lane & 15; // half-warp per axis
@@ -143,6 +149,54 @@ struct GatherOut {
     int r0, c0, wr, wc;
 };
 
+// acc += U V^T over the staged hits [0, kpad) (kpad a multiple of 8; the
+// planes are zero past the staged hits): U = us [tile row][hit], V = vs [tile
+// column][hit]. Warp w owns rows 16 (w / 2) .. +15 and columns 16 (w % 2) ..
+// +15 (two n-tiles). Three-product TF32 split (lo hi + hi lo + hi hi), so the
+// products keep about 22 significant bits, accumulated in fp32.
+__device__ __forceinline__ void tile_mma(float (&acc)[2][4], const float (*us)[WT_KP],
+                                         const float (*vs)[WT_KP], int kpad, int warp, int lane) {
+    const int g = lane >> 2, q = lane & 3;
+    const int m0 = (warp >> 1) * 16, n0 = (warp & 1) * 16;
+#pragma unroll 2
+    for (int k0 = 0; k0 < kpad; k0 += 8) {
+        const float av[4] = {us[m0 + g][k0 + q], us[m0 + g + 8][k0 + q], us[m0 + g][k0 + q + 4],
+                             us[m0 + g + 8][k0 + q + 4]};
+        unsigned ah[4], al[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            ah[e] = tf32_bits(av[e]);
+            al[e] = tf32_bits(av[e] - __uint_as_float(ah[e]));
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            const int c = n0 + nt * 8 + g;
+            const float bv[2] = {vs[c][k0 + q], vs[c][k0 + q + 4]};
+            unsigned bh[2], bl[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                bh[e] = tf32_bits(bv[e]);
+                bl[e] = tf32_bits(bv[e] - __uint_as_float(bh[e]));
+            }
+            mma_tf32(acc[nt], al, bh);
+            mma_tf32(acc[nt], ah, bl);
+            mma_tf32(acc[nt], ah, bh);
+        }
+    }
+}
+
+// Zero columns [0, kpad) of both staged planes (kpad a multiple of 4).
+__device__ __forceinline__ void zero_planes(float (*us)[WT_KP], float (*vs)[WT_KP], int kpad,
+                                            int t) {
+    const int per_row = kpad >> 2, per_plane = TS * per_row;
+    for (int e = t; e < 2 * per_plane; e += WT_THREADS) {
+        const int pl = e >= per_plane, rem = e - pl * per_plane;
+        const int r = rem / per_row, c4 = rem - r * per_row;
+        float(*dst)[WT_KP] = pl ? vs : us;
+        *reinterpret_cast<float4 *>(&dst[r][4 * c4]) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
 __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, int no, int ni,
                                                                    int modes_o, int modes_i,
                                                                    int tiles_c,
@@ -151,12 +205,13 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
     pdl_wait();
     __shared__ int sbeg[MAX_SCAN], scls[MAX_SCAN], spre[MAX_SCAN + 1];
     __shared__ int wtot[WT_THREADS / 32];
-    __shared__ __align__(16) float us[WT_STAGE][TS];
-    __shared__ __align__(16) float vs[WT_STAGE][TS];
+    // Staged hits: us[r][h] = amp_h m_out,h at tile row r, vs[c][h] = m_in,h at
+    // tile column c (images folded modulo N), zero off the footprints.
+    __shared__ __align__(16) float us[TS][WT_KP];
+    __shared__ __align__(16) float vs[TS][WT_KP];
     __shared__ int cand[WT_THREADS], ccls[WT_THREADS];
     __shared__ int4 cspan[WT_THREADS];
     __shared__ float camp[WT_THREADS];
-    __shared__ unsigned rmask[WT_STAGE]; // tile rows each staged atom covers
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int trow = blockIdx.x / tiles_c, tcol = blockIdx.x - trow * tiles_c;
     const int R0 = out.r0 + trow * TS, C0 = out.c0 + tcol * TS;
@@ -280,7 +335,6 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
     }
     __syncthreads();
     const int total = spre[nscan];
-    const int r0 = (t >> 3) * 2, c0 = (t & 7) * 4;
     const int aw = axis_words(modes_o);
     float acc[2][4] = {};
 
@@ -323,108 +377,93 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
         }
         __syncthreads();
         for (int h0 = 0; h0 < n; h0 += WT_STAGE) {
-            const int nb = min(WT_STAGE, n - h0);
-            // 3. Stage: odd warps the tile columns (m_in), even warps the rows
-            // (amp * m_out). A warp stages four hits per pass, eight lanes per
-            // hit and four tile sites per lane; warps 0-1 take hit groups
-            // 0-3, 8-11, ..., warps 2-3 groups 4-7, 12-15, ... Main pass:
-            // classes with stored masses and no second image (independent
-            // loads); a second pass evaluates the rest of the same hits.
-            {
-                const int side = warp & 1, half = warp >> 1;
-                const int sub = lane >> 3, q = lane & 7;
-                const int lim = side ? TC : TR, nn = side ? ni : no;
-                const int site0 = (side ? C0 : R0) + 4 * q;
-                float(*dst)[TS] = side ? vs : us;
-                bool rest = false;
-#pragma unroll 2
-                for (int s0 = 4 * half; s0 < nb; s0 += 8) {
-                    const int s2 = s0 + sub;
-                    unsigned nib = 0;
-                    if (s2 < nb) {
-                        const int4 qs = cspan[h0 + s2];
-                        const int f = side ? qs.z : qs.x, F = side ? qs.w : qs.y;
-                        const int c = ccls[h0 + s2];
-                        const long long atom = cand[h0 + s2];
-                        const bool stored = c >= 0 && c < NFINE && F <= nn;
-                        const float *src = c == 0 ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
-                                                  : cache + (atom * 2 + side) * CACHE_SITES;
-                        int j = site0 - f;
-                        j += j < 0 ? nn : 0;
-                        float v[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int ju = j + u >= nn ? j + u - nn : j + u;
-                            const bool row = 4 * q + u < lim;
-                            const bool inside = row && ju < F;
-                            v[u] = stored && inside ? src[ju] : 0.f;
-                            // With F > N every tile site is covered by some image.
-                            nib |= (inside || (row && F > nn)) ? 1u << u : 0u;
-                        }
-                        if (side == 0) {
-                            const float amp = camp[h0 + s2];
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) v[u] *= amp;
-                        }
-                        *reinterpret_cast<float4 *>(&dst[s2][4 * q]) = make_float4(v[0], v[1], v[2], v[3]);
-                        rest |= !stored;
-                    }
-                    if (side == 0) {
-                        unsigned m = nib << (4 * q);
-                        m |= __shfl_xor_sync(0xffffffffu, m, 1);
-                        m |= __shfl_xor_sync(0xffffffffu, m, 2);
-                        m |= __shfl_xor_sync(0xffffffffu, m, 4);
-                        if (s2 < nb && q == 0) rmask[s2] = m;
-                    }
-                }
-                __syncwarp();
-                if (__any_sync(0xffffffffu, rest)) {
-                    const int p = lane, site = (side ? C0 : R0) + p;
-                    for (int s2 = 4 * half; s2 < nb; s2 += (s2 & 3) == 3 ? 5 : 1) {
-                        const int4 qs = cspan[h0 + s2];
-                        const int f = side ? qs.z : qs.x, F = side ? qs.w : qs.y;
-                        const int c = ccls[h0 + s2];
-                        if (c >= 0 && c < NFINE && F <= nn) continue;
-                        const long long atom = cand[h0 + s2];
-                        int j = site - f;
-                        j += j < 0 ? nn : 0;
-                        float v = 0.f;
-                        if (p < lim && j < F) {
-                            const float *blk = tv.rec + atom * tv.words + 4 + side * aw;
-                            if (c == 0) {
-                                const float *sv = tv.sites + atom * SITE_FLOATS + side * 3 * REACH;
-                                for (; j < F; j += nn) v += sv[j];
-                            } else if (c > 0 && c < NFINE) {
-                                const float *cv = cache + (atom * 2 + side) * CACHE_SITES;
-                                for (; j < F; j += nn) v += cv[j];
-                            } else if (c >= NFINE) {
-                                AxisCoef<8> ac;
-                                ac.load_mass(blk);
-                                for (; j < F; j += nn) v += ac.mass(j);
-                            } else {
-                                // Unbinned geometry: any mode count.
-                                const int modes = side ? modes_i : modes_o;
-                                for (; j < F; j += nn) v += site_mass(blk, modes, j, F);
-                            }
-                        }
-                        dst[s2][p] = side ? v : v * camp[h0 + s2];
-                    }
-                }
-            }
+            const int nb = min(WT_STAGE, n - h0), kpad = (nb + 7) & ~7;
+            zero_planes(us, vs, kpad, t);
             __syncthreads();
-            // Each warp owns tile rows 8w .. 8w+7 and skips atoms that miss them.
-            const unsigned wrows = 0xFFu << (8 * warp);
-#pragma unroll 4
-            for (int s2 = 0; s2 < nb; ++s2) {
-                if (!(rmask[s2] & wrows)) continue;
-                const float2 u = *reinterpret_cast<const float2 *>(&us[s2][r0]);
-                const float4 v = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
-                const float uu[2] = {u.x, u.y}, vv[4] = {v.x, v.y, v.z, v.w};
+            // 3. Stage, one thread per (hit, axis): warps 0-1 the rows (amp m_out),
+            // warps 2-3 the columns (m_in). Classes with stored masses and a
+            // footprint of at most N sites (one image per tile site) write the
+            // covered sites, at most two runs of the cyclic footprint; the other
+            // hits are evaluated in a second pass (one lane per tile site).
+            bool rest = false;
+            {
+                const int side = t >> 6, s2 = t & 63;
+                if (s2 < nb) {
+                    const int4 qs = cspan[h0 + s2];
+                    const int f = side ? qs.z : qs.x, F = side ? qs.w : qs.y;
+                    const int c = ccls[h0 + s2];
+                    const int nn = side ? ni : no, lim = side ? TC : TR;
+                    if (c >= 0 && c < NFINE && F <= nn) {
+                        const long long atom = cand[h0 + s2];
+                        const float *src = c < SITE_CLASSES ? tv.sites + atom * SITE_FLOATS + side * 3 * REACH
+                                                  : cache + (atom * 2 + side) * CACHE_SITES;
+                        const float scale = side ? 1.f : camp[h0 + s2];
+                        float(*dst)[WT_KP] = side ? vs : us;
+                        // Footprint index of tile site 0 (f and the tile origin lie in
+                        // [0, N)); tile sites [0, F - j0) and [N - j0, N - j0 + F).
+                        int j0 = (side ? C0 : R0) - f;
+                        j0 += j0 < 0 ? nn : 0;
+                        const int a_end = j0 < F ? min(lim, F - j0) : 0;
+                        const int b0 = nn - j0, b_end = min(lim, b0 + F);
+                        // Eight independent loads in flight per chunk.
+                        for (int r0 = 0; r0 < a_end; r0 += 8) {
+                            float v[8];
 #pragma unroll
-                for (int ii = 0; ii < 2; ++ii)
+                            for (int u = 0; u < 8; ++u) v[u] = r0 + u < a_end ? src[j0 + r0 + u] : 0.f;
 #pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(uu[ii], vv[jj], acc[ii][jj]);
+                            for (int u = 0; u < 8; ++u)
+                                if (r0 + u < a_end) dst[r0 + u][s2] = scale * v[u];
+                        }
+                        for (int r0 = b0; r0 < b_end; r0 += 8) {
+                            float v[8];
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) v[u] = r0 + u < b_end ? src[r0 + u - b0] : 0.f;
+#pragma unroll
+                            for (int u = 0; u < 8; ++u)
+                                if (r0 + u < b_end) dst[r0 + u][s2] = scale * v[u];
+                        }
+                    } else {
+                        rest = true;
+                    }
+                }
             }
+            if (__syncthreads_or(rest)) {
+                const int side = warp >> 1, sub = warp & 1;
+                const int lim = side ? TC : TR, nn = side ? ni : no;
+                const int p = lane, site = (side ? C0 : R0) + p;
+                float(*dst)[WT_KP] = side ? vs : us;
+                for (int s2 = sub; s2 < nb; s2 += 2) {
+                    const int4 qs = cspan[h0 + s2];
+                    const int f = side ? qs.z : qs.x, F = side ? qs.w : qs.y;
+                    const int c = ccls[h0 + s2];
+                    if (c >= 0 && c < NFINE && F <= nn) continue;
+                    const long long atom = cand[h0 + s2];
+                    int j = site - f;
+                    j += j < 0 ? nn : 0;
+                    float v = 0.f;
+                    if (p < lim && j < F) {
+                        const float *blk = tv.rec + atom * tv.words + 4 + side * aw;
+                        if (c >= 0 && c < SITE_CLASSES) {
+                            const float *sv = tv.sites + atom * SITE_FLOATS + side * 3 * REACH;
+                            for (; j < F; j += nn) v += sv[j];
+                        } else if (c >= SITE_CLASSES && c < NFINE) {
+                            const float *cv = cache + (atom * 2 + side) * CACHE_SITES;
+                            for (; j < F; j += nn) v += cv[j];
+                        } else if (c >= NFINE) {
+                            AxisCoef<8> ac;
+                            ac.load_mass(blk);
+                            for (; j < F; j += nn) v += ac.mass(j);
+                        } else {
+                            // Unbinned geometry: any mode count.
+                            const int modes = side ? modes_i : modes_o;
+                            for (; j < F; j += nn) v += site_mass(blk, modes, j, F);
+                        }
+                    }
+                    if (p < TS) dst[p][s2] = side ? v : v * camp[h0 + s2];
+                }
+                __syncthreads();
+            }
+            tile_mma(acc, us, vs, kpad, warp, lane);
             __syncthreads();
         }
     }
@@ -481,60 +520,58 @@ __global__ void __launch_bounds__(WT_THREADS, 8) weight_gather_kernel(Table tv, 
             for (; i < np && nn < PER_PASS; ++i)
                 if (pnode[i] >= 0) key[nn++] = pnode[i]; // CTA-uniform
             if (nn == 0) break;
+            // Terms k PF + f: rows phi_f of node k (warp k, lane = tile row),
+            // columns R_a[f] (every thread); columns up to the MMA's multiple
+            // of 8 are zero.
+            const int nt = nn * PF, kpad = (nt + 7) & ~7;
             if (warp < nn) {
                 const int l = key[warp] >> 16, a = key[warp] & 0xFFFF;
                 const int T = g.pl_T[l], F = g.pl_K[l] * T;
                 float phi[PF];
                 const bool on = lane < TR && pair_basis(R0 + lane - a * T, F, no, phi);
 #pragma unroll
-                for (int f = 0; f < PF; ++f) us[warp * PF + f][lane] = on ? phi[f] : 0.f;
-                const unsigned m = __ballot_sync(0xffffffffu, on);
-                if (lane < PF) rmask[warp * PF + lane] = m;
+                for (int f = 0; f < PF; ++f) us[lane][warp * PF + f] = on ? phi[f] : 0.f;
             }
-            for (int e = t; e < nn * PF * TS; e += WT_THREADS) {
+            for (int e = t; e < nt * TS; e += WT_THREADS) {
                 const int k = e / (PF * TS), rem = e - k * (PF * TS);
                 const int f = rem / TS, c = rem - f * TS;
                 const int l = key[k] >> 16, a = key[k] & 0xFFFF;
                 const float *rb = tv.pair_buf + g.pl_buf[l] + ((long long)a * PF + f) * ni + C0;
-                vs[k * PF + f][c] = c < TC ? rb[c] : 0.f;
+                vs[c][k * PF + f] = c < TC ? rb[c] : 0.f;
+            }
+            for (int e = t; e < 2 * TS * (kpad - nt); e += WT_THREADS) {
+                const int pl = e >= TS * (kpad - nt), rem = e - pl * TS * (kpad - nt);
+                const int r = rem / (kpad - nt), k = nt + rem - r * (kpad - nt);
+                (pl ? vs : us)[r][k] = 0.f;
             }
             __syncthreads();
-            const unsigned wrows = 0xFFu << (8 * warp);
-#pragma unroll 1
-            for (int s2 = 0; s2 < nn * PF; ++s2) {
-                if (!(rmask[s2] & wrows)) continue;
-                const float2 uu = *reinterpret_cast<const float2 *>(&us[s2][r0]);
-                const float4 vv = *reinterpret_cast<const float4 *>(&vs[s2][c0]);
-                const float ua[2] = {uu.x, uu.y}, va[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-                for (int ii = 0; ii < 2; ++ii)
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) acc[ii][jj] = fmaf(ua[ii], va[jj], acc[ii][jj]);
-            }
+            tile_mma(acc, us, vs, kpad, warp, lane);
             __syncthreads();
         }
     }
 
+    // Accumulator of warp w, n-tile nt: rows 16 (w / 2) + g (+8), columns
+    // 16 (w % 2) + 8 nt + 2q (+1).
     float vmax = 0.f;
+    {
+        const int g = lane >> 2, q = lane & 3;
 #pragma unroll
-    for (int ii = 0; ii < 2; ++ii) {
-        const int r = r0 + ii;
-        if (r >= TR) continue;
-        const long long row = R0 - out.r0 + r;
+        for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-            const int c = c0 + jj;
-            if (c >= TC) continue;
-            const long long col = C0 - out.c0 + c;
-            const float v = acc[ii][jj];
-            vmax = fmaxf(vmax, fabsf(v));
-            if (out.w) out.w[row * out.ldw + col] = v;
-            if (out.hi) {
-                const float h = tf32_rna(v);
-                out.hi[row * out.lds + col] = h;
-                out.lo[row * out.lds + col] = tf32_rna(v - h);
+            for (int e = 0; e < 4; ++e) {
+                const int r = (warp >> 1) * 16 + g + (e >= 2 ? 8 : 0);
+                const int c = (warp & 1) * 16 + nt * 8 + 2 * q + (e & 1);
+                if (r >= TR || c >= TC) continue;
+                const long long row = R0 - out.r0 + r, col = C0 - out.c0 + c;
+                const float v = acc[nt][e];
+                vmax = fmaxf(vmax, fabsf(v));
+                if (out.w) out.w[row * out.ldw + col] = v;
+                if (out.hi) {
+                    const float h = tf32_rna(v);
+                    out.hi[row * out.lds + col] = h;
+                    out.lo[row * out.lds + col] = tf32_rna(v - h);
+                }
             }
-        }
     }
     if (out.amax) block_max_to(out.amax, vmax);
 }
