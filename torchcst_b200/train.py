@@ -6,11 +6,12 @@ gradient is written over Y in one pass (with its loss partials and max |dY|),
 every buffer is allocated once, and the step is a fixed sequence of native
 launches on the current stream:
 
-    decode/route -> bin sort (count, column prefix, scatter) -> weight (mass
-    cache, owner-pair coefficients and expansion, tile gather with max |W|,
-    f16 split) | f16 split of X -> GEMM Y -> MSE dY -> f16 split of dY ->
-    GEMM dX -> GEMM dW (split-K) -> pullback (split-K sum, three footprint
-    classes, owner-pair projection and gradients, wide atoms) -> optimizer
+    decode/route -> bin sort (count, column prefix, scatter) | site values ->
+    weight (mass cache, owner-pair coefficients and expansion, tile gather with
+    max |W|, f16 split) | scalar fetch, f16 split of X -> GEMM Y -> MSE dY ->
+    f16 split of dY -> GEMM dX | GEMM dW (split-K) -> pullback (split-K sum,
+    four footprint classes, owner-pair projection and gradients, wide atoms) ->
+    optimizer
 
 The optimizer reads its per-step scalars (bias corrections) from a pinned host
 ring through its device mapping (the host writes the step's slot before
@@ -108,7 +109,7 @@ class OptimizerScalars:
 
 
 class MSETrainStep(OptimizerScalars):
-    LAUNCHES_PER_STEP = 24  # native kernels; torch adds the loss sum, one clear and one copy
+    LAUNCHES_PER_STEP = 27  # native kernels; torch adds the loss sum and one clear
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
                  process_group=None, world_rows=None):
