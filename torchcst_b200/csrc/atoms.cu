@@ -381,29 +381,33 @@ __device__ inline void write_axis_block(float *blk, const Route &r, double R, co
 }
 
 // Site values (m, dm/dmu, dm/dR on the first REACH footprint sites of each
-// axis) of the atoms of the site classes, from their records: two threads per
-// atom (one per axis), like the decode. cos / sin of pi t_j for consecutive
-// sites by rotation from site 0 (t_j = phase0 + 2 j / F): one sincospif for the
-// start and one for the step instead of one per site. Runs beside the sort,
-// which does not read the site values.
+// axis) of the atoms of the site classes, from their records: eight threads per
+// atom, four per axis, each owning SITE_RUN consecutive sites. cos / sin of
+// pi t_j for consecutive sites by rotation from the thread's first site
+// (t_j = phase0 + 2 j / F): two sincospif per thread instead of one per site.
+// Runs beside the sort, which does not read the site values.
+constexpr int SITE_PARTS = 4, SITE_RUN = REACH / SITE_PARTS;
+static_assert(SITE_RUN % 4 == 0, "whole float4 chunks per thread");
+
 __global__ void __launch_bounds__(256) site_values_kernel(Table tv) {
     pdl_wait();
     const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    const long long a = tid >> 1;
-    const int side = int(tid & 1);
+    const long long a = tid / (2 * SITE_PARTS);
+    const int side = int(tid / SITE_PARTS) & 1, part = int(tid % SITE_PARTS);
     if (a >= tv.atoms) return;
     const int4 span = tv.spans[a];
     if (span.y <= 0 || span.w <= 0 || max(span.y, span.w) > REACH) return;
+    const int F = side ? span.w : span.y, j0 = part * SITE_RUN;
+    if (j0 >= F) return;
     AxisCoef<8> ac;
     ac.load(tv.rec + a * (long long)tv.words + 4 + side * axis_words(8));
-    const int F = ac.F;
     float4 *s4 = reinterpret_cast<float4 *>(const_cast<float *>(tv.sites) + a * SITE_FLOATS +
                                             side * 3 * REACH);
     float sj, cj, sd, cd;
-    sincospif(ac.phase0, &sj, &cj);
+    sincospif(ac.phase0 + 2.0f * float(j0) / float(F), &sj, &cj);
     sincospif(2.0f / float(F), &sd, &cd);
-#pragma unroll 2
-    for (int q = 0; q < REACH / 4; ++q) {
+#pragma unroll
+    for (int q = j0 / 4; q < (j0 + SITE_RUN) / 4; ++q) {
         if (4 * q < F) {
             SiteVals v[4];
 #pragma unroll
@@ -880,7 +884,8 @@ extern "C" int tcst_decode_route(const float *p_dev, int64_t atoms, const tcst_a
     SideStreams side(st, g.nclass > 0 ? 1 : 0);
     rc = side.status();
     if (!rc && g.nclass > 0) {
-        const cudaError_t e = launch_pdl(site_values_kernel, dim3(unsigned((2 * atoms + 255) / 256)),
+        const long long threads = 2LL * SITE_PARTS * atoms;
+        const cudaError_t e = launch_pdl(site_values_kernel, dim3(unsigned((threads + 255) / 256)),
                                          dim3(256), 0, side[0], tv);
         if (e != cudaSuccess) rc = tcst_cuda_check(e, "site_values_kernel");
     }
