@@ -403,8 +403,8 @@ def rowband_config5(pg, world, rank, dev, steps, warmup):
     whole 16,384-row step over ``world`` bands), timed with CUDA events over
     ``steps`` steps, max over ranks; plus a per-phase breakdown of one more
     step (events at the phase boundaries on the main stream, max over ranks),
-    the bytes each rank receives in the all-gathers, and the time of one
-    all-gather of a dY band block measured alone."""
+    the bytes of the dX all-reduce (each rank's share of dX, summed over the
+    ranks) and the time of one such all-reduce measured alone."""
     import torch
     import torch.distributed as dist
     from torchcst_b200 import CSTAdamW, CSTLinear, ChebyshevSpec, chart_presets, kernels
@@ -447,34 +447,34 @@ def rowband_config5(pg, world, rank, dev, steps, warmup):
     phases = torch.tensor([a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])],
                           device=dev)
     step.check_status()
-    # One dY-band all-gather alone (the step's largest collective).
+    # One dX all-reduce alone (the step's largest collective: each rank's share
+    # of dX = dY_band W_band, rows x N_in fp32, summed over the ranks).
     nb = band(n, rank, world)[1]
     coll_ms = 0.0
     if pg is not None:
-        src = torch.empty(rows, nb, device=dev)
-        dst = torch.empty(world, rows, nb, device=dev)
-        dist.all_gather_into_tensor(dst, src, group=pg)
+        buf = torch.empty(rows, n, device=dev)
+        dist.all_reduce(buf, group=pg)
         torch.cuda.synchronize()
         e0.record()
         for _ in range(3):
-            dist.all_gather_into_tensor(dst, src, group=pg)
+            dist.all_reduce(buf, group=pg)
         e1.record()
         torch.cuda.synchronize()
         c = torch.tensor([e0.elapsed_time(e1) / 3], device=dev)
         dist.all_reduce(c, op=dist.ReduceOp.MAX)
         coll_ms = float(c.item())
-        del src, dst
+        del buf
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         dist.all_reduce(phases, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
-    received = 2 * (world - 1) * rows * nb * 4  # dY and dX column blocks from the others
+    dx_bytes = rows * n * 4 if world > 1 else 0
     return {"metric": EXTRA[5]["metric"], "value": 1000.0 / ms, "unit": "steps/s",
             "ms_per_step": ms, "n_gpus": world, "steps": steps, "scaling": "strong",
             "parallelism": f"rowband{world}", "band_rows": nb,
             "effective_tflops": 3 * 2.0 * rows * n * n / (ms * 1e-3) / 1e12,
             "phases_ms": {name: float(v) for (name, _), v in zip(marks[1:], phases.tolist())},
-            "allgather_bytes_received_per_step": received,
-            "allgather_dy_block_ms": coll_ms,
+            "dx_allreduce_bytes": dx_bytes,
+            "dx_allreduce_alone_ms": coll_ms,
             "gradient_allreduce_bytes": 262144 * 16 if world > 1 else 0,
             "loss": float(loss), "config": EXTRA[5]["config"]}, step
 
@@ -570,8 +570,8 @@ def run_config5(args):
                     "api": "RowBandMSETrainStep(x, target) per rank"},
             "gpu_launches": RowBandMSETrainStep.LAUNCHES_PER_STEP * args.steps,
             "phases_ms": info["phases_ms"],
-            "allgather_bytes_received_per_step": info["allgather_bytes_received_per_step"],
-            "allgather_dy_block_ms": info["allgather_dy_block_ms"],
+            "dx_allreduce_bytes": info["dx_allreduce_bytes"],
+            "dx_allreduce_alone_ms": info["dx_allreduce_alone_ms"],
             "roofline": roofline, "clocks": clocks, "loss": info["loss"]}
     if rank == 0:
         print(json.dumps(line), flush=True)
