@@ -68,7 +68,7 @@ class RowBandMSETrainStep(OptimizerScalars):
     """Eager MSE training step of one layer sharded by output-row bands over a
     process group (NCCL); ``process_group=None`` runs the whole layer as one band."""
 
-    LAUNCHES_PER_STEP = 25  # native kernels (decode, site values, sort, assembly, splits, GEMMs, pullback, scalar fetch, optimizer)
+    LAUNCHES_PER_STEP = 26  # native kernels (decode, site values, sort, window assembly, splits, GEMMs, banded pullback, scalar fetch, optimizer)
 
     def __init__(self, layer: CSTLinear, optimizer: CSTAdamW, rows: int, *, need_dx=True,
                  process_group=None):
