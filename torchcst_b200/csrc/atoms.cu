@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -37,7 +38,7 @@ namespace tcst {
 namespace {
 struct SideSet {
     std::mutex mu;
-    bool ready = false;
+    std::atomic<bool> ready{false};
     cudaStream_t s[SideStreams::MAX];
     cudaEvent_t fork, join[SideStreams::MAX];
 };
@@ -61,6 +62,27 @@ cudaError_t create_side_set(SideSet &set, int dev) {
 }
 } // namespace
 
+// Launch priority: the library's side streams run at the device's least
+// priority, every other stream (the caller's, which carries the step's
+// dependent chain) at its greatest, so that when both have blocks waiting the
+// chain's go first.
+int launch_priority(cudaStream_t stream) {
+    static int least = 0, greatest = 0;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) {
+            cudaGetLastError();
+            least = greatest = 0;
+        }
+    });
+    for (int d = 0; d < MAX_SIDE_DEVICES; ++d) {
+        if (!g_sides[d].ready.load(std::memory_order_acquire)) continue;
+        for (int i = 0; i < SideStreams::MAX; ++i)
+            if (g_sides[d].s[i] == stream) return least;
+    }
+    return greatest;
+}
+
 SideStreams::SideStreams(cudaStream_t st, int n) : st_(st) {
     // The calling stream belongs to the current device (as for every launch
     // here); cudaStreamGetDevice is not permitted while the stream captures.
@@ -78,12 +100,12 @@ SideStreams::SideStreams(cudaStream_t st, int n) : st_(st) {
     SideSet &set = g_sides[dev];
     set.mu.lock();
     set_ = &set;
-    if (!set.ready) {
+    if (!set.ready.load(std::memory_order_acquire)) {
         if ((e = create_side_set(set, dev)) != cudaSuccess) {
             rc_ = tcst_cuda_check(e, "side stream creation");
             return;
         }
-        set.ready = true;
+        set.ready.store(true, std::memory_order_release);
     }
     if ((e = cudaEventRecord(set.fork, st)) != cudaSuccess) {
         rc_ = tcst_cuda_check(e, "cudaEventRecord (fork)");
