@@ -644,7 +644,7 @@ __global__ void __launch_bounds__(SORT_THREADS) bin_count_kernel(Table tv) {
 // warp writes its running prefixes. The last CTA to finish (ticket in
 // tv.sync, which the decode reset) scans the totals into the bin starts
 // tv.offsets.
-constexpr int COL_SEGS = 8;
+constexpr int COL_SEGS = 16;
 constexpr int COL_RUN = 16; // segment lengths up to this stay in registers
 
 __global__ void __launch_bounds__(COL_SEGS * 32) bin_column_kernel(Table tv) {
