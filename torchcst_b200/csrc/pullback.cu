@@ -31,7 +31,11 @@
 
 namespace tcst {
 
-constexpr int P0_THREADS = 256;
+// Site-class pullback CTAs: 128 threads (32 quads or 16 octets per pass), about
+// the atoms a first-site bin holds in the first training steps; six CTAs fit
+// per SM (75 registers), so the 1,024 bins of a 1024 x 1024 layer take little
+// more than one wave (256 threads left most quads idle in three CTAs per SM).
+constexpr int P0_THREADS = 128;
 constexpr int PC_THREADS = 256;
 constexpr int PC_WARPS = PC_THREADS / 32;
 
