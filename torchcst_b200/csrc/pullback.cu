@@ -550,7 +550,8 @@ using namespace tcst;
 template <int E>
 static int launch_classes(const Table &tv, const AxisCfg &oa, const AxisCfg &ia, float *g_dev,
                           int64_t ldg, int split, int64_t split_stride, int b0, int bn,
-                          float4 *grad, cudaStream_t st, cudaStream_t st1, cudaStream_t st2) {
+                          float4 *grad, cudaStream_t st, cudaStream_t st1, cudaStream_t st2,
+                          cudaStream_t st3) {
     const BinGeom &geo = tv.geom;
     static bool configured = false;
     if (!configured) {
@@ -572,8 +573,8 @@ static int launch_classes(const Table &tv, const AxisCfg &oa, const AxisCfg &ia,
                              split, split_stride, b0, bn, grad));
         TCST_CUDA(cudaGetLastError());
     }
-    // The two cached classes share a stream: few atoms reach them early in
-    // training.
+    // The two cached classes on streams of their own: few atoms reach them early
+    // in training, but later each takes as long as the site classes together.
     if (geo.nclass > 2) {
         TCST_CUDA(launch_pdl(pullback_class_kernel<64, E>, dim3(unsigned(geo.tr[2] * geo.tc[2])),
                              dim3(PC_THREADS), class_smem<64, E>(), st2, tv, 2, oa.sites, ia.sites,
@@ -583,7 +584,7 @@ static int launch_classes(const Table &tv, const AxisCfg &oa, const AxisCfg &ia,
     if (geo.nclass > 3) {
         TCST_CUDA(launch_pdl(pullback_class_kernel<128, E>,
                              dim3(unsigned(geo.tr[3] * geo.tc[3])), dim3(PC_THREADS),
-                             class_smem<128, E>(), st2, tv, 3, oa.sites, ia.sites, g_dev, ldg,
+                             class_smem<128, E>(), st3, tv, 3, oa.sites, ia.sites, g_dev, ldg,
                              split, split_stride, b0, bn, grad));
         TCST_CUDA(cudaGetLastError());
     }
@@ -641,14 +642,15 @@ static int pullback(const char *name, const void *atom_table_dev, int64_t atoms,
     }
     // The class kernels, the owner-pair kernels and the wide kernel write
     // disjoint atoms' gradients: they run side by side on four side streams
-    // beside the class-0 kernel, joined before returning.
+    // beside the class-0 kernel (class 3 ahead of the wide kernel on the fourth),
+    // joined before returning.
     SideStreams side(st, 4);
     if ((rc = side.status())) return rc;
     if (geo.nclass > 0) {
         rc = geo.fe == TS ? launch_classes<TS>(tv, oa, ia, g_dev, ldg, split, split_stride, b0,
-                                               bn, grad, st, side[0], side[1])
+                                               bn, grad, st, side[0], side[1], side[3])
                           : launch_classes<2 * TS>(tv, oa, ia, g_dev, ldg, split, split_stride,
-                                                   b0, bn, grad, st, side[0], side[1]);
+                                                   b0, bn, grad, st, side[0], side[1], side[3]);
     }
     // Atoms of active owner pairs (their grads), then coarse classes, inactive
     // pair bins and invalid atoms (all atoms when unbinned): their range starts
